@@ -1,0 +1,471 @@
+"""Per-rank executor: model, KV pools, step metadata, CUDA graphs, sampling.
+
+Reference: ``llmserve/engine/model_runner.py`` (init ``:30-74``, RPC ``:87-115``, warm-up and KV
+sizing ``:186-229``, metadata ``:258-338``, graphs ``:383-418``).  Differences by design:
+
+* KV pools are ``k/v_cache[L, blocks, kv_heads, block_size, head_dim]`` (see ``ops.attention``)
+  plus an EAGLE3 draft pool with the same block ids;
+* prefill metadata carries per-sequence key lengths for the paged varlen kernel and the LM-head
+  row selection; every prefill reads K/V from the pool (one kernel path for plain, chunked,
+  prefix-cached and verify batches);
+* greedy sampling is vocab-parallel (per-shard max/index, then a 12-byte-per-row exchange); other
+  samplers receive full logits on every rank and rank 0's choice is broadcast;
+* the sampler set on rank 0 (``runner.sampler = ...``, as the benchmarks do) is mirrored to the
+  workers through the RPC channel;
+* decode CUDA graphs also hold the LM head, so one replay yields the logit shard.
+"""
+import os
+
+import numpy as np
+import torch
+
+from llmserve_b200.config import Config
+from llmserve_b200.engine.rpc import RpcChannel, RpcTimeout
+from llmserve_b200.engine.scheduler import SchedulerOutput
+from llmserve_b200.engine.sequence import Sequence
+from llmserve_b200.models.qwen3 import Qwen3ForCausalLM
+from llmserve_b200.ops import attention as attn_ops
+from llmserve_b200.ops import sampling as sampling_ops
+from llmserve_b200.parallel import state as tp
+from llmserve_b200.utils.context import get_context, reset_context, set_context
+from llmserve_b200.utils.loader import init_dummy_weights, load_model
+
+
+class Sampler:
+    """Temperature sampling by exponential race (``llmserve/layers/sampler.py``)."""
+    is_greedy = False
+
+    def __init__(self, seed: int = 0):
+        self.seed = seed
+        self.calls = 0
+
+    def __call__(self, logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tensor:
+        self.calls += 1
+        return sampling_ops.sample(logits, temperatures, self.seed * 1000003 + self.calls)
+
+
+class GreedySampler:
+    """Argmax sampler; on a tensor-parallel runner it never gathers full logits."""
+    is_greedy = True
+
+    def __call__(self, logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tensor:
+        return sampling_ops.argmax(logits)
+
+
+def _to_device(values, dtype, device) -> torch.Tensor:
+    t = torch.as_tensor(values, dtype=dtype)
+    if device.type == "cuda":
+        return t.pin_memory().to(device, non_blocking=True)
+    return t
+
+
+class ModelRunner:
+
+    def __init__(self, config: Config, rank: int, channel_name: str | None = None, parent_pid: int | None = None):
+        self.config = config
+        hf = config.hf_config
+        self.hf_config = hf
+        self.block_size = config.kvcache_block_size
+        self.enforce_eager = config.enforce_eager
+        self.world_size = config.tensor_parallel_size
+        self.rank = rank
+        self.is_cuda = config.device == "cuda"
+        if self.is_cuda:
+            self.device = torch.device("cuda", config.device_offset + rank)
+            torch.cuda.set_device(self.device)
+        else:
+            self.device = torch.device("cpu")
+        tp.init_tensor_parallel(rank, self.world_size, config.distributed_init_method, self.device,
+                                config.comm_timeout_s)
+        self.dtype = hf.dtype if self.is_cuda else torch.float32
+        self.channel = None
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+
+        prev_dtype = torch.get_default_dtype()
+        torch.set_default_dtype(self.dtype)
+        with torch.device(self.device):
+            self.model = Qwen3ForCausalLM(hf, quant_config=config.quant_config)
+        torch.set_default_dtype(prev_dtype)
+        if config.load_format == "dummy":
+            init_dummy_weights(self.model, seed=config.seed)
+        else:
+            load_model(self.model, config.model)
+        self.model.eval()
+
+        self._sampler = Sampler(config.seed)
+        from llmserve_b200.engine.speculative_executor import SpeculativeExecutor
+        self.spec = SpeculativeExecutor(self)
+        self.draft_model = self.spec.load_draft_model()
+        self.speculative_gamma = config.speculative_gamma
+        self.speculative_tree_nodes = config.speculative_tree_nodes
+        self.speculative_accept_mode = config.speculative_accept_mode
+        self.speculative_trace = config.speculative_trace
+
+        if self.is_cuda and self.world_size > 1 and config.fused_collectives:
+            from llmserve_b200.parallel.comm import FusedComm
+            tp.set_fused_comm(FusedComm.create(self.device, hf.hidden_size, config.max_num_batched_tokens,
+                                               timeout_s=config.comm_timeout_s))
+
+        self.graphs = {}
+        self.graph_pool = None
+        self.decode_workspace = None
+        self.warmup_model()
+        self.allocate_kv_cache()
+        if self.is_cuda and not self.enforce_eager:
+            self.capture_cudagraph()
+
+        if self.world_size > 1:
+            name = channel_name or "llmserve_b200"
+            if rank == 0:
+                self.channel = RpcChannel(name, self.world_size - 1, create=True)
+                tp.barrier()
+            else:
+                tp.barrier()
+                self.channel = RpcChannel(name, self.world_size - 1, create=False)
+                self._parent_pid = parent_pid or os.getppid()
+                self.loop()
+
+    # ---- sampler (settable on rank 0, mirrored to the workers) -------------------------------
+    @property
+    def sampler(self):
+        return self._sampler
+
+    @sampler.setter
+    def sampler(self, value):
+        if self.channel is not None and self.rank == 0:
+            self.channel.send("_set_sampler", value)
+        self._sampler = value
+
+    def _set_sampler(self, value):
+        self._sampler = value
+
+    # ---- control plane -----------------------------------------------------------------------
+    def exit(self):
+        if self.channel is not None and self.rank == 0:
+            try:
+                self.channel.wait_acks(self.config.comm_timeout_s)
+            except Exception:
+                pass
+        self.graphs = {}
+        self.graph_pool = None
+        if self.is_cuda:
+            torch.cuda.synchronize()
+        if self.world_size > 1:
+            try:
+                tp.barrier()
+            except Exception:
+                pass
+        if self.channel is not None:
+            self.channel.close()
+        tp.destroy_tensor_parallel()
+
+    def loop(self):
+        worker = self.rank - 1
+        while True:
+            try:
+                method, args = self.channel.recv(worker, idle_timeout_s=5.0, parent_pid=self._parent_pid)
+            except RpcTimeout:
+                break
+            try:
+                getattr(self, method)(*args)
+                self.channel.ack(worker, True)
+            except Exception as e:
+                self.channel.ack(worker, False, f"{type(e).__name__}: {e}")
+                raise
+            if method == "exit":
+                break
+
+    def call(self, method: str, *args):
+        if self.channel is not None and self.rank == 0:
+            self.channel.check_workers()
+            self.channel.send(method, *args)
+        return getattr(self, method)(*args)
+
+    # ---- memory ------------------------------------------------------------------------------
+    def _kv_block_bytes(self) -> int:
+        hf = self.hf_config
+        nkv = hf.num_key_value_heads // self.world_size
+        esize = torch.tensor([], dtype=self.dtype).element_size()
+        per = 2 * hf.num_hidden_layers * self.block_size * nkv * hf.head_dim * esize
+        if self.draft_model is not None:
+            d = self.draft_model
+            per += 2 * self.block_size * d.num_kv_heads * d.head_dim * esize
+        return per
+
+    def _bind_pools(self, k_cache, v_cache, dk=None, dv=None):
+        empty = torch.tensor([])
+        for i, layer in enumerate(self.model.model.layers):
+            layer.self_attn.attn.k_cache = k_cache[i] if k_cache is not None else empty
+            layer.self_attn.attn.v_cache = v_cache[i] if v_cache is not None else empty
+        if self.draft_model is not None:
+            self.draft_model.bind_kv_cache(dk if dk is not None else empty, dv if dv is not None else empty)
+
+    @torch.inference_mode()
+    def warmup_model(self):
+        """One maximal prefill on a scratch pool to measure peak activation memory."""
+        self.warmup_pool_bytes = 0
+        if not self.is_cuda:
+            return
+        torch.cuda.empty_cache()
+        torch.cuda.reset_peak_memory_stats(self.device)
+        cfg, hf = self.config, self.hf_config
+        seq_len = min(cfg.max_num_batched_tokens, cfg.max_model_len)
+        num_seqs = max(1, min(cfg.max_num_batched_tokens // seq_len, cfg.max_num_seqs))
+        need = -(-seq_len // self.block_size)
+        nkv = hf.num_key_value_heads // self.world_size
+        shape = (hf.num_hidden_layers, need * num_seqs, nkv, self.block_size, hf.head_dim)
+        k = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        v = torch.zeros_like(k)
+        dk = dv = None
+        if self.draft_model is not None:
+            d = self.draft_model
+            dk = torch.zeros(need * num_seqs, d.num_kv_heads, self.block_size, d.head_dim,
+                             dtype=self.dtype, device=self.device)
+            dv = torch.zeros_like(dk)
+        self.warmup_pool_bytes = sum(t.numel() * t.element_size() for t in (k, v, dk, dv) if t is not None)
+        self._bind_pools(k, v, dk, dv)
+        seqs = [Sequence([0] * seq_len) for _ in range(num_seqs)]
+        for i, s in enumerate(seqs):
+            s.num_scheduled_tokens = seq_len
+            s.block_table = list(range(i * need, (i + 1) * need))
+        self.run(SchedulerOutput(seqs, seqs, [], seq_len * num_seqs), warmup=True)
+        self.spec.clear_all()
+        torch.cuda.synchronize()
+        self._bind_pools(None, None)
+        del k, v, dk, dv
+        torch.cuda.empty_cache()
+
+    def allocate_kv_cache(self):
+        cfg, hf = self.config, self.hf_config
+        block_bytes = self._kv_block_bytes()
+        if self.is_cuda:
+            free, total = torch.cuda.mem_get_info(self.device)
+            used = total - free
+            stats = torch.cuda.memory_stats(self.device)
+            peak = stats["allocated_bytes.all.peak"] - self.warmup_pool_bytes
+            current = stats["allocated_bytes.all.current"]
+            budget = int(total * cfg.gpu_memory_utilization - used - peak + current)
+            blocks = budget // block_bytes
+            if cfg.num_kvcache_blocks > 0:
+                blocks = min(blocks, cfg.num_kvcache_blocks)
+            if self.world_size > 1:
+                t = torch.tensor([blocks], device=self.device)
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+                blocks = int(t.item())
+        else:
+            blocks = cfg.num_kvcache_blocks if cfg.num_kvcache_blocks > 0 else 64
+        if cfg.max_kvcache_blocks > 0:
+            blocks = min(blocks, cfg.max_kvcache_blocks)
+        if blocks <= 0:
+            raise RuntimeError("no memory left for the KV cache")
+        cfg.num_kvcache_blocks = blocks
+        nkv = hf.num_key_value_heads // self.world_size
+        shape = (hf.num_hidden_layers, blocks, nkv, self.block_size, hf.head_dim)
+        self.k_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        self.v_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        self.draft_k_cache = self.draft_v_cache = None
+        if self.draft_model is not None:
+            d = self.draft_model
+            dshape = (blocks, d.num_kv_heads, self.block_size, d.head_dim)
+            self.draft_k_cache = torch.zeros(dshape, dtype=self.dtype, device=self.device)
+            self.draft_v_cache = torch.zeros(dshape, dtype=self.dtype, device=self.device)
+        self._bind_pools(self.k_cache, self.v_cache, self.draft_k_cache, self.draft_v_cache)
+        if self.is_cuda:
+            max_ctx = cfg.max_model_len + cfg.speculative_gamma + 16
+            heads = max(hf.num_attention_heads // self.world_size,
+                        self.draft_model.num_heads if self.draft_model is not None else 0)
+            self.decode_workspace = attn_ops.DecodeWorkspace(
+                max(cfg.max_num_seqs, 16), heads, hf.head_dim, max_ctx, self.device)
+
+    def get_memory_metrics(self) -> dict:
+        seen, model_bytes = set(), 0
+        for t in list(self.model.parameters()) + list(self.model.buffers()):
+            if t.numel() == 0:
+                continue
+            key = (str(t.device), t.untyped_storage().data_ptr())
+            if key not in seen:
+                seen.add(key)
+                model_bytes += t.untyped_storage().nbytes()
+        kv_bytes = (self.k_cache.numel() + self.v_cache.numel()) * self.k_cache.element_size()
+        out = {
+            "model_runtime_bytes": model_bytes,
+            "kv_cache_bytes": kv_bytes,
+            "kv_block_bytes": kv_bytes // max(self.config.num_kvcache_blocks, 1),
+        }
+        if self.is_cuda:
+            _, total = torch.cuda.mem_get_info(self.device)
+            out.update({
+                "cuda_allocated_bytes": torch.cuda.memory_allocated(self.device),
+                "cuda_reserved_bytes": torch.cuda.memory_reserved(self.device),
+                "cuda_peak_allocated_bytes": torch.cuda.max_memory_allocated(self.device),
+                "cuda_total_bytes": total,
+            })
+        return out
+
+    # ---- step metadata -----------------------------------------------------------------------
+    def prepare_block_tables(self, seqs: list[Sequence]) -> torch.Tensor:
+        width = max(1, max(len(s.block_table) for s in seqs))
+        rows = np.zeros((len(seqs), width), dtype=np.int32)
+        for i, s in enumerate(seqs):
+            rows[i, :len(s.block_table)] = s.block_table
+        self.h2d_bytes += rows.nbytes
+        return _to_device(rows, torch.int32, self.device)
+
+    def _slots(self, seq: Sequence, start: int, end: int) -> np.ndarray:
+        pos = np.arange(start, end, dtype=np.int64)
+        table = np.asarray(seq.block_table, dtype=np.int64)
+        return table[pos // self.block_size] * self.block_size + pos % self.block_size
+
+    def prepare_prefill(self, seqs: list[Sequence], decode_seqs: list[Sequence] | None = None):
+        decode_ids = {s.seq_id for s in (decode_seqs or [])}
+        ids, pos, slots = [], [], []
+        cu_q, cu_k, lens_k, last = [0], [0], [], []
+        max_q = max_k = 0
+        for s in seqs:
+            if s.seq_id in decode_ids:
+                start, q = len(s) - 1, 1
+            else:
+                start, q = min(s.num_cached_tokens, len(s) - 1), s.num_scheduled_tokens
+            end = start + q
+            ids.extend(s.token_ids[start:end])
+            pos.extend(range(start, end))
+            slots.append(self._slots(s, start, end))
+            cu_q.append(cu_q[-1] + q)
+            cu_k.append(cu_k[-1] + end)
+            lens_k.append(end)
+            last.append(cu_q[-1] - 1)
+            max_q, max_k = max(max_q, q), max(max_k, end)
+        d = self.device
+        slot_arr = np.concatenate(slots)
+        self.h2d_bytes += 16 * len(ids) + 4 * len(slot_arr) + 16 * len(seqs) + 8
+        set_context(
+            True,
+            cu_seqlens_q=_to_device(cu_q, torch.int32, d),
+            cu_seqlens_k=_to_device(cu_k, torch.int32, d),
+            max_seqlen_q=max_q, max_seqlen_k=max_k,
+            slot_mapping=_to_device(slot_arr, torch.int32, d),
+            block_tables=self.prepare_block_tables(seqs),
+            seqlens_k=_to_device(lens_k, torch.int32, d),
+            last_token_indices=_to_device(last, torch.int64, d),
+            decode_workspace=self.decode_workspace,
+        )
+        return _to_device(ids, torch.int64, d), _to_device(pos, torch.int64, d)
+
+    def prepare_decode(self, seqs: list[Sequence]):
+        n = len(seqs)
+        ids = np.empty(n, dtype=np.int64)
+        pos = np.empty(n, dtype=np.int64)
+        slots = np.empty(n, dtype=np.int32)
+        lens = np.empty(n, dtype=np.int32)
+        for i, s in enumerate(seqs):
+            L = len(s)
+            ids[i], pos[i], lens[i] = s.last_token, L - 1, L
+            slots[i] = s.block_table[(L - 1) // self.block_size] * self.block_size + (L - 1) % self.block_size
+        d = self.device
+        self.h2d_bytes += ids.nbytes + pos.nbytes + slots.nbytes + lens.nbytes
+        set_context(False, slot_mapping=_to_device(slots, torch.int32, d), context_lens=_to_device(lens, torch.int32, d),
+                    block_tables=self.prepare_block_tables(seqs), decode_workspace=self.decode_workspace)
+        return _to_device(ids, torch.int64, d), _to_device(pos, torch.int64, d)
+
+    def prepare_sample(self, seqs: list[Sequence]) -> torch.Tensor:
+        self.h2d_bytes += 4 * len(seqs)
+        return _to_device([s.temperature for s in seqs], torch.float32, self.device)
+
+    # ---- forward -----------------------------------------------------------------------------
+    @torch.inference_mode()
+    def run_model(self, input_ids, positions, is_prefill: bool) -> torch.Tensor:
+        """Hidden states -> this rank's logit shard (decode uses a CUDA graph when captured)."""
+        bs = input_ids.shape[0]
+        if is_prefill or not self.graphs or bs > self.graph_bs[-1]:
+            return self.model.compute_logits(self.model(input_ids, positions))
+        ctx = get_context()
+        gbs = next(x for x in self.graph_bs if x >= bs)
+        v = self.graph_vars
+        v["input_ids"][:bs].copy_(input_ids)
+        v["positions"][:bs].copy_(positions)
+        v["slot_mapping"].fill_(-1)
+        v["slot_mapping"][:bs].copy_(ctx.slot_mapping)
+        v["context_lens"].fill_(1)
+        v["context_lens"][:bs].copy_(ctx.context_lens)
+        width = ctx.block_tables.shape[1]
+        v["block_tables"][:bs, :width].copy_(ctx.block_tables)
+        self.graphs[gbs].replay()
+        return v["logits"][:bs]
+
+    def sample_tokens(self, logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tensor:
+        """Token ids on every rank from the local logit shard."""
+        if getattr(self.sampler, "is_greedy", False):
+            vals, idx = sampling_ops.local_argmax(logits)
+            return tp.vocab_parallel_argmax(vals, idx, self.model.lm_head.vocab_start)
+        full = tp.gather_logits(logits)
+        tokens = self.sampler(full, temperatures).to(torch.int64).reshape(-1)
+        return tp.broadcast(tokens.contiguous(), 0)
+
+    @torch.inference_mode()
+    def run(self, scheduler_output: SchedulerOutput, warmup: bool = False) -> list[int] | None:
+        seqs = scheduler_output.scheduled_seqs
+        prefill, decodes = scheduler_output.prefill_seqs, scheduler_output.decode_seqs
+        is_prefill = bool(prefill)
+        input_ids, positions = self.prepare_prefill(seqs, decodes) if is_prefill else self.prepare_decode(decodes)
+        temperatures = self.prepare_sample(seqs)
+        use_draft = self.draft_model is not None and not warmup
+        if use_draft:
+            self.spec.note_plain_step(decodes)
+        if is_prefill and use_draft:
+            hidden, aux = self.model.forward_with_eagle3_aux(input_ids, positions)
+            logits = self.model.compute_logits(hidden)
+        else:
+            aux = None
+            logits = self.run_model(input_ids, positions, is_prefill)
+        tokens = self.sample_tokens(logits, temperatures)
+        token_list = tokens.tolist()
+        self.d2h_bytes += 8 * len(token_list)
+        if aux is not None:
+            self.spec.after_prefill(seqs, decodes, aux, token_list)
+        reset_context()
+        return token_list if self.rank == 0 else None
+
+    # ---- CUDA graphs -------------------------------------------------------------------------
+    @torch.inference_mode()
+    def capture_cudagraph(self):
+        cfg = self.config
+        max_bs = min(cfg.max_num_seqs, 512)
+        max_blocks = -(-(cfg.max_model_len + cfg.speculative_gamma + 2) // self.block_size)
+        d = self.device
+        v = {
+            "input_ids": torch.zeros(max_bs, dtype=torch.int64, device=d),
+            "positions": torch.zeros(max_bs, dtype=torch.int64, device=d),
+            "slot_mapping": torch.full((max_bs,), -1, dtype=torch.int32, device=d),
+            "context_lens": torch.ones(max_bs, dtype=torch.int32, device=d),
+            "block_tables": torch.zeros(max_bs, max_blocks, dtype=torch.int32, device=d),
+            "logits": torch.zeros(max_bs, self.model.lm_head.shard_size, dtype=self.dtype, device=d),
+        }
+        self.graph_bs = [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
+        self.graphs, self.graph_pool = {}, None
+        for bs in reversed(self.graph_bs):
+            g = torch.cuda.CUDAGraph()
+            set_context(False, slot_mapping=v["slot_mapping"][:bs], context_lens=v["context_lens"][:bs],
+                        block_tables=v["block_tables"][:bs], decode_workspace=self.decode_workspace)
+            v["logits"][:bs] = self.model.compute_logits(self.model(v["input_ids"][:bs], v["positions"][:bs]))
+            with torch.cuda.graph(g, self.graph_pool):
+                v["logits"][:bs] = self.model.compute_logits(self.model(v["input_ids"][:bs], v["positions"][:bs]))
+            if self.graph_pool is None:
+                self.graph_pool = g.pool()
+            self.graphs[bs] = g
+            torch.cuda.synchronize()
+            reset_context()
+        self.graph_vars = v
+
+    # ---- speculative entry points (called through the RPC by name) -----------------------------
+    def run_speculative_batch(self, seqs):
+        return self.spec.run_speculative_batch(seqs)
+
+    def run_speculative_single(self, seq):
+        return self.spec.run_speculative_batch([seq])[0]
+
+    def run_speculative_tree_single(self, seq):
+        return self.spec.run_speculative_tree_single(seq)
+
+    def clear_speculative_state(self, seq_ids):
+        self.spec.clear_speculative_state(seq_ids)

@@ -1,0 +1,135 @@
+"""Paged attention over a KV pool laid out ``[num_blocks, kv_heads, block_size, head_dim]``.
+
+One layout serves every path: a 64-key tile of one head is a contiguous 16 KiB run, so the
+prefill kernel streams it with bulk copies, and a whole block of a layer is one contiguous
+region for the prefill->decode KV push.
+
+* ``decode_attention``  -- one query token per sequence (``flash_attn_with_kvcache`` in the
+  reference, ``llmserve/layers/attention.py:130-132``).  sm_100a split-KV kernel with the query
+  heads of one KV head packed together (GQA), followed by a log-sum-exp combine.
+* ``prefill_attention`` -- varlen causal attention of a query chunk against the paged keys of
+  its sequence (``flash_attn_varlen_func(..., block_table)`` in the reference, ``:121-126``):
+  covers plain prefill, chunked prefill, prefix-cache hits and the packed EAGLE3 verify.
+  Query ``j`` of a chunk of ``q_len`` against ``k_len`` keys sees keys ``< k_len - q_len + j + 1``.
+* ``tree_attention``    -- EAGLE3 tree verify: prefix keys from the pool (all visible) plus the
+  tree nodes' own keys under an ancestor mask (``attention.py:77-109`` of the reference).
+"""
+import math
+
+import torch
+
+from llmserve_b200.ops._ext import C
+
+
+def _gather_pages(cache: torch.Tensor, block_table: torch.Tensor, length: int) -> torch.Tensor:
+    """[num_blocks, nkv, bs, hd] -> [length, nkv, hd] for one sequence."""
+    bs = cache.shape[2]
+    nblk = -(-length // bs)
+    pages = cache[block_table[:nblk].long()]
+    return pages.permute(0, 2, 1, 3).reshape(nblk * bs, cache.shape[1], cache.shape[3])[:length]
+
+
+def _attend(q, k, v, scale, mask=None):
+    """q [Lq, nh, hd], k/v [Lk, nkv, hd] -> [Lq, nh, hd] (fp32 math)."""
+    group = q.shape[1] // k.shape[1]
+    qf = q.float().transpose(0, 1)
+    kf = k.float().repeat_interleave(group, dim=1).transpose(0, 1)
+    vf = v.float().repeat_interleave(group, dim=1).transpose(0, 1)
+    s = torch.matmul(qf, kf.transpose(1, 2)) * scale
+    if mask is not None:
+        s = s.masked_fill(~mask.unsqueeze(0), float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.matmul(p, vf).transpose(0, 1).to(q.dtype)
+
+
+def decode_attention_ref(q, k_cache, v_cache, block_tables, context_lens, scale):
+    out = torch.empty_like(q)
+    for b in range(q.shape[0]):
+        n = int(context_lens[b])
+        k = _gather_pages(k_cache, block_tables[b], n)
+        v = _gather_pages(v_cache, block_tables[b], n)
+        out[b] = _attend(q[b:b + 1], k, v, scale)[0]
+    return out
+
+
+def prefill_attention_ref(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, scale):
+    out = torch.empty_like(q)
+    cu_q = cu_seqlens_q.tolist()
+    for i in range(len(cu_q) - 1):
+        qs, qe = cu_q[i], cu_q[i + 1]
+        lq, lk = qe - qs, int(seqlens_k[i])
+        k = _gather_pages(k_cache, block_tables[i], lk)
+        v = _gather_pages(v_cache, block_tables[i], lk)
+        qpos = torch.arange(lk - lq, lk).unsqueeze(1)
+        mask = torch.arange(lk).unsqueeze(0) <= qpos
+        out[qs:qe] = _attend(q[qs:qe], k, v, scale, mask.to(q.device))
+    return out
+
+
+def tree_attention_ref(q, k_cache, v_cache, block_table, prefix_len, tree_k, tree_v, tree_mask, scale):
+    pk = _gather_pages(k_cache, block_table, prefix_len)
+    pv = _gather_pages(v_cache, block_table, prefix_len)
+    k = torch.cat([pk, tree_k.to(pk.dtype)], 0)
+    v = torch.cat([pv, tree_v.to(pv.dtype)], 0)
+    mask = torch.cat([torch.ones(q.shape[0], prefix_len, dtype=torch.bool, device=q.device),
+                      tree_mask.to(q.device, torch.bool)], dim=1)
+    return _attend(q, k, v, scale, mask)
+
+
+DECODE_PARTITION = 512   # keys per split of the split-KV decode kernel
+
+
+class DecodeWorkspace:
+    """Scratch for split-KV partial results, sized once for the largest batch so decode kernels
+    can be captured in CUDA graphs (the kernel itself allocates nothing)."""
+
+    def __init__(self, max_batch: int, num_heads: int, head_dim: int, max_context: int, device):
+        self.max_batch = max_batch
+        self.max_splits = max(1, -(-max_context // DECODE_PARTITION))
+        self.partial_out = torch.empty(max_batch * num_heads * self.max_splits * head_dim,
+                                       dtype=torch.float32, device=device)
+        self.partial_ml = torch.empty(max_batch * num_heads * self.max_splits * 2,
+                                      dtype=torch.float32, device=device)
+
+
+def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, workspace=None):
+    if not q.is_cuda:
+        return decode_attention_ref(q, k_cache, v_cache, block_tables, context_lens, scale)
+    B, nh, hd = q.shape
+    cap = block_tables.shape[1] * k_cache.shape[2]
+    if workspace is None or workspace.max_batch < B or workspace.max_splits * DECODE_PARTITION < cap:
+        workspace = DecodeWorkspace(B, nh, hd, cap, q.device)
+    out = torch.empty_like(q)
+    C().decode_attention(out, q.contiguous(), k_cache, v_cache, block_tables, context_lens, float(scale),
+                         workspace.partial_out, workspace.partial_ml, workspace.max_splits, DECODE_PARTITION)
+    return out
+
+
+def prefill_attention(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, scale, max_seqlen_q: int):
+    if not q.is_cuda:
+        return prefill_attention_ref(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, scale)
+    out = torch.empty_like(q)
+    C().prefill_attention(out, q.contiguous(), k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables,
+                          float(scale), int(max_seqlen_q))
+    return out
+
+
+def tree_attention(q, k_cache, v_cache, block_table, prefix_len, tree_k, tree_v, tree_mask, scale,
+                   mask_bits=None):
+    """``tree_mask [n_q, n_tree]`` bool; on CUDA the kernel takes one int32 ancestor bitmask per
+    query row (``mask_bits``, at most 32 tree nodes)."""
+    if not q.is_cuda:
+        return tree_attention_ref(q, k_cache, v_cache, block_table, prefix_len, tree_k, tree_v,
+                                  tree_mask, scale)
+    if mask_bits is None:
+        n = tree_mask.shape[1]
+        w = 1 << torch.arange(n, dtype=torch.int64, device=q.device)
+        mask_bits = (tree_mask.to(q.device).long() * w).sum(1).to(torch.int32)
+    out = torch.empty_like(q)
+    C().tree_attention(out, q.contiguous(), k_cache, v_cache, block_table.to(torch.int32), int(prefix_len),
+                       tree_k.contiguous(), tree_v.contiguous(), mask_bits, float(scale))
+    return out
+
+
+def default_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,75 @@
+"""Dense bf16 linear layers on the sm_100a tensor cores (tcgen05 + TMEM, operands by TMA).
+
+``y[T, N] = x[T, K] @ w[N, K]^T``.  The kernel computes the transposed product: weight rows are
+the UMMA M dimension (128 per tile) and tokens are the N dimension (16..256), so a decode batch
+of a few dozen tokens still fills a 128-row tensor-core tile and the weight stream -- which sets
+decode speed -- is read exactly once.  When there are fewer output tiles than SMs, K is split
+across CTAs; the fp32 partials are then reduced by a kernel that also applies the layer's
+post-op (plain store, residual add + RMSNorm, or the tensor-parallel all-reduce in
+``llmserve_b200.parallel.fused``).  The reference runs these through cuBLAS
+(``F.linear`` in ``llmserve/layers/linear.py:57``).
+"""
+import torch
+import torch.nn.functional as F
+
+from llmserve_b200.ops._ext import C
+
+NUM_SMS = 148
+TILE_M = 128          # weight rows per CTA
+TILE_K = 64           # K elements per pipeline stage (128 B rows -> 128B swizzle)
+MAX_TILE_T = 256      # tokens per CTA (UMMA N limit)
+
+
+def choose_splits(T: int, N: int, K: int) -> int:
+    """Split K until the grid covers the SMs about once (weights are streamed once either way)."""
+    tiles = (-(-N // TILE_M)) * (-(-T // MAX_TILE_T))
+    k_tiles = -(-K // TILE_K)
+    splits = 1
+    while tiles * splits * 2 <= NUM_SMS * 1.25 and k_tiles // (splits * 2) >= 4:
+        splits *= 2
+    return splits
+
+
+def linear_ref(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    return F.linear(x, w, bias)
+
+
+_EMPTY = {}
+
+
+def _empty(device, dtype):
+    key = (device, dtype)
+    if key not in _EMPTY:
+        _EMPTY[key] = torch.empty(0, device=device, dtype=dtype)
+    return _EMPTY[key]
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    if not x.is_cuda:
+        return linear_ref(x, w, bias)
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    T, K = x2.shape
+    N = w.shape[0]
+    out = torch.empty(T, N, dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out.view(*x.shape[:-1], N)
+    splits = choose_splits(T, N, K)
+    if splits == 1:
+        C().gemm_bf16(out, x2, w, _empty(x.device, torch.float32), 1)
+    else:
+        partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
+        C().gemm_bf16(_empty(x.device, x.dtype), x2, w, partials, splits)
+        C().splitk_reduce(out, partials)
+    if bias is not None:
+        out += bias
+    return out.view(*x.shape[:-1], N)
+
+
+def linear_partials(x: torch.Tensor, w: torch.Tensor, splits: int, partials: torch.Tensor | None = None):
+    """fp32 split-K partials ``[splits, T, N]`` (not reduced)."""
+    T, K = x.shape
+    N = w.shape[0]
+    if partials is None:
+        partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
+    C().gemm_bf16(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits)
+    return partials
