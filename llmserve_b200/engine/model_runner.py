@@ -66,6 +66,7 @@ class ModelRunner:
         hf = config.hf_config
         self.hf_config = hf
         self.block_size = config.kvcache_block_size
+        Sequence.block_size = config.kvcache_block_size
         self.enforce_eager = config.enforce_eager
         self.world_size = config.tensor_parallel_size
         self.rank = rank
@@ -75,6 +76,9 @@ class ModelRunner:
             torch.cuda.set_device(self.device)
         else:
             self.device = torch.device("cpu")
+            if self.world_size > 1:
+                # CPU tier: split the cores between ranks instead of oversubscribing them
+                torch.set_num_threads(max(1, (os.cpu_count() or 1) // self.world_size))
         tp.init_tensor_parallel(rank, self.world_size, config.distributed_init_method, self.device,
                                 config.comm_timeout_s)
         self.dtype = hf.dtype if self.is_cuda else torch.float32
@@ -167,14 +171,16 @@ class ModelRunner:
                 method, args = self.channel.recv(worker, idle_timeout_s=5.0, parent_pid=self._parent_pid)
             except RpcTimeout:
                 break
+            if method == "exit":
+                self.channel.ack(worker, True)
+                self.exit()
+                break
             try:
                 getattr(self, method)(*args)
                 self.channel.ack(worker, True)
             except Exception as e:
                 self.channel.ack(worker, False, f"{type(e).__name__}: {e}")
                 raise
-            if method == "exit":
-                break
 
     def call(self, method: str, *args):
         if self.channel is not None and self.rank == 0:
