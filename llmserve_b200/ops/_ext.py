@@ -26,3 +26,31 @@ def available() -> bool:
         return True
     except RuntimeError:
         return False
+
+
+_STATUS = {}
+
+ERROR_NAMES = {1: "TMA stage wait timed out", 2: "free-stage wait timed out", 3: "accumulator wait timed out",
+               4: "peer flag wait timed out", 5: "out-of-range slot/block index skipped"}
+
+
+def status(device):
+    """Per-device int32 word in which kernels record a bounded-wait timeout or a skipped bad
+    index instead of trapping; read it with :func:`check_status`."""
+    import torch
+    key = str(device)
+    t = _STATUS.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS[key] = t
+    return t
+
+
+def check_status(device, reset: bool = True):
+    """Raise if a kernel on ``device`` recorded an error since the last check (syncs the device)."""
+    t = status(device)
+    code = int(t.item())
+    if code and reset:
+        t.zero_()
+    if code:
+        raise RuntimeError(f"llmserve_b200 kernel error {code}: {ERROR_NAMES.get(code, 'unknown')}")

@@ -1,0 +1,48 @@
+// Python bindings of the llmserve_b200 sm_100a kernels (module llmserve_b200._C).
+#include <torch/extension.h>
+
+namespace lsb {
+void rms_norm(at::Tensor out, at::Tensor x, at::Tensor w, double eps);
+void add_rms_norm(at::Tensor out, at::Tensor res_out, at::Tensor x, at::Tensor residual, at::Tensor w, double eps);
+void silu_and_mul(at::Tensor out, at::Tensor x);
+void embedding(at::Tensor out, at::Tensor ids, at::Tensor table, at::Tensor status);
+void qkv_rope(at::Tensor q_out, at::Tensor k_out, at::Tensor qkv, at::Tensor positions, at::Tensor cos_sin,
+              at::Tensor q_w, at::Tensor k_w, double eps, at::Tensor k_cache, at::Tensor v_cache,
+              at::Tensor slot_mapping, int64_t nh, int64_t nkv, int64_t hd, bool store, at::Tensor status);
+void store_kvcache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slots,
+                   at::Tensor status);
+void commit_tree_kv(at::Tensor tk, at::Tensor tv, at::Tensor kc, at::Tensor vc, at::Tensor nodes, at::Tensor slots,
+                    at::Tensor status);
+void splitk_reduce(at::Tensor out, at::Tensor partials);
+void splitk_reduce_add_rmsnorm(at::Tensor out, at::Tensor res_out, at::Tensor partials, at::Tensor residual,
+                               at::Tensor w, double eps);
+void argmax_rows(at::Tensor out_idx, at::Tensor out_val, at::Tensor logits);
+void sample_rows(at::Tensor out, at::Tensor logits, at::Tensor temps, int64_t seed);
+void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
+                      at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, int64_t max_splits,
+                      int64_t partition);
+void prefill_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,
+                       at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_seqlen_q);
+void tree_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bt, int64_t prefix_len,
+                    at::Tensor tk, at::Tensor tv, at::Tensor mask_bits, double scale);
+void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status);
+}  // namespace lsb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "llmserve_b200 sm_100a kernels";
+  m.def("rms_norm", &lsb::rms_norm);
+  m.def("add_rms_norm", &lsb::add_rms_norm);
+  m.def("silu_and_mul", &lsb::silu_and_mul);
+  m.def("embedding", &lsb::embedding);
+  m.def("qkv_rope", &lsb::qkv_rope);
+  m.def("store_kvcache", &lsb::store_kvcache);
+  m.def("commit_tree_kv", &lsb::commit_tree_kv);
+  m.def("splitk_reduce", &lsb::splitk_reduce);
+  m.def("splitk_reduce_add_rmsnorm", &lsb::splitk_reduce_add_rmsnorm);
+  m.def("argmax_rows", &lsb::argmax_rows);
+  m.def("sample_rows", &lsb::sample_rows);
+  m.def("decode_attention", &lsb::decode_attention);
+  m.def("prefill_attention", &lsb::prefill_attention);
+  m.def("tree_attention", &lsb::tree_attention);
+  m.def("gemm_bf16", &lsb::gemm_bf16);
+}

@@ -1,0 +1,357 @@
+// bf16 GEMM on the 5th-generation tensor cores: Y[T, N] = X[T, K] . W[N, K]^T.
+//
+// One CTA computes a 128 (weight rows) x BN (tokens) output tile over a K range:
+//   warp 0, one lane : TMA producer, streams 128x64 W and BNx64 X tiles (128B swizzle) into a
+//                      STAGES-deep shared-memory ring (mbarrier "full" with tx-count);
+//   warp 1, one lane : MMA issuer, four tcgen05.mma (K=16 each) per stage into a TMEM
+//                      accumulator, tcgen05.commit frees the stage ("empty") when its MMAs are done;
+//   all 4 warps      : epilogue, tcgen05.ld 32 lanes x 16 columns at a time (warp w owns TMEM
+//                      lanes 32w..32w+31 = output features), store bf16 (or fp32 split-K partials)
+//                      with the feature index contiguous across the warp.
+// The weight matrix is the UMMA "A" (M = 128 rows) and the tokens are "B" (N = BN), so a decode
+// batch of a few dozen tokens still fills the tensor core's M dimension and the weights -- the
+// bytes that bound decode -- are read once.  K is split over gridDim.z when the tile grid alone
+// would leave SMs idle; the caller then reduces the fp32 partials (fused with the next op).
+//
+// Every mbarrier wait is bounded; a timeout records an error code in `status`, stops issuing
+// work, waits (bounded) for the TMA copies already in flight, frees TMEM and returns.
+// No TMA multicast is used anywhere (the kernel runs under tensor parallelism).
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace lsb {
+namespace {
+
+#define LSB_CHECK(cond, msg) TORCH_CHECK(cond, "llmserve_b200: ", msg)
+
+constexpr int BM = 128;
+constexpr int BK = 64;   // 64 bf16 = 128 bytes: one 128B swizzle atom per row
+constexpr int kSmemBudget = 200 * 1024;
+
+// ---- descriptors --------------------------------------------------------------------------
+// Shared-memory matrix descriptor (tcgen05 "matrix descriptor"), K-major, 128B swizzle:
+// start address >> 4 in bits [0,14), leading-byte-offset (unused for swizzled K-major, 1) in
+// [16,30), stride-byte-offset = 1024 B (8 rows x 128 B) >> 4 in [32,46), descriptor version 1 in
+// [46,48), layout type 2 (128B swizzle) in [61,64).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor for kind::f16: fp32 accumulate (bits 4-5 = 1), A = B = bf16
+// (bits 7-9 = 1, 10-12 = 1), both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+template <int N>
+__host__ __device__ constexpr uint32_t idesc_bf16_f32() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// ---- PTX wrappers ----------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kW = BM * BK * 2;           // 16 KiB
+  static constexpr int kX = BN * BK * 2;
+  static constexpr int kStage = kW + kX;           // multiple of 1024
+  static constexpr int kBarOff = STAGES * kStage;
+  static constexpr int kBytes = kBarOff + (2 * STAGES + 1) * 8 + 16 + 1024;   // + alignment slack
+};
+
+template <int BN>
+constexpr int tmem_cols() {
+  return BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_w,
+                                                           const __grid_constant__ CUtensorMap tm_x,
+                                                           bf16* __restrict__ out, float* __restrict__ partials,
+                                                           int T, int N, int k_tiles, int k_tiles_per_split,
+                                                           int* __restrict__ status) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BM, t0 = blockIdx.y * BN;
+  const int kt_begin = blockIdx.z * k_tiles_per_split;
+  const int kt_end = min(k_tiles, kt_begin + k_tiles_per_split);
+  const int nk = max(0, kt_end - kt_begin);
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_x);
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(tmem_cols<BN>()));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && nk > 0) {
+      int issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        const uint32_t phase = (i / STAGES) & 1;
+        if (!mbar_wait(&empty[s], phase ^ 1)) {
+          record_error(status, kTimeoutSmemEmpty);
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        if (*((volatile int*)&abort_flag)) break;
+        uint8_t* st = smem + s * L::kStage;
+        mbar_expect_tx(&full[s], L::kStage);
+        const int kx = (kt_begin + i) * BK;
+        tma_load_2d(st, &tm_w, &full[s], kx, n0);
+        tma_load_2d(st + L::kW, &tm_x, &full[s], kx, t0);
+        issued[s] = i + 1;
+      }
+      if (*((volatile int*)&abort_flag)) {
+        // drain: wait (bounded) for every stage's most recent copy to land before leaving
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s] > 0) mbar_wait(&full[s], ((issued[s] - 1) / STAGES) & 1);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && nk > 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32<BN>();
+      bool ok = true;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES;
+        const uint32_t phase = (i / STAGES) & 1;
+        if (!mbar_wait(&full[s], phase) || *((volatile int*)&abort_flag)) {
+          record_error(status, kTimeoutTmaFull);
+          atomicExch(&abort_flag, 1);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t wa = smem_u32(smem + s * L::kStage);
+        const uint32_t xa = wa + L::kW;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+          tc_mma(tmem, smem_desc_sw128(wa + k * 32), smem_desc_sw128(xa + k * 32), idesc, (i | k) != 0);
+        tc_commit(&empty[s]);
+      }
+      if (ok) tc_commit(accum);
+    }
+    __syncwarp();
+  }
+
+  // ---- epilogue ---------------------------------------------------------------------------------
+  bool have = nk > 0;
+  if (have) {
+    if (!mbar_wait(accum, 0) || *((volatile int*)&abort_flag)) {
+      record_error(status, kTimeoutAccum);
+      have = false;
+    }
+  }
+  tc_fence_after();
+  const int feat = n0 + warp * 32 + lane;
+  const uint32_t row_addr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 16) {
+    uint32_t r[16];
+    if (have) {
+      tc_ld16(row_addr + c0, r);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) r[j] = 0u;
+    }
+    if (feat < N) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int t = t0 + c0 + j;
+        if (t < T) {
+          const float v = __uint_as_float(r[j]);
+          if (partials != nullptr)
+            partials[((size_t)blockIdx.z * T + t) * N + feat] = v;
+          else
+            out[(size_t)t * N + feat] = to_b(v);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols<BN>()));
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  LSB_CHECK(fn != nullptr, "cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with a (box_rows x 64) box.
+CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t row_stride_elems, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride_elems * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  LSB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
+struct MapKey {
+  const void* p;
+  int64_t rows, cols, stride;
+  int box;
+  bool operator==(const MapKey& o) const {
+    return p == o.p && rows == o.rows && cols == o.cols && stride == o.stride && box == o.box;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.p) ^ (std::hash<int64_t>()(k.rows) * 31) ^ (std::hash<int64_t>()(k.cols) * 131) ^
+           (size_t)k.box;
+  }
+};
+
+// Weight maps are built once per (pointer, shape); activations change every call.
+const CUtensorMap& weight_map(const at::Tensor& w) {
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  static std::mutex mu;
+  MapKey key{w.data_ptr(), w.size(0), w.size(1), w.stride(0), BM};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it == cache.end()) it = cache.emplace(key, make_map(w.data_ptr(), w.size(0), w.size(1), w.stride(0), BM)).first;
+  return it->second;
+}
+
+template <int BN, int STAGES>
+void launch(const at::Tensor& x, const at::Tensor& w, bf16* out, float* partials, int splits, int* status) {
+  using L = GemmSmem<BN, STAGES>;
+  static_assert(L::kStage % 1024 == 0, "stage size must keep 1024-byte alignment");
+  const int T = x.size(0), K = x.size(1), N = w.size(0);
+  const int k_tiles = (K + BK - 1) / BK;
+  const int kps = (k_tiles + splits - 1) / splits;
+  const CUtensorMap mx = make_map(x.data_ptr(), T, K, x.stride(0), BN);
+  const CUtensorMap& mw = weight_map(w);
+  auto kern = gemm_bf16_kernel<BN, STAGES>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    configured = true;
+  }
+  dim3 grid((N + BM - 1) / BM, (T + BN - 1) / BN, splits);
+  kern<<<grid, 128, L::kBytes, at::cuda::getCurrentCUDAStream()>>>(mw, mx, out, partials, T, N, k_tiles, kps, status);
+}
+
+template <int BN>
+constexpr int stages_for() {
+  constexpr int st = kSmemBudget / GemmSmem<BN, 1>::kStage;
+  return st > 8 ? 8 : st;
+}
+
+}  // namespace
+
+int* status_ptr(const at::Tensor& status);
+
+// out: bf16 [T, N] when splits == 1; partials: fp32 [splits, T, N] otherwise.
+void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status) {
+  LSB_CHECK(x.is_cuda() && w.is_cuda(), "gemm operands must be CUDA tensors");
+  LSB_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
+  LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm shape mismatch");
+  LSB_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "gemm operands must be K-contiguous");
+  LSB_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "row strides must be 16-byte multiples");
+  LSB_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+            "gemm operands must be 16-byte aligned");
+  const int T = x.size(0), N = w.size(0);
+  LSB_CHECK(splits >= 1 && splits <= 64, "splits out of range");
+  bf16* o = nullptr;
+  float* p = nullptr;
+  if (splits == 1 && partials.numel() == 0) {
+    LSB_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)T * N, "bad out");
+    o = (bf16*)out.data_ptr();
+  } else {
+    LSB_CHECK(partials.scalar_type() == at::kFloat && partials.is_contiguous() &&
+                  partials.numel() == splits * (int64_t)T * N, "bad partials");
+    p = partials.data_ptr<float>();
+  }
+  if (T == 0 || N == 0) return;
+  const at::cuda::CUDAGuard g(x.device());
+  int* st = status_ptr(status);
+  if (T <= 16) launch<16, stages_for<16>()>(x, w, o, p, splits, st);
+  else if (T <= 32) launch<32, stages_for<32>()>(x, w, o, p, splits, st);
+  else if (T <= 64) launch<64, stages_for<64>()>(x, w, o, p, splits, st);
+  else if (T <= 128) launch<128, stages_for<128>()>(x, w, o, p, splits, st);
+  else launch<256, stages_for<256>()>(x, w, o, p, splits, st);
+}
+
+}  // namespace lsb

@@ -12,7 +12,7 @@ post-op (plain store, residual add + RMSNorm, or the tensor-parallel all-reduce 
 import torch
 import torch.nn.functional as F
 
-from llmserve_b200.ops._ext import C
+from llmserve_b200.ops._ext import C, status
 
 NUM_SMS = 148
 TILE_M = 128          # weight rows per CTA
@@ -55,10 +55,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -
         return out.view(*x.shape[:-1], N)
     splits = choose_splits(T, N, K)
     if splits == 1:
-        C().gemm_bf16(out, x2, w, _empty(x.device, torch.float32), 1)
+        C().gemm_bf16(out, x2, w, _empty(x.device, torch.float32), 1, status(x.device))
     else:
         partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
-        C().gemm_bf16(_empty(x.device, x.dtype), x2, w, partials, splits)
+        C().gemm_bf16(_empty(x.device, x.dtype), x2, w, partials, splits, status(x.device))
         C().splitk_reduce(out, partials)
     if bias is not None:
         out += bias
@@ -71,5 +71,5 @@ def linear_partials(x: torch.Tensor, w: torch.Tensor, splits: int, partials: tor
     N = w.shape[0]
     if partials is None:
         partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
-    C().gemm_bf16(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits)
+    C().gemm_bf16(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits, status(x.device))
     return partials

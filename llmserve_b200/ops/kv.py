@@ -9,14 +9,15 @@
 """
 import torch
 
-from llmserve_b200.ops._ext import C
+from llmserve_b200.ops._ext import C, status
 from llmserve_b200.ops.rope import store_kv_ref
 
 
 def store_kvcache(k, v, k_cache, v_cache, slot_mapping):
     if not k.is_cuda:
         return store_kv_ref(k, v, k_cache, v_cache, slot_mapping)
-    C().store_kvcache(k.contiguous(), v.contiguous(), k_cache, v_cache, slot_mapping)
+    C().store_kvcache(k.contiguous(), v.contiguous(), k_cache, v_cache, slot_mapping.to(torch.int32),
+                      status(k.device))
 
 
 def commit_tree_kv_ref(tree_k, tree_v, k_cache, v_cache, node_indices, slot_mapping):
@@ -41,12 +42,12 @@ def commit_tree_kv(tree_k, tree_v, k_cache, v_cache, node_indices, slot_mapping)
     if not tree_k.is_cuda:
         return commit_tree_kv_ref(tree_k, tree_v, k_cache, v_cache, node_indices, slot_mapping)
     C().commit_tree_kv(tree_k.contiguous(), tree_v.contiguous(), k_cache, v_cache,
-                       node_indices.to(torch.int32), slot_mapping.to(torch.int32))
+                       node_indices.to(torch.int32), slot_mapping.to(torch.int32), status(tree_k.device))
 
 
 def embedding(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
     if not ids.is_cuda:
         return torch.nn.functional.embedding(ids, table)
     out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
-    C().embedding(out, ids.contiguous(), table)
+    C().embedding(out, ids.contiguous(), table, status(table.device))
     return out

@@ -11,7 +11,7 @@ bound cache (tree verify) a sibling kernel returns rotated q and k instead.
 """
 import torch
 
-from llmserve_b200.ops._ext import C
+from llmserve_b200.ops._ext import C, status
 from llmserve_b200.ops.norm import rms_norm_ref
 
 
@@ -57,13 +57,14 @@ def qkv_norm_rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps,
         qkv = qkv.contiguous()
         q = torch.empty(T, num_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
         if k_cache is not None and k_cache.numel():
-            C().qkv_norm_rope_store(q, qkv, positions, cos_sin, _opt(q_norm_w, qkv.device),
-                                    _opt(k_norm_w, qkv.device), eps, k_cache, v_cache, slot_mapping,
-                                    num_heads, num_kv_heads, head_dim)
+            C().qkv_rope(q, q, qkv, positions, cos_sin, _opt(q_norm_w, qkv.device),
+                         _opt(k_norm_w, qkv.device), eps, k_cache, v_cache, slot_mapping,
+                         num_heads, num_kv_heads, head_dim, True, status(qkv.device))
             return q, None, None
         k = torch.empty(T, num_kv_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
-        C().qkv_norm_rope(q, k, qkv, positions, cos_sin, _opt(q_norm_w, qkv.device),
-                          _opt(k_norm_w, qkv.device), eps, num_heads, num_kv_heads, head_dim)
+        e = _opt(None, qkv.device)
+        C().qkv_rope(q, k, qkv, positions, cos_sin, _opt(q_norm_w, qkv.device), _opt(k_norm_w, qkv.device),
+                     eps, e, e, e, num_heads, num_kv_heads, head_dim, False, status(qkv.device))
         v = qkv[:, qs + ks:].reshape(T, num_kv_heads, head_dim)
         return q, k, v
     q = qkv[:, :qs].reshape(T, num_heads, head_dim)

@@ -1,0 +1,204 @@
+"""sm_100a kernels against fp32 PyTorch references of the same ops (small shapes)."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from llmserve_b200.ops import activation, attention, gemm, kv, norm, rope, sampling  # noqa: E402
+from llmserve_b200.ops._ext import C, check_status  # noqa: E402
+
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _status():
+    C()
+    yield
+    check_status(torch.device(DEV))
+
+
+@pytest.mark.parametrize("T", [1, 7, 16, 33, 64, 100, 256, 300])
+@pytest.mark.parametrize("N,K", [(128, 64), (384, 256), (1000, 512), (256, 4096)])
+def test_gemm_matches_fp32(T, N, K):
+    g = torch.Generator(device=DEV).manual_seed(T * 7 + N + K)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) * 0.05).bfloat16()
+    ref = x.float() @ w.float().t()
+    out = gemm.linear(x, w)
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("splits", [2, 4, 8])
+def test_gemm_split_k_partials_sum(splits):
+    x = torch.randn(48, 2048, device=DEV).bfloat16()
+    w = (torch.randn(512, 2048, device=DEV) * 0.05).bfloat16()
+    parts = gemm.linear_partials(x, w, splits)
+    ref = x.float() @ w.float().t()
+    assert rel_err(parts.sum(0), ref) < 1e-3
+
+
+def test_rms_norm_and_add():
+    x = torch.randn(37, 4096, device=DEV).bfloat16()
+    r = torch.randn(37, 4096, device=DEV).bfloat16()
+    w = (1 + 0.1 * torch.randn(4096, device=DEV)).bfloat16()
+    assert rel_err(norm.rms_norm(x, w, 1e-6), norm.rms_norm_ref(x.cpu(), w.cpu(), 1e-6).to(DEV)) < 5e-3
+    o, res = norm.add_rms_norm(x, r, w, 1e-6)
+    ro, rres = norm.add_rms_norm_ref(x.cpu(), r.cpu(), w.cpu(), 1e-6)
+    assert rel_err(o, ro.to(DEV)) < 5e-3
+    assert rel_err(res, rres.to(DEV)) < 5e-3
+
+
+def test_splitk_reduce_add_rmsnorm():
+    parts = torch.randn(4, 9, 512, device=DEV)
+    r = torch.randn(9, 512, device=DEV).bfloat16()
+    w = torch.ones(512, device=DEV).bfloat16()
+    out = torch.empty(9, 512, device=DEV, dtype=torch.bfloat16)
+    res = torch.empty_like(out)
+    C().splitk_reduce_add_rmsnorm(out, res, parts, r, w, 1e-6)
+    ro, rres = norm.add_rms_norm_ref(parts.sum(0).bfloat16().cpu(), r.cpu(), w.cpu(), 1e-6)
+    assert rel_err(out, ro.to(DEV)) < 5e-3 and rel_err(res, rres.to(DEV)) < 5e-3
+
+
+def test_silu_and_mul():
+    x = torch.randn(13, 2 * 1024, device=DEV).bfloat16()
+    assert rel_err(activation.silu_and_mul(x), activation.silu_and_mul_ref(x.cpu()).to(DEV)) < 5e-3
+
+
+def test_embedding():
+    table = torch.randn(1000, 256, device=DEV).bfloat16()
+    ids = torch.randint(0, 1000, (17,), device=DEV)
+    assert torch.equal(kv.embedding(ids, table), table[ids])
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("qknorm", [True, False])
+def test_qkv_norm_rope_store(hd, qknorm):
+    T, nh, nkv, bs, nblk = 21, 8, 2, 16, 8
+    qkv = torch.randn(T, (nh + 2 * nkv) * hd, device=DEV).bfloat16()
+    pos = torch.randint(0, 500, (T,), device=DEV)
+    cs = rope.build_cos_sin_cache(hd, 1024, 1e6).to(DEV)
+    qw = (1 + 0.1 * torch.randn(hd, device=DEV)).bfloat16() if qknorm else None
+    kw = (1 + 0.1 * torch.randn(hd, device=DEV)).bfloat16() if qknorm else None
+    kc = torch.zeros(nblk, nkv, bs, hd, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(nblk * bs, device=DEV)[:T].int()
+    slots[3] = -1
+    q, _, _ = rope.qkv_norm_rope_store(qkv, pos, cs, qw, kw, 1e-6, kc, vc, slots, nh, nkv, hd)
+    kc_ref, vc_ref = torch.zeros_like(kc).cpu(), torch.zeros_like(vc).cpu()
+    q_ref, k_ref, v_ref = rope.qkv_norm_rope_store(qkv.cpu(), pos.cpu(), cs.cpu(), None if qw is None else qw.cpu(),
+                                                   None if kw is None else kw.cpu(), 1e-6, kc_ref, vc_ref,
+                                                   slots.cpu(), nh, nkv, hd)
+    assert rel_err(q, q_ref.to(DEV)) < 5e-3
+    assert rel_err(kc, kc_ref.to(DEV)) < 5e-3
+    assert torch.equal(vc.cpu(), vc_ref)
+    qn, kn, vn = rope.qkv_norm_rope_store(qkv, pos, cs, qw, kw, 1e-6, None, None, None, nh, nkv, hd)
+    assert rel_err(qn, q_ref.to(DEV)) < 5e-3 and rel_err(kn, k_ref.to(DEV)) < 5e-3
+
+
+def _pool(nblk, nkv, bs, hd, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    kc = torch.randn(nblk, nkv, bs, hd, device=DEV, generator=g).bfloat16()
+    vc = torch.randn(nblk, nkv, bs, hd, device=DEV, generator=g).bfloat16()
+    return kc, vc
+
+
+@pytest.mark.parametrize("bs", [16, 256])
+@pytest.mark.parametrize("hd,nh,nkv", [(128, 32, 8), (64, 4, 2), (128, 4, 1)])
+def test_decode_attention(bs, hd, nh, nkv):
+    lens = [1, 5, 64, 65, 300, 513, 1200]
+    B = len(lens)
+    maxblk = max(-(-L // bs) for L in lens)
+    nblk = B * maxblk + 3
+    kc, vc = _pool(nblk, nkv, bs, hd)
+    perm = torch.randperm(nblk)[: B * maxblk].view(B, maxblk).int().to(DEV)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    q = torch.randn(B, nh, hd, device=DEV).bfloat16()
+    scale = 1 / math.sqrt(hd)
+    out = attention.decode_attention(q, kc, vc, perm, ctx, scale)
+    ref = attention.decode_attention_ref(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), perm.cpu(), ctx.cpu(), scale)
+    assert rel_err(out, ref.to(DEV)) < 1e-2
+
+
+@pytest.mark.parametrize("bs", [16, 256])
+@pytest.mark.parametrize("hd,nh,nkv", [(128, 8, 2), (64, 4, 2)])
+def test_prefill_attention_varlen_paged(bs, hd, nh, nkv):
+    # (q_len, k_len): plain prefill, chunk with cached prefix, verify-sized chunks
+    shapes = [(37, 37), (130, 200), (4, 301), (64, 64), (1, 9)]
+    maxblk = max(-(-k // bs) for _, k in shapes)
+    nblk = len(shapes) * maxblk
+    kc, vc = _pool(nblk, nkv, bs, hd, seed=3)
+    tables = torch.arange(nblk, dtype=torch.int32, device=DEV)[torch.randperm(nblk)].view(len(shapes), maxblk)
+    cu = [0]
+    for ql, _ in shapes:
+        cu.append(cu[-1] + ql)
+    q = torch.randn(cu[-1], nh, hd, device=DEV).bfloat16()
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=DEV)
+    ks = torch.tensor([k for _, k in shapes], dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(hd)
+    out = attention.prefill_attention(q, kc, vc, cu_t, ks, tables, scale, max(s[0] for s in shapes))
+    ref = attention.prefill_attention_ref(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), cu_t.cpu(), ks.cpu(),
+                                          tables.cpu(), scale)
+    assert rel_err(out, ref.to(DEV)) < 1e-2
+
+
+def test_tree_attention():
+    from llmserve_b200.speculative.tree import build_fixed_tree_topology
+    hd, nh, nkv, bs = 128, 8, 2, 16
+    topo = build_fixed_tree_topology(10)
+    n = len(topo.parents)
+    kc, vc = _pool(20, nkv, bs, hd, seed=5)
+    table = torch.randperm(20)[:10].int().to(DEV)
+    prefix = 133
+    q = torch.randn(n, nh, hd, device=DEV).bfloat16()
+    tk = torch.randn(n, nkv, hd, device=DEV).bfloat16()
+    tv = torch.randn(n, nkv, hd, device=DEV).bfloat16()
+    mask = topo.attention_mask(DEV)
+    out = attention.tree_attention(q, kc, vc, table, prefix, tk, tv, mask, 0.088)
+    ref = attention.tree_attention_ref(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), table.cpu(), prefix,
+                                       tk.cpu().float(), tv.cpu().float(), mask.cpu(), 0.088)
+    assert rel_err(out, ref.to(DEV)) < 1e-2
+
+
+def test_store_kvcache_and_tree_commit():
+    nkv, hd, bs = 2, 128, 16
+    kc = torch.zeros(4, nkv, bs, hd, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    k = torch.randn(5, nkv, hd, device=DEV).bfloat16()
+    v = torch.randn(5, nkv, hd, device=DEV).bfloat16()
+    slots = torch.tensor([3, 17, -1, 40, 63], dtype=torch.int32, device=DEV)
+    kv.store_kvcache(k, v, kc, vc, slots)
+    kr, vr = torch.zeros_like(kc).cpu(), torch.zeros_like(vc).cpu()
+    rope.store_kv_ref(k.cpu(), v.cpu(), kr, vr, slots.cpu())
+    assert torch.equal(kc.cpu(), kr) and torch.equal(vc.cpu(), vr)
+    L = 3
+    tk = torch.randn(L, 6, nkv, hd, device=DEV).bfloat16()
+    tv = torch.randn(L, 6, nkv, hd, device=DEV).bfloat16()
+    KC = torch.zeros(L, 4, nkv, bs, hd, device=DEV, dtype=torch.bfloat16)
+    VC = torch.zeros_like(KC)
+    nodes = torch.tensor([0, 2, 5], dtype=torch.int32, device=DEV)
+    sl = torch.tensor([7, 8, 33], dtype=torch.int32, device=DEV)
+    kv.commit_tree_kv(tk, tv, KC, VC, nodes, sl)
+    KR, VR = torch.zeros_like(KC).cpu(), torch.zeros_like(VC).cpu()
+    kv.commit_tree_kv_ref(tk.cpu(), tv.cpu(), KR, VR, nodes.cpu(), sl.cpu())
+    assert torch.equal(KC.cpu(), KR) and torch.equal(VC.cpu(), VR)
+
+
+def test_argmax_and_sampling():
+    logits = torch.randn(9, 151936 // 8, device=DEV).bfloat16()
+    logits[3, 100] = 50.0
+    logits[3, 7] = 50.0   # tie -> lowest index
+    idx = sampling.argmax(logits)
+    assert torch.equal(idx.cpu(), logits.float().cpu().argmax(-1))
+    assert int(idx[3]) == 7
+    temps = torch.full((9,), 0.7, device=DEV)
+    got = sampling.sample(logits.float(), temps, 1234)
+    want = sampling.sample(logits.float().cpu(), temps.cpu(), 1234)
+    assert (got.cpu() == want).float().mean() >= 8 / 9
