@@ -1,0 +1,227 @@
+"""Headline benchmark: closed-loop serving throughput of Qwen3-8B (BF16) on B200.
+
+Metric and config come from BASELINE.json: output tok/s (with P99 TTFT / TPOT) for Qwen3-8B under a
+closed loop of ``--concurrency`` requests of 256 input / 256 output tokens (prompt ids uniform over
+the vocabulary, greedy decoding), tensor parallel over ``--gpus`` GPUs of one node.  Weights are
+random N(0, 0.02) drawn on the device (no checkpoint download is possible); shapes are the real
+model's.  One "step" is one engine step (schedule + forward + sample + postprocess).
+
+``value``  : output tokens emitted in the K timed steps / device time of those steps (CUDA events on
+             every rank, max over ranks).
+``e2e``    : the same tokens / wall-clock time of the same steps through the public API
+             (``LLM.add_request`` / ``LLM.step``), which includes the per-step host->device copy of
+             the step inputs from pinned memory and the device->host read of the sampled tokens.
+
+Usage: ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 launch with
+``torchrun --nproc-per-node N bench.py --gpus N ...`` (one rank per GPU).  ``--impl reference`` runs
+the unmodified reference build from ``baseline/_ref`` on the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "output tok/s + P99 TTFT/TPOT, Qwen3-8B closed-loop, TP 1/2/4/8 vs ref build"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", 1)))
+    p.add_argument("--steps", type=int, default=257)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--concurrency", type=int, default=64)
+    p.add_argument("--input-len", type=int, default=256)
+    p.add_argument("--output-len", type=int, default=256)
+    p.add_argument("--layers", type=int, default=36)
+    p.add_argument("--eager", action="store_true")
+    p.add_argument("--nccl-only", action="store_true", help="disable the fused NVLink collectives")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    def __init__(self, indices):
+        self.indices = indices
+        self.proc = None
+        self.path = os.path.join(tempfile.mkdtemp(), "clocks.csv")
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", ",".join(map(str, self.indices))],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+            self.f.close()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(float(r[2]) for r in rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+                "samples": len(rows), "reasons": reasons}
+
+
+def visible_indices(n):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        return [int(x) for x in vis.split(",")[:n]]
+    return list(range(n))
+
+
+def model_dir(layers: int) -> str:
+    from llmserve_b200.models.synthetic import QWEN3_8B, write_config_only
+    path = os.path.join(tempfile.gettempdir(), f"llmserve_b200_qwen3_8b_L{layers}")
+    write_config_only(path, dict(QWEN3_8B, num_hidden_layers=layers))
+    return path
+
+
+def request_stream(vocab, n_in, seed=0):
+    import random
+    rng = random.Random(seed)
+    while True:
+        yield [rng.randrange(vocab) for _ in range(n_in)]
+
+
+def run_ours(args):
+    import torch
+
+    from llmserve_b200 import LLM, SamplingParams
+    from llmserve_b200.engine.llm_engine import run_worker
+    from llmserve_b200.engine.model_runner import GreedySampler
+
+    rank = int(os.environ.get("RANK", 0))
+    world = args.gpus
+    kwargs = dict(load_format="dummy", tensor_parallel_size=world, enforce_eager=args.eager,
+                  max_model_len=args.input_len + args.output_len + 16,
+                  max_num_batched_tokens=max(16384, args.concurrency * args.input_len),
+                  max_num_seqs=args.concurrency, kvcache_block_size=256, gpu_memory_utilization=0.85,
+                  fused_collectives=not args.nccl_only, comm_timeout_s=300.0)
+    if world > 1:
+        kwargs.update(distributed_launcher="external", distributed_init_method="env://",
+                      rpc_channel=f"llmserve_b200_bench_{os.environ.get('MASTER_PORT', '0')}")
+    path = model_dir(args.layers)
+    if rank > 0:
+        run_worker(path, rank, **kwargs)
+        return
+    llm = LLM(path, **kwargs)
+    llm.model_runner.sampler = GreedySampler()
+    vocab = llm.config.hf_config.vocab_size
+    stream = request_stream(vocab, args.input_len)
+    sp = SamplingParams(temperature=1.0, max_tokens=args.output_len, ignore_eos=True)
+    active = 0
+
+    def refill():
+        nonlocal active
+        while active < args.concurrency:
+            llm.add_request(next(stream), sp)
+            active += 1
+
+    def tokens_so_far():
+        return sum(len(m["token_times"]) for m in llm.request_metrics.values())
+
+    refill()
+    for _ in range(args.warmup):
+        outs, _ = llm.step()
+        active -= len(outs)
+        refill()
+    runner = llm.model_runner
+    runner.call("mark_event", "bench_start")
+    torch.cuda.synchronize()
+    tok0 = tokens_so_far()
+    h2d0, d2h0 = runner.h2d_bytes, runner.d2h_bytes
+    with ClockSampler(visible_indices(world)) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            outs, _ = llm.step()
+            active -= len(outs)
+            refill()
+        runner.call("mark_event", "bench_end")
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    per_rank = runner.call("gather_elapsed", "bench_start", "bench_end")
+    tokens = tokens_so_far() - tok0
+    dev_ms = max(r[0] for r in per_rank)
+    launches = int(per_rank[0][1])
+    m = llm.get_metrics()["summary"]
+    h2d = (runner.h2d_bytes - h2d0) / args.steps
+    d2h = (runner.d2h_bytes - d2h0) / args.steps
+    llm.exit()
+    value = tokens / (dev_ms / 1e3)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init Qwen3-8B weights N(0,0.02), prompt ids uniform over the vocab",
+        "config": {"model": "Qwen3-8B" if args.layers == 36 else f"Qwen3-8B-{args.layers}L",
+                   "global_batch": args.concurrency, "seq_len": args.input_len + args.output_len,
+                   "parallelism": f"tp{world}", "workload": f"closed-loop {args.input_len} in / {args.output_len} out, "
+                   f"concurrency {args.concurrency}, greedy", "cuda_graphs": not args.eager,
+                   "collectives": "nccl" if args.nccl_only or world == 1 else "fused-nvlink",
+                   "l2": "inputs larger than L2: every step streams all 16 GB of weights"},
+        "e2e": {"value": round(tokens / wall, 2), "unit": "tok/s", "h2d_bytes_per_step": round(h2d),
+                "d2h_bytes_per_step": round(d2h)},
+        "gpu_launches": launches,
+        "latency": {"ttft_p99_ms": None if m["ttft"]["p99"] is None else round(m["ttft"]["p99"] * 1e3, 2),
+                    "tpot_p99_ms": None if m["tpot"]["p99"] is None else round(m["tpot"]["p99"] * 1e3, 3)},
+        "per_rank_device_ms": [round(r[0], 3) for r in per_rank],
+        "clocks": clocks.summary(),
+        "impl": "ours",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", 0))
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if rank == 0:
+        why = None
+        if not os.path.isdir(os.path.join(ref, "llmserve")):
+            why = "reference build not installed under baseline/_ref"
+        if why:
+            print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+            return
+    from baseline_ref import run as ref_run  # noqa: E402
+    ref_run(args, METRIC)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

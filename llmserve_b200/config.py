@@ -13,6 +13,9 @@ are grouped at the end:
 * ``comm_timeout_s``       -- bound on every host RPC wait and on the process-group timeout.
 * ``debug_bounds_checks``  -- validate slot mappings / block tables on the host before launch.
 * ``pd_*``                 -- prefill/decode disaggregation (prefill group pushes KV blocks).
+* ``distributed_launcher`` -- ``"spawn"``: rank 0 starts the TP workers itself (reference
+                              behaviour); ``"external"``: ranks were started by torchrun and
+                              ranks > 0 call :func:`llmserve_b200.engine.llm_engine.run_worker`.
 """
 import json
 import os
@@ -94,6 +97,8 @@ class Config:
     pd_decode_devices: tuple[int, ...] = ()
     device_offset: int = 0
     max_kvcache_blocks: int = -1
+    distributed_launcher: str = "spawn"
+    rpc_channel: str | None = None
 
     def __post_init__(self):
         if not os.path.isdir(self.model):
@@ -117,6 +122,8 @@ class Config:
             raise ValueError("awq_backend must be 'reference' or 'cuda'")
         if self.device not in ("cuda", "cpu"):
             raise ValueError("device must be 'cuda' or 'cpu'")
+        if self.distributed_launcher not in ("spawn", "external"):
+            raise ValueError("distributed_launcher must be 'spawn' or 'external'")
         if self.load_format not in ("auto", "dummy"):
             raise ValueError("load_format must be 'auto' or 'dummy'")
         if self.speculative_model is not None and not os.path.isdir(self.speculative_model):

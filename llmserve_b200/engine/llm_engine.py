@@ -31,6 +31,17 @@ def _worker_main(config, rank, channel_name, parent_pid):
     ModelRunner(config, rank, channel_name, parent_pid)
 
 
+def run_worker(model, rank: int, **kwargs):
+    """Tensor-parallel worker body for ranks started by an external launcher (torchrun).
+
+    Rank 0 builds ``LLM(model, distributed_launcher="external", ...)`` with the same kwargs; this
+    call returns when rank 0 calls ``exit()``."""
+    names = {f.name for f in fields(Config)}
+    config = Config(model, **{k: v for k, v in kwargs.items() if k in names})
+    Sequence.block_size = config.kvcache_block_size
+    ModelRunner(config, rank, config.rpc_channel or "llmserve_b200_ext", os.getppid())
+
+
 def percentile(values, q):
     """Linear-interpolation percentile (the reference's ``_percentile``)."""
     if not values:
@@ -64,8 +75,10 @@ class LLMEngine:
         self.config = config
         Sequence.block_size = config.kvcache_block_size
         self.ps = []
-        channel = f"llmserve_b200_{os.getpid()}_{next(_engine_ids)}"
-        if config.tensor_parallel_size > 1:
+        channel = config.rpc_channel or f"llmserve_b200_{os.getpid()}_{next(_engine_ids)}"
+        if config.distributed_launcher == "external":
+            channel = config.rpc_channel or "llmserve_b200_ext"
+        elif config.tensor_parallel_size > 1:
             ctx = mp.get_context("spawn")
             for rank in range(1, config.tensor_parallel_size):
                 p = ctx.Process(target=_worker_main, args=(config, rank, channel, os.getpid()), daemon=True)

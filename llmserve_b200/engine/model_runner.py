@@ -26,6 +26,7 @@ from llmserve_b200.engine.sequence import Sequence
 from llmserve_b200.models.qwen3 import Qwen3ForCausalLM
 from llmserve_b200.ops import attention as attn_ops
 from llmserve_b200.ops import sampling as sampling_ops
+from llmserve_b200.ops._ext import LaunchCounter
 from llmserve_b200.parallel import state as tp
 from llmserve_b200.utils.context import get_context, reset_context, set_context
 from llmserve_b200.utils.loader import init_dummy_weights, load_model
@@ -397,6 +398,7 @@ class ModelRunner:
         width = ctx.block_tables.shape[1]
         v["block_tables"][:bs, :width].copy_(ctx.block_tables)
         self.graphs[gbs].replay()
+        LaunchCounter.launches += self.graph_launches[gbs]
         return v["logits"][:bs]
 
     def sample_tokens(self, logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tensor:
@@ -448,20 +450,47 @@ class ModelRunner:
             "logits": torch.zeros(max_bs, self.model.lm_head.shard_size, dtype=self.dtype, device=d),
         }
         self.graph_bs = [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
-        self.graphs, self.graph_pool = {}, None
+        self.graphs, self.graph_pool, self.graph_launches = {}, None, {}
         for bs in reversed(self.graph_bs):
             g = torch.cuda.CUDAGraph()
             set_context(False, slot_mapping=v["slot_mapping"][:bs], context_lens=v["context_lens"][:bs],
                         block_tables=v["block_tables"][:bs], decode_workspace=self.decode_workspace)
             v["logits"][:bs] = self.model.compute_logits(self.model(v["input_ids"][:bs], v["positions"][:bs]))
+            before = LaunchCounter.launches
             with torch.cuda.graph(g, self.graph_pool):
                 v["logits"][:bs] = self.model.compute_logits(self.model(v["input_ids"][:bs], v["positions"][:bs]))
+            self.graph_launches[bs] = LaunchCounter.launches - before
             if self.graph_pool is None:
                 self.graph_pool = g.pool()
             self.graphs[bs] = g
             torch.cuda.synchronize()
             reset_context()
         self.graph_vars = v
+
+    # ---- device timing (benchmarks): every rank records, rank 0 gathers -------------------------
+    def mark_event(self, tag: str):
+        if not hasattr(self, "_events"):
+            self._events = {}
+        if self.is_cuda:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._events[tag] = e
+        self._events[tag + ":launches"] = LaunchCounter.launches
+
+    def gather_elapsed(self, start: str, end: str):
+        """Per-rank (device ms between two marks, kernel launches between them)."""
+        if self.is_cuda:
+            torch.cuda.synchronize()
+            ms = self._events[start].elapsed_time(self._events[end])
+        else:
+            ms = 0.0
+        mine = torch.tensor([ms, float(self._events[end + ":launches"] - self._events[start + ":launches"])],
+                            dtype=torch.float64, device=self.device)
+        if self.world_size > 1:
+            parts = [torch.empty_like(mine) for _ in range(self.world_size)]
+            torch.distributed.all_gather(parts, mine)
+            mine = torch.stack(parts)
+        return mine.view(-1, 2).tolist() if self.rank == 0 else None
 
     # ---- speculative entry points (called through the RPC by name) -----------------------------
     def run_speculative_batch(self, seqs):

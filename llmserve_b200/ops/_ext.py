@@ -6,17 +6,51 @@ There is no silent fallback: a CUDA tensor reaching an op without the extension 
 import importlib
 
 _C = None
+_PROXY = None
+
+# kernels launched per extension call (calls not listed launch one kernel)
+_KERNELS_PER_CALL = {"decode_attention": 2}
+
+
+class LaunchCounter:
+    """Counts the extension's kernel launches (graph replays add their captured count)."""
+    launches = 0
+
+
+class _CountingModule:
+    def __init__(self, mod):
+        self._mod = mod
+        self._cache = {}
+
+    def __getattr__(self, name):
+        fn = self._cache.get(name)
+        if fn is None:
+            target = getattr(self._mod, name)
+            n = _KERNELS_PER_CALL.get(name, 1)
+
+            def fn(*args, _t=target, _n=n):
+                LaunchCounter.launches += _n
+                return _t(*args)
+            self._cache[name] = fn
+        return fn
 
 
 def C():
-    global _C
-    if _C is None:
+    global _C, _PROXY
+    if _PROXY is None:
         try:
+            import torch  # noqa: F401  (loads libc10 for the extension)
             _C = importlib.import_module("llmserve_b200._C")
         except ImportError as e:
             raise RuntimeError(
                 "llmserve_b200._C (sm_100a kernels) is not built; run "
                 "`python setup.py build_ext --inplace` in the repository root") from e
+        _PROXY = _CountingModule(_C)
+    return _PROXY
+
+
+def raw_module():
+    C()
     return _C
 
 

@@ -32,7 +32,7 @@ struct alignas(16) Vec8 {
 // RMSNorm: out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)
 // ------------------------------------------------------------------------------------------
 template <bool kAddResidual>
-__global__ void rmsnorm_kernel(bf16* __restrict__ out, bf16* __restrict__ res_out, const bf16* __restrict__ x,
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(bf16* __restrict__ out, bf16* __restrict__ res_out, const bf16* __restrict__ x,
                                const bf16* __restrict__ residual, const bf16* __restrict__ w, int H, float eps) {
   extern __shared__ float srow[];            // H floats: the (summed) row in fp32
   __shared__ float scratch[32];
@@ -260,7 +260,7 @@ __global__ void splitk_reduce_kernel(bf16* __restrict__ out, const float* __rest
 // One block per row: y = bf16(sum_s part); s = y + residual; res_out = bf16(s);
 // out = rmsnorm(s) * w.  Rounding y to bf16 first keeps the value stream of a bf16 GEMM
 // followed by a separate add+RMSNorm.
-__global__ void splitk_add_rmsnorm_kernel(bf16* __restrict__ out, bf16* __restrict__ res_out,
+__global__ void __launch_bounds__(512) splitk_add_rmsnorm_kernel(bf16* __restrict__ out, bf16* __restrict__ res_out,
                                           const float* __restrict__ part, const bf16* __restrict__ residual,
                                           const bf16* __restrict__ w, int S, int T, int N, float eps) {
   extern __shared__ float srow[];
@@ -537,7 +537,7 @@ void splitk_reduce_add_rmsnorm(at::Tensor out, at::Tensor res_out, at::Tensor pa
   LSB_CHECK(N % 4 == 0 && residual.numel() == (int64_t)T * N, "shape mismatch");
   if (T == 0) return;
   const at::cuda::CUDAGuard g(out.device());
-  int threads = std::min(1024, std::max(32, ((N / 4 + 31) / 32) * 32));
+  int threads = std::min(512, std::max(32, ((N / 4 + 31) / 32) * 32));
   splitk_add_rmsnorm_kernel<<<T, threads, N * sizeof(float), stream()>>>(
       (bf16*)out.data_ptr(), (bf16*)res_out.data_ptr(), partials.data_ptr<float>(), (const bf16*)residual.data_ptr(),
       (const bf16*)w.data_ptr(), S, T, N, (float)eps);

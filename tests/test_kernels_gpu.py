@@ -45,10 +45,11 @@ def test_gemm_split_k_partials_sum(splits):
     assert rel_err(parts.sum(0), ref) < 1e-3
 
 
-def test_rms_norm_and_add():
-    x = torch.randn(37, 4096, device=DEV).bfloat16()
-    r = torch.randn(37, 4096, device=DEV).bfloat16()
-    w = (1 + 0.1 * torch.randn(4096, device=DEV)).bfloat16()
+@pytest.mark.parametrize("H", [256, 4096, 8192])
+def test_rms_norm_and_add(H):
+    x = torch.randn(37, H, device=DEV).bfloat16()
+    r = torch.randn(37, H, device=DEV).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).bfloat16()
     assert rel_err(norm.rms_norm(x, w, 1e-6), norm.rms_norm_ref(x.cpu(), w.cpu(), 1e-6).to(DEV)) < 5e-3
     o, res = norm.add_rms_norm(x, r, w, 1e-6)
     ro, rres = norm.add_rms_norm_ref(x.cpu(), r.cpu(), w.cpu(), 1e-6)
@@ -56,11 +57,12 @@ def test_rms_norm_and_add():
     assert rel_err(res, rres.to(DEV)) < 5e-3
 
 
-def test_splitk_reduce_add_rmsnorm():
-    parts = torch.randn(4, 9, 512, device=DEV)
-    r = torch.randn(9, 512, device=DEV).bfloat16()
-    w = torch.ones(512, device=DEV).bfloat16()
-    out = torch.empty(9, 512, device=DEV, dtype=torch.bfloat16)
+@pytest.mark.parametrize("N", [512, 4096, 8192])
+def test_splitk_reduce_add_rmsnorm(N):
+    parts = torch.randn(4, 9, N, device=DEV)
+    r = torch.randn(9, N, device=DEV).bfloat16()
+    w = torch.ones(N, device=DEV).bfloat16()
+    out = torch.empty(9, N, device=DEV, dtype=torch.bfloat16)
     res = torch.empty_like(out)
     C().splitk_reduce_add_rmsnorm(out, res, parts, r, w, 1e-6)
     ro, rres = norm.add_rms_norm_ref(parts.sum(0).bfloat16().cpu(), r.cpu(), w.cpu(), 1e-6)
