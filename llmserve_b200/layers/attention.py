@@ -24,7 +24,7 @@ class Attention(nn.Module):
     def forward(self, qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
                 q_norm_w: torch.Tensor | None, k_norm_w: torch.Tensor | None, eps: float) -> torch.Tensor:
         ctx = get_context()
-        T = qkv.shape[0]
+        T = positions.shape[0]
         if ctx.tree_attention_mask is not None:
             q, k, v = rope_ops.qkv_norm_rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps,
                                                    None, None, None, self.num_heads, self.num_kv_heads,

@@ -107,6 +107,16 @@ class MergedColumnParallelLinear(ColumnParallelLinear):
 class QKVParallelLinear(ColumnParallelLinear):
     """q, k and v projections stored as [q heads | k heads | v heads] of this rank."""
 
+    def forward_partials(self, x):
+        """On CUDA with split K: the fp32 partials ``[S, T, W]`` (the QK-norm/RoPE kernel reduces
+        them); otherwise the projection output."""
+        if x.is_cuda and self.quant_method is None and self.bias is None:
+            x2 = x.reshape(-1, x.shape[-1])
+            splits = gemm.choose_splits(x2.shape[0], self.weight.shape[0], x2.shape[1])
+            if splits > 1:
+                return gemm.linear_partials(x2.contiguous(), self.weight, splits)
+        return self.forward(x)
+
     def __init__(self, hidden_size, head_size, total_num_heads, total_num_kv_heads=None, bias=False,
                  quant_config=None):
         world = tp.get_tp_size()

@@ -67,7 +67,7 @@ class Qwen3Attention(nn.Module):
             self.k_norm = RMSNorm(self.head_dim, eps=self.eps)
 
     def attention_core(self, positions, h):
-        qkv = self.qkv_proj(h)
+        qkv = self.qkv_proj.forward_partials(h)
         qw = None if self.qkv_bias else self.q_norm.weight
         kw = None if self.qkv_bias else self.k_norm.weight
         return self.attn(qkv, positions, self.cos_sin, qw, kw, self.eps)

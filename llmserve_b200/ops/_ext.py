@@ -9,7 +9,7 @@ _C = None
 _PROXY = None
 
 # kernels launched per extension call (calls not listed launch one kernel)
-_KERNELS_PER_CALL = {"decode_attention": 2}
+_KERNELS_PER_CALL = {}
 
 
 class LaunchCounter:

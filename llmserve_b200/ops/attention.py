@@ -6,7 +6,8 @@ region for the prefill->decode KV push.
 
 * ``decode_attention``  -- one query token per sequence (``flash_attn_with_kvcache`` in the
   reference, ``llmserve/layers/attention.py:130-132``).  sm_100a split-KV kernel with the query
-  heads of one KV head packed together (GQA), followed by a log-sum-exp combine.
+  heads of one KV head packed together (GQA); the last CTA of a (sequence, KV head) merges the
+  splits (log-sum-exp), so one launch per layer.
 * ``prefill_attention`` -- varlen causal attention of a query chunk against the paged keys of
   its sequence (``flash_attn_varlen_func(..., block_table)`` in the reference, ``:121-126``):
   covers plain prefill, chunked prefill, prefix-cache hits and the packed EAGLE3 verify.
@@ -76,7 +77,14 @@ def tree_attention_ref(q, k_cache, v_cache, block_table, prefix_len, tree_k, tre
     return _attend(q, k, v, scale, mask)
 
 
-DECODE_PARTITION = 512   # keys per split of the split-KV decode kernel
+DECODE_PARTITION = 128   # key granularity of a split (the kernel widens splits for large batches)
+
+
+def decode_partition(batch: int, kv_heads: int) -> int:
+    """Keys per split: short splits (more CTAs) for small batches, long pipelined splits once the
+    (sequence, kv head) pairs alone fill the GPU."""
+    pairs = batch * kv_heads
+    return 128 if pairs < 148 else 256 if pairs < 296 else 512
 
 
 class DecodeWorkspace:
@@ -85,11 +93,13 @@ class DecodeWorkspace:
 
     def __init__(self, max_batch: int, num_heads: int, head_dim: int, max_context: int, device):
         self.max_batch = max_batch
-        self.max_splits = max(1, -(-max_context // DECODE_PARTITION))
+        self.max_splits = max(1, -(-max_context // 128))
         self.partial_out = torch.empty(max_batch * num_heads * self.max_splits * head_dim,
                                        dtype=torch.float32, device=device)
         self.partial_ml = torch.empty(max_batch * num_heads * self.max_splits * 2,
                                       dtype=torch.float32, device=device)
+        # per (sequence, kv head) split-completion counters; the merging CTA resets its counter
+        self.counters = torch.zeros(max_batch * num_heads, dtype=torch.int32, device=device)
 
 
 def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, workspace=None):
@@ -97,11 +107,13 @@ def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, wor
         return decode_attention_ref(q, k_cache, v_cache, block_tables, context_lens, scale)
     B, nh, hd = q.shape
     cap = block_tables.shape[1] * k_cache.shape[2]
-    if workspace is None or workspace.max_batch < B or workspace.max_splits * DECODE_PARTITION < cap:
+    if workspace is None or workspace.max_batch < B or workspace.max_splits * 128 < cap:
         workspace = DecodeWorkspace(B, nh, hd, cap, q.device)
     out = torch.empty_like(q)
+    part = decode_partition(B, k_cache.shape[1])
     C().decode_attention(out, q.contiguous(), k_cache, v_cache, block_tables, context_lens, float(scale),
-                         workspace.partial_out, workspace.partial_ml, workspace.max_splits, DECODE_PARTITION)
+                         workspace.partial_out, workspace.partial_ml, workspace.counters,
+                         -(-workspace.max_splits * 128 // part), part)
     return out
 
 

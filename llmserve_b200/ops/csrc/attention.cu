@@ -149,25 +149,33 @@ __device__ __forceinline__ void qk16(float* s0, float* s1, const uint32_t (*qa)[
 // ------------------------------------------------------------------------------------------
 // Decode
 // ------------------------------------------------------------------------------------------
+// grid (B, kv_heads, Z): CTA z handles splits z, z+Z, ... of `partition` keys each.  A split's
+// result is written straight to `out` when the context has one split; otherwise it goes to the
+// workspace and the CTA that finishes the last split of (b, kv head) -- detected with a per-pair
+// counter that it resets afterwards -- merges all splits.
 template <int HD>
 __global__ void __launch_bounds__(NTHREADS) decode_kernel(
     bf16* __restrict__ out, const bf16* __restrict__ q, const bf16* __restrict__ kc, const bf16* __restrict__ vc,
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ context_lens, float scale_log2,
-    float* __restrict__ part_o, float* __restrict__ part_ml, int max_splits, int partition, int nh, int nkv, int bs) {
+    float* __restrict__ part_o, float* __restrict__ part_ml, int* __restrict__ counters, int max_splits,
+    int partition, int nh, int nkv, int bs) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) char smem[];
+  __shared__ int is_last;
   bf16* sk[2] = {reinterpret_cast<bf16*>(smem), reinterpret_cast<bf16*>(smem + 2 * KT * HD * 2)};
   bf16* sv[2] = {reinterpret_cast<bf16*>(smem + KT * HD * 2), reinterpret_cast<bf16*>(smem + 3 * KT * HD * 2)};
-  const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int b = blockIdx.x, kvh = blockIdx.y;
   const int G = nh / nkv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int ctx = context_lens[b];
-  const int kstart = split * partition;
-  if (kstart >= ctx && !(split == 0)) return;
-  const int kend = min(kstart + partition, ctx);
   const int nsplits = (ctx + partition - 1) / partition;
   const int* bt = block_tables + (size_t)b * bt_stride;
-
-  // Q fragments: rows = packed heads (row r -> head kvh*G + r, valid r < G)
+  if (nsplits == 0) {
+    if (blockIdx.z == 0)
+      for (int i = threadIdx.x; i < G * HD; i += NTHREADS) out[((size_t)b * nh + kvh * G) * HD + i] = to_b(0.f);
+    return;
+  }
   uint32_t qa[HD / 16][4];
   {
     const int r0 = lane >> 2, c = (lane & 3) * 2;
@@ -185,109 +193,116 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(
       qa[kk][3] = ld(r0 + 8, col + 8);
     }
   }
-  float o[HD / 8][4];
+  float* so = reinterpret_cast<float*>(smem);   // [4 warps][16 rows][HD] once the tiles are consumed
+  float* sm = so + 4 * 16 * HD;
+  float* sl = sm + 64;
+  const int g = lane >> 2, c2 = (lane & 3) * 2;
+  for (int split = blockIdx.z; split < nsplits; split += gridDim.z) {
+    const int kstart = split * partition;
+    const int kend = min(kstart + partition, ctx);
+    const int ntiles = (kend - kstart + KT - 1) / KT;
+    float o[HD / 8][4];
 #pragma unroll
-  for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-
-  const int ntiles = kend > kstart ? (kend - kstart + KT - 1) / KT : 0;
-  if (ntiles > 0) {
+    for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    __syncthreads();   // shared memory is reused across splits
     load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, kstart, kend, kvh, nkv, bs);
     cp_async_commit();
-  }
-  for (int t = 0; t < ntiles; ++t) {
-    if (t + 1 < ntiles) {
-      load_kv_tile<HD>(sk[(t + 1) & 1], sv[(t + 1) & 1], kc, vc, bt, kstart + (t + 1) * KT, kend, kvh, nkv, bs);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+    for (int t = 0; t < ntiles; ++t) {
+      if (t + 1 < ntiles) {
+        load_kv_tile<HD>(sk[(t + 1) & 1], sv[(t + 1) & 1], kc, vc, bt, kstart + (t + 1) * KT, kend, kvh, nkv, bs);
+        cp_async_commit();
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+      const int key0 = warp * 16;
+      float s0[4], s1[4];
+      qk16<HD>(s0, s1, qa, smem_u32(sk[t & 1]), key0);
+      const int kbase = kstart + t * KT + key0 + (lane & 3) * 2;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int kp = kbase + (i & 1);
+        s0[i] = kp < kend ? s0[i] * scale_log2 : -INFINITY;
+        s1[i] = kp + 8 < kend ? s1[i] * scale_log2 : -INFINITY;
+      }
+      softmax_pv<HD>(s0, s1, m, l, o, smem_u32(sv[t & 1]), key0);
+      __syncthreads();
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
+      l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
     }
     __syncthreads();
-    const int key0 = warp * 16;
-    float s0[4], s1[4];
-    qk16<HD>(s0, s1, qa, smem_u32(sk[t & 1]), key0);
-    const int kbase = kstart + t * KT + key0 + (lane & 3) * 2;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int kp = kbase + (i & 1);
-      s0[i] = kp < kend ? s0[i] * scale_log2 : -INFINITY;
-      s1[i] = kp + 8 < kend ? s1[i] * scale_log2 : -INFINITY;
+    for (int n = 0; n < HD / 8; ++n) {
+      so[(warp * 16 + g) * HD + n * 8 + c2] = o[n][0];
+      so[(warp * 16 + g) * HD + n * 8 + c2 + 1] = o[n][1];
+      so[(warp * 16 + g + 8) * HD + n * 8 + c2] = o[n][2];
+      so[(warp * 16 + g + 8) * HD + n * 8 + c2 + 1] = o[n][3];
     }
-    softmax_pv<HD>(s0, s1, m, l, o, smem_u32(sv[t & 1]), key0);
+    if ((lane & 3) == 0) {
+      sm[warp * 16 + g] = m[0];
+      sm[warp * 16 + g + 8] = m[1];
+      sl[warp * 16 + g] = l[0];
+      sl[warp * 16 + g + 8] = l[1];
+    }
     __syncthreads();
-  }
-  // quad-reduce the per-lane row sums
+    for (int idx = threadIdx.x; idx < G * HD; idx += NTHREADS) {
+      const int r = idx / HD, d = idx % HD;
+      float M = -INFINITY;
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
-    l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
-  }
-  // cross-warp merge through shared memory (reuses the tile buffers)
-  float* so = reinterpret_cast<float*>(smem);                // [4 warps][16 rows][HD]
-  float* sm = so + 4 * 16 * HD;                               // [4][16] max
-  float* sl = sm + 64;                                        // [4][16] sum
-  const int g = lane >> 2, c2 = (lane & 3) * 2;
+      for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float L = 0.f, O = 0.f;
 #pragma unroll
-  for (int n = 0; n < HD / 8; ++n) {
-    so[(warp * 16 + g) * HD + n * 8 + c2] = o[n][0];
-    so[(warp * 16 + g) * HD + n * 8 + c2 + 1] = o[n][1];
-    so[(warp * 16 + g + 8) * HD + n * 8 + c2] = o[n][2];
-    so[(warp * 16 + g + 8) * HD + n * 8 + c2 + 1] = o[n][3];
-  }
-  if ((lane & 3) == 0) {
-    sm[warp * 16 + g] = m[0];
-    sm[warp * 16 + g + 8] = m[1];
-    sl[warp * 16 + g] = l[0];
-    sl[warp * 16 + g + 8] = l[1];
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < G * HD; idx += NTHREADS) {
-    const int r = idx / HD, d = idx % HD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
-    const float Mu = M == -INFINITY ? 0.f : M;
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const float f = exp2f(sm[w * 16 + r] - Mu);
-      L += sl[w * 16 + r] * f;
-      O += so[(w * 16 + r) * HD + d] * f;
-    }
-    const int h = kvh * G + r;
-    if (nsplits <= 1) {
-      out[((size_t)b * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
-    } else {
-      const size_t base = ((size_t)b * nh + h) * max_splits + split;
-      part_o[base * HD + d] = O;
-      if (d == 0) {
-        part_ml[base * 2] = M;
-        part_ml[base * 2 + 1] = L;
+      for (int w = 0; w < 4; ++w) {
+        const float f = exp2f(sm[w * 16 + r] - Mu);
+        L += sl[w * 16 + r] * f;
+        O += so[(w * 16 + r) * HD + d] * f;
+      }
+      const int h = kvh * G + r;
+      if (nsplits == 1) {
+        out[((size_t)b * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
+      } else {
+        const size_t base = ((size_t)b * nh + h) * max_splits + split;
+        part_o[base * HD + d] = O;
+        if (d == 0) {
+          part_ml[base * 2] = M;
+          part_ml[base * 2 + 1] = L;
+        }
       }
     }
-  }
-}
-
-template <int HD>
-__global__ void decode_combine_kernel(bf16* __restrict__ out, const float* __restrict__ part_o,
-                                      const float* __restrict__ part_ml, const int* __restrict__ context_lens,
-                                      int max_splits, int partition, int nh) {
-  const int b = blockIdx.x, h = blockIdx.y;
-  const int ns = (context_lens[b] + partition - 1) / partition;
-  if (ns <= 1) return;
-  const size_t base = ((size_t)b * nh + h) * max_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, part_ml[(base + s) * 2]);
-  const float Mu = M == -INFINITY ? 0.f : M;
-  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < ns; ++s) {
-      const float f = exp2f(part_ml[(base + s) * 2] - Mu);
-      L += part_ml[(base + s) * 2 + 1] * f;
-      O += part_o[(base + s) * HD + d] * f;
+    if (nsplits == 1) continue;
+    // publish this split; the CTA that completes the last one merges them all
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int* cnt = counters + (size_t)b * nkv + kvh;
+      const int prev = atomicAdd(cnt, 1);
+      is_last = prev == nsplits - 1;
+      if (is_last) *cnt = 0;
     }
-    out[((size_t)b * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
+    __syncthreads();
+    if (!is_last) continue;
+    __threadfence();
+    for (int idx = threadIdx.x; idx < G * HD; idx += NTHREADS) {
+      const int r = idx / HD, d = idx % HD;
+      const int h = kvh * G + r;
+      const size_t base = ((size_t)b * nh + h) * max_splits;
+      float M = -INFINITY;
+      for (int sp = 0; sp < nsplits; ++sp) M = fmaxf(M, __ldcg(&part_ml[(base + sp) * 2]));
+      const float Mu = M == -INFINITY ? 0.f : M;
+      float L = 0.f, O = 0.f;
+      for (int sp = 0; sp < nsplits; ++sp) {
+        const float f = exp2f(__ldcg(&part_ml[(base + sp) * 2]) - Mu);
+        L += __ldcg(&part_ml[(base + sp) * 2 + 1]) * f;
+        O += __ldcg(&part_o[(base + sp) * HD + d]) * f;
+      }
+      out[((size_t)b * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
+    }
   }
 }
 
@@ -299,6 +314,8 @@ __global__ void __launch_bounds__(NTHREADS) prefill_kernel(
     bf16* __restrict__ out, const bf16* __restrict__ q, const bf16* __restrict__ kc, const bf16* __restrict__ vc,
     const int* __restrict__ cu_q, const int* __restrict__ seqlens_k, const int* __restrict__ block_tables,
     int bt_stride, float scale_log2, int nh, int nkv, int bs, int tiles_per_seq) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(128) char smem[];
   bf16* sq = reinterpret_cast<bf16*>(smem);
   bf16* sk[2] = {reinterpret_cast<bf16*>(smem + KT * HD * 2), reinterpret_cast<bf16*>(smem + 3 * KT * HD * 2)};
@@ -396,6 +413,8 @@ __global__ void tree_kernel(bf16* __restrict__ out, const bf16* __restrict__ q, 
                             const bf16* __restrict__ vc, const int* __restrict__ bt, int prefix_len,
                             const bf16* __restrict__ tk, const bf16* __restrict__ tv, int n_tree,
                             const int* __restrict__ mask_bits, float scale_log2, int nh, int nkv, int bs) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int PER = HD / 32;
   __shared__ float sm[4], sl[4], so[4][HD];
   const int qi = blockIdx.x, h = blockIdx.y, kvh = h / (nh / nkv);
@@ -462,34 +481,34 @@ void check_pool(const at::Tensor& kc, const at::Tensor& vc) {
 constexpr int decode_smem(int hd) { return 4 * KT * hd * 2 > (4 * 16 * hd + 128) * 4 ? 4 * KT * hd * 2 : (4 * 16 * hd + 128) * 4; }
 
 void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
-                      at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, int64_t max_splits,
-                      int64_t partition) {
+                      at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, at::Tensor counters,
+                      int64_t max_splits, int64_t partition) {
   check_pool(kc, vc);
   LSB_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q must be bf16 [B, nh, hd]");
   LSB_CHECK(block_tables.scalar_type() == at::kInt && block_tables.is_contiguous(), "block_tables must be int32");
   LSB_CHECK(context_lens.scalar_type() == at::kInt, "context_lens must be int32");
+  LSB_CHECK(counters.scalar_type() == at::kInt, "counters must be int32");
   const int B = q.size(0), nh = q.size(1), hd = q.size(2), nkv = kc.size(1), bs = kc.size(2);
   LSB_CHECK(kc.size(3) == hd && nh % nkv == 0 && nh / nkv <= 16, "head layout unsupported (group size <= 16)");
   LSB_CHECK(partition % KT == 0, "partition must be a multiple of 64");
   LSB_CHECK(block_tables.size(1) * (int64_t)bs <= max_splits * partition, "workspace has too few splits");
   LSB_CHECK(part_o.numel() >= (int64_t)B * nh * max_splits * hd && part_ml.numel() >= (int64_t)B * nh * max_splits * 2,
             "decode workspace too small");
+  LSB_CHECK(counters.numel() >= (int64_t)B * nkv, "decode counters too small");
   if (B == 0) return;
   const at::cuda::CUDAGuard g(q.device());
-  dim3 grid(B, nkv, max_splits);
+  // CTAs per (sequence, kv head): one when the batch alone gives >= 2 waves, else enough to fill the SMs
+  const int z = (int)std::max<int64_t>(1, std::min<int64_t>(max_splits, (148 * 3 + B * nkv - 1) / (B * nkv)));
+  dim3 grid(B, nkv, z);
   const float sl = (float)scale * kLog2e;
 #define LSB_DEC(HD)                                                                                                \
   do {                                                                                                             \
     const int smem = decode_smem(HD);                                                                              \
     cudaFuncSetAttribute(decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                    \
-    decode_kernel<HD><<<grid, NTHREADS, smem, stream()>>>(                                                         \
-        (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(),   \
-        block_tables.data_ptr<int>(), block_tables.size(1), context_lens.data_ptr<int>(), sl,                        \
-        part_o.data_ptr<float>(), part_ml.data_ptr<float>(), max_splits, partition, nh, nkv, bs);                  \
-    decode_combine_kernel<HD><<<dim3(B, nh), HD, 0, stream()>>>((bf16*)out.data_ptr(), part_o.data_ptr<float>(),   \
-                                                                part_ml.data_ptr<float>(),                         \
-                                                                context_lens.data_ptr<int>(), max_splits,          \
-                                                                partition, nh);                                    \
+    launch_pdl(decode_kernel<HD>, grid, NTHREADS, smem, stream(), (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), \
+               (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(), block_tables.data_ptr<int>(),               \
+               (int)block_tables.size(1), context_lens.data_ptr<int>(), sl, part_o.data_ptr<float>(),             \
+               part_ml.data_ptr<float>(), counters.data_ptr<int>(), (int)max_splits, (int)partition, nh, nkv, bs); \
   } while (0)
   if (hd == 128) LSB_DEC(128);
   else if (hd == 64) LSB_DEC(64);
@@ -513,7 +532,7 @@ void prefill_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor v
   do {                                                                                                            \
     const int smem = 5 * KT * HD * 2;                                                                             \
     cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                  \
-    prefill_kernel<HD><<<grid, NTHREADS, smem, stream()>>>(                                                       \
+    launch_pdl(prefill_kernel<HD>, grid, NTHREADS, smem, stream(),                                                        \
         (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(),  \
         cu_q.data_ptr<int>(), seqlens_k.data_ptr<int>(), block_tables.data_ptr<int>(), block_tables.size(1), sl,   \
         nh, nkv, bs, tiles);                                                                                      \
@@ -534,12 +553,12 @@ void tree_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, 
   const at::cuda::CUDAGuard g(q.device());
   const float sl = (float)scale * kLog2e;
   if (hd == 128)
-    tree_kernel<128><<<dim3(n, nh), 128, 0, stream()>>>(
+    launch_pdl(tree_kernel<128>, dim3(n, nh), 128, 0, stream(), 
         (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(),
         bt.data_ptr<int>(), prefix_len, (const bf16*)tk.data_ptr(), (const bf16*)tv.data_ptr(), tk.size(0),
         mask_bits.data_ptr<int>(), sl, nh, nkv, bs);
   else if (hd == 64)
-    tree_kernel<64><<<dim3(n, nh), 128, 0, stream()>>>(
+    launch_pdl(tree_kernel<64>, dim3(n, nh), 128, 0, stream(), 
         (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(),
         bt.data_ptr<int>(), prefix_len, (const bf16*)tk.data_ptr(), (const bf16*)tv.data_ptr(), tk.size(0),
         mask_bits.data_ptr<int>(), sl, nh, nkv, bs);

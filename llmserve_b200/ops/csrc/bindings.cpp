@@ -19,13 +19,14 @@ void splitk_reduce_add_rmsnorm(at::Tensor out, at::Tensor res_out, at::Tensor pa
 void argmax_rows(at::Tensor out_idx, at::Tensor out_val, at::Tensor logits);
 void sample_rows(at::Tensor out, at::Tensor logits, at::Tensor temps, int64_t seed);
 void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
-                      at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, int64_t max_splits,
-                      int64_t partition);
+                      at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, at::Tensor counters,
+                      int64_t max_splits, int64_t partition);
 void prefill_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,
                        at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_seqlen_q);
 void tree_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bt, int64_t prefix_len,
                     at::Tensor tk, at::Tensor tv, at::Tensor mask_bits, double scale);
-void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status);
+void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status,
+               int64_t max_stages);
 }  // namespace lsb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -44,5 +45,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &lsb::decode_attention);
   m.def("prefill_attention", &lsb::prefill_attention);
   m.def("tree_attention", &lsb::tree_attention);
-  m.def("gemm_bf16", &lsb::gemm_bf16);
+  m.def("gemm_bf16", &lsb::gemm_bf16, py::arg("out"), py::arg("x"), py::arg("w"), py::arg("partials"),
+        py::arg("splits"), py::arg("status"), py::arg("max_stages") = 0);
 }

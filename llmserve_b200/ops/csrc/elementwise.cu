@@ -8,6 +8,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <cstdlib>
+#include <tuple>
+
 #include "common.cuh"
 
 namespace lsb {
@@ -34,6 +37,8 @@ struct alignas(16) Vec8 {
 template <bool kAddResidual>
 __global__ void __launch_bounds__(1024) rmsnorm_kernel(bf16* __restrict__ out, bf16* __restrict__ res_out, const bf16* __restrict__ x,
                                const bf16* __restrict__ residual, const bf16* __restrict__ w, int H, float eps) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float srow[];            // H floats: the (summed) row in fp32
   __shared__ float scratch[32];
   const int row = blockIdx.x;
@@ -77,6 +82,8 @@ int norm_threads(int H) {
 // SiLU-mul: out[t, i] = bf16(silu(x[t, i]) * x[t, I + i])
 // ------------------------------------------------------------------------------------------
 __global__ void silu_mul_kernel(bf16* __restrict__ out, const bf16* __restrict__ x, int I, int64_t total_vec) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int vec_per_row = I / 8;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total_vec; v += stride) {
@@ -99,6 +106,8 @@ __global__ void silu_mul_kernel(bf16* __restrict__ out, const bf16* __restrict__
 // ------------------------------------------------------------------------------------------
 __global__ void embedding_kernel(bf16* __restrict__ out, const int64_t* __restrict__ ids, const bf16* __restrict__ table,
                                  int H, int64_t V, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t id = ids[blockIdx.x];
   bf16* o = out + (size_t)blockIdx.x * H;
   if (id < 0 || id >= V) {
@@ -117,13 +126,16 @@ __global__ void embedding_kernel(bf16* __restrict__ out, const int64_t* __restri
 // Lane l owns dims [l*P, l*P+P) of the first half and the same offsets in the second half
 // (P = hd/64), which are exactly the pairs the rotation mixes.
 // ------------------------------------------------------------------------------------------
-template <int P, bool kStore>
+template <int P, bool kStore, int S>
 __global__ void qkv_rope_kernel(bf16* __restrict__ q_out, bf16* __restrict__ k_out, const bf16* __restrict__ qkv,
+                                const float* __restrict__ part,
                                 const int64_t* __restrict__ positions, const float* __restrict__ cos_sin,
                                 const bf16* __restrict__ q_w, const bf16* __restrict__ k_w, float eps,
                                 bf16* __restrict__ k_cache, bf16* __restrict__ v_cache,
                                 const int* __restrict__ slot_mapping, int T, int nh, int nkv, int block_size,
                                 int64_t num_slots, int* status) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int HD = 64 * P;
   constexpr int HALF = HD / 2;
   const int warps_per_block = blockDim.x >> 5;
@@ -132,13 +144,38 @@ __global__ void qkv_rope_kernel(bf16* __restrict__ q_out, bf16* __restrict__ k_o
   const int lane = threadIdx.x & 31;
   const int nheads = nh + 2 * nkv;
   if (head >= nheads) return;
-  const bf16* src = qkv + (size_t)t * nheads * HD + (size_t)head * HD;
+  const size_t row_off = (size_t)t * nheads * HD + (size_t)head * HD;
   const int d0 = lane * P;
   float a[P], b[P];
+  if constexpr (S == 0) {
+    const bf16* src = qkv + row_off;
 #pragma unroll
-  for (int j = 0; j < P; ++j) {
-    a[j] = to_f(src[d0 + j]);
-    b[j] = to_f(src[HALF + d0 + j]);
+    for (int j = 0; j < P; ++j) {
+      a[j] = to_f(src[d0 + j]);
+      b[j] = to_f(src[HALF + d0 + j]);
+    }
+  } else {
+    // fused split-K reduction of the QKV projection (rounded to bf16 like a bf16 GEMM output)
+    const size_t plane = (size_t)T * nheads * HD;
+    float pa[S][P], pb[S][P];
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        pa[s][j] = __ldcg(part + s * plane + row_off + d0 + j);
+        pb[s][j] = __ldcg(part + s * plane + row_off + HALF + d0 + j);
+      }
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      float x = 0.f, y = 0.f;
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        x += pa[s][j];
+        y += pb[s][j];
+      }
+      a[j] = to_f(to_b(x));
+      b[j] = to_f(to_b(y));
+    }
   }
   const bool is_q = head < nh, is_k = !is_q && head < nh + nkv;
   if (is_q || is_k) {
@@ -204,6 +241,8 @@ __global__ void qkv_rope_kernel(bf16* __restrict__ q_out, bf16* __restrict__ k_o
 __global__ void store_kv_kernel(const bf16* __restrict__ k, const bf16* __restrict__ v, bf16* __restrict__ k_cache,
                                 bf16* __restrict__ v_cache, const int* __restrict__ slots, int nkv, int hd,
                                 int block_size, int64_t num_slots, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x, h = blockIdx.y;
   const int slot = slots[t];
   if (slot < 0) return;
@@ -225,6 +264,8 @@ __global__ void commit_tree_kv_kernel(const bf16* __restrict__ tk, const bf16* _
                                       bf16* __restrict__ vc, const int* __restrict__ nodes, const int* __restrict__ slots,
                                       int n_nodes, int nkv, int hd, int block_size, int64_t blocks_per_layer,
                                       int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int layer = blockIdx.x, j = blockIdx.y, h = blockIdx.z;
   const int node = nodes[j], slot = slots[j];
   if (node < 0 || node >= n_nodes || slot < 0 || slot >= blocks_per_layer * block_size) {
@@ -244,6 +285,8 @@ __global__ void commit_tree_kv_kernel(const bf16* __restrict__ tk, const bf16* _
 // split-K reductions (partials fp32 [S, T, N])
 // ------------------------------------------------------------------------------------------
 __global__ void splitk_reduce_kernel(bf16* __restrict__ out, const float* __restrict__ part, int S, int64_t TN) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x * 4;
   for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < TN; i += stride) {
     float4 acc = *reinterpret_cast<const float4*>(part + i);
@@ -259,34 +302,70 @@ __global__ void splitk_reduce_kernel(bf16* __restrict__ out, const float* __rest
 
 // One block per row: y = bf16(sum_s part); s = y + residual; res_out = bf16(s);
 // out = rmsnorm(s) * w.  Rounding y to bf16 first keeps the value stream of a bf16 GEMM
-// followed by a separate add+RMSNorm.
+// followed by a separate add+RMSNorm.  All split loads of a thread are issued before any use
+// (compile-time split count), so the row costs one memory latency, not one per split.
+template <int S>
 __global__ void __launch_bounds__(512) splitk_add_rmsnorm_kernel(bf16* __restrict__ out, bf16* __restrict__ res_out,
-                                          const float* __restrict__ part, const bf16* __restrict__ residual,
-                                          const bf16* __restrict__ w, int S, int T, int N, float eps) {
+                                                                 const float* __restrict__ part,
+                                                                 const bf16* __restrict__ residual,
+                                                                 const bf16* __restrict__ w, int S_rt, int T, int N,
+                                                                 float eps) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float srow[];
   __shared__ float scratch[32];
   const int row = blockIdx.x;
   const int64_t TN = (int64_t)T * N;
+  const int nsplit = S > 0 ? S : S_rt;
   float ss = 0.f;
   for (int i = threadIdx.x * 4; i < N; i += blockDim.x * 4) {
     const int64_t off = (int64_t)row * N + i;
-    float4 acc = *reinterpret_cast<const float4*>(part + off);
-    for (int s = 1; s < S; ++s) {
-      const float4 p = *reinterpret_cast<const float4*>(part + s * TN + off);
-      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (S > 0) {
+      float4 p[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) p[s] = __ldcg(reinterpret_cast<const float4*>(part + s * TN + off));
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        acc.x += p[s].x; acc.y += p[s].y; acc.z += p[s].z; acc.w += p[s].w;
+      }
+    } else {
+      for (int s = 0; s < nsplit; ++s) {
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(part + s * TN + off));
+        acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+      }
     }
-    const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+    const uint2 rraw = *reinterpret_cast<const uint2*>(residual + off);
+    const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rraw.x);
+    const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rraw.y);
+    float v[4] = {to_f(to_b(acc.x)) + __low2float(r01), to_f(to_b(acc.y)) + __high2float(r01),
+                  to_f(to_b(acc.z)) + __low2float(r23), to_f(to_b(acc.w)) + __high2float(r23)};
+    __nv_bfloat162 o01 = __floats2bfloat162_rn(v[0], v[1]), o23 = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 oraw;
+    oraw.x = *reinterpret_cast<uint32_t*>(&o01);
+    oraw.y = *reinterpret_cast<uint32_t*>(&o23);
+    *reinterpret_cast<uint2*>(res_out + off) = oraw;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float v = to_f(to_b(a[j])) + to_f(residual[off + j]);
-      res_out[off + j] = to_b(v);
-      srow[i + j] = v;
-      ss += v * v;
+      srow[i + j] = v[j];
+      ss += v[j] * v[j];
     }
   }
   const float inv = rsqrtf(block_sum(ss, scratch) / N + eps);
-  for (int i = threadIdx.x; i < N; i += blockDim.x)
-    out[(int64_t)row * N + i] = to_b(to_f(to_b(srow[i] * inv)) * to_f(w[i]));
+  for (int i = threadIdx.x * 4; i < N; i += blockDim.x * 4) {
+    const uint2 wraw = *reinterpret_cast<const uint2*>(w + i);
+    const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wraw.x);
+    const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wraw.y);
+    const float wv[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = to_f(to_b(to_f(to_b(srow[i + j] * inv)) * wv[j]));
+    __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0], o[1]), o23 = __floats2bfloat162_rn(o[2], o[3]);
+    uint2 oraw;
+    oraw.x = *reinterpret_cast<uint32_t*>(&o01);
+    oraw.y = *reinterpret_cast<uint32_t*>(&o23);
+    *reinterpret_cast<uint2*>(out + (int64_t)row * N + i) = oraw;
+  }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -338,6 +417,8 @@ __device__ __forceinline__ float load_f<float>(const float* p, int64_t i) { retu
 template <typename T>
 __global__ void argmax_kernel(int64_t* __restrict__ out_idx, float* __restrict__ out_val, const T* __restrict__ logits,
                               int64_t V) {
+  pdl_trigger();
+  pdl_wait();
   const T* row = logits + (int64_t)blockIdx.x * V;
   ArgBest best{-INFINITY, INT64_MAX};
   for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
@@ -364,6 +445,8 @@ __device__ __forceinline__ float counter_uniform(uint64_t seed, uint64_t idx) {
 template <typename T>
 __global__ void sample_kernel(int64_t* __restrict__ out, const T* __restrict__ logits, const float* __restrict__ temps,
                               int64_t V, uint64_t seed) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t r = blockIdx.x;
   const T* row = logits + r * V;
   const float inv_t = 1.f / temps[r];
@@ -384,6 +467,14 @@ int grid_for(int64_t work, int threads) {
 
 }  // namespace
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LLMSERVE_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
 int* status_ptr(const at::Tensor& status) { return status.defined() && status.numel() ? status.data_ptr<int>() : nullptr; }
 
 // ---- host launchers ---------------------------------------------------------------------------
@@ -396,7 +487,7 @@ void rms_norm(at::Tensor out, at::Tensor x, at::Tensor w, double eps) {
   const int64_t rows = x.numel() / H;
   if (rows == 0) return;
   const at::cuda::CUDAGuard g(x.device());
-  rmsnorm_kernel<false><<<rows, norm_threads(H), H * sizeof(float), stream()>>>(
+  launch_pdl(rmsnorm_kernel<false>, rows, norm_threads(H), H * sizeof(float), stream(), 
       (bf16*)out.data_ptr(), nullptr, (const bf16*)x.data_ptr(), nullptr, (const bf16*)w.data_ptr(), H, (float)eps);
 }
 
@@ -410,7 +501,7 @@ void add_rms_norm(at::Tensor out, at::Tensor res_out, at::Tensor x, at::Tensor r
   const int64_t rows = x.numel() / H;
   if (rows == 0) return;
   const at::cuda::CUDAGuard g(x.device());
-  rmsnorm_kernel<true><<<rows, norm_threads(H), H * sizeof(float), stream()>>>(
+  launch_pdl(rmsnorm_kernel<true>, rows, norm_threads(H), H * sizeof(float), stream(), 
       (bf16*)out.data_ptr(), (bf16*)res_out.data_ptr(), (const bf16*)x.data_ptr(), (const bf16*)residual.data_ptr(),
       (const bf16*)w.data_ptr(), H, (float)eps);
 }
@@ -423,7 +514,7 @@ void silu_and_mul(at::Tensor out, at::Tensor x) {
   const int64_t vec = out.numel() / 8;
   if (vec == 0) return;
   const at::cuda::CUDAGuard g(x.device());
-  silu_mul_kernel<<<grid_for(vec, 256), 256, 0, stream()>>>((bf16*)out.data_ptr(), (const bf16*)x.data_ptr(), I, vec);
+  launch_pdl(silu_mul_kernel, grid_for(vec, 256), 256, 0, stream(), (bf16*)out.data_ptr(), (const bf16*)x.data_ptr(), I, vec);
 }
 
 void embedding(at::Tensor out, at::Tensor ids, at::Tensor table, at::Tensor status) {
@@ -434,7 +525,7 @@ void embedding(at::Tensor out, at::Tensor ids, at::Tensor table, at::Tensor stat
   LSB_CHECK(H % 8 == 0, "embedding width must be a multiple of 8");
   if (ids.numel() == 0) return;
   const at::cuda::CUDAGuard g(table.device());
-  embedding_kernel<<<ids.numel(), 128, 0, stream()>>>((bf16*)out.data_ptr(), ids.data_ptr<int64_t>(),
+  launch_pdl(embedding_kernel, ids.numel(), 128, 0, stream(), (bf16*)out.data_ptr(), ids.data_ptr<int64_t>(),
                                                       (const bf16*)table.data_ptr(), H, table.size(0),
                                                       status_ptr(status));
 }
@@ -442,14 +533,25 @@ void embedding(at::Tensor out, at::Tensor ids, at::Tensor table, at::Tensor stat
 void qkv_rope(at::Tensor q_out, at::Tensor k_out, at::Tensor qkv, at::Tensor positions, at::Tensor cos_sin,
               at::Tensor q_w, at::Tensor k_w, double eps, at::Tensor k_cache, at::Tensor v_cache,
               at::Tensor slot_mapping, int64_t nh, int64_t nkv, int64_t hd, bool store, at::Tensor status) {
-  check_bf16(qkv, "qkv");
+  // qkv: bf16 [T, W], or fp32 split-K partials [S, T, W] (S in 1, 2, 4, 8)
+  const bool from_partials = qkv.scalar_type() == at::kFloat;
+  int S = 0;
+  if (from_partials) {
+    LSB_CHECK(qkv.dim() == 3 && qkv.is_contiguous(), "qkv partials must be contiguous [S, T, W]");
+    S = qkv.size(0);
+    LSB_CHECK(S == 1 || S == 2 || S == 4 || S == 8, "qkv partial count must be 1, 2, 4 or 8");
+    LSB_CHECK(store, "partials input needs the paged-store variant");
+    qkv = qkv.view({S * qkv.size(1), qkv.size(2)});
+  } else {
+    check_bf16(qkv, "qkv");
+  }
   check_bf16(q_out, "q_out");
   LSB_CHECK(positions.scalar_type() == at::kLong, "positions must be int64");
   LSB_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin cache must be fp32");
   LSB_CHECK(cos_sin.size(1) == hd, "cos_sin width must equal head_dim");
   LSB_CHECK(hd == 64 || hd == 128, "head_dim must be 64 or 128");
   LSB_CHECK(qkv.size(1) == (nh + 2 * nkv) * hd, "qkv width mismatch");
-  const int T = qkv.size(0);
+  const int T = from_partials ? qkv.size(0) / S : qkv.size(0);
   if (T == 0) return;
   const bf16* qw = q_w.numel() ? (const bf16*)q_w.data_ptr() : nullptr;
   const bf16* kw = k_w.numel() ? (const bf16*)k_w.data_ptr() : nullptr;
@@ -469,17 +571,27 @@ void qkv_rope(at::Tensor q_out, at::Tensor k_out, at::Tensor qkv, at::Tensor pos
   const int warps = 4;
   dim3 grid(T, (heads + warps - 1) / warps);
   const at::cuda::CUDAGuard g(qkv.device());
-#define LSB_ROPE(P, S)                                                                                         \
-  qkv_rope_kernel<P, S><<<grid, warps * 32, 0, stream()>>>(                                                    \
-      (bf16*)q_out.data_ptr(), S ? nullptr : (bf16*)k_out.data_ptr(), (const bf16*)qkv.data_ptr(),             \
-      positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(), qw, kw, (float)eps,                          \
-      S ? (bf16*)k_cache.data_ptr() : nullptr, S ? (bf16*)v_cache.data_ptr() : nullptr,                        \
-      S ? slot_mapping.data_ptr<int>() : nullptr, T, nh, nkv, block_size, num_slots, status_ptr(status))
-  if (hd == 128) {
-    if (store) LSB_ROPE(2, true); else LSB_ROPE(2, false);
-  } else {
-    if (store) LSB_ROPE(1, true); else LSB_ROPE(1, false);
+#define LSB_ROPE(P, ST, SP)                                                                                     \
+  launch_pdl(qkv_rope_kernel<P, ST, SP>, grid, warps * 32, 0, stream(), (bf16*)q_out.data_ptr(),              \
+             ST ? nullptr : (bf16*)k_out.data_ptr(), SP ? nullptr : (const bf16*)qkv.data_ptr(),                  \
+             SP ? qkv.data_ptr<float>() : nullptr, positions.data_ptr<int64_t>(), cos_sin.data_ptr<float>(), qw, \
+             kw, (float)eps, ST ? (bf16*)k_cache.data_ptr() : nullptr, ST ? (bf16*)v_cache.data_ptr() : nullptr,  \
+             ST ? slot_mapping.data_ptr<int>() : nullptr, T, (int)nh, (int)nkv, block_size, num_slots,            \
+             status_ptr(status))
+#define LSB_ROPE_S(P)                       \
+  switch (S) {                              \
+    case 0: LSB_ROPE(P, true, 0); break;    \
+    case 1: LSB_ROPE(P, true, 1); break;    \
+    case 2: LSB_ROPE(P, true, 2); break;    \
+    case 4: LSB_ROPE(P, true, 4); break;    \
+    default: LSB_ROPE(P, true, 8); break;   \
   }
+  if (hd == 128) {
+    if (store) { LSB_ROPE_S(2) } else LSB_ROPE(2, false, 0);
+  } else {
+    if (store) { LSB_ROPE_S(1) } else LSB_ROPE(1, false, 0);
+  }
+#undef LSB_ROPE_S
 #undef LSB_ROPE
 }
 
@@ -494,7 +606,7 @@ void store_kvcache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_
   LSB_CHECK(hd % 8 == 0 && k_cache.size(1) == nkv && k_cache.size(3) == hd, "cache shape mismatch");
   if (T == 0) return;
   const at::cuda::CUDAGuard g(k.device());
-  store_kv_kernel<<<dim3(T, nkv), 32, 0, stream()>>>((const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(),
+  launch_pdl(store_kv_kernel, dim3(T, nkv), 32, 0, stream(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(),
                                                       (bf16*)k_cache.data_ptr(), (bf16*)v_cache.data_ptr(),
                                                       slots.data_ptr<int>(), nkv, hd, k_cache.size(2),
                                                       k_cache.size(0) * k_cache.size(2), status_ptr(status));
@@ -510,7 +622,7 @@ void commit_tree_kv(at::Tensor tk, at::Tensor tv, at::Tensor kc, at::Tensor vc, 
   const int m = nodes.numel();
   if (m == 0) return;
   const at::cuda::CUDAGuard g(tk.device());
-  commit_tree_kv_kernel<<<dim3(L, m, nkv), 32, 0, stream()>>>(
+  launch_pdl(commit_tree_kv_kernel, dim3(L, m, nkv), 32, 0, stream(), 
       (const bf16*)tk.data_ptr(), (const bf16*)tv.data_ptr(), (bf16*)kc.data_ptr(), (bf16*)vc.data_ptr(),
       nodes.data_ptr<int>(), slots.data_ptr<int>(), n, nkv, hd, kc.size(3), kc.size(1), status_ptr(status));
 }
@@ -523,7 +635,7 @@ void splitk_reduce(at::Tensor out, at::Tensor partials) {
   LSB_CHECK(partials.numel() == S * TN && TN % 4 == 0, "partials shape mismatch");
   if (TN == 0) return;
   const at::cuda::CUDAGuard g(out.device());
-  splitk_reduce_kernel<<<grid_for(TN / 4, 256), 256, 0, stream()>>>((bf16*)out.data_ptr(), partials.data_ptr<float>(),
+  launch_pdl(splitk_reduce_kernel, grid_for(TN / 4, 256), 256, 0, stream(), (bf16*)out.data_ptr(), partials.data_ptr<float>(),
                                                                      S, TN);
 }
 
@@ -538,9 +650,18 @@ void splitk_reduce_add_rmsnorm(at::Tensor out, at::Tensor res_out, at::Tensor pa
   if (T == 0) return;
   const at::cuda::CUDAGuard g(out.device());
   int threads = std::min(512, std::max(32, ((N / 4 + 31) / 32) * 32));
-  splitk_add_rmsnorm_kernel<<<T, threads, N * sizeof(float), stream()>>>(
-      (bf16*)out.data_ptr(), (bf16*)res_out.data_ptr(), partials.data_ptr<float>(), (const bf16*)residual.data_ptr(),
-      (const bf16*)w.data_ptr(), S, T, N, (float)eps);
+  auto args = std::make_tuple((bf16*)out.data_ptr(), (bf16*)res_out.data_ptr(), partials.data_ptr<float>(),
+                              (const bf16*)residual.data_ptr(), (const bf16*)w.data_ptr(), S, T, N, (float)eps);
+  auto go = [&](auto kern) {
+    std::apply([&](auto... a) { launch_pdl(kern, T, threads, N * sizeof(float), stream(), a...); }, args);
+  };
+  switch (S) {
+    case 1: go(splitk_add_rmsnorm_kernel<1>); break;
+    case 2: go(splitk_add_rmsnorm_kernel<2>); break;
+    case 4: go(splitk_add_rmsnorm_kernel<4>); break;
+    case 8: go(splitk_add_rmsnorm_kernel<8>); break;
+    default: go(splitk_add_rmsnorm_kernel<0>); break;
+  }
 }
 
 void argmax_rows(at::Tensor out_idx, at::Tensor out_val, at::Tensor logits) {
@@ -549,10 +670,10 @@ void argmax_rows(at::Tensor out_idx, at::Tensor out_val, at::Tensor logits) {
   if (B == 0) return;
   const at::cuda::CUDAGuard g(logits.device());
   if (logits.scalar_type() == at::kBFloat16)
-    argmax_kernel<bf16><<<B, 1024, 0, stream()>>>(out_idx.data_ptr<int64_t>(), out_val.data_ptr<float>(),
+    launch_pdl(argmax_kernel<bf16>, B, 1024, 0, stream(), out_idx.data_ptr<int64_t>(), out_val.data_ptr<float>(),
                                                   (const bf16*)logits.data_ptr(), V);
   else if (logits.scalar_type() == at::kFloat)
-    argmax_kernel<float><<<B, 1024, 0, stream()>>>(out_idx.data_ptr<int64_t>(), out_val.data_ptr<float>(),
+    launch_pdl(argmax_kernel<float>, B, 1024, 0, stream(), out_idx.data_ptr<int64_t>(), out_val.data_ptr<float>(),
                                                    logits.data_ptr<float>(), V);
   else
     LSB_CHECK(false, "argmax supports bf16 and fp32 logits");
@@ -564,10 +685,10 @@ void sample_rows(at::Tensor out, at::Tensor logits, at::Tensor temps, int64_t se
   if (B == 0) return;
   const at::cuda::CUDAGuard g(logits.device());
   if (logits.scalar_type() == at::kBFloat16)
-    sample_kernel<bf16><<<B, 1024, 0, stream()>>>(out.data_ptr<int64_t>(), (const bf16*)logits.data_ptr(),
+    launch_pdl(sample_kernel<bf16>, B, 1024, 0, stream(), out.data_ptr<int64_t>(), (const bf16*)logits.data_ptr(),
                                                   temps.data_ptr<float>(), V, (uint64_t)seed);
   else
-    sample_kernel<float><<<B, 1024, 0, stream()>>>(out.data_ptr<int64_t>(), logits.data_ptr<float>(),
+    launch_pdl(sample_kernel<float>, B, 1024, 0, stream(), out.data_ptr<int64_t>(), logits.data_ptr<float>(),
                                                    temps.data_ptr<float>(), V, (uint64_t)seed);
 }
 

@@ -145,11 +145,22 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  pdl_trigger();
   if (warp == 0) {
-    if (lane == 0 && nk > 0) {
+    if (lane == 0) {
+      // Weights never depend on the previous kernel: stream the first stages of W before waiting
+      // for the predecessor (programmatic dependent launch), then the activations.
+      const int pre = nk < STAGES ? nk : STAGES;
+      for (int i = 0; i < pre; ++i) {
+        mbar_expect_tx(&full[i], L::kStage);
+        tma_load_2d(smem + i * L::kStage, &tm_w, &full[i], (kt_begin + i) * BK, n0);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(smem + i * L::kStage + L::kW, &tm_x, &full[i], (kt_begin + i) * BK, t0);
       int issued[STAGES];
-      for (int s = 0; s < STAGES; ++s) issued[s] = 0;
-      for (int i = 0; i < nk; ++i) {
+      for (int s = 0; s < STAGES; ++s) issued[s] = s < pre ? s + 1 : 0;
+      for (int i = pre; i < nk; ++i) {
         const int s = i % STAGES;
         const uint32_t phase = (i / STAGES) & 1;
         if (!mbar_wait(&empty[s], phase ^ 1)) {
@@ -170,9 +181,12 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
         for (int s = 0; s < STAGES; ++s)
           if (issued[s] > 0) mbar_wait(&full[s], ((issued[s] - 1) / STAGES) & 1);
       }
+    } else {
+      pdl_wait();
     }
     __syncwarp();
   } else if (warp == 1) {
+    pdl_wait();
     if (lane == 0 && nk > 0) {
       constexpr uint32_t idesc = idesc_bf16_f32<BN>();
       bool ok = true;
@@ -196,6 +210,8 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
       if (ok) tc_commit(accum);
     }
     __syncwarp();
+  } else {
+    pdl_wait();
   }
 
   // ---- epilogue ---------------------------------------------------------------------------------
@@ -310,7 +326,8 @@ void launch(const at::Tensor& x, const at::Tensor& w, bf16* out, float* partials
     configured = true;
   }
   dim3 grid((N + BM - 1) / BM, (T + BN - 1) / BN, splits);
-  kern<<<grid, 128, L::kBytes, at::cuda::getCurrentCUDAStream()>>>(mw, mx, out, partials, T, N, k_tiles, kps, status);
+  launch_pdl(kern, grid, dim3(128), L::kBytes, at::cuda::getCurrentCUDAStream(), mw, mx, out, partials, T, N, k_tiles,
+             kps, status);
 }
 
 template <int BN>
@@ -324,7 +341,8 @@ constexpr int stages_for() {
 int* status_ptr(const at::Tensor& status);
 
 // out: bf16 [T, N] when splits == 1; partials: fp32 [splits, T, N] otherwise.
-void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status) {
+void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status,
+               int64_t max_stages) {
   LSB_CHECK(x.is_cuda() && w.is_cuda(), "gemm operands must be CUDA tensors");
   LSB_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
   LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm shape mismatch");
@@ -347,6 +365,13 @@ void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, 
   if (T == 0 || N == 0) return;
   const at::cuda::CUDAGuard g(x.device());
   int* st = status_ptr(status);
+  if (max_stages > 0 && max_stages <= 4 && T <= 64) {
+    // shallow ring: two CTAs fit on one SM and overlap each other's prologue / epilogue
+    if (T <= 16) launch<16, 4>(x, w, o, p, splits, st);
+    else if (T <= 32) launch<32, 4>(x, w, o, p, splits, st);
+    else launch<64, 4>(x, w, o, p, splits, st);
+    return;
+  }
   if (T <= 16) launch<16, stages_for<16>()>(x, w, o, p, splits, st);
   else if (T <= 32) launch<32, stages_for<32>()>(x, w, o, p, splits, st);
   else if (T <= 64) launch<64, stages_for<64>()>(x, w, o, p, splits, st);

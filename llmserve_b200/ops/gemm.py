@@ -20,14 +20,25 @@ TILE_K = 64           # K elements per pipeline stage (128 B rows -> 128B swizzl
 MAX_TILE_T = 256      # tokens per CTA (UMMA N limit)
 
 
+SMALL_T = 64          # up to here the 4-stage ring is used, two CTAs per SM
+
+
 def choose_splits(T: int, N: int, K: int) -> int:
-    """Split K until the grid covers the SMs about once (weights are streamed once either way)."""
+    """Split K so the grid fills the CTA slots about once (weights are streamed once either way).
+
+    Decode-sized token tiles (T <= 64) run two CTAs per SM (296 slots) with >= 8 K tiles each;
+    larger tiles run one CTA per SM.  (Chosen from a per-shape sweep on B200.)"""
     tiles = (-(-N // TILE_M)) * (-(-T // MAX_TILE_T))
     k_tiles = -(-K // TILE_K)
+    slots, min_kt = (2 * NUM_SMS, 8) if T <= SMALL_T else (int(NUM_SMS * 1.25), 4)
     splits = 1
-    while tiles * splits * 2 <= NUM_SMS * 1.25 and k_tiles // (splits * 2) >= 4:
+    while tiles * splits * 2 <= slots and k_tiles // (splits * 2) >= min_kt:
         splits *= 2
     return splits
+
+
+def _stages(T: int) -> int:
+    return 4 if T <= SMALL_T else 0
 
 
 def linear_ref(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
@@ -55,10 +66,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -
         return out.view(*x.shape[:-1], N)
     splits = choose_splits(T, N, K)
     if splits == 1:
-        C().gemm_bf16(out, x2, w, _empty(x.device, torch.float32), 1, status(x.device))
+        C().gemm_bf16(out, x2, w, _empty(x.device, torch.float32), 1, status(x.device), _stages(T))
     else:
         partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
-        C().gemm_bf16(_empty(x.device, x.dtype), x2, w, partials, splits, status(x.device))
+        C().gemm_bf16(_empty(x.device, x.dtype), x2, w, partials, splits, status(x.device), _stages(T))
         C().splitk_reduce(out, partials)
     if bias is not None:
         out += bias
@@ -71,5 +82,5 @@ def linear_partials(x: torch.Tensor, w: torch.Tensor, splits: int, partials: tor
     N = w.shape[0]
     if partials is None:
         partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
-    C().gemm_bf16(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits, status(x.device))
+    C().gemm_bf16(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits, status(x.device), _stages(T))
     return partials

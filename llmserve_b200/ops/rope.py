@@ -50,7 +50,18 @@ def _opt(w, device):
 def qkv_norm_rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps,
                         k_cache, v_cache, slot_mapping, num_heads, num_kv_heads, head_dim):
     """Split ``qkv [T, (nh+2nkv)*hd]``; return rotated ``(q, k, v)``.  With a bound cache the CUDA
-    path stores k/v into it and returns ``(q, None, None)``."""
+    path stores k/v into it and returns ``(q, None, None)``.  On CUDA ``qkv`` may also be the fp32
+    split-K partials ``[S, T, W]`` of the QKV projection, reduced inside the kernel."""
+    if qkv.dtype == torch.float32 and qkv.dim() == 3 and qkv.is_cuda:
+        if k_cache is None or not k_cache.numel():
+            qkv = qkv.sum(0).to(torch.bfloat16)
+            return qkv_norm_rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps, k_cache, v_cache,
+                                       slot_mapping, num_heads, num_kv_heads, head_dim)
+        T = qkv.shape[1]
+        q = torch.empty(T, num_heads, head_dim, dtype=torch.bfloat16, device=qkv.device)
+        C().qkv_rope(q, q, qkv, positions, cos_sin, _opt(q_norm_w, qkv.device), _opt(k_norm_w, qkv.device), eps,
+                     k_cache, v_cache, slot_mapping, num_heads, num_kv_heads, head_dim, True, status(qkv.device))
+        return q, None, None
     T = qkv.shape[0]
     qs, ks = num_heads * head_dim, num_kv_heads * head_dim
     if qkv.is_cuda:

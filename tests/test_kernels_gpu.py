@@ -204,3 +204,20 @@ def test_argmax_and_sampling():
     got = sampling.sample(logits.float(), temps, 1234)
     want = sampling.sample(logits.float().cpu(), temps.cpu(), 1234)
     assert (got.cpu() == want).float().mean() >= 8 / 9
+
+
+@pytest.mark.parametrize("S", [2, 4, 8])
+def test_qkv_rope_from_splitk_partials(S):
+    T, nh, nkv, hd, bs, nblk = 9, 8, 2, 128, 256, 2
+    W = (nh + 2 * nkv) * hd
+    parts = torch.randn(S, T, W, device=DEV) * 0.5
+    pos = torch.arange(T, device=DEV) * 7
+    cs = rope.build_cos_sin_cache(hd, 1024, 1e6).to(DEV)
+    qw = (1 + 0.1 * torch.randn(hd, device=DEV)).bfloat16()
+    kw = (1 + 0.1 * torch.randn(hd, device=DEV)).bfloat16()
+    slots = torch.arange(T, dtype=torch.int32, device=DEV) + 17
+    kc1 = torch.zeros(nblk, nkv, bs, hd, device=DEV, dtype=torch.bfloat16)
+    vc1, kc2, vc2 = torch.zeros_like(kc1), torch.zeros_like(kc1), torch.zeros_like(kc1)
+    q1, _, _ = rope.qkv_norm_rope_store(parts, pos, cs, qw, kw, 1e-6, kc1, vc1, slots, nh, nkv, hd)
+    q2, _, _ = rope.qkv_norm_rope_store(parts.sum(0).bfloat16(), pos, cs, qw, kw, 1e-6, kc2, vc2, slots, nh, nkv, hd)
+    assert rel_err(q1, q2) < 2e-3 and rel_err(kc1, kc2) < 2e-3 and rel_err(vc1, vc2) < 2e-3
