@@ -109,7 +109,8 @@ class ModelRunner:
 
         if self.is_cuda and self.world_size > 1 and config.fused_collectives:
             from llmserve_b200.parallel.comm import FusedComm
-            tp.set_fused_comm(FusedComm.create(self.device, hf.hidden_size, config.max_num_batched_tokens,
+            tp.set_fused_comm(FusedComm.create(self.device, hf.hidden_size, max(config.max_num_seqs, 64)
+                                               * (config.speculative_gamma + 1 if config.speculative_model else 1),
                                                timeout_s=config.comm_timeout_s))
 
         self.graphs = {}
@@ -164,6 +165,18 @@ class ModelRunner:
         if self.channel is not None:
             self.channel.close()
         tp.destroy_tensor_parallel()
+        # release device memory so another engine can be built in this process
+        self._bind_pools(None, None)
+        self.k_cache = self.v_cache = self.draft_k_cache = self.draft_v_cache = None
+        self.decode_workspace = None
+        self.graph_vars = None
+        if self.is_cuda:
+            import gc
+            self.model = self.model.to("meta") if hasattr(self.model, "to") else None
+            if self.draft_model is not None:
+                self.draft_model = self.draft_model.to("meta")
+            gc.collect()
+            torch.cuda.empty_cache()
 
     def loop(self):
         worker = self.rank - 1

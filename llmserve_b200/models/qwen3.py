@@ -127,7 +127,8 @@ class Qwen3Model(nn.Module):
             if aux_layer_ids is not None:
                 for j, want in enumerate(aux_layer_ids):
                     if want == i:
-                        aux[j] = residual
+                        # fused collectives return views of reusable buffers: keep a copy
+                        aux[j] = residual.clone()
             next_norm = self.layers[i + 1].input_layernorm if i + 1 < n else self.norm
             h, residual = layer.forward_fused(positions, h, residual, next_norm)
         if aux_layer_ids is not None:

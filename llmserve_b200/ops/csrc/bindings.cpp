@@ -27,6 +27,14 @@ void tree_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, 
                     at::Tensor tk, at::Tensor tv, at::Tensor mask_bits, double scale);
 void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status,
                int64_t max_stages);
+int64_t comm_alloc(int64_t nbytes);
+void comm_free(int64_t p);
+at::Tensor comm_ipc_handle(int64_t p);
+int64_t comm_open_handle(at::Tensor handle);
+void comm_close_handle(int64_t p);
+void fused_allreduce_add_rmsnorm(std::vector<int64_t> part, std::vector<int64_t> out, std::vector<int64_t> res,
+                                 std::vector<int64_t> flags, at::Tensor res_in, at::Tensor w, int64_t rank, int64_t S,
+                                 int64_t T, int64_t N, double eps, at::Tensor status);
 }  // namespace lsb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -45,6 +53,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &lsb::decode_attention);
   m.def("prefill_attention", &lsb::prefill_attention);
   m.def("tree_attention", &lsb::tree_attention);
+  m.def("comm_alloc", &lsb::comm_alloc);
+  m.def("comm_free", &lsb::comm_free);
+  m.def("comm_ipc_handle", &lsb::comm_ipc_handle);
+  m.def("comm_open_handle", &lsb::comm_open_handle);
+  m.def("comm_close_handle", &lsb::comm_close_handle);
+  m.def("fused_allreduce_add_rmsnorm", &lsb::fused_allreduce_add_rmsnorm);
   m.def("gemm_bf16", &lsb::gemm_bf16, py::arg("out"), py::arg("x"), py::arg("w"), py::arg("partials"),
         py::arg("splits"), py::arg("status"), py::arg("max_stages") = 0);
 }
