@@ -140,6 +140,9 @@ class Scheduler:
                 break
             if not seq.block_table:
                 self.block_manager.allocate(seq)
+                # a prefix-cache hit shrinks the work (the reference keeps the pre-hit count here,
+                # which schedules more query tokens than remain)
+                todo = max(seq.num_tokens - seq.num_cached_tokens, 1)
             seq.num_scheduled_tokens = min(todo, budget)
             if seq.num_scheduled_tokens == todo:
                 seq.status = SequenceStatus.RUNNING

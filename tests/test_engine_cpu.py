@@ -1,0 +1,143 @@
+"""End-to-end engine on the CPU fp32 path.
+
+Tiny random Qwen3-style decoder (2 layers, hidden 256, 4/2 heads, head_dim 64, MLP 512, vocab
+1024), 1-layer EAGLE3 draft over aux layers {0, 1, 1} with a 512-token draft vocabulary, paged KV
+with block 16 and 64 blocks, prefix caching; 8 requests with prompts of 8-64 uniform random ids
+and 32 output tokens, greedy, gamma = 3: speculative output equals non-speculative output token
+for token.  Also: chunked prefill, tree speculation, rejection mode, metrics schema, prefix hits.
+"""
+import os
+
+import pytest
+import torch
+
+from llmserve_b200 import LLM, SamplingParams
+from llmserve_b200.engine.model_runner import GreedySampler
+from llmserve_b200.models.synthetic import TINY, write_eagle3_checkpoint, write_qwen3_checkpoint
+
+
+@pytest.fixture(scope="module")
+def ckpts(tmp_path_factory):
+    d = tmp_path_factory.mktemp("ckpt")
+    tgt = write_qwen3_checkpoint(str(d / "target"), TINY, seed=0)
+    draft = write_eagle3_checkpoint(str(d / "draft"), TINY, draft_vocab=512, seed=0)
+    return tgt, draft
+
+
+def _prompts(n=8, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(8, 65, (n,), generator=g).tolist()
+    return [torch.randint(0, 1024, (L,), generator=g).tolist() for L in lens]
+
+
+def _run(path, prompts, max_tokens=32, **kw):
+    kw.setdefault("num_kvcache_blocks", 64)
+    llm = LLM(path, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, **kw)
+    llm.model_runner.sampler = GreedySampler()
+    out = llm.generate(prompts, SamplingParams(temperature=0.5, max_tokens=max_tokens, ignore_eos=True),
+                       use_tqdm=False)
+    metrics = llm.get_metrics()
+    llm.exit()
+    return [o["token_ids"] for o in out], metrics
+
+
+def test_speculative_equals_baseline_config0(ckpts):
+    tgt, draft = ckpts
+    prompts = _prompts()
+    base, _ = _run(tgt, prompts)
+    spec, m = _run(tgt, prompts, speculative_model=draft, speculative_gamma=3)
+    assert base == spec
+    s = m["summary"]["speculative"]
+    assert s["steps"] > 0 and s["draft_tokens"] == 3 * s["steps"]
+    assert all(len(t) == 32 for t in spec)
+
+
+def test_chunked_prefill_and_small_budget_match(ckpts):
+    tgt, _ = ckpts
+    prompts = _prompts(6, seed=3)
+    base, _ = _run(tgt, prompts, max_tokens=12)
+    chunked, _ = _run(tgt, prompts, max_tokens=12, enable_chunked_prefill=True, max_num_batched_tokens=24)
+    assert base == chunked
+
+
+def test_chunked_prefill_with_speculation(ckpts):
+    tgt, draft = ckpts
+    prompts = _prompts(5, seed=4)
+    base, _ = _run(tgt, prompts, max_tokens=16)
+    spec, _ = _run(tgt, prompts, max_tokens=16, enable_chunked_prefill=True, max_num_batched_tokens=40,
+                   speculative_model=draft)
+    assert base == spec
+
+
+def test_tree_speculation_equals_baseline(ckpts):
+    tgt, draft = ckpts
+    prompts = _prompts(1, seed=5)
+    base, _ = _run(tgt, prompts, max_tokens=20)
+    for nodes in (6, 10):
+        tree, m = _run(tgt, prompts, max_tokens=20, speculative_model=draft, speculative_tree_nodes=nodes)
+        assert base == tree
+        assert m["summary"]["speculative"]["gamma_counts"] == {str(nodes): m["summary"]["speculative"]["steps"]}
+
+
+def test_rejection_mode_runs_and_emits(ckpts):
+    tgt, draft = ckpts
+    llm = LLM(tgt, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=64,
+              speculative_model=draft, speculative_accept_mode="rejection", speculative_trace=True)
+    out = llm.generate(_prompts(3, seed=6), SamplingParams(temperature=0.8, max_tokens=10, ignore_eos=True),
+                       use_tqdm=False)
+    req = llm.get_metrics()["requests"]
+    llm.exit()
+    assert all(len(o["token_ids"]) == 10 for o in out)
+    assert any(r["speculative_trace"] for r in req)
+
+
+def test_prefix_cache_hit_gives_same_tokens(ckpts):
+    tgt, _ = ckpts
+    shared = list(range(5, 5 + 48))
+    prompts = [shared + [7, 8], shared + [9]]
+    llm = LLM(tgt, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=64)
+    llm.model_runner.sampler = GreedySampler()
+    sp = SamplingParams(max_tokens=6, ignore_eos=True)
+    first = llm.generate([prompts[0]], sp, use_tqdm=False)[0]["token_ids"]
+    second = llm.generate([prompts[1]], sp, use_tqdm=False)[0]["token_ids"]
+    llm.exit()
+    fresh, _ = _run(tgt, [prompts[1]], max_tokens=6)
+    assert second == fresh[0]
+    assert len(first) == 6
+
+
+def test_metrics_schema_keys(ckpts):
+    tgt, _ = ckpts
+    _, m = _run(tgt, _prompts(2, seed=8), max_tokens=4)
+    s = m["summary"]
+    for key in ("num_requests", "num_finished", "num_failed", "total_output_tokens", "wall_time", "throughput",
+                "ttft", "burst_itl", "itl", "output_event_latency", "speculative_step_latency", "tpot",
+                "request_latency", "speculative", "kv_cache"):
+        assert key in s
+    for key in ("total_blocks", "used_blocks", "free_blocks", "reserved_blocks", "preemptions",
+                "model_runtime_bytes", "kv_cache_bytes"):
+        assert key in s["kv_cache"]
+    r = m["requests"][0]
+    for key in ("seq_id", "prompt_tokens", "output_tokens", "success", "arrival_time", "first_token_time",
+                "token_times", "finish_time", "ttft", "burst_itl", "output_event_latency", "latency"):
+        assert key in r
+    assert s["num_finished"] == 2 and s["tpot"]["p99"] is not None
+
+
+def test_string_prompt_without_tokenizer_files(ckpts):
+    tgt, _ = ckpts
+    llm = LLM(tgt, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=32)
+    out = llm.generate(["hello"], SamplingParams(max_tokens=3, ignore_eos=True), use_tqdm=False)
+    llm.exit()
+    assert len(out[0]["token_ids"]) == 3 and isinstance(out[0]["text"], str)
+
+
+def test_dummy_load_format_and_reset_metrics(tmp_path):
+    from llmserve_b200.models.synthetic import write_config_only
+    path = write_config_only(str(tmp_path / "cfg"), TINY)
+    llm = LLM(path, device="cpu", load_format="dummy", enforce_eager=True, kvcache_block_size=16, max_model_len=128,
+              num_kvcache_blocks=16)
+    llm.generate([[1, 2, 3]], SamplingParams(max_tokens=2, ignore_eos=True), use_tqdm=False)
+    llm.reset_metrics()
+    assert llm.get_metrics()["summary"]["num_requests"] == 0
+    llm.exit()

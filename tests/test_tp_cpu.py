@@ -1,0 +1,145 @@
+"""Tensor parallelism over gloo CPU ranks, and failure handling of the host control plane.
+
+Failures are injected on the host only (no GPU): a worker whose call raises must surface as an
+exception on rank 0 instead of a hang; a worker whose rank 0 disappeared must exit on its own;
+RPC waits are bounded.
+"""
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from llmserve_b200 import LLM, SamplingParams
+from llmserve_b200.engine.model_runner import GreedySampler
+from llmserve_b200.engine.rpc import RpcChannel, RpcTimeout
+from llmserve_b200.models.synthetic import TINY, write_eagle3_checkpoint, write_qwen3_checkpoint
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.fixture(scope="module")
+def ckpts(tmp_path_factory):
+    d = tmp_path_factory.mktemp("tp")
+    return (write_qwen3_checkpoint(str(d / "t"), TINY, seed=1),
+            write_eagle3_checkpoint(str(d / "d"), TINY, draft_vocab=512, seed=1))
+
+
+def _gen(path, tp, draft=None, **kw):
+    llm = LLM(path, device="cpu", enforce_eager=True, num_kvcache_blocks=64, kvcache_block_size=16, max_model_len=256,
+              tensor_parallel_size=tp, speculative_model=draft, comm_timeout_s=60,
+              distributed_init_method=f"tcp://127.0.0.1:{_port()}", **kw)
+    llm.model_runner.sampler = GreedySampler()
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, 1024, (int(n),), generator=g).tolist() for n in (9, 33, 17, 50)]
+    out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=12, ignore_eos=True), use_tqdm=False)]
+    llm.exit()
+    return out
+
+
+def test_tp2_gloo_matches_tp1_with_and_without_speculation(ckpts):
+    tgt, draft = ckpts
+    ref = _gen(tgt, 1)
+    assert _gen(tgt, 2) == ref
+    assert _gen(tgt, 2, draft) == ref
+
+
+def test_tp2_gloo_temperature_sampling_is_rank_consistent(ckpts):
+    tgt, _ = ckpts
+    llm = LLM(tgt, device="cpu", enforce_eager=True, num_kvcache_blocks=64, kvcache_block_size=16, max_model_len=256,
+              tensor_parallel_size=2, distributed_init_method=f"tcp://127.0.0.1:{_port()}")
+    out = llm.generate([[3, 4, 5]] * 3, SamplingParams(temperature=1.0, max_tokens=8, ignore_eos=True), use_tqdm=False)
+    llm.exit()     # would hang or raise if ranks had diverged (their collectives would mismatch)
+    assert all(len(o["token_ids"]) == 8 for o in out)
+
+
+def _raising_worker(name):
+    ch = RpcChannel(name, 1, create=False)
+    method, args = ch.recv(0, idle_timeout_s=1.0, parent_pid=os.getppid())
+    ch.ack(0, False, f"ValueError: injected failure in {method}")
+    ch.close()
+
+
+def test_worker_exception_surfaces_on_rank0():
+    name = f"lsb_test_{os.getpid()}_a"
+    ch = RpcChannel(name, 1, create=True)
+    p = mp.get_context("spawn").Process(target=_raising_worker, args=(name,))
+    p.start()
+    ch.send("run", 1, 2)
+    with pytest.raises(RuntimeError, match="injected failure"):
+        ch.wait_acks(30)
+    p.join(10)
+    ch.close()
+
+
+def _orphan_worker(name, q):
+    ch = RpcChannel(name, 1, create=False)
+    t = time.monotonic()
+    try:
+        ch.recv(0, idle_timeout_s=0.2, parent_pid=999999999)   # a pid that does not exist
+    except RpcTimeout:
+        q.put(time.monotonic() - t)
+    ch.close()
+
+
+def test_orphaned_worker_exits_on_its_own():
+    name = f"lsb_test_{os.getpid()}_b"
+    ch = RpcChannel(name, 1, create=True)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_orphan_worker, args=(name, q))
+    p.start()
+    waited = q.get(timeout=30)
+    p.join(10)
+    ch.close()
+    assert waited < 5 and p.exitcode == 0
+
+
+def test_ack_wait_is_bounded():
+    ch = RpcChannel(f"lsb_test_{os.getpid()}_c", 1, create=True)
+    ch.send("noop")
+    t = time.monotonic()
+    with pytest.raises(RpcTimeout):
+        ch.wait_acks(0.3)
+    assert time.monotonic() - t < 3
+    ch.close()
+
+
+def _rank_main(rank, world, port, fail_rank, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=3))
+    t = torch.ones(4)
+    dist.all_reduce(t)
+    if rank == fail_rank:
+        q.put((rank, "left"))
+        return                        # leaves between steps, with nothing in flight
+    t0 = time.monotonic()
+    try:
+        dist.all_reduce(t)
+        q.put((rank, "no-error"))
+    except Exception:
+        q.put((rank, f"error after {time.monotonic() - t0:.1f}s"))
+
+
+def test_process_group_timeout_ends_collective_after_rank_loss():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_rank_main, args=(r, 2, port, 1, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=60) for _ in range(2))
+    for p in ps:
+        p.join(30)
+    assert res[1] == "left"
+    assert res[0].startswith("error")
