@@ -1,0 +1,161 @@
+"""Checkpoint formats (AutoAWQ GEMM g128, EAGLE3 RedHat / SpecForge, HF Qwen3 loading with TP
+slicing) and the speculative acceptance algorithms, against the reference where importable."""
+import json
+import os
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from llmserve_b200.models.eagle3 import (Eagle3Speculator, normalize_eagle3_config, normalize_eagle3_weight_name,
+                                         validate_eagle3_target_config)
+from llmserve_b200.models.synthetic import TINY, awq_quantize_dense, write_awq_checkpoint, write_eagle3_checkpoint
+from llmserve_b200.quantization.awq import (AWQRuntimeConfig, awq_reference_linear, dequantize_awq_gemm,
+                                            pack_awq_int4, unpack_awq_int4)
+from llmserve_b200.speculative.sampling import (greedy_accept_batch, greedy_accept_from_ids,
+                                                speculative_accept_greedy_from_logits, speculative_accept_reject)
+from llmserve_b200.speculative.tree import build_fixed_tree_topology, select_greedy_tree_path
+from tests.support import reference_module
+
+
+# ---- AWQ -------------------------------------------------------------------------------------
+def test_awq_pack_unpack_roundtrip_and_reference_order():
+    ref = reference_module("llmserve.layers.quantization.awq")
+    codes = torch.randint(0, 16, (32, 64), dtype=torch.int32)
+    packed = pack_awq_int4(codes)
+    assert torch.equal(unpack_awq_int4(packed), codes)
+    assert torch.equal(ref.unpack_awq_int4(packed), codes)
+    qz = pack_awq_int4(torch.randint(0, 16, (1, 64), dtype=torch.int32).repeat(1, 1))
+    qw = pack_awq_int4(torch.randint(0, 16, (128, 64), dtype=torch.int32))
+    sc = torch.rand(1, 64).bfloat16()
+    assert torch.equal(dequantize_awq_gemm(qw, qz, sc, group_size=128), ref.dequantize_awq_gemm(qw, qz, sc, group_size=128))
+
+
+def test_awq_rtn_quantization_is_close():
+    w = torch.randn(256, 512) * 0.02
+    qw, qz, sc = awq_quantize_dense(w)
+    deq = dequantize_awq_gemm(qw, qz, sc, group_size=128).float().t()
+    assert ((deq - w).norm() / w.norm()).item() < 0.12
+    x = torch.randn(4, 512).bfloat16()
+    y = awq_reference_linear(x, qw, qz, sc, group_size=128)
+    assert y.shape == (4, 256)
+
+
+def test_awq_config_validation():
+    good = SimpleNamespace(dtype=torch.bfloat16, quantization_config=dict(
+        quant_method="awq", backend="autoawq", bits=4, group_size=128, version="gemm", zero_point=True))
+    assert AWQRuntimeConfig.from_hf_config(good).pack_factor == 8
+    for key, bad in (("bits", 8), ("group_size", 64), ("version", "gemv"), ("zero_point", False)):
+        cfg = SimpleNamespace(dtype=torch.bfloat16, quantization_config=dict(good.quantization_config, **{key: bad}))
+        with pytest.raises(ValueError, match=key):
+            AWQRuntimeConfig.from_hf_config(cfg)
+
+
+def test_awq_checkpoint_loads_with_tp_slicing_on_cpu(tmp_path):
+    """AutoAWQ checkpoint through the engine loader; TP=2 shards of a packed layer concatenate back."""
+    from llmserve_b200.layers.linear import MergedColumnParallelLinear, RowParallelLinear
+    from llmserve_b200.parallel import state as tp
+    cfg = AWQRuntimeConfig(4, 128, True, "gemm", "autoawq", torch.bfloat16)
+    w = torch.randn(512, 256) * 0.02
+    qw, qz, sc = awq_quantize_dense(w)
+    shards = []
+    for rank in range(2):
+        tp._tp.rank, tp._tp.world_size = rank, 2
+        try:
+            lin = RowParallelLinear(256, 512, quant_config=cfg)
+            for name, t in (("qweight", qw), ("qzeros", qz), ("scales", sc)):
+                p = getattr(lin, name)
+                p.weight_loader(p, t)
+            shards.append(lin.qweight.data.clone())
+        finally:
+            tp._tp.rank, tp._tp.world_size = 0, 1
+    assert torch.equal(torch.cat(shards, 0), qw)
+
+
+# ---- EAGLE3 ----------------------------------------------------------------------------------
+def test_eagle3_config_and_name_normalization_match_reference():
+    ref = reference_module("llmserve.models.eagle3")
+    nested = json.load(open(os.path.join(write_eagle3_checkpoint("/tmp/lsb_e3_nested", TINY, 512), "config.json")))
+    assert normalize_eagle3_config(nested) == ref.normalize_eagle3_config(nested)
+    with pytest.raises(ValueError, match="conflicting"):
+        normalize_eagle3_config({"hidden_size": 1, "transformer_layer_config": {"hidden_size": 2}})
+    for name in ("layers.0.self_attn.q_proj.weight", "fc.weight", "midlayer.mlp.up_proj.weight"):
+        assert normalize_eagle3_weight_name(name) == ref.normalize_eagle3_weight_name(name)
+    with pytest.raises(ValueError, match="vocab_size"):
+        validate_eagle3_target_config(normalize_eagle3_config(nested), dict(TINY, vocab_size=5))
+
+
+@pytest.mark.parametrize("nested", [True, False])
+def test_eagle3_loads_redhat_and_specforge_layouts(tmp_path, nested):
+    from llmserve_b200.models.synthetic import write_qwen3_checkpoint
+    tgt = write_qwen3_checkpoint(str(tmp_path / "t"), TINY)
+    d = write_eagle3_checkpoint(str(tmp_path / "d"), TINY, 512, nested=nested)
+    m = Eagle3Speculator.from_pretrained(d, target_model_path=tgt)
+    from safetensors import safe_open
+    with safe_open(os.path.join(tgt, "model-00001-of-00001.safetensors"), "pt") as f:
+        assert torch.equal(m.embed_tokens.weight.data, f.get_tensor("model.embed_tokens.weight"))
+    logits = torch.zeros(2, 512)
+    logits[0, 5] = 1
+    logits[1, 100] = 1
+    ids = m.greedy_sample(logits)
+    assert ids.tolist() == [5 + int(m.d2t[5]), 100 + int(m.d2t[100])]
+    mapped = m.map_draft_logits(logits)
+    assert mapped.shape == (2, 1024) and torch.isinf(mapped).sum() == 2 * (1024 - 512)
+
+
+def test_eagle3_missing_embedding_without_target_raises(tmp_path):
+    d = write_eagle3_checkpoint(str(tmp_path / "d"), TINY, 512)
+    with pytest.raises(ValueError, match="target_model_path"):
+        Eagle3Speculator.from_pretrained(d)
+
+
+# ---- acceptance ------------------------------------------------------------------------------
+def test_greedy_acceptance_matches_reference():
+    ref = reference_module("llmserve.speculative.sampling")
+    g = torch.Generator().manual_seed(0)
+    for _ in range(50):
+        logits = torch.randn(4, 9, generator=g)
+        target = logits.argmax(-1)
+        drafts = target[:3].clone()
+        k = int(torch.randint(0, 4, (1,), generator=g))
+        if k < 3:
+            drafts[k] = (drafts[k] + 1) % 9
+        a = speculative_accept_greedy_from_logits(logits, drafts)
+        b = ref.speculative_accept_greedy_from_logits(logits, drafts)
+        assert (a.token_ids, a.num_accepted, a.accepted_all) == (b.token_ids, b.num_accepted, b.accepted_all)
+        acc, fin = greedy_accept_batch(target.view(1, 4), drafts.view(1, 3))
+        assert int(acc[0]) == a.num_accepted and int(fin[0]) == a.final_token_id
+
+
+def test_rejection_sampling_preserves_target_distribution():
+    torch.manual_seed(0)
+    p = torch.tensor([[0.5, 0.3, 0.2], [0.2, 0.2, 0.6]])
+    q = torch.tensor([[0.2, 0.6, 0.2]])
+    counts = torch.zeros(3)
+    n = 20000
+    for _ in range(n):
+        draft = torch.multinomial(q[0], 1)
+        res = speculative_accept_reject(p, q, draft)
+        counts[res.token_ids[0]] += 1
+    assert torch.allclose(counts / n, p[0], atol=0.015)
+
+
+def test_tree_path_selection_matches_reference():
+    ref = reference_module("llmserve.speculative.tree")
+    for nodes in (6, 10):
+        topo = build_fixed_tree_topology(nodes)
+        rt = ref.build_fixed_tree_topology(nodes)
+        assert torch.equal(topo.attention_mask(), rt.attention_mask())
+        g = torch.Generator().manual_seed(nodes)
+        for _ in range(30):
+            logits = torch.randn(len(topo.parents), 5, generator=g)
+            drafts = torch.randint(0, 5, (nodes,), generator=g).tolist()
+            a = select_greedy_tree_path(topo, drafts, logits.argmax(-1).tolist())
+            b = ref.select_greedy_tree_path(rt, drafts, logits)
+            assert (a.token_ids, a.commit_node_indices, a.final_node_index, a.accepted_all) == \
+                (b.token_ids, b.commit_node_indices, b.final_node_index, b.accepted_all)
+
+
+def test_greedy_from_ids_bonus():
+    r = greedy_accept_from_ids([1, 2, 3, 4], [1, 2, 3])
+    assert r.token_ids == [1, 2, 3, 4] and r.accepted_all

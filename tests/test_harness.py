@@ -1,0 +1,209 @@
+"""Benchmark harness with a fake clock and a fake engine (no model), plus metric parity with the
+reference harness where it is importable."""
+import json
+import random
+from types import SimpleNamespace
+
+import pytest
+
+from benchmarks.arrivals import poisson_arrival_times
+from benchmarks.metrics import percentile, summarize_serving_run, summarize_values
+from benchmarks.run_suite import execute_suite
+from benchmarks.runtime import run_closed_loop, run_poisson
+from benchmarks.schema import compact_request_record
+from benchmarks.serve import run_point
+from benchmarks.suite import aggregate_results, build_summary_rows, expand_suite
+from benchmarks.workloads import WorkloadClass, build_request_specs, class_counts, iter_request_specs
+from tests.support import reference_module
+
+
+class FakeClock:
+    def __init__(self):
+        self.t = 100.0
+
+    def __call__(self):
+        return self.t
+
+    def sleep(self, dt):
+        self.t += max(dt, 1e-6)   # a real sleep always lets time pass
+
+
+class FakeEngine:
+    """Emits one token per request per step; each step takes 10 ms of fake time."""
+
+    def __init__(self, clock, step_s=0.01):
+        self.clock, self.step_s = clock, step_s
+        self.reqs = {}
+        self.next_id = 0
+        self.last_step_events = {}
+        self.model_runner = SimpleNamespace(sampler=None)
+
+    def add_request(self, prompt, sp):
+        sid = self.next_id
+        self.next_id += 1
+        self.reqs[sid] = dict(seq_id=sid, prompt_tokens=len(prompt), output_tokens=0, target=sp.max_tokens,
+                              arrival_time=self.clock(), first_token_time=None, token_times=[], output_event_times=[],
+                              finish_time=None, success=False, failure_reason=None)
+        return sid
+
+    def is_finished(self):
+        return all(r["finish_time"] is not None for r in self.reqs.values())
+
+    def step(self):
+        self.clock.t += self.step_s
+        now = self.clock()
+        done = []
+        ids = [i for i, r in self.reqs.items() if r["finish_time"] is None]
+        for i in ids:
+            r = self.reqs[i]
+            r["output_tokens"] += 1
+            r["token_times"].append(now)
+            r["output_event_times"].append(now)
+            r["first_token_time"] = r["first_token_time"] or now
+            if r["output_tokens"] == r["target"]:
+                r["finish_time"], r["success"] = now, True
+                done.append((i, [0] * r["output_tokens"]))
+        self.last_step_events = {"step_end": now, "scheduled_seq_ids": ids, "waiting_queue_size": 0,
+                                 "running_queue_size": len(ids)}
+        return done, len(ids)
+
+    def get_metrics(self):
+        return {"summary": {"kv_cache": {"total_blocks": 10}}, "requests": [dict(r) for r in self.reqs.values()]}
+
+    def reset_metrics(self):
+        self.reqs.clear()
+
+    def exit(self):
+        pass
+
+
+def _sp(spec):
+    return SimpleNamespace(max_tokens=spec.output_len)
+
+
+def test_class_counts_largest_remainder_and_specs():
+    classes = [WorkloadClass("short", 0.8, 4, 2), WorkloadClass("long", 0.2, 8, 2)]
+    assert class_counts(classes, 7) == [6, 1]
+    specs = build_request_specs(classes, 10, seed=3)
+    assert [s.request_id for s in specs] == list(range(10))
+    assert sum(s.request_class == "long" for s in specs) == 2
+    assert build_request_specs(classes, 10, seed=3) == specs
+    it = iter_request_specs(classes, seed=0, cycle_size=5)
+    assert [next(it).request_id for _ in range(12)] == list(range(12))
+
+
+def test_workloads_and_arrivals_match_reference():
+    ref = _ref_bench("workloads")
+    ref_a = _ref_bench("arrivals")
+    classes = [WorkloadClass("a", 1, 5, 3), WorkloadClass("b", 2, 7, 1)]
+    rclasses = [ref.WorkloadClass("a", 1, 5, 3), ref.WorkloadClass("b", 2, 7, 1)]
+    ours = build_request_specs(classes, 13, seed=5)
+    theirs = ref.build_request_specs(rclasses, 13, seed=5)
+    assert [(s.request_class, s.prompt_token_ids) for s in ours] == [(s.request_class, s.prompt_token_ids) for s in theirs]
+    assert poisson_arrival_times(9, 1.5, 2) == ref_a.poisson_arrival_times(9, 1.5, 2)
+
+
+def _ref_bench(name):
+    import importlib
+    import sys
+    reference_module("llmserve.sampling_params")   # puts the reference root on sys.path (or skips)
+    saved = {k: sys.modules.pop(k) for k in list(sys.modules) if k == "benchmarks" or k.startswith("benchmarks.")}
+    root = [p for p in sys.path if p.endswith("reference") or p.endswith("_ref")][0]
+    sys.path.insert(0, root)
+    try:
+        return importlib.import_module(f"benchmarks.{name}")
+    finally:
+        sys.path.remove(root)
+        for k in list(sys.modules):
+            if k == "benchmarks" or k.startswith("benchmarks."):
+                sys.modules.pop(k)
+        sys.modules.update(saved)
+
+
+def test_percentiles_match_reference():
+    ref = _ref_bench("metrics")
+    rng = random.Random(0)
+    vals = [rng.random() for _ in range(37)]
+    for q in (0, 50, 90, 99, 100):
+        assert percentile(vals, q) == pytest.approx(ref.percentile(vals, q))
+    assert summarize_values(vals) == ref.summarize_values(vals)
+
+
+def test_closed_loop_window_rules():
+    clock = FakeClock()
+    eng = FakeEngine(clock)
+    classes = [WorkloadClass("decode", 1, 4, 5)]
+    obs = run_closed_loop(eng, iter_request_specs(classes, 0), max_concurrency=3, warmup_seconds=0.05,
+                          measurement_seconds=0.2, make_sampling_params=_sp, clock=clock)
+    assert obs["duration"] == 0.2
+    for r in obs["latency_requests"]:
+        assert r["arrival_time"] >= obs["measurement_start"] and r["finish_time"] < obs["measurement_end"]
+    assert obs["window_output_tokens"] > 0 and eng.is_finished()
+    metrics = summarize_serving_run(obs["latency_requests"], obs["duration"])
+    assert metrics["latency"]["overall"]["tpot"]["p50"] == pytest.approx(0.01)
+
+
+def test_poisson_run_admits_by_arrival_and_sleeps():
+    clock = FakeClock()
+    eng = FakeEngine(clock)
+    specs = build_request_specs([WorkloadClass("d", 1, 3, 2)], 4, seed=1)
+    arrivals = [0.0, 0.5, 0.5, 2.0]
+    obs = run_poisson(eng, specs, arrivals, _sp, clock=clock, sleep=clock.sleep)
+    assert obs["admitted"] == 4
+    assert [r["request_id"] for r in obs["requests"]] == [0, 1, 2, 3]
+    assert obs["duration"] >= 2.0
+
+
+def test_run_point_and_schema_with_fake_engine():
+    clock = FakeClock()
+    suite = json.load(open("benchmarks/suites/smoke.json"))
+    point = expand_suite(suite)[0]
+    result = run_point(point, "/models/tiny", speculative_model="/models/draft",
+                       engine_factory=lambda m, **kw: FakeEngine(clock), make_sampling_params=_sp, clock=clock,
+                       sleep=clock.sleep, metadata={"git_commit": "abc"})
+    assert result["schema_version"] == 2 and result["complete"]
+    assert result["config"]["model"] == "tiny"
+    assert set(result["requests"][0]) >= {"ttft_ms", "tpot_ms", "e2e_ms", "burst_itl_ms", "speculative"}
+    rows = build_summary_rows([result])
+    assert rows[0]["output_throughput_tps"] > 0
+
+
+def test_suite_expansion_ids_and_aggregate():
+    suite = json.load(open("benchmarks/suites/formal-closed-loop.json"))
+    pts = expand_suite(suite)
+    assert pts[0]["point_id"] == "eagle-closed-loop-baseline-concurrency-1-r1"
+    assert {p["workload_seed"] for p in pts} == {0, 1, 2}
+    res = [{"complete": True, "config": p, "metrics": {"x": {"y": float(i)}}} for i, p in enumerate(pts[:4])]
+    rows = aggregate_results(res, "metrics.x.y")
+    assert any(r["ratio_to_baseline"] is not None for r in rows)
+
+
+def test_suite_expansion_matches_reference():
+    ref = _ref_bench("suite")
+    for name in ("smoke", "formal-closed-loop", "formal-poisson"):
+        suite = json.load(open(f"benchmarks/suites/{name}.json"))
+        assert expand_suite(suite) == ref.expand_suite(suite)
+
+
+def test_execute_suite_records_failures_and_continues(tmp_path):
+    suite = json.load(open("benchmarks/suites/smoke.json"))
+    calls = []
+
+    def runner(cmd, **kw):
+        calls.append(cmd)
+        return SimpleNamespace(returncode=1, stderr="boom /secret/model/path")
+
+    rc = execute_suite(suite, tmp_path, "/secret/model/path", None, {"git_commit": "c0"}, command_runner=runner)
+    assert rc == 1 and len(calls) == 4
+    manifest = json.loads((tmp_path / "manifest.json").read_text())
+    assert manifest["failed_points"] == 4
+    run = json.loads(next((tmp_path / "runs").iterdir()).read_text())
+    assert "/secret" not in run["error"]["message"] and run["complete"] is False
+    assert (tmp_path / "summary.csv").exists()
+
+
+def test_compact_record_units():
+    rec = compact_request_record(dict(seq_id=1, request_class="d", arrival_time=1.0, first_token_time=1.5,
+                                      finish_time=2.5, output_tokens=3, prompt_tokens=4, success=True,
+                                      token_times=[1.5, 2.0, 2.5], output_event_times=[1.5, 2.5]))
+    assert rec["ttft_ms"] == 500 and rec["tpot_ms"] == 500 and rec["e2e_ms"] == 1500
