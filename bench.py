@@ -211,7 +211,8 @@ def run_reference(args):
         if why:
             print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
             return
-    from baseline_ref import run as ref_run  # noqa: E402
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    from ref_arm import run as ref_run  # noqa: E402
     ref_run(args, METRIC)
 
 

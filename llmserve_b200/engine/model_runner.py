@@ -395,24 +395,13 @@ class ModelRunner:
     # ---- forward -----------------------------------------------------------------------------
     @torch.inference_mode()
     def run_model(self, input_ids, positions, is_prefill: bool) -> torch.Tensor:
-        """Hidden states -> this rank's logit shard (decode uses a CUDA graph when captured)."""
-        bs = input_ids.shape[0]
-        if is_prefill or not self.graphs or bs > self.graph_bs[-1]:
-            return self.model.compute_logits(self.model(input_ids, positions))
-        ctx = get_context()
-        gbs = next(x for x in self.graph_bs if x >= bs)
-        v = self.graph_vars
-        v["input_ids"][:bs].copy_(input_ids)
-        v["positions"][:bs].copy_(positions)
-        v["slot_mapping"].fill_(-1)
-        v["slot_mapping"][:bs].copy_(ctx.slot_mapping)
-        v["context_lens"].fill_(1)
-        v["context_lens"][:bs].copy_(ctx.context_lens)
-        width = ctx.block_tables.shape[1]
-        v["block_tables"][:bs, :width].copy_(ctx.block_tables)
-        self.graphs[gbs].replay()
-        LaunchCounter.launches += self.graph_launches[gbs]
-        return v["logits"][:bs]
+        """Hidden states -> this rank's logit shard (eager path; decode graphs go through
+        ``_decode_graph_step``)."""
+        return self.model.compute_logits(self.model(input_ids, positions))
+
+    def _use_graph(self, decodes, is_prefill) -> bool:
+        return (not is_prefill and bool(self.graphs) and len(decodes) <= self.graph_bs[-1]
+                and max(len(s.block_table) for s in decodes) <= self.graph_W)
 
     def sample_tokens(self, logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tensor:
         """Token ids on every rank from the local logit shard."""
@@ -428,11 +417,22 @@ class ModelRunner:
         seqs = scheduler_output.scheduled_seqs
         prefill, decodes = scheduler_output.prefill_seqs, scheduler_output.decode_seqs
         is_prefill = bool(prefill)
+        if self.draft_model is not None and not warmup:
+            self.spec.note_plain_step(decodes)
+        if self._use_graph(decodes, is_prefill):
+            logits, vals, idx = self._decode_graph_step(decodes)
+            if getattr(self.sampler, "is_greedy", False):
+                tokens = tp.vocab_parallel_argmax(vals, idx, self.model.lm_head.vocab_start)
+            else:
+                tokens = self.sample_tokens(logits, self.prepare_sample(seqs))
+            host = self.graph_tokens_host[:len(decodes)]
+            host.copy_(tokens)
+            token_list = host.tolist()
+            self.d2h_bytes += 8 * len(token_list)
+            return token_list if self.rank == 0 else None
         input_ids, positions = self.prepare_prefill(seqs, decodes) if is_prefill else self.prepare_decode(decodes)
         temperatures = self.prepare_sample(seqs)
         use_draft = self.draft_model is not None and not warmup
-        if use_draft:
-            self.spec.note_plain_step(decodes)
         if is_prefill and use_draft:
             hidden, aux = self.model.forward_with_eagle3_aux(input_ids, positions)
             logits = self.model.compute_logits(hidden)
@@ -450,35 +450,84 @@ class ModelRunner:
     # ---- CUDA graphs -------------------------------------------------------------------------
     @torch.inference_mode()
     def capture_cudagraph(self):
+        """Decode graphs per batch bucket.  All step inputs live in ONE packed int32 device buffer
+        (ids, positions, slots, context lengths, block tables) filled by one host-to-device copy
+        from a pinned staging buffer; the graph also holds the LM head and the greedy argmax."""
         cfg = self.config
         max_bs = min(cfg.max_num_seqs, 512)
-        max_blocks = -(-(cfg.max_model_len + cfg.speculative_gamma + 2) // self.block_size)
+        W = -(-(cfg.max_model_len + cfg.speculative_gamma + 2) // self.block_size)
         d = self.device
+        n = max_bs * (4 + W)                       # ids, pos, slots, lens, tables (int32 each)
+        self.graph_pack = torch.zeros(n, dtype=torch.int32, device=d)
+        self.graph_pack_host = torch.zeros(n, dtype=torch.int32, pin_memory=True)
+        self.graph_pack_np = self.graph_pack_host.numpy()
+        self.graph_tokens_host = torch.zeros(max_bs, dtype=torch.int64, pin_memory=True)
+        pk = self.graph_pack
         v = {
-            "input_ids": torch.zeros(max_bs, dtype=torch.int64, device=d),
-            "positions": torch.zeros(max_bs, dtype=torch.int64, device=d),
-            "slot_mapping": torch.full((max_bs,), -1, dtype=torch.int32, device=d),
-            "context_lens": torch.ones(max_bs, dtype=torch.int32, device=d),
-            "block_tables": torch.zeros(max_bs, max_blocks, dtype=torch.int32, device=d),
+            "ids32": pk[0:max_bs], "pos32": pk[max_bs:2 * max_bs],
+            "slot_mapping": pk[2 * max_bs:3 * max_bs], "context_lens": pk[3 * max_bs:4 * max_bs],
+            "block_tables": pk[4 * max_bs:].view(max_bs, W),
             "logits": torch.zeros(max_bs, self.model.lm_head.shard_size, dtype=self.dtype, device=d),
+            "tok_val": torch.zeros(max_bs, dtype=torch.float32, device=d),
+            "tok_idx": torch.zeros(max_bs, dtype=torch.int64, device=d),
         }
+        self.graph_W = W
         self.graph_bs = [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
         self.graphs, self.graph_pool, self.graph_launches = {}, None, {}
+        self.graph_vars = v
+        v["context_lens"].fill_(1)
         for bs in reversed(self.graph_bs):
             g = torch.cuda.CUDAGraph()
-            set_context(False, slot_mapping=v["slot_mapping"][:bs], context_lens=v["context_lens"][:bs],
-                        block_tables=v["block_tables"][:bs], decode_workspace=self.decode_workspace)
-            v["logits"][:bs] = self.model.compute_logits(self.model(v["input_ids"][:bs], v["positions"][:bs]))
+            self._graph_body(bs)                   # warm-up outside capture
             before = LaunchCounter.launches
             with torch.cuda.graph(g, self.graph_pool):
-                v["logits"][:bs] = self.model.compute_logits(self.model(v["input_ids"][:bs], v["positions"][:bs]))
+                self._graph_body(bs)
             self.graph_launches[bs] = LaunchCounter.launches - before
             if self.graph_pool is None:
                 self.graph_pool = g.pool()
             self.graphs[bs] = g
             torch.cuda.synchronize()
             reset_context()
-        self.graph_vars = v
+
+    def _graph_body(self, bs: int):
+        v = self.graph_vars
+        set_context(False, slot_mapping=v["slot_mapping"][:bs], context_lens=v["context_lens"][:bs],
+                    block_tables=v["block_tables"][:bs], decode_workspace=self.decode_workspace)
+        ids = v["ids32"][:bs].long()
+        pos = v["pos32"][:bs].long()
+        v["logits"][:bs] = self.model.compute_logits(self.model(ids, pos))
+        sampling_ops.local_argmax_into(v["logits"][:bs], v["tok_val"][:bs], v["tok_idx"][:bs])
+
+    def _decode_graph_step(self, seqs: list[Sequence]):
+        """Pack the step inputs, one H2D copy, replay; returns the logits shard view and the
+        per-shard argmax (value, index) views of the graph outputs."""
+        bs = len(seqs)
+        gbs = next(x for x in self.graph_bs if x >= bs)
+        max_bs, W = self.graph_vars["ids32"].shape[0], self.graph_W
+        a = self.graph_pack_np
+        bsz = self.block_size
+        lens = np.fromiter((len(s) for s in seqs), dtype=np.int32, count=bs)
+        a[0:bs] = [s.last_token for s in seqs]
+        a[max_bs:max_bs + bs] = lens - 1
+        last_blocks = np.fromiter((s.block_table[(len(s) - 1) // bsz] for s in seqs), dtype=np.int32, count=bs)
+        a[2 * max_bs:2 * max_bs + bs] = last_blocks * bsz + (lens - 1) % bsz
+        a[3 * max_bs:3 * max_bs + bs] = lens
+        tables = a[4 * max_bs:].reshape(max_bs, W)
+        for i, s in enumerate(seqs):
+            t = s.block_table
+            tables[i, :len(t)] = t
+        if gbs > bs:
+            a[bs:gbs] = 0
+            a[max_bs + bs:max_bs + gbs] = 0
+            a[2 * max_bs + bs:2 * max_bs + gbs] = -1
+            a[3 * max_bs + bs:3 * max_bs + gbs] = 1
+        nbytes = (4 * max_bs + gbs * W) * 4
+        self.h2d_bytes += nbytes
+        self.graph_pack[: 4 * max_bs + gbs * W].copy_(self.graph_pack_host[: 4 * max_bs + gbs * W], non_blocking=True)
+        self.graphs[gbs].replay()
+        LaunchCounter.launches += self.graph_launches[gbs]
+        v = self.graph_vars
+        return v["logits"][:bs], v["tok_val"][:bs], v["tok_idx"][:bs]
 
     # ---- device timing (benchmarks): every rank records, rank 0 gathers -------------------------
     def mark_event(self, tag: str):

@@ -7,6 +7,7 @@ the sm_100a GEMM (``llmserve_b200.ops.gemm``) or the W4A16 kernel.  ``RowParalle
 ``forward_add_norm``, which fuses split-K reduction, the TP all-reduce, the residual add and the
 following RMSNorm on the CUDA path.
 """
+import os
 import torch
 from torch import nn
 
@@ -86,7 +87,28 @@ class ColumnParallelLinear(LinearBase):
 
 
 class MergedColumnParallelLinear(ColumnParallelLinear):
-    """gate_proj and up_proj stored side by side: [gate shard | up shard] on each rank."""
+    """gate_proj and up_proj stored side by side: [gate shard | up shard] on each rank.
+
+    With ``LLMSERVE_SILU_EPILOGUE=1`` the dense CUDA weight is permuted after loading
+    (``interleave_for_silu``) so the GEMM applies SiLU-mul in its epilogue and ``forward_silu``
+    returns ``silu(gate) * up`` directly.  It is off by default: on the Qwen3-8B decode step the
+    epilogue forces one K split for gate_up (192 CTAs on 148 SMs) and measured about 1% slower
+    than split-K GEMM + separate SiLU-mul kernel."""
+
+    interleaved = False
+
+    def interleave_for_silu(self):
+        if os.environ.get("LLMSERVE_SILU_EPILOGUE", "0") == "1" \
+                and self.quant_method is None and self.weight.is_cuda and len(self.output_sizes) == 2 \
+                and self.output_sizes[0] == self.output_sizes[1] and (self.output_sizes[0] // self.tp_size) % 64 == 0:
+            self.weight.data = gemm.interleave_gate_up(self.weight.data)
+            self.interleaved = True
+
+    def forward_silu(self, x):
+        if self.interleaved:
+            return gemm.linear_silu(x, self.weight)
+        from llmserve_b200.ops import activation
+        return activation.silu_and_mul(self.forward(x))
 
     def __init__(self, input_size, output_sizes: list[int], bias=False, quant_config=None):
         if quant_config is not None and any(s % quant_config.pack_factor for s in output_sizes):

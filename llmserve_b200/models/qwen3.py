@@ -85,7 +85,7 @@ class Qwen3MLP(nn.Module):
                                            quant_config=quant_config)
 
     def up(self, h):
-        return activation.silu_and_mul(self.gate_up_proj(h))
+        return self.gate_up_proj.forward_silu(h)
 
 
 class Qwen3DecoderLayer(nn.Module):
@@ -154,6 +154,10 @@ class Qwen3ForCausalLM(nn.Module):
         self.lm_head = ParallelLMHead(config.vocab_size, config.hidden_size)
         self.tie_word_embeddings = bool(config.tie_word_embeddings)
         self.eagle3_aux_layer_ids = tuple(get_eagle3_aux_layer_ids(config.num_hidden_layers))
+
+    def post_load(self):
+        for layer in self.model.layers:
+            layer.mlp.gate_up_proj.interleave_for_silu()
 
     def tie_weights(self):
         if self.tie_word_embeddings:

@@ -201,7 +201,7 @@ void check_pool(const at::Tensor& kc, const at::Tensor& vc) {
 
 void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
                       at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, at::Tensor counters,
-                      int64_t max_splits, int64_t partition) {
+                      int64_t max_splits, int64_t partition, int64_t grid_z) {
   check_pool(kc, vc);
   LSB_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q must be bf16 [B, nh, hd]");
   LSB_CHECK(block_tables.scalar_type() == at::kInt && block_tables.is_contiguous(), "block_tables must be int32");
@@ -217,7 +217,8 @@ void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc
   if (B == 0) return;
   const at::cuda::CUDAGuard g(q.device());
   // CTAs per (sequence, kv head): one when the batch alone gives >= 2 waves, else enough to fill the SMs
-  const int z = (int)std::max<int64_t>(1, std::min<int64_t>(max_splits, (148 * 3 + B * nkv - 1) / (B * nkv)));
+  const int z = grid_z > 0 ? (int)std::min<int64_t>(grid_z, max_splits)
+                           : (int)std::max<int64_t>(1, std::min<int64_t>(max_splits, (148 * 3 + B * nkv - 1) / (B * nkv)));
   dim3 grid(B, nkv, z);
   const float sl = (float)scale * kLog2e;
 #define LSB_DEC(HD)                                                                                                \

@@ -144,7 +144,6 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(
     float* __restrict__ part_o, float* __restrict__ part_ml, int* __restrict__ counters, int max_splits,
     int partition, int nh, int nkv, int bs) {
   pdl_trigger();
-  pdl_wait();
   extern __shared__ __align__(128) char smem[];
   __shared__ int is_last;
   bf16* sk[2] = {reinterpret_cast<bf16*>(smem), reinterpret_cast<bf16*>(smem + 2 * KT * HD * 2)};
@@ -152,9 +151,24 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int G = nh / nkv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // Context lengths and block tables are written by the host before the step's first kernel, and
+  // only the newest position's K/V (ctx - 1) is written by the kernel just before this one.  So
+  // the first tile, when it ends before that position, is streamed before waiting on the
+  // predecessor (programmatic dependent launch), overlapping it with the QKV projection.
   const int ctx = context_lens[b];
   const int nsplits = (ctx + partition - 1) / partition;
   const int* bt = block_tables + (size_t)b * bt_stride;
+  bool prefetched = false;
+  if ((int)blockIdx.z < nsplits) {
+    const int ks = blockIdx.z * partition;
+    const int ke = min(ks + partition, ctx);
+    if (min(ks + KT, ke) <= ctx - 1) {
+      load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, ks, ke, kvh, nkv, bs);
+      cp_async_commit();
+      prefetched = true;
+    }
+  }
+  pdl_wait();
   if (nsplits == 0) {
     if (blockIdx.z == 0)
       for (int i = threadIdx.x; i < G * HD; i += NTHREADS) out[((size_t)b * nh + kvh * G) * HD + i] = to_b(0.f);
@@ -190,8 +204,11 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(
     for (int n = 0; n < HD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
     __syncthreads();   // shared memory is reused across splits
-    load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, kstart, kend, kvh, nkv, bs);
-    cp_async_commit();
+    if (!prefetched) {
+      load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, kstart, kend, kvh, nkv, bs);
+      cp_async_commit();
+    }
+    prefetched = false;
     for (int t = 0; t < ntiles; ++t) {
       if (t + 1 < ntiles) {
         load_kv_tile<HD>(sk[(t + 1) & 1], sv[(t + 1) & 1], kc, vc, bt, kstart + (t + 1) * KT, kend, kvh, nkv, bs);

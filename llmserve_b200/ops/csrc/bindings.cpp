@@ -20,7 +20,7 @@ void argmax_rows(at::Tensor out_idx, at::Tensor out_val, at::Tensor logits);
 void sample_rows(at::Tensor out, at::Tensor logits, at::Tensor temps, int64_t seed);
 void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
                       at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, at::Tensor counters,
-                      int64_t max_splits, int64_t partition);
+                      int64_t max_splits, int64_t partition, int64_t grid_z);
 void prefill_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,
                        at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_seqlen_q);
 void tree_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bt, int64_t prefix_len,
@@ -35,6 +35,8 @@ void comm_close_handle(int64_t p);
 void fused_allreduce_add_rmsnorm(std::vector<int64_t> part, std::vector<int64_t> out, std::vector<int64_t> res,
                                  std::vector<int64_t> flags, at::Tensor res_in, at::Tensor w, int64_t rank, int64_t S,
                                  int64_t T, int64_t N, double eps, at::Tensor status);
+void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages);
+void splitk_silu(at::Tensor out, at::Tensor partials);
 }  // namespace lsb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -50,7 +52,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("splitk_reduce_add_rmsnorm", &lsb::splitk_reduce_add_rmsnorm);
   m.def("argmax_rows", &lsb::argmax_rows);
   m.def("sample_rows", &lsb::sample_rows);
-  m.def("decode_attention", &lsb::decode_attention);
+  m.def("decode_attention", &lsb::decode_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_tables"), py::arg("context_lens"), py::arg("scale"), py::arg("part_o"), py::arg("part_ml"),
+        py::arg("counters"), py::arg("max_splits"), py::arg("partition"), py::arg("grid_z") = 0);
   m.def("prefill_attention", &lsb::prefill_attention);
   m.def("tree_attention", &lsb::tree_attention);
   m.def("comm_alloc", &lsb::comm_alloc);
@@ -59,6 +63,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_open_handle", &lsb::comm_open_handle);
   m.def("comm_close_handle", &lsb::comm_close_handle);
   m.def("fused_allreduce_add_rmsnorm", &lsb::fused_allreduce_add_rmsnorm);
+  m.def("gemm_bf16_silu", &lsb::gemm_bf16_silu);
+  m.def("splitk_silu", &lsb::splitk_silu);
   m.def("gemm_bf16", &lsb::gemm_bf16, py::arg("out"), py::arg("x"), py::arg("w"), py::arg("partials"),
         py::arg("splits"), py::arg("status"), py::arg("max_stages") = 0);
 }

@@ -368,6 +368,28 @@ __global__ void __launch_bounds__(512) splitk_add_rmsnorm_kernel(bf16* __restric
   }
 }
 
+// split-K reduction of an interleaved gate/up projection + SiLU-mul -> bf16 [T, N/2]
+__global__ void splitk_silu_kernel(bf16* __restrict__ out, const float* __restrict__ part, int S, int T, int N) {
+  pdl_trigger();
+  pdl_wait();
+  const int half = N / 2;
+  const int64_t total = (int64_t)T * half;
+  const int64_t TN = (int64_t)T * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / half;
+    const int j = (int)(i % half);
+    const int64_t gidx = t * N + (j / 64) * 128 + (j % 64);
+    float g = 0.f, u = 0.f;
+    for (int s = 0; s < S; ++s) {
+      g += __ldcg(part + s * TN + gidx);
+      u += __ldcg(part + s * TN + gidx + 64);
+    }
+    g = to_f(to_b(g));
+    u = to_f(to_b(u));
+    out[i] = to_b(g / (1.f + expf(-g)) * u);
+  }
+}
+
 // ------------------------------------------------------------------------------------------
 // Row argmax (lowest index on ties) and exponential-race sampling
 // ------------------------------------------------------------------------------------------
@@ -662,6 +684,17 @@ void splitk_reduce_add_rmsnorm(at::Tensor out, at::Tensor res_out, at::Tensor pa
     case 8: go(splitk_add_rmsnorm_kernel<8>); break;
     default: go(splitk_add_rmsnorm_kernel<0>); break;
   }
+}
+
+void splitk_silu(at::Tensor out, at::Tensor partials) {
+  check_bf16(out, "out");
+  LSB_CHECK(partials.scalar_type() == at::kFloat && partials.is_contiguous() && partials.dim() == 3, "bad partials");
+  const int S = partials.size(0), T = partials.size(1), N = partials.size(2);
+  LSB_CHECK(N % 128 == 0 && out.numel() == (int64_t)T * (N / 2), "interleaved gate/up shape mismatch");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard g(out.device());
+  launch_pdl(splitk_silu_kernel, grid_for((int64_t)T * N / 2, 256), 256, 0, stream(), (bf16*)out.data_ptr(),
+             partials.data_ptr<float>(), S, T, N);
 }
 
 void argmax_rows(at::Tensor out_idx, at::Tensor out_val, at::Tensor logits) {

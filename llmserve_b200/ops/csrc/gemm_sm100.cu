@@ -103,7 +103,9 @@ constexpr int tmem_cols() {
   return BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
 }
 
-template <int BN, int STAGES>
+// EPI 0: bf16 output [T, N] or fp32 split-K partials; EPI 1: SiLU-mul of an interleaved gate/up
+// weight (rows 128i..128i+63 gate, +64..+127 up) -> bf16 [T, N/2].
+template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                            const __grid_constant__ CUtensorMap tm_x,
                                                            bf16* __restrict__ out, float* __restrict__ partials,
@@ -225,27 +227,62 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
   tc_fence_after();
   const int feat = n0 + warp * 32 + lane;
   const uint32_t row_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  if constexpr (EPI == 0) {
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 16) {
-    uint32_t r[16];
-    if (have) {
-      tc_ld16(row_addr + c0, r);
-    } else {
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      if (have) {
+        tc_ld16(row_addr + c0, r);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) r[j] = 0u;
-    }
-    if (feat < N) {
+        for (int j = 0; j < 16; ++j) r[j] = 0u;
+      }
+      if (feat < N) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int t = t0 + c0 + j;
-        if (t < T) {
-          const float v = __uint_as_float(r[j]);
-          if (partials != nullptr)
-            partials[((size_t)blockIdx.z * T + t) * N + feat] = v;
-          else
-            out[(size_t)t * N + feat] = to_b(v);
+        for (int j = 0; j < 16; ++j) {
+          const int t = t0 + c0 + j;
+          if (t < T) {
+            const float v = __uint_as_float(r[j]);
+            if (partials != nullptr)
+              partials[((size_t)blockIdx.z * T + t) * N + feat] = v;
+            else
+              out[(size_t)t * N + feat] = to_b(v);
+          }
         }
       }
+    }
+  } else {
+    // warps 2-3 hold the up rows: hand them to warps 0-1 (same row offset) through shared memory
+    float* xch = reinterpret_cast<float*>(smem);            // stage buffers are free now
+    const int half_row = (warp & 1) * 32 + lane;             // 0..63
+    const int out_n = N / 2;
+    const int out_col = blockIdx.x * (BM / 2) + half_row;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      if (have) {
+        tc_ld16(row_addr + c0, r);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) r[j] = 0u;
+      }
+      if (warp >= 2) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xch[half_row * 17 + j] = __uint_as_float(r[j]);
+      }
+      __syncthreads();
+      if (warp < 2 && out_col < out_n) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int t = t0 + c0 + j;
+          if (t < T) {
+            const float g = to_f(to_b(__uint_as_float(r[j])));
+            const float u = to_f(to_b(xch[half_row * 17 + j]));
+            out[(size_t)t * out_n + out_col] = to_b(g / (1.f + expf(-g)) * u);
+          }
+        }
+      }
+      __syncthreads();
     }
   }
   tc_fence_before();
@@ -310,7 +347,7 @@ const CUtensorMap& weight_map(const at::Tensor& w) {
   return it->second;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI = 0>
 void launch(const at::Tensor& x, const at::Tensor& w, bf16* out, float* partials, int splits, int* status) {
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kStage % 1024 == 0, "stage size must keep 1024-byte alignment");
@@ -319,7 +356,7 @@ void launch(const at::Tensor& x, const at::Tensor& w, bf16* out, float* partials
   const int kps = (k_tiles + splits - 1) / splits;
   const CUtensorMap mx = make_map(x.data_ptr(), T, K, x.stride(0), BN);
   const CUtensorMap& mw = weight_map(w);
-  auto kern = gemm_bf16_kernel<BN, STAGES>;
+  auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
@@ -339,6 +376,29 @@ constexpr int stages_for() {
 }  // namespace
 
 int* status_ptr(const at::Tensor& status);
+
+// SiLU-gated projection with an interleaved gate/up weight [N, K] (N = 2 * I, interleaved per 64
+// rows): out = silu(gate) * up as bf16 [T, I], in the GEMM epilogue (no split-K).
+void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages) {
+  LSB_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+            "gemm operands must be bf16 CUDA tensors");
+  LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1) && x.stride(1) == 1 && w.stride(1) == 1,
+            "gemm shape mismatch");
+  LSB_CHECK(w.size(0) % BM == 0, "interleaved gate/up weight must have a multiple of 128 rows");
+  const int T = x.size(0), N = w.size(0);
+  LSB_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)T * (N / 2),
+            "bad out");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard g(x.device());
+  bf16* o = (bf16*)out.data_ptr();
+  int* st = status_ptr(status);
+  const bool shallow = max_stages > 0 && max_stages <= 4;
+  if (T <= 16) { if (shallow) launch<16, 4, 1>(x, w, o, nullptr, 1, st); else launch<16, stages_for<16>(), 1>(x, w, o, nullptr, 1, st); }
+  else if (T <= 32) { if (shallow) launch<32, 4, 1>(x, w, o, nullptr, 1, st); else launch<32, stages_for<32>(), 1>(x, w, o, nullptr, 1, st); }
+  else if (T <= 64) { if (shallow) launch<64, 4, 1>(x, w, o, nullptr, 1, st); else launch<64, stages_for<64>(), 1>(x, w, o, nullptr, 1, st); }
+  else if (T <= 128) launch<128, stages_for<128>(), 1>(x, w, o, nullptr, 1, st);
+  else launch<256, stages_for<256>(), 1>(x, w, o, nullptr, 1, st);
+}
 
 // out: bf16 [T, N] when splits == 1; partials: fp32 [splits, T, N] otherwise.
 void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status,

@@ -84,3 +84,29 @@ def linear_partials(x: torch.Tensor, w: torch.Tensor, splits: int, partials: tor
         partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
     C().gemm_bf16(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits, status(x.device), _stages(T))
     return partials
+
+
+def interleave_gate_up(w: torch.Tensor) -> torch.Tensor:
+    """[gate (I rows) ; up (I rows)] -> rows interleaved per 64: g0..g63, u0..u63, g64.., so every
+    128-row tile of the GEMM holds matching gate and up rows (I % 64 == 0)."""
+    I = w.shape[0] // 2
+    g, u = w[:I].view(I // 64, 64, -1), w[I:].view(I // 64, 64, -1)
+    return torch.stack([g, u], dim=1).reshape(2 * I, -1).contiguous()
+
+
+def linear_silu(x: torch.Tensor, w_interleaved: torch.Tensor, max_splits: int = 8) -> torch.Tensor:
+    """``silu(x @ gate^T) * (x @ up^T)`` for an interleaved gate/up weight, fused in the GEMM
+    epilogue (or in the split-K reduction when K is split)."""
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    T, K = x2.shape
+    N = w_interleaved.shape[0]
+    out = torch.empty(T, N // 2, dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out
+    splits = min(choose_splits(T, N, K), max_splits)
+    if splits == 1:
+        C().gemm_bf16_silu(out, x2, w_interleaved, status(x.device), _stages(T))
+    else:
+        partials = linear_partials(x2, w_interleaved, splits)
+        C().splitk_silu(out, partials)
+    return out

@@ -35,6 +35,16 @@ def local_argmax(logits: torch.Tensor):
     return vals, out
 
 
+def local_argmax_into(logits: torch.Tensor, values: torch.Tensor, indices: torch.Tensor) -> None:
+    """``local_argmax`` writing into caller-owned ``values`` (fp32) / ``indices`` (int64)."""
+    if not logits.is_cuda:
+        v, i = logits.float().max(dim=-1)
+        values.copy_(v)
+        indices.copy_(i)
+        return
+    C().argmax_rows(indices, values, logits.contiguous())
+
+
 def noise_uniform_ref(shape, seed: int) -> torch.Tensor:
     """Uniforms in (0, 1) identical to the CUDA kernel's (SplitMix64 finaliser of a counter)."""
     rows, cols = shape

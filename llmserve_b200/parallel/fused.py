@@ -12,11 +12,15 @@ finishes the layer:
 This replaces ``dist.all_reduce`` (``llmserve/layers/linear.py:234-235``) plus the separate
 ``add_rms_forward`` of the reference.
 """
+import os
 import torch
 
 from llmserve_b200.ops import gemm, norm as norm_ops
 from llmserve_b200.ops._ext import C
 from llmserve_b200.parallel import state as tp
+
+# the reduction epilogue reads every split; 4 costs the GEMM almost nothing (B200 sweep)
+ROW_PARALLEL_MAX_SPLITS = int(os.environ.get("LLMSERVE_ROW_SPLITS", "64"))
 
 
 def row_parallel_add_norm(x, weight, residual, norm_weight, eps, fused=None):
@@ -26,7 +30,7 @@ def row_parallel_add_norm(x, weight, residual, norm_weight, eps, fused=None):
     world = tp.get_tp_size()
     if fused is not None and world > 1 and fused.can_handle(T, N):
         return fused.row_parallel_add_norm(x, weight, residual, norm_weight, eps)
-    splits = gemm.choose_splits(T, N, K)
+    splits = min(gemm.choose_splits(T, N, K), ROW_PARALLEL_MAX_SPLITS)
     partials = gemm.linear_partials(x, weight, splits)
     if world == 1:
         out = torch.empty(T, N, dtype=x.dtype, device=x.device)

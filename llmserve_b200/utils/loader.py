@@ -30,6 +30,8 @@ def _post_load(model: nn.Module):
         qm = getattr(module, "quant_method", None)
         if qm is not None:
             qm.process_weights_after_loading(module)
+    if hasattr(model, "post_load"):
+        model.post_load()
 
 
 def load_model(model: nn.Module, path: str):

@@ -221,3 +221,22 @@ def test_qkv_rope_from_splitk_partials(S):
     q1, _, _ = rope.qkv_norm_rope_store(parts, pos, cs, qw, kw, 1e-6, kc1, vc1, slots, nh, nkv, hd)
     q2, _, _ = rope.qkv_norm_rope_store(parts.sum(0).bfloat16(), pos, cs, qw, kw, 1e-6, kc2, vc2, slots, nh, nkv, hd)
     assert rel_err(q1, q2) < 2e-3 and rel_err(kc1, kc2) < 2e-3 and rel_err(vc1, vc2) < 2e-3
+
+
+@pytest.mark.parametrize("T", [1, 16, 64, 200])
+@pytest.mark.parametrize("I,K", [(512, 256), (1536, 4096)])
+def test_gate_up_silu_fused_epilogue(T, I, K):
+    g = torch.Generator(device=DEV).manual_seed(T + I)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(2 * I, K, device=DEV, generator=g) * 0.05).bfloat16()
+    ref = activation.silu_and_mul_ref((x.float() @ w.float().t()).bfloat16().cpu()).to(DEV)
+    wi = gemm.interleave_gate_up(w)
+    out = gemm.linear_silu(x, wi)
+    assert rel_err(out, ref) < 1e-2
+    out2 = gemm.linear_silu(x, wi, max_splits=1)
+    assert rel_err(out2, ref) < 1e-2
+    # forced split-K path through the interleaved reduction
+    parts = gemm.linear_partials(x, wi, 4)
+    o3 = torch.empty(T, I, device=DEV, dtype=torch.bfloat16)
+    C().splitk_silu(o3, parts)
+    assert rel_err(o3, ref) < 1e-2
