@@ -6,6 +6,8 @@ B200's HBM), which removes the reference's per-forward all-reduce of ``[T, H]``
 its logit shard; greedy decoding combines per-shard (max, index) pairs and only temperature
 sampling gathers full rows (``embed_head.py:56-66`` gathers every row to rank 0).
 """
+import os
+
 import torch
 from torch import nn
 
@@ -45,9 +47,25 @@ class ParallelLMHead(nn.Module):
     def weight_loader(self, param, loaded):
         param.data.copy_(loaded.narrow(0, self.vocab_start, self.shard_size))
 
+    packed_weight = None
+
+    @property
+    def gemm_weight(self):
+        return self.packed_weight if self.packed_weight is not None else self.weight
+
+    def pack_for_gemm(self):
+        """Tile-pack the (untied) head for the GEMM; see ``LinearBase.pack_for_gemm``."""
+        if os.environ.get("LLMSERVE_PACK_WEIGHTS", "1") == "0" or not self.weight.is_cuda \
+                or self.packed_weight is not None:
+            return
+        pw = gemm.pack_weight(self.weight.data)
+        self.register_buffer("weight_tiles", pw.data, persistent=False)
+        self.packed_weight = pw
+        self.weight.data = torch.empty(0, dtype=self.weight.dtype, device=self.weight.device)
+
     def forward(self, x: torch.Tensor, all_tokens: bool = False) -> torch.Tensor:
         """Logit shard ``[rows, V / tp]``; in prefill only each sequence's last row."""
         ctx = get_context()
         if not all_tokens and ctx.is_prefill and ctx.last_token_indices is not None:
             x = x.index_select(0, ctx.last_token_indices)
-        return gemm.linear(x, self.weight)
+        return gemm.linear(x, self.gemm_weight)

@@ -47,10 +47,29 @@ class LinearBase(nn.Module):
         else:
             self.register_parameter("bias", None)
 
+    packed_weight = None
+
+    @property
+    def gemm_weight(self):
+        """The operand handed to the GEMM: the packed tile image once ``pack_for_gemm`` ran."""
+        return self.packed_weight if self.packed_weight is not None else self.weight
+
+    def pack_for_gemm(self):
+        """After loading: re-store the dense CUDA weight as ``gemm.PackedWeight`` (tile-contiguous,
+        pre-swizzled) and release the row-major copy.  The tile image is kept as a buffer so
+        memory accounting still sees it."""
+        if (os.environ.get("LLMSERVE_PACK_WEIGHTS", "1") == "0" or self.quant_method is not None
+                or not self.weight.is_cuda or getattr(self, "interleaved", False) or self.packed_weight is not None):
+            return
+        pw = gemm.pack_weight(self.weight.data)
+        self.register_buffer("weight_tiles", pw.data, persistent=False)
+        self.packed_weight = pw
+        self.weight.data = torch.empty(0, dtype=self.weight.dtype, device=self.weight.device)
+
     def apply_linear(self, x: torch.Tensor, bias=True) -> torch.Tensor:
         if self.quant_method is not None:
             return self.quant_method.apply(self, x)
-        return gemm.linear(x, self.weight, self.bias if bias else None)
+        return gemm.linear(x, self.gemm_weight, self.bias if bias else None)
 
     @staticmethod
     def _pack_factor(param, dim: int) -> int:
@@ -134,9 +153,10 @@ class QKVParallelLinear(ColumnParallelLinear):
         them); otherwise the projection output."""
         if x.is_cuda and self.quant_method is None and self.bias is None:
             x2 = x.reshape(-1, x.shape[-1])
-            splits = gemm.choose_splits(x2.shape[0], self.weight.shape[0], x2.shape[1])
+            w = self.gemm_weight
+            splits = gemm.choose_splits(x2.shape[0], w.shape[0], x2.shape[1])
             if splits > 1:
-                return gemm.linear_partials(x2.contiguous(), self.weight, splits)
+                return gemm.linear_partials(x2.contiguous(), w, splits)
         return self.forward(x)
 
     def __init__(self, hidden_size, head_size, total_num_heads, total_num_kv_heads=None, bias=False,
@@ -186,7 +206,7 @@ class RowParallelLinear(LinearBase):
         """``(rmsnorm(allreduce(x @ W^T) + residual) * w, allreduce(..) + residual)``."""
         if x.is_cuda and self.quant_method is None and self.bias is None:
             from llmserve_b200.parallel import fused as fused_ops
-            return fused_ops.row_parallel_add_norm(x, self.weight, residual, norm_weight, eps,
+            return fused_ops.row_parallel_add_norm(x, self.gemm_weight, residual, norm_weight, eps,
                                                    tp.get_fused_comm())
         y = self.forward(x)
         return norm_ops.add_rms_norm(y, residual, norm_weight, eps)

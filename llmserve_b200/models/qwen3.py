@@ -156,8 +156,18 @@ class Qwen3ForCausalLM(nn.Module):
         self.eagle3_aux_layer_ids = tuple(get_eagle3_aux_layer_ids(config.num_hidden_layers))
 
     def post_load(self):
+        """After weights are loaded: optional SiLU interleave of gate_up, then tile-pack every dense
+        projection (and the untied LM head) for the sm_100a GEMM."""
+        from llmserve_b200.layers.linear import LinearBase
         for layer in self.model.layers:
             layer.mlp.gate_up_proj.interleave_for_silu()
+        for m in self.modules():
+            if isinstance(m, LinearBase):
+                m.pack_for_gemm()
+        if not self.tie_word_embeddings:
+            self.lm_head.pack_for_gemm()
+        if torch.cuda.is_available():
+            torch.cuda.empty_cache()
 
     def tie_weights(self):
         if self.tie_word_embeddings:

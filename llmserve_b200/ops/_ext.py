@@ -72,10 +72,13 @@ def status(device):
     """Per-device int32 word in which kernels record a bounded-wait timeout or a skipped bad
     index instead of trapping; read it with :func:`check_status`."""
     import torch
-    key = str(device)
+    d = torch.device(device)
+    if d.type == "cuda" and d.index is None:
+        d = torch.device("cuda", torch.cuda.current_device())
+    key = str(d)
     t = _STATUS.get(key)
     if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=device)
+        t = torch.zeros(1, dtype=torch.int32, device=d)
         _STATUS[key] = t
     return t
 

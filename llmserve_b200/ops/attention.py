@@ -5,9 +5,11 @@ prefill kernel streams it with bulk copies, and a whole block of a layer is one 
 region for the prefill->decode KV push.
 
 * ``decode_attention``  -- one query token per sequence (``flash_attn_with_kvcache`` in the
-  reference, ``llmserve/layers/attention.py:130-132``).  sm_100a split-KV kernel with the query
-  heads of one KV head packed together (GQA); the last CTA of a (sequence, KV head) merges the
-  splits (log-sum-exp), so one launch per layer.
+  reference, ``llmserve/layers/attention.py:130-132``).  Persistent sm_100a kernel: one CTA per
+  SM pair slot, a producer warp streams K/V pages with 2-D tensor copies (128B swizzle) through a
+  3-stage ring, four warps run the GQA math with the query heads of one KV head packed together; chunks of
+  long contexts are merged (log-sum-exp) by the CTA that finishes last, so one launch per layer.
+  The earlier cp.async split-KV kernel remains for block sizes the tensor copy cannot tile.
 * ``prefill_attention`` -- varlen causal attention of a query chunk against the paged keys of
   its sequence (``flash_attn_varlen_func(..., block_table)`` in the reference, ``:121-126``):
   covers plain prefill, chunked prefill, prefix-cache hits and the packed EAGLE3 verify.
@@ -16,10 +18,12 @@ region for the prefill->decode KV push.
   tree nodes' own keys under an ancestor mask (``attention.py:77-109`` of the reference).
 """
 import math
+import os
 
 import torch
 
-from llmserve_b200.ops._ext import C
+from llmserve_b200.ops._ext import C, status
+from llmserve_b200.ops.gemm import NUM_SMS
 
 
 def _gather_pages(cache: torch.Tensor, block_table: torch.Tensor, length: int) -> torch.Tensor:
@@ -102,6 +106,19 @@ class DecodeWorkspace:
         self.counters = torch.zeros(max_batch * num_heads, dtype=torch.int32, device=device)
 
 
+_DECODE_TMA = os.environ.get("LLMSERVE_DECODE_TMA", "1") != "0"
+_TMA_PARTITION = int(os.environ.get("LLMSERVE_DECODE_TMA_PARTITION", "0"))
+
+
+def tma_partition(batch: int, kv_heads: int) -> int:
+    """Keys per work item of the persistent TMA decode kernel: enough items to keep every SM's ring
+    busy and to even out the round-robin tail, without paying a partial merge on every chunk."""
+    if _TMA_PARTITION:
+        return _TMA_PARTITION
+    pairs = batch * kv_heads
+    return 128 if pairs < NUM_SMS else 256 if pairs < 2 * NUM_SMS else 512
+
+
 def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, workspace=None):
     if not q.is_cuda:
         return decode_attention_ref(q, k_cache, v_cache, block_tables, context_lens, scale)
@@ -110,6 +127,11 @@ def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, wor
     if workspace is None or workspace.max_batch < B or workspace.max_splits * 128 < cap:
         workspace = DecodeWorkspace(B, nh, hd, cap, q.device)
     out = torch.empty_like(q)
+    if _DECODE_TMA and C().decode_tma_supported(k_cache.shape[2], hd):
+        C().decode_attention_tma(out, q.contiguous(), k_cache, v_cache, block_tables, context_lens, float(scale),
+                                 workspace.partial_out, workspace.partial_ml, workspace.counters,
+                                 workspace.max_splits, tma_partition(B, k_cache.shape[1]), status(q.device))
+        return out
     part = decode_partition(B, k_cache.shape[1])
     C().decode_attention(out, q.contiguous(), k_cache, v_cache, block_tables, context_lens, float(scale),
                          workspace.partial_out, workspace.partial_ml, workspace.counters,

@@ -37,6 +37,12 @@ void fused_allreduce_add_rmsnorm(std::vector<int64_t> part, std::vector<int64_t>
                                  int64_t T, int64_t N, double eps, at::Tensor status);
 void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages);
 void splitk_silu(at::Tensor out, at::Tensor partials);
+void gemm_bf16_packed(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, at::Tensor partials, int64_t splits,
+                      at::Tensor status, int64_t max_stages);
+void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
+                          at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml,
+                          at::Tensor counters, int64_t max_splits, int64_t partition, at::Tensor status);
+bool decode_tma_supported(int64_t block_size, int64_t head_dim);
 }  // namespace lsb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -52,6 +58,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("splitk_reduce_add_rmsnorm", &lsb::splitk_reduce_add_rmsnorm);
   m.def("argmax_rows", &lsb::argmax_rows);
   m.def("sample_rows", &lsb::sample_rows);
+  m.def("decode_attention_tma", &lsb::decode_attention_tma);
+  m.def("gemm_bf16_packed", &lsb::gemm_bf16_packed);
+  m.def("decode_tma_supported", &lsb::decode_tma_supported);
   m.def("decode_attention", &lsb::decode_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("context_lens"), py::arg("scale"), py::arg("part_o"), py::arg("part_ml"),
         py::arg("counters"), py::arg("max_splits"), py::arg("partition"), py::arg("grid_z") = 0);

@@ -21,6 +21,7 @@
 #include <c10/cuda/CUDAStream.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -34,6 +35,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;   // 64 bf16 = 128 bytes: one 128B swizzle atom per row
 constexpr int kSmemBudget = 200 * 1024;
+constexpr int kGroupT = 8;   // token tiles per raster group
 
 // ---- descriptors --------------------------------------------------------------------------
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"), K-major, 128B swizzle:
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
                                                            const __grid_constant__ CUtensorMap tm_x,
                                                            bf16* __restrict__ out, float* __restrict__ partials,
                                                            int T, int N, int k_tiles, int k_tiles_per_split,
-                                                           int* __restrict__ status) {
+                                                           int packed, int* __restrict__ status) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -121,8 +123,22 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BM, t0 = blockIdx.y * BN;
+  // Tile order: blockIdx.x enumerates (weight tile, token tile) pairs in groups of kGroupT token
+  // tiles, token tile fastest, so the CTAs resident at one time cover a ~18 x 8 block of the
+  // output and re-read W and X from L2 rather than HBM.  With one token tile (decode) this is
+  // the plain weight-tile order.
+  const int num_m = (N + BM - 1) / BM, num_t = (T + BN - 1) / BN;
+  const int per_group = kGroupT * num_m;
+  const int grp = blockIdx.x / per_group, rem = blockIdx.x - grp * per_group;
+  const int first_t = grp * kGroupT;
+  const int gsz = min(num_t - first_t, kGroupT);
+  const int m_tile = rem / gsz, t_tile = first_t + rem % gsz;
+  const int n0 = m_tile * BM, t0 = t_tile * BN;
   const int kt_begin = blockIdx.z * k_tiles_per_split;
+  // W tile coordinates: row-major [N, K] (tensor map with 128B swizzle), or the packed layout in
+  // which tile (m, kt) is 128 consecutive pre-swizzled 128-byte rows (one contiguous 16 KiB run).
+  auto w_x = [&](int kt) { return packed ? 0 : kt * BK; };
+  auto w_y = [&](int kt) { return packed ? (m_tile * k_tiles + kt) * BM : n0; };
   const int kt_end = min(k_tiles, kt_begin + k_tiles_per_split);
   const int nk = max(0, kt_end - kt_begin);
 
@@ -155,7 +171,7 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
       const int pre = nk < STAGES ? nk : STAGES;
       for (int i = 0; i < pre; ++i) {
         mbar_expect_tx(&full[i], L::kStage);
-        tma_load_2d(smem + i * L::kStage, &tm_w, &full[i], (kt_begin + i) * BK, n0);
+        tma_load_2d(smem + i * L::kStage, &tm_w, &full[i], w_x(kt_begin + i), w_y(kt_begin + i));
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i)
@@ -174,7 +190,7 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
         uint8_t* st = smem + s * L::kStage;
         mbar_expect_tx(&full[s], L::kStage);
         const int kx = (kt_begin + i) * BK;
-        tma_load_2d(st, &tm_w, &full[s], kx, n0);
+        tma_load_2d(st, &tm_w, &full[s], w_x(kt_begin + i), w_y(kt_begin + i));
         tma_load_2d(st + L::kW, &tm_x, &full[s], kx, t0);
         issued[s] = i + 1;
       }
@@ -256,7 +272,7 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
     float* xch = reinterpret_cast<float*>(smem);            // stage buffers are free now
     const int half_row = (warp & 1) * 32 + lane;             // 0..63
     const int out_n = N / 2;
-    const int out_col = blockIdx.x * (BM / 2) + half_row;
+    const int out_col = m_tile * (BM / 2) + half_row;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       uint32_t r[16];
@@ -308,14 +324,16 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with a (box_rows x 64) box.
-CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t row_stride_elems, int box_rows) {
+CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int64_t row_stride_elems, int box_rows,
+                     bool swizzle = true) {
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)row_stride_elems * 2};
   cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   LSB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return m;
@@ -325,8 +343,9 @@ struct MapKey {
   const void* p;
   int64_t rows, cols, stride;
   int box;
+  bool packed;
   bool operator==(const MapKey& o) const {
-    return p == o.p && rows == o.rows && cols == o.cols && stride == o.stride && box == o.box;
+    return p == o.p && rows == o.rows && cols == o.cols && stride == o.stride && box == o.box && packed == o.packed;
   }
 };
 struct MapKeyHash {
@@ -336,35 +355,43 @@ struct MapKeyHash {
   }
 };
 
-// Weight maps are built once per (pointer, shape); activations change every call.
-const CUtensorMap& weight_map(const at::Tensor& w) {
+}  // namespace
+
+// Weight maps are built once per (pointer, shape); activations change every call.  A packed
+// weight is a [rows, 64] bf16 tensor already in the swizzled shared-memory image, so its map
+// copies 128 x 64 boxes without swizzling.
+const CUtensorMap& weight_map(const at::Tensor& w, bool packed) {
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
   static std::mutex mu;
-  MapKey key{w.data_ptr(), w.size(0), w.size(1), w.stride(0), BM};
+  MapKey key{w.data_ptr(), w.size(0), w.size(1), w.stride(0), BM, packed};
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
-  if (it == cache.end()) it = cache.emplace(key, make_map(w.data_ptr(), w.size(0), w.size(1), w.stride(0), BM)).first;
+  if (it == cache.end())
+    it = cache.emplace(key, make_map(w.data_ptr(), w.size(0), w.size(1), w.stride(0), BM, !packed)).first;
   return it->second;
 }
 
+namespace {
+
 template <int BN, int STAGES, int EPI = 0>
-void launch(const at::Tensor& x, const at::Tensor& w, bf16* out, float* partials, int splits, int* status) {
+void launch(const at::Tensor& x, const at::Tensor& w, int N, bool packed, bf16* out, float* partials, int splits,
+            int* status) {
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kStage % 1024 == 0, "stage size must keep 1024-byte alignment");
-  const int T = x.size(0), K = x.size(1), N = w.size(0);
+  const int T = x.size(0), K = x.size(1);
   const int k_tiles = (K + BK - 1) / BK;
   const int kps = (k_tiles + splits - 1) / splits;
   const CUtensorMap mx = make_map(x.data_ptr(), T, K, x.stride(0), BN);
-  const CUtensorMap& mw = weight_map(w);
+  const CUtensorMap& mw = weight_map(w, packed);
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     configured = true;
   }
-  dim3 grid((N + BM - 1) / BM, (T + BN - 1) / BN, splits);
+  dim3 grid(((N + BM - 1) / BM) * ((T + BN - 1) / BN), 1, splits);
   launch_pdl(kern, grid, dim3(128), L::kBytes, at::cuda::getCurrentCUDAStream(), mw, mx, out, partials, T, N, k_tiles,
-             kps, status);
+             kps, (int)packed, status);
 }
 
 template <int BN>
@@ -376,6 +403,18 @@ constexpr int stages_for() {
 }  // namespace
 
 int* status_ptr(const at::Tensor& status);
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
+
+
+// Token counts from which the persistent 2-SM kernel replaces the one-SM tile kernel.
+static int pair_min_tokens() {
+  static int v = [] {
+    const char* e = std::getenv("LLMSERVE_PAIR_GEMM_MIN_T");
+    return e ? std::atoi(e) : 512;
+  }();
+  return v;
+}
 
 // SiLU-gated projection with an interleaved gate/up weight [N, K] (N = 2 * I, interleaved per 64
 // rows): out = silu(gate) * up as bf16 [T, I], in the GEMM epilogue (no split-K).
@@ -393,24 +432,39 @@ void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor statu
   bf16* o = (bf16*)out.data_ptr();
   int* st = status_ptr(status);
   const bool shallow = max_stages > 0 && max_stages <= 4;
-  if (T <= 16) { if (shallow) launch<16, 4, 1>(x, w, o, nullptr, 1, st); else launch<16, stages_for<16>(), 1>(x, w, o, nullptr, 1, st); }
-  else if (T <= 32) { if (shallow) launch<32, 4, 1>(x, w, o, nullptr, 1, st); else launch<32, stages_for<32>(), 1>(x, w, o, nullptr, 1, st); }
-  else if (T <= 64) { if (shallow) launch<64, 4, 1>(x, w, o, nullptr, 1, st); else launch<64, stages_for<64>(), 1>(x, w, o, nullptr, 1, st); }
-  else if (T <= 128) launch<128, stages_for<128>(), 1>(x, w, o, nullptr, 1, st);
-  else launch<256, stages_for<256>(), 1>(x, w, o, nullptr, 1, st);
+#define LSB_SILU(BNV)                                                                  \
+  do {                                                                                 \
+    if (shallow) launch<BNV, 4, 1>(x, w, N, false, o, nullptr, 1, st);                 \
+    else launch<BNV, stages_for<BNV>(), 1>(x, w, N, false, o, nullptr, 1, st);         \
+  } while (0)
+  if (T <= 16) LSB_SILU(16);
+  else if (T <= 32) LSB_SILU(32);
+  else if (T <= 64) LSB_SILU(64);
+  else if (T <= 128) launch<128, stages_for<128>(), 1>(x, w, N, false, o, nullptr, 1, st);
+  else launch<256, stages_for<256>(), 1>(x, w, N, false, o, nullptr, 1, st);
+#undef LSB_SILU
 }
 
-// out: bf16 [T, N] when splits == 1; partials: fp32 [splits, T, N] otherwise.
-void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status,
-               int64_t max_stages) {
+void gemm_bf16_pair(void* out, bool out_f32, const at::Tensor& x, const at::Tensor& w, int N, bool packed, int* status);
+
+// Shared dispatch.  w: row-major [N, K], or (packed) the [rows, 64] pre-swizzled tile image of a
+// weight with N logical rows (rows padded to 256, K to 64).
+static void gemm_dispatch(at::Tensor out, at::Tensor x, at::Tensor w, int64_t N, bool packed, at::Tensor partials,
+                          int64_t splits, at::Tensor status, int64_t max_stages) {
   LSB_CHECK(x.is_cuda() && w.is_cuda(), "gemm operands must be CUDA tensors");
   LSB_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
-  LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "gemm shape mismatch");
+  LSB_CHECK(x.dim() == 2 && w.dim() == 2, "gemm operands must be 2-D");
   LSB_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "gemm operands must be K-contiguous");
   LSB_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "row strides must be 16-byte multiples");
   LSB_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
             "gemm operands must be 16-byte aligned");
-  const int T = x.size(0), N = w.size(0);
+  const int T = x.size(0);
+  if (packed) {
+    const int64_t kt = (x.size(1) + BK - 1) / BK, mt = (N + 255) / 256 * 2;
+    LSB_CHECK(w.size(1) == BK && w.is_contiguous() && w.size(0) == mt * kt * BM, "packed weight shape mismatch");
+  } else {
+    LSB_CHECK(x.size(1) == w.size(1) && w.size(0) == N, "gemm shape mismatch");
+  }
   LSB_CHECK(splits >= 1 && splits <= 64, "splits out of range");
   bf16* o = nullptr;
   float* p = nullptr;
@@ -425,18 +479,36 @@ void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, 
   if (T == 0 || N == 0) return;
   const at::cuda::CUDAGuard g(x.device());
   int* st = status_ptr(status);
-  if (max_stages > 0 && max_stages <= 4 && T <= 64) {
-    // shallow ring: two CTAs fit on one SM and overlap each other's prologue / epilogue
-    if (T <= 16) launch<16, 4>(x, w, o, p, splits, st);
-    else if (T <= 32) launch<32, 4>(x, w, o, p, splits, st);
-    else launch<64, 4>(x, w, o, p, splits, st);
+  const int n = (int)N;
+  if (splits == 1 && T >= pair_min_tokens() && N % 8 == 0) {
+    gemm_bf16_pair(o != nullptr ? (void*)o : (void*)p, o == nullptr, x, w, n, packed, st);
     return;
   }
-  if (T <= 16) launch<16, stages_for<16>()>(x, w, o, p, splits, st);
-  else if (T <= 32) launch<32, stages_for<32>()>(x, w, o, p, splits, st);
-  else if (T <= 64) launch<64, stages_for<64>()>(x, w, o, p, splits, st);
-  else if (T <= 128) launch<128, stages_for<128>()>(x, w, o, p, splits, st);
-  else launch<256, stages_for<256>()>(x, w, o, p, splits, st);
+  if (max_stages > 0 && max_stages <= 4 && T <= 64) {
+    // shallow ring: two CTAs fit on one SM and overlap each other's prologue / epilogue
+    if (T <= 16) launch<16, 4>(x, w, n, packed, o, p, splits, st);
+    else if (T <= 32) launch<32, 4>(x, w, n, packed, o, p, splits, st);
+    else launch<64, 4>(x, w, n, packed, o, p, splits, st);
+    return;
+  }
+  if (T <= 16) launch<16, stages_for<16>()>(x, w, n, packed, o, p, splits, st);
+  else if (T <= 32) launch<32, stages_for<32>()>(x, w, n, packed, o, p, splits, st);
+  else if (T <= 64) launch<64, stages_for<64>()>(x, w, n, packed, o, p, splits, st);
+  else if (T <= 128) launch<128, stages_for<128>()>(x, w, n, packed, o, p, splits, st);
+  else launch<256, stages_for<256>()>(x, w, n, packed, o, p, splits, st);
+}
+
+// out: bf16 [T, N] when splits == 1; partials: fp32 [splits, T, N] otherwise.
+void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status,
+               int64_t max_stages) {
+  LSB_CHECK(w.dim() == 2, "gemm weight must be 2-D");
+  gemm_dispatch(out, x, w, w.size(0), false, partials, splits, status, max_stages);
+}
+
+// Same with a packed weight (see gemm.pack_weight) of n logical rows.
+void gemm_bf16_packed(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, at::Tensor partials, int64_t splits,
+                      at::Tensor status, int64_t max_stages) {
+  gemm_dispatch(out, x, w, n, true, partials, splits, status, max_stages);
 }
 
 }  // namespace lsb

@@ -41,8 +41,73 @@ def _stages(T: int) -> int:
     return 4 if T <= SMALL_T else 0
 
 
-def linear_ref(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+class PackedWeight:
+    """A weight ``[N, K]`` stored as 128 x 64 tiles in tile order ``(row tile, k tile)``, each tile
+    the exact 16 KiB image the GEMM keeps in shared memory (128-byte rows, 16-byte chunks XOR-
+    swizzled by row).  A K-range of one row tile is then one contiguous run of HBM, which the
+    decode GEMM streams with sequential DRAM pages instead of 128-byte pieces of 128 rows.
+    Rows are zero-padded to a multiple of 256 (the 2-SM tile) and K to a multiple of 64."""
+
+    def __init__(self, data: torch.Tensor, n: int, k: int):
+        self.data, self.n, self.k = data, n, k
+
+    @property
+    def shape(self):
+        return (self.n, self.k)
+
+    @property
+    def device(self):
+        return self.data.device
+
+    @property
+    def dtype(self):
+        return self.data.dtype
+
+    def unpack(self) -> torch.Tensor:
+        return unpack_weight(self)
+
+
+def _swizzle_index(device):
+    r = torch.arange(TILE_M, device=device).view(TILE_M, 1)
+    p = torch.arange(8, device=device).view(1, 8)
+    return p ^ (r & 7)           # physical chunk p of row r holds logical chunk p ^ (r & 7)
+
+
+def pack_weight(w: torch.Tensor) -> PackedWeight:
+    N, K = w.shape
+    Np, Kp = -(-N // 256) * 256, -(-K // TILE_K) * TILE_K
+    if (Np, Kp) != (N, K):
+        wp = torch.zeros(Np, Kp, dtype=w.dtype, device=w.device)
+        wp[:N, :K] = w
+    else:
+        wp = w
+    mt, kt = Np // TILE_M, Kp // TILE_K
+    tiles = wp.view(mt, TILE_M, kt, 8, 8).permute(0, 2, 1, 3, 4)          # [mt, kt, 128, chunk, 8]
+    idx = _swizzle_index(w.device).view(1, 1, TILE_M, 8, 1).expand(mt, kt, TILE_M, 8, 8)
+    packed = torch.gather(tiles, 3, idx).contiguous().view(-1, TILE_K)
+    return PackedWeight(packed, N, K)
+
+
+def unpack_weight(pw: PackedWeight) -> torch.Tensor:
+    Np, Kp = -(-pw.n // 256) * 256, -(-pw.k // TILE_K) * TILE_K
+    mt, kt = Np // TILE_M, Kp // TILE_K
+    tiles = pw.data.view(mt, kt, TILE_M, 8, 8)
+    idx = _swizzle_index(pw.device).view(1, 1, TILE_M, 8, 1).expand(mt, kt, TILE_M, 8, 8)
+    logical = torch.gather(tiles, 3, idx)                                  # XOR swizzle is its own inverse
+    return logical.permute(0, 2, 1, 3, 4).reshape(Np, Kp)[: pw.n, : pw.k].contiguous()
+
+
+def linear_ref(x: torch.Tensor, w, bias: torch.Tensor | None = None) -> torch.Tensor:
+    if isinstance(w, PackedWeight):
+        w = w.unpack()
     return F.linear(x, w, bias)
+
+
+def _gemm(out, x, w, partials, splits, T):
+    if isinstance(w, PackedWeight):
+        C().gemm_bf16_packed(out, x, w.data, w.n, partials, splits, status(x.device), _stages(T))
+    else:
+        C().gemm_bf16(out, x, w, partials, splits, status(x.device), _stages(T))
 
 
 _EMPTY = {}
@@ -66,10 +131,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -
         return out.view(*x.shape[:-1], N)
     splits = choose_splits(T, N, K)
     if splits == 1:
-        C().gemm_bf16(out, x2, w, _empty(x.device, torch.float32), 1, status(x.device), _stages(T))
+        _gemm(out, x2, w, _empty(x.device, torch.float32), 1, T)
     else:
         partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
-        C().gemm_bf16(_empty(x.device, x.dtype), x2, w, partials, splits, status(x.device), _stages(T))
+        _gemm(_empty(x.device, x.dtype), x2, w, partials, splits, T)
         C().splitk_reduce(out, partials)
     if bias is not None:
         out += bias
@@ -82,7 +147,7 @@ def linear_partials(x: torch.Tensor, w: torch.Tensor, splits: int, partials: tor
     N = w.shape[0]
     if partials is None:
         partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
-    C().gemm_bf16(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits, status(x.device), _stages(T))
+    _gemm(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits, T)
     return partials
 
 

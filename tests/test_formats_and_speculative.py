@@ -159,3 +159,22 @@ def test_tree_path_selection_matches_reference():
 def test_greedy_from_ids_bonus():
     r = greedy_accept_from_ids([1, 2, 3, 4], [1, 2, 3])
     assert r.token_ids == [1, 2, 3, 4] and r.accepted_all
+
+
+def test_pack_weight_layout_roundtrip():
+    """Packed GEMM weights: tile (m, kt) is 128 rows of 64 elements whose 16-byte chunks are
+    XOR-swizzled by row; unpacking restores the weight exactly (padding dropped)."""
+    from llmserve_b200.ops import gemm
+    w = torch.arange(300 * 136, dtype=torch.float32).view(300, 136).to(torch.bfloat16)
+    pw = gemm.pack_weight(w)
+    assert pw.shape == (300, 136)
+    assert pw.data.shape == (512 // 128 * 3 * 128, 64)        # rows padded to 512, K to 192
+    assert torch.equal(pw.unpack(), w)
+    wp = torch.zeros(512, 192, dtype=torch.bfloat16)
+    wp[:300, :136] = w
+    kt_count = 3
+    for m, kt, r, p in [(0, 0, 0, 0), (1, 2, 5, 3), (2, 1, 127, 7), (3, 0, 9, 1)]:
+        row = (m * kt_count + kt) * 128 + r
+        logical_chunk = p ^ (r & 7)
+        expect = wp[m * 128 + r, kt * 64 + logical_chunk * 8: kt * 64 + logical_chunk * 8 + 8]
+        assert torch.equal(pw.data[row, p * 8: p * 8 + 8], expect)

@@ -7,7 +7,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 from llmserve_b200.ops import activation, attention, gemm, kv, norm, rope, sampling  # noqa: E402
-from llmserve_b200.ops._ext import C, check_status  # noqa: E402
+from llmserve_b200.ops._ext import C, check_status, status  # noqa: E402
 
 DEV = "cuda"
 
@@ -34,6 +34,40 @@ def test_gemm_matches_fp32(T, N, K):
     out = gemm.linear(x, w)
     torch.cuda.synchronize()
     assert rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("T,N,K", [(512, 256, 64), (777, 1000, 520), (1024, 6144, 4096), (2304, 4104, 1024),
+                                   (4096, 24576, 256)])
+def test_pair_gemm_matches_fp32(T, N, K):
+    """Prefill-sized token counts run the persistent 2-SM (cta_group::2) kernel: ragged T and N,
+    K not a multiple of the 64-wide stage, several tiles per cluster."""
+    g = torch.Generator(device=DEV).manual_seed(T + N + K)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) * 0.05).bfloat16()
+    ref = x.float() @ w.float().t()
+    out = gemm.linear(x, w)
+    parts = gemm.linear_partials(x, w, 1)         # fp32 output variant
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-2
+    assert rel_err(parts[0], ref) < 1e-4
+    assert torch.isfinite(parts).all()
+
+
+@pytest.mark.parametrize("T", [1, 17, 64, 300, 1024])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (1000, 520), (6144, 1024)])
+def test_packed_gemm_matches_fp32(T, N, K):
+    """Tile-packed weights (decode kernel for small T, 2-SM kernel for large T, split-K partials)."""
+    g = torch.Generator(device=DEV).manual_seed(T + N + K + 1)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) * 0.05).bfloat16()
+    pw = gemm.pack_weight(w)
+    assert torch.equal(pw.unpack(), w)
+    ref = x.float() @ w.float().t()
+    out = gemm.linear(x, pw)
+    parts = gemm.linear_partials(x, pw, 2 if K >= 1024 else 1)
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-2
+    assert rel_err(parts.sum(0), ref) < 1e-4
 
 
 @pytest.mark.parametrize("splits", [2, 4, 8])
@@ -112,7 +146,7 @@ def _pool(nblk, nkv, bs, hd, seed=0):
     return kc, vc
 
 
-@pytest.mark.parametrize("bs", [16, 256])
+@pytest.mark.parametrize("bs", [16, 32, 64, 256])
 @pytest.mark.parametrize("hd,nh,nkv", [(128, 32, 8), (64, 4, 2), (128, 4, 1)])
 def test_decode_attention(bs, hd, nh, nkv):
     lens = [1, 5, 64, 65, 300, 513, 1200]
@@ -127,6 +161,46 @@ def test_decode_attention(bs, hd, nh, nkv):
     out = attention.decode_attention(q, kc, vc, perm, ctx, scale)
     ref = attention.decode_attention_ref(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), perm.cpu(), ctx.cpu(), scale)
     assert rel_err(out, ref.to(DEV)) < 1e-2
+
+
+@pytest.mark.parametrize("B,partition", [(3, 128), (40, 128), (80, 256), (80, 512)])
+def test_decode_attention_tma_poisoned_pool(B, partition):
+    """Persistent TMA decode kernel: pool slots past each context hold NaN (the kernel must mask
+    K and zero V there), many chunks per context, repeated launches (self-resetting counters)
+    and agreement with the cp.async split-KV kernel."""
+    hd, nh, nkv, bs = 128, 32, 8, 256
+    g = torch.Generator(device=DEV).manual_seed(B)
+    lens = torch.randint(1, 1500, (B,), generator=g, device=DEV).tolist()
+    maxblk = max(-(-L // bs) for L in lens)
+    nblk = B * maxblk + 2
+    kc = torch.full((nblk, nkv, bs, hd), float("nan"), device=DEV).bfloat16()
+    vc = torch.full_like(kc, float("nan"))
+    perm = torch.randperm(nblk, generator=g, device=DEV)[: B * maxblk].view(B, maxblk).int()
+    for b, L in enumerate(lens):
+        for j in range(-(-L // bs)):
+            n = min(bs, L - j * bs)
+            blk = int(perm[b, j])
+            kc[blk, :, :n] = torch.randn(nkv, n, hd, device=DEV, generator=g).bfloat16()
+            vc[blk, :, :n] = torch.randn(nkv, n, hd, device=DEV, generator=g).bfloat16()
+    ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    q = torch.randn(B, nh, hd, device=DEV, generator=g).bfloat16()
+    scale = 1 / math.sqrt(hd)
+    ws = attention.DecodeWorkspace(B, nh, hd, maxblk * bs, DEV)
+    ref = attention.decode_attention_ref(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), perm.cpu(), ctx.cpu(),
+                                         scale).to(DEV)
+    for _ in range(3):
+        out = torch.empty_like(q)
+        C().decode_attention_tma(out, q, kc, vc, perm, ctx, scale, ws.partial_out, ws.partial_ml, ws.counters,
+                                 ws.max_splits, partition, status(torch.device(DEV)))
+        torch.cuda.synchronize()
+        assert torch.isfinite(out.float()).all()
+        assert rel_err(out, ref) < 1e-2
+    assert int(ws.counters.abs().sum()) == 0
+    old = torch.empty_like(q)
+    C().decode_attention(old, q, kc, vc, perm, ctx, scale, ws.partial_out, ws.partial_ml, ws.counters,
+                         -(-ws.max_splits * 128 // 256), 256, 0)
+    torch.cuda.synchronize()
+    assert torch.isfinite(old.float()).all() and rel_err(out, old) < 5e-3
 
 
 @pytest.mark.parametrize("bs", [16, 256])
