@@ -1,0 +1,372 @@
+// W4A16 GEMM for AutoAWQ (4-bit, group 128, zero point) weights on the 5th-generation tensor
+// cores: Y[T, N] = X[T, K] . dequant(W)[N, K]^T,  dequant(w) = (q - z) * s per group of 128 K.
+//
+// Same swap-AB tiling as the bf16 kernel (128 output features = UMMA M, tokens = UMMA N), with a
+// dequantisation stage between the copy and the MMA:
+//   warp 0, lane 0 : producer.  Per 64-wide K step it bulk-copies the 4 KiB int4 tile of 128
+//                    features (load-time repacked so one feature's 64 codes are 8 consecutive
+//                    words), the 1 KiB scale/zero words of the tile's group, and the activation
+//                    tile (2-D tensor copy, 128B swizzle) into a deep ring (12 stages for decode).
+//   warps 2..5     : dequantisers.  Thread r owns feature r: each 32-bit word holds 8 codes placed
+//                    so that (word >> 4i) & 0x000F000F | 0x43004300 is the bf16 pair (128+q, 128+q')
+//                    (exponent 2^7, codes in the low mantissa bits, exact); (pair - (128+z)) * s in
+//                    bf16x2 gives round((q - z) * s).  The result is stored into a double-buffered
+//                    bf16 operand tile in the 128B-swizzled K-major layout the MMA reads.
+//   warp 1, lane 0 : MMA issuer, four tcgen05.mma (K = 16) per K step into a TMEM accumulator;
+//                    commits free the ring stage and the operand buffer.
+//   warps 2..5     : epilogue (tcgen05.ld), bf16 output or fp32 split-K partials.
+// Every wait is bounded (a timeout records an error code and the roles drain and return).
+// No TMA multicast is used.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace lsb {
+
+CUtensorMap activation_map(const at::Tensor& x, int box_rows);
+int* status_ptr(const at::Tensor& status);
+
+namespace {
+
+constexpr int QBM = 128;                 // features per CTA
+constexpr int QBK = 64;                  // K per step
+constexpr int kQTile = QBM * QBK / 2;    // 4 KiB of int4 codes
+constexpr int kSZTile = QBM * 8;         // 1 KiB: (s, s) and (128+z, 128+z) bf16 pairs per feature
+constexpr int kWTile = QBM * QBK * 2;    // 16 KiB bf16 operand
+
+template <int BN, int STAGES>
+struct QSmem {
+  static constexpr int kX = BN * QBK * 2;
+  static constexpr int kStage = kX + kQTile + kSZTile;      // X first (1024-aligned sizes)
+  static constexpr int kWOff = STAGES * kStage;             // two bf16 operand buffers
+  static constexpr int kBarOff = kWOff + 2 * kWTile;
+  static constexpr int kBytes = kBarOff + (2 * STAGES + 5) * 8 + 16 + 1024;
+};
+
+template <int BN>
+constexpr int qstages() {
+  constexpr int budget = 200 * 1024 - 2 * kWTile;
+  constexpr int st = budget / QSmem<BN, 1>::kStage;
+  return st > 12 ? 12 : st;
+}
+
+template <int BN>
+constexpr int qtmem_cols() {
+  return BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+}
+
+__device__ __forceinline__ uint64_t qdesc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+template <int N>
+__host__ __device__ constexpr uint32_t qidesc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(QBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_x(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void qmma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void qcommit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void qld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t bf2_sub_mul(uint32_t w, uint32_t z2, uint32_t s2) {
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&w);
+  const __nv_bfloat162 z = *reinterpret_cast<const __nv_bfloat162*>(&z2);
+  const __nv_bfloat162 s = *reinterpret_cast<const __nv_bfloat162*>(&s2);
+  a = __hmul2(__hsub2(a, z), s);
+  return *reinterpret_cast<uint32_t*>(&a);
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1) awq_gemm_kernel(const __grid_constant__ CUtensorMap tm_x,
+                                                          const uint32_t* __restrict__ qtiles,
+                                                          const uint2* __restrict__ sztiles, bf16* __restrict__ out,
+                                                          float* __restrict__ partials, int T, int N, int k_tiles,
+                                                          int k_tiles_per_split, int* __restrict__ status) {
+  using L = QSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* wfull = empty + STAGES;    // [2]
+  uint64_t* wempty = wfull + 2;        // [2]
+  uint64_t* accum = wempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  __shared__ int abort_flag;
+  volatile int* aborted = &abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (N + QBM - 1) / QBM, num_t = (T + BN - 1) / BN;
+  const int m_tile = blockIdx.x % num_m, t_tile = blockIdx.x / num_m;
+  (void)num_t;
+  const int n0 = m_tile * QBM, t0 = t_tile * BN;
+  const int kt_begin = blockIdx.z * k_tiles_per_split;
+  const int kt_end = min(k_tiles, kt_begin + k_tiles_per_split);
+  const int nk = max(0, kt_end - kt_begin);
+  const int groups = k_tiles / 2;   // group 128 = two K steps
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&wfull[b], 4);    // one arrive per dequant warp
+      mbar_init(&wempty[b], 1);
+    }
+    mbar_init(accum, 1);
+    fence_barrier_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_x) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(qtmem_cols<BN>()));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // weights and scales do not depend on the previous kernel: issue the first stages' copies
+      // of them before waiting on it (programmatic dependent launch), then the activations
+      const int pre = nk < STAGES ? nk : STAGES;
+      for (int i = 0; i < pre; ++i) {
+        const int kt = kt_begin + i;
+        uint8_t* st = smem + i * L::kStage;
+        mbar_expect_tx(&full[i], L::kStage);
+        bulk_g2s(smem_u32(st + L::kX), qtiles + ((size_t)m_tile * k_tiles + kt) * (kQTile / 4), kQTile, &full[i]);
+        bulk_g2s(smem_u32(st + L::kX + kQTile), sztiles + ((size_t)m_tile * groups + kt / 2) * QBM, kSZTile,
+                 &full[i]);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) tma_x(smem_u32(smem + i * L::kStage), &tm_x, &full[i], (kt_begin + i) * QBK, t0);
+      int last[STAGES];
+      for (int s = 0; s < STAGES; ++s) last[s] = s < pre ? s : -1;
+      for (int i = pre; i < nk; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&empty[s], ((i / STAGES) & 1) ^ 1) || *aborted) {
+          record_error(status, kTimeoutSmemEmpty);
+          *aborted = 1;
+          break;
+        }
+        const int kt = kt_begin + i;
+        uint8_t* st = smem + s * L::kStage;
+        mbar_expect_tx(&full[s], L::kStage);
+        tma_x(smem_u32(st), &tm_x, &full[s], kt * QBK, t0);
+        bulk_g2s(smem_u32(st + L::kX), qtiles + ((size_t)m_tile * k_tiles + kt) * (kQTile / 4), kQTile, &full[s]);
+        bulk_g2s(smem_u32(st + L::kX + kQTile), sztiles + ((size_t)m_tile * groups + kt / 2) * QBM, kSZTile,
+                 &full[s]);
+        last[s] = i;
+      }
+      // drain (bounded): every issued copy has landed before the CTA may leave
+      for (int s = 0; s < STAGES; ++s)
+        if (last[s] >= 0) mbar_wait(&full[s], (last[s] / STAGES) & 1);
+    } else {
+      pdl_wait();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0 && nk > 0) {
+      constexpr uint32_t idesc = qidesc<BN>();
+      bool ok = true;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % STAGES, b = i & 1;
+        // the operand buffer (dequantised by warps 2..5) and, directly, the activation tile
+        if (!mbar_wait(&wfull[b], (i >> 1) & 1) || !mbar_wait(&full[s], (i / STAGES) & 1) || *aborted) {
+          record_error(status, kTimeoutTmaFull);
+          *aborted = 1;
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t wa = smem_u32(smem + L::kWOff + b * kWTile);
+        const uint32_t xa = smem_u32(smem + s * L::kStage);
+#pragma unroll
+        for (int k = 0; k < QBK / 16; ++k) qmma(tmem, qdesc_sw128(wa + k * 32), qdesc_sw128(xa + k * 32), idesc, (i | k) != 0);
+        qcommit(&empty[s]);
+        qcommit(&wempty[b]);
+      }
+      if (ok) qcommit(accum);
+    }
+    __syncwarp();
+  } else {
+    // ---- dequantise: thread r (0..127) owns feature row r of the tile ----
+    pdl_wait();
+    const int r = threadIdx.x - 64;
+    bool ok = true;
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % STAGES, b = i & 1;
+      if (!mbar_wait(&full[s], (i / STAGES) & 1) || !mbar_wait(&wempty[b], ((i >> 1) & 1) ^ 1) || *aborted) {
+        record_error(status, kTimeoutTmaFull);
+        *aborted = 1;
+        ok = false;
+        break;
+      }
+      const uint8_t* st = smem + s * L::kStage;
+      const uint4* qrow = reinterpret_cast<const uint4*>(st + L::kX + r * 32);
+      const uint2 sz = reinterpret_cast<const uint2*>(st + L::kX + kQTile)[r];
+      const uint4 qa = qrow[0], qb = qrow[1];
+      const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      const uint32_t wbase = smem_u32(smem + L::kWOff + b * kWTile) + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t v = words[c];
+        uint32_t d[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d[j] = bf2_sub_mul(((v >> (4 * j)) & 0x000F000Fu) | 0x43004300u, sz.y, sz.x);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(wbase + (((c ^ (r & 7))) << 4)), "r"(d[0]),
+                     "r"(d[1]), "r"(d[2]), "r"(d[3])
+                     : "memory");
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&wfull[b])) : "memory");
+    }
+    (void)ok;
+
+    // ---- epilogue: warp w reads TMEM lanes 32*(w%4)..+31 ----
+    const int q = warp & 3;
+    bool have = nk > 0 && ok;
+    if (have && (!mbar_wait(accum, 0) || *aborted)) {
+      record_error(status, kTimeoutAccum);
+      have = false;
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const int feat = n0 + q * 32 + lane;
+    const uint32_t row_addr = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t rr[16];
+      if (have) {
+        qld16(row_addr + c0, rr);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) rr[j] = 0u;
+      }
+      if (feat < N) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int t = t0 + c0 + j;
+          if (t < T) {
+            const float v = __uint_as_float(rr[j]);
+            if (partials != nullptr)
+              partials[((size_t)blockIdx.z * T + t) * N + feat] = v;
+            else
+              out[(size_t)t * N + feat] = to_b(v);
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(qtmem_cols<BN>()));
+  }
+}
+
+template <int BN>
+void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out, float* partials,
+                int splits, int* status) {
+  constexpr int ST = qstages<BN>();
+  using L = QSmem<BN, ST>;
+  static_assert(L::kStage % 1024 == 0, "stage size must keep 1024-byte alignment");
+  const int T = x.size(0), K = x.size(1);
+  const int k_tiles = K / QBK;
+  const int kps = (k_tiles + splits - 1) / splits;
+  const CUtensorMap mx = activation_map(x, BN);
+  auto kern = awq_gemm_kernel<BN, ST>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    configured = true;
+  }
+  dim3 grid(((N + QBM - 1) / QBM) * ((T + BN - 1) / BN), 1, splits);
+  launch_pdl(kern, grid, dim3(192), L::kBytes, at::cuda::getCurrentCUDAStream(), mx,
+             (const uint32_t*)qt.data_ptr(), (const uint2*)sz.data_ptr(), out, partials, T, N, k_tiles, kps, status);
+}
+
+}  // namespace
+
+// x [T, K] bf16; qtiles int32 [ceil(N/128), K/64, 128, 8]; sztiles int32 [ceil(N/128), K/128, 128, 2];
+// out bf16 [T, N] (splits == 1) or partials fp32 [splits, T, N].
+void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, at::Tensor partials,
+              int64_t splits, at::Tensor status) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
+              "llmserve_b200: AWQ GEMM activations must be bf16 [T, K], K-contiguous");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "llmserve_b200: AWQ GEMM activations must be 16-byte aligned");
+  const int T = x.size(0), K = x.size(1), N = (int)n;
+  TORCH_CHECK(K % 128 == 0, "llmserve_b200: AWQ K must be a multiple of the group size 128");
+  const int64_t mt = (N + QBM - 1) / QBM;
+  TORCH_CHECK(qtiles.is_contiguous() && qtiles.scalar_type() == at::kInt && qtiles.numel() == mt * (K / QBK) * QBM * 8,
+              "llmserve_b200: AWQ qtiles shape mismatch");
+  TORCH_CHECK(sztiles.is_contiguous() && sztiles.scalar_type() == at::kInt &&
+                  sztiles.numel() == mt * (K / 128) * QBM * 2,
+              "llmserve_b200: AWQ scale/zero tiles shape mismatch");
+  TORCH_CHECK(splits >= 1 && splits <= 64, "llmserve_b200: splits out of range");
+  bf16* o = nullptr;
+  float* p = nullptr;
+  if (splits == 1 && partials.numel() == 0) {
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)T * N,
+                "llmserve_b200: bad AWQ out");
+    o = (bf16*)out.data_ptr();
+  } else {
+    TORCH_CHECK(partials.scalar_type() == at::kFloat && partials.is_contiguous() &&
+                    partials.numel() == splits * (int64_t)T * N,
+                "llmserve_b200: bad AWQ partials");
+    p = partials.data_ptr<float>();
+  }
+  if (T == 0 || N == 0) return;
+  const at::cuda::CUDAGuard g(x.device());
+  int* st = status_ptr(status);
+  if (T <= 16) awq_launch<16>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  else if (T <= 32) awq_launch<32>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  else if (T <= 64) awq_launch<64>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  else if (T <= 128) awq_launch<128>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  else awq_launch<256>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+}
+
+}  // namespace lsb

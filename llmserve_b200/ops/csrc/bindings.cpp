@@ -43,6 +43,8 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
                           at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml,
                           at::Tensor counters, int64_t max_splits, int64_t partition, at::Tensor status);
 bool decode_tma_supported(int64_t block_size, int64_t head_dim);
+void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, at::Tensor partials,
+              int64_t splits, at::Tensor status);
 }  // namespace lsb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -60,6 +62,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample_rows", &lsb::sample_rows);
   m.def("decode_attention_tma", &lsb::decode_attention_tma);
   m.def("gemm_bf16_packed", &lsb::gemm_bf16_packed);
+  m.def("awq_gemm", &lsb::awq_gemm);
   m.def("decode_tma_supported", &lsb::decode_tma_supported);
   m.def("decode_attention", &lsb::decode_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("context_lens"), py::arg("scale"), py::arg("part_o"), py::arg("part_ml"),

@@ -406,6 +406,11 @@ int* status_ptr(const at::Tensor& status);
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return encode_fn(); }
 
+// 128B-swizzled map over activations x [T, K] with (box_rows x 64) boxes.
+CUtensorMap activation_map(const at::Tensor& x, int box_rows) {
+  return make_map(x.data_ptr(), x.size(0), x.size(1), x.stride(0), box_rows);
+}
+
 
 // Token counts from which the persistent 2-SM kernel replaces the one-SM tile kernel.
 static int pair_min_tokens() {

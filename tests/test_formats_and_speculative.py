@@ -178,3 +178,16 @@ def test_pack_weight_layout_roundtrip():
         logical_chunk = p ^ (r & 7)
         expect = wp[m * 128 + r, kt * 64 + logical_chunk * 8: kt * 64 + logical_chunk * 8 + 8]
         assert torch.equal(pw.data[row, p * 8: p * 8 + 8], expect)
+
+
+def test_awq_repack_matches_autoawq_dequant():
+    """The load-time repack for the W4A16 kernel keeps every (q - z) * s of the AutoAWQ tensors."""
+    from llmserve_b200.ops import awq as awq_ops
+    from llmserve_b200.quantization.awq import dequantize_awq_gemm
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(200, 384, generator=g) * 0.05
+    qw, qz, sc = awq_quantize_dense(w)
+    ref = dequantize_awq_gemm(qw, qz, sc.bfloat16(), group_size=128)
+    packed = awq_ops.prepare_awq_weights(qw, qz, sc.bfloat16(), 128)
+    assert packed.qtiles.shape == (2, 6, 128, 8) and packed.sztiles.shape == (2, 3, 128, 2)
+    assert torch.equal(awq_ops.dequantize_packed(packed), ref.t().contiguous())
