@@ -42,6 +42,8 @@ def parse():
     p.add_argument("--output-len", type=int, default=256)
     p.add_argument("--layers", type=int, default=36)
     p.add_argument("--eager", action="store_true")
+    p.add_argument("--awq", action="store_true",
+                   help="AutoAWQ 4-bit g128 Qwen3-8B (random codes/zeros, |N(0,1)|*0.01 scales) on the W4A16 kernel")
     p.add_argument("--nccl-only", action="store_true", help="disable the fused NVLink collectives")
     return p.parse_args()
 
@@ -99,10 +101,13 @@ def visible_indices(n):
     return list(range(n))
 
 
-def model_dir(layers: int) -> str:
-    from llmserve_b200.models.synthetic import QWEN3_8B, write_config_only
-    path = os.path.join(tempfile.gettempdir(), f"llmserve_b200_qwen3_8b_L{layers}")
-    write_config_only(path, dict(QWEN3_8B, num_hidden_layers=layers))
+def model_dir(layers: int, awq: bool = False) -> str:
+    from llmserve_b200.models.synthetic import AWQ_QUANT_CONFIG, QWEN3_8B, write_config_only
+    cfg = dict(QWEN3_8B, num_hidden_layers=layers)
+    if awq:
+        cfg.update(torch_dtype="bfloat16", quantization_config=dict(AWQ_QUANT_CONFIG))
+    path = os.path.join(tempfile.gettempdir(), f"llmserve_b200_qwen3_8b_L{layers}{'_awq' if awq else ''}")
+    write_config_only(path, cfg)
     return path
 
 
@@ -130,7 +135,7 @@ def run_ours(args):
     if world > 1:
         kwargs.update(distributed_launcher="external", distributed_init_method="env://",
                       rpc_channel=f"llmserve_b200_bench_{os.environ.get('MASTER_PORT', '0')}")
-    path = model_dir(args.layers)
+    path = model_dir(args.layers, args.awq)
     if rank > 0:
         run_worker(path, rank, **kwargs)
         return
@@ -183,7 +188,7 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init Qwen3-8B weights N(0,0.02), prompt ids uniform over the vocab",
-        "config": {"model": "Qwen3-8B" if args.layers == 36 else f"Qwen3-8B-{args.layers}L",
+        "config": {"model": ("Qwen3-8B" if args.layers == 36 else f"Qwen3-8B-{args.layers}L") + ("-AWQ" if args.awq else ""),
                    "global_batch": args.concurrency, "seq_len": args.input_len + args.output_len,
                    "parallelism": f"tp{world}", "workload": f"closed-loop {args.input_len} in / {args.output_len} out, "
                    f"concurrency {args.concurrency}, greedy", "cuda_graphs": not args.eager,

@@ -51,8 +51,18 @@ class LinearBase(nn.Module):
 
     @property
     def gemm_weight(self):
-        """The operand handed to the GEMM: the packed tile image once ``pack_for_gemm`` ran."""
+        """The operand handed to the GEMM: the AWQ tiles of a quantised layer, the packed tile
+        image once ``pack_for_gemm`` ran, else the row-major weight."""
+        awq = getattr(self, "awq_packed", None)
+        if awq is not None:
+            return awq
         return self.packed_weight if self.packed_weight is not None else self.weight
+
+    @property
+    def fused_gemm_ok(self) -> bool:
+        """Whether the split-K partial paths (QKV reducer, fused add+RMSNorm) apply: a dense
+        weight, or AWQ weights repacked for the W4A16 kernel; no bias."""
+        return self.bias is None and (self.quant_method is None or getattr(self, "awq_packed", None) is not None)
 
     def pack_for_gemm(self):
         """After loading: re-store the dense CUDA weight as ``gemm.PackedWeight`` (tile-contiguous,
@@ -151,10 +161,10 @@ class QKVParallelLinear(ColumnParallelLinear):
     def forward_partials(self, x):
         """On CUDA with split K: the fp32 partials ``[S, T, W]`` (the QK-norm/RoPE kernel reduces
         them); otherwise the projection output."""
-        if x.is_cuda and self.quant_method is None and self.bias is None:
+        if x.is_cuda and self.fused_gemm_ok:
             x2 = x.reshape(-1, x.shape[-1])
             w = self.gemm_weight
-            splits = gemm.choose_splits(x2.shape[0], w.shape[0], x2.shape[1])
+            splits = gemm.splits_for(x2.shape[0], w)
             if splits > 1:
                 return gemm.linear_partials(x2.contiguous(), w, splits)
         return self.forward(x)
@@ -204,7 +214,7 @@ class RowParallelLinear(LinearBase):
 
     def forward_add_norm(self, x: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor, eps: float):
         """``(rmsnorm(allreduce(x @ W^T) + residual) * w, allreduce(..) + residual)``."""
-        if x.is_cuda and self.quant_method is None and self.bias is None:
+        if x.is_cuda and self.fused_gemm_ok:
             from llmserve_b200.parallel import fused as fused_ops
             return fused_ops.row_parallel_add_norm(x, self.gemm_weight, residual, norm_weight, eps,
                                                    tp.get_fused_comm())

@@ -37,6 +37,10 @@ class AWQPacked:
     n: int
     k: int
 
+    @property
+    def shape(self):
+        return (self.n, self.k)
+
 
 def _wrap_int32(v: torch.Tensor) -> torch.Tensor:
     return torch.where(v >= 2**31, v - 2**32, v).to(torch.int32)
@@ -71,13 +75,14 @@ def prepare_awq_weights(qweight: torch.Tensor, qzeros: torch.Tensor, scales: tor
 
 
 def choose_awq_splits(T: int, n: int, k: int) -> int:
-    """Split K so about one CTA per SM runs (one CTA fits per SM); at least 8 K steps per split."""
+    """Split K so the grid fills the two CTA slots of every SM about once; >= 8 K steps per split."""
     bn = 16 if T <= 16 else 32 if T <= 32 else 64 if T <= 64 else 128 if T <= 128 else 256
     tiles = (-(-n // TILE_N)) * (-(-T // bn))
     k_tiles = k // TILE_K
-    if tiles >= NUM_SMS:
+    slots = 2 * NUM_SMS
+    if tiles >= slots:
         return 1
-    return max(1, min(NUM_SMS // tiles, k_tiles // 8, 16))
+    return max(1, min(slots // tiles, k_tiles // 8, 16))
 
 
 def awq_linear(x: torch.Tensor, packed: AWQPacked) -> torch.Tensor:

@@ -6,21 +6,24 @@
 //   warp 0, lane 0 : producer.  Per 64-wide K step it bulk-copies the 4 KiB int4 tile of 128
 //                    features (load-time repacked so one feature's 64 codes are 8 consecutive
 //                    words), the 1 KiB scale/zero words of the tile's group, and the activation
-//                    tile (2-D tensor copy, 128B swizzle) into a deep ring (12 stages for decode).
-//   warps 2..5     : dequantisers.  Thread r owns feature r: each 32-bit word holds 8 codes placed
+//                    tile (2-D tensor copy, 128B swizzle) into a ring (6 stages for decode).
+//   warps 2..9     : dequantisers (two CTAs per SM).  Thread t owns half of feature t % 128: each
+//                    32-bit word holds 8 codes placed
 //                    so that (word >> 4i) & 0x000F000F | 0x43004300 is the bf16 pair (128+q, 128+q')
 //                    (exponent 2^7, codes in the low mantissa bits, exact); (pair - (128+z)) * s in
 //                    bf16x2 gives round((q - z) * s).  The result is stored into a double-buffered
 //                    bf16 operand tile in the 128B-swizzled K-major layout the MMA reads.
 //   warp 1, lane 0 : MMA issuer, four tcgen05.mma (K = 16) per K step into a TMEM accumulator;
 //                    commits free the ring stage and the operand buffer.
-//   warps 2..5     : epilogue (tcgen05.ld), bf16 output or fp32 split-K partials.
+//   warps 2..9     : epilogue (tcgen05.ld), bf16 output or fp32 split-K partials.
 // Every wait is bounded (a timeout records an error code and the roles drain and return).
 // No TMA multicast is used.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <cudaTypedefs.h>
+
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -37,21 +40,23 @@ constexpr int kQTile = QBM * QBK / 2;    // 4 KiB of int4 codes
 constexpr int kSZTile = QBM * 8;         // 1 KiB: (s, s) and (128+z, 128+z) bf16 pairs per feature
 constexpr int kWTile = QBM * QBK * 2;    // 16 KiB bf16 operand
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int WB>
 struct QSmem {
   static constexpr int kX = BN * QBK * 2;
   static constexpr int kStage = kX + kQTile + kSZTile;      // X first (1024-aligned sizes)
-  static constexpr int kWOff = STAGES * kStage;             // two bf16 operand buffers
-  static constexpr int kBarOff = kWOff + 2 * kWTile;
-  static constexpr int kBytes = kBarOff + (2 * STAGES + 5) * 8 + 16 + 1024;
+  static constexpr int kWOff = STAGES * kStage;             // WB bf16 operand buffers
+  static constexpr int kBarOff = kWOff + WB * kWTile;
+  static constexpr int kBytes = kBarOff + (2 * STAGES + 2 * WB + 1) * 8 + 16 + 1024;
 };
 
-template <int BN>
+// WB operand buffers; shared memory budget per CTA (two CTAs per SM when WB == 2).
+template <int BN, int WB>
 constexpr int qstages() {
-  constexpr int budget = 200 * 1024 - 2 * kWTile;
-  constexpr int st = budget / QSmem<BN, 1>::kStage;
-  return st > 12 ? 12 : st;
+  constexpr int budget = (WB == 2 ? 110 : 200) * 1024 - WB * kWTile;
+  constexpr int st = budget / QSmem<BN, 1, WB>::kStage;
+  return st > 8 ? 8 : st < 2 ? 2 : st;
 }
+constexpr int kQThreads = 320;   // producer warp, MMA warp, 8 dequant / epilogue warps
 
 template <int BN>
 constexpr int qtmem_cols() {
@@ -112,20 +117,20 @@ __device__ __forceinline__ uint32_t bf2_sub_mul(uint32_t w, uint32_t z2, uint32_
   return *reinterpret_cast<uint32_t*>(&a);
 }
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1) awq_gemm_kernel(const __grid_constant__ CUtensorMap tm_x,
+template <int BN, int STAGES, int WB>
+__global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                           const uint32_t* __restrict__ qtiles,
                                                           const uint2* __restrict__ sztiles, bf16* __restrict__ out,
                                                           float* __restrict__ partials, int T, int N, int k_tiles,
                                                           int k_tiles_per_split, int* __restrict__ status) {
-  using L = QSmem<BN, STAGES>;
+  using L = QSmem<BN, STAGES, WB>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* empty = full + STAGES;
-  uint64_t* wfull = empty + STAGES;    // [2]
-  uint64_t* wempty = wfull + 2;        // [2]
-  uint64_t* accum = wempty + 2;
+  uint64_t* wfull = empty + STAGES;    // [WB]
+  uint64_t* wempty = wfull + WB;       // [WB]
+  uint64_t* accum = wempty + WB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   __shared__ int abort_flag;
   volatile int* aborted = &abort_flag;
@@ -146,8 +151,8 @@ __global__ void __launch_bounds__(192, 1) awq_gemm_kernel(const __grid_constant_
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&wfull[b], 4);    // one arrive per dequant warp
+    for (int b = 0; b < WB; ++b) {
+      mbar_init(&wfull[b], 8);    // one arrive per dequant warp
       mbar_init(&wempty[b], 1);
     }
     mbar_init(accum, 1);
@@ -211,9 +216,9 @@ __global__ void __launch_bounds__(192, 1) awq_gemm_kernel(const __grid_constant_
       constexpr uint32_t idesc = qidesc<BN>();
       bool ok = true;
       for (int i = 0; i < nk; ++i) {
-        const int s = i % STAGES, b = i & 1;
-        // the operand buffer (dequantised by warps 2..5) and, directly, the activation tile
-        if (!mbar_wait(&wfull[b], (i >> 1) & 1) || !mbar_wait(&full[s], (i / STAGES) & 1) || *aborted) {
+        const int s = i % STAGES, b = i % WB;
+        // the operand buffer (dequantised by warps 2..9) and, directly, the activation tile
+        if (!mbar_wait(&wfull[b], (i / WB) & 1) || !mbar_wait(&full[s], (i / STAGES) & 1) || *aborted) {
           record_error(status, kTimeoutTmaFull);
           *aborted = 1;
           ok = false;
@@ -231,27 +236,32 @@ __global__ void __launch_bounds__(192, 1) awq_gemm_kernel(const __grid_constant_
     }
     __syncwarp();
   } else {
-    // ---- dequantise: thread r (0..127) owns feature row r of the tile ----
+    // ---- dequantise: thread t owns half h = t / 128 (words 4h..4h+3) of feature row r = t % 128 ----
     pdl_wait();
-    const int r = threadIdx.x - 64;
+    const int t = threadIdx.x - 64;
+    const int r = t & 127, h = t >> 7;
     bool ok = true;
     for (int i = 0; i < nk; ++i) {
-      const int s = i % STAGES, b = i & 1;
-      if (!mbar_wait(&full[s], (i / STAGES) & 1) || !mbar_wait(&wempty[b], ((i >> 1) & 1) ^ 1) || *aborted) {
+      const int s = i % STAGES, b = i % WB;
+      if (!mbar_wait(&full[s], (i / STAGES) & 1) || !mbar_wait(&wempty[b], ((i / WB) & 1) ^ 1) || *aborted) {
         record_error(status, kTimeoutTmaFull);
         *aborted = 1;
         ok = false;
         break;
       }
-      const uint8_t* st = smem + s * L::kStage;
-      const uint4* qrow = reinterpret_cast<const uint4*>(st + L::kX + r * 32);
-      const uint2 sz = reinterpret_cast<const uint2*>(st + L::kX + kQTile)[r];
-      const uint4 qa = qrow[0], qb = qrow[1];
-      const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+      // explicit shared-space loads (a generic load of shared memory takes the slower L1 path)
+      const uint32_t st = smem_u32(smem + s * L::kStage);
+      uint32_t words[4];
+      uint2 sz;
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(words[0]), "=r"(words[1]), "=r"(words[2]), "=r"(words[3])
+                   : "r"(st + L::kX + r * 32 + h * 16));
+      asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(sz.x), "=r"(sz.y) : "r"(st + L::kX + kQTile + r * 8));
       const uint32_t wbase = smem_u32(smem + L::kWOff + b * kWTile) + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t v = words[c];
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c = h * 4 + cc;
+        const uint32_t v = words[cc];
         uint32_t d[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) d[j] = bf2_sub_mul(((v >> (4 * j)) & 0x000F000Fu) | 0x43004300u, sz.y, sz.x);
@@ -263,37 +273,41 @@ __global__ void __launch_bounds__(192, 1) awq_gemm_kernel(const __grid_constant_
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&wfull[b])) : "memory");
     }
-    (void)ok;
 
-    // ---- epilogue: warp w reads TMEM lanes 32*(w%4)..+31 ----
+    // ---- epilogue: warp w reads TMEM lanes 32*(w%4)..+31; warps 2-5 and 6-9 split the columns ----
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int kCols = BN >= 32 ? BN / 2 : BN;
     bool have = nk > 0 && ok;
     if (have && (!mbar_wait(accum, 0) || *aborted)) {
       record_error(status, kTimeoutAccum);
       have = false;
     }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int feat = n0 + q * 32 + lane;
-    const uint32_t row_addr = tmem + ((uint32_t)(q * 32) << 16);
+    if (BN >= 32 || half == 0) {
+      const int feat = n0 + q * 32 + lane;
+      const uint32_t row_addr = tmem + ((uint32_t)(q * 32) << 16);
+      const int cbeg = BN >= 32 ? half * kCols : 0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      uint32_t rr[16];
-      if (have) {
-        qld16(row_addr + c0, rr);
-      } else {
+      for (int c0 = cbeg; c0 < cbeg + kCols; c0 += 16) {
+        uint32_t rr[16];
+        if (have) {
+          qld16(row_addr + c0, rr);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) rr[j] = 0u;
-      }
-      if (feat < N) {
+          for (int j = 0; j < 16; ++j) rr[j] = 0u;
+        }
+        if (feat < N) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = t0 + c0 + j;
-          if (t < T) {
-            const float v = __uint_as_float(rr[j]);
-            if (partials != nullptr)
-              partials[((size_t)blockIdx.z * T + t) * N + feat] = v;
-            else
-              out[(size_t)t * N + feat] = to_b(v);
+          for (int j = 0; j < 16; ++j) {
+            const int tok = t0 + c0 + j;
+            if (tok < T) {
+              const float v = __uint_as_float(rr[j]);
+              if (partials != nullptr)
+                partials[((size_t)blockIdx.z * T + tok) * N + feat] = v;
+              else
+                out[(size_t)tok * N + feat] = to_b(v);
+            }
           }
         }
       }
@@ -307,25 +321,42 @@ __global__ void __launch_bounds__(192, 1) awq_gemm_kernel(const __grid_constant_
   }
 }
 
-template <int BN>
+template <int BN, int WB>
 void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out, float* partials,
                 int splits, int* status) {
-  constexpr int ST = qstages<BN>();
-  using L = QSmem<BN, ST>;
+  constexpr int ST = qstages<BN, WB>();
+  using L = QSmem<BN, ST, WB>;
   static_assert(L::kStage % 1024 == 0, "stage size must keep 1024-byte alignment");
   const int T = x.size(0), K = x.size(1);
   const int k_tiles = K / QBK;
   const int kps = (k_tiles + splits - 1) / splits;
   const CUtensorMap mx = activation_map(x, BN);
-  auto kern = awq_gemm_kernel<BN, ST>;
+  auto kern = awq_gemm_kernel<BN, ST, WB>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     configured = true;
   }
   dim3 grid(((N + QBM - 1) / QBM) * ((T + BN - 1) / BN), 1, splits);
-  launch_pdl(kern, grid, dim3(192), L::kBytes, at::cuda::getCurrentCUDAStream(), mx,
+  launch_pdl(kern, grid, dim3(kQThreads), L::kBytes, at::cuda::getCurrentCUDAStream(), mx,
              (const uint32_t*)qt.data_ptr(), (const uint2*)sz.data_ptr(), out, partials, T, N, k_tiles, kps, status);
+}
+
+int awq_wbuf() {
+  static int v = [] {
+    const char* e = std::getenv("LLMSERVE_AWQ_WBUF");
+    return e ? std::atoi(e) : 2;
+  }();
+  return v;
+}
+
+template <int BN>
+void awq_launch_any(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out,
+                    float* partials, int splits, int* status) {
+  const int wb = awq_wbuf();
+  if (wb >= 8) awq_launch<BN, 8>(x, qt, sz, N, out, partials, splits, status);
+  else if (wb >= 4) awq_launch<BN, 4>(x, qt, sz, N, out, partials, splits, status);
+  else awq_launch<BN, 2>(x, qt, sz, N, out, partials, splits, status);
 }
 
 }  // namespace
@@ -362,11 +393,11 @@ void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztile
   if (T == 0 || N == 0) return;
   const at::cuda::CUDAGuard g(x.device());
   int* st = status_ptr(status);
-  if (T <= 16) awq_launch<16>(x, qtiles, sztiles, N, o, p, (int)splits, st);
-  else if (T <= 32) awq_launch<32>(x, qtiles, sztiles, N, o, p, (int)splits, st);
-  else if (T <= 64) awq_launch<64>(x, qtiles, sztiles, N, o, p, (int)splits, st);
-  else if (T <= 128) awq_launch<128>(x, qtiles, sztiles, N, o, p, (int)splits, st);
-  else awq_launch<256>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  if (T <= 16) awq_launch_any<16>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  else if (T <= 32) awq_launch_any<32>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  else if (T <= 64) awq_launch_any<64>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  else if (T <= 128) awq_launch_any<128>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  else awq_launch_any<256>(x, qtiles, sztiles, N, o, p, (int)splits, st);
 }
 
 }  // namespace lsb

@@ -103,8 +103,21 @@ def linear_ref(x: torch.Tensor, w, bias: torch.Tensor | None = None) -> torch.Te
     return F.linear(x, w, bias)
 
 
+def splits_for(T: int, w) -> int:
+    """K splits for a [T, K] x W^T product; W dense, tile-packed or AWQ-packed.  AWQ splits are
+    rounded down to a power of two (the fused QKV reducer takes 1, 2, 4 or 8 partials)."""
+    from llmserve_b200.ops import awq as awq_ops
+    if isinstance(w, awq_ops.AWQPacked):
+        s = min(awq_ops.choose_awq_splits(T, w.n, w.k), 8)
+        return 1 << (s.bit_length() - 1)
+    return choose_splits(T, w.shape[0], w.shape[1])
+
+
 def _gemm(out, x, w, partials, splits, T):
-    if isinstance(w, PackedWeight):
+    from llmserve_b200.ops import awq as awq_ops
+    if isinstance(w, awq_ops.AWQPacked):
+        C().awq_gemm(out, x, w.qtiles, w.sztiles, w.n, partials, splits, status(x.device))
+    elif isinstance(w, PackedWeight):
         C().gemm_bf16_packed(out, x, w.data, w.n, partials, splits, status(x.device), _stages(T))
     else:
         C().gemm_bf16(out, x, w, partials, splits, status(x.device), _stages(T))
@@ -129,7 +142,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -
     out = torch.empty(T, N, dtype=x.dtype, device=x.device)
     if T == 0:
         return out.view(*x.shape[:-1], N)
-    splits = choose_splits(T, N, K)
+    splits = splits_for(T, w)
     if splits == 1:
         _gemm(out, x2, w, _empty(x.device, torch.float32), 1, T)
     else:

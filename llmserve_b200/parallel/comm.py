@@ -95,7 +95,7 @@ class FusedComm:
         T, K = x.shape
         N = weight.shape[0]
         from llmserve_b200.parallel.fused import ROW_PARALLEL_MAX_SPLITS
-        splits = min(gemm.choose_splits(T, N, K), ROW_PARALLEL_MAX_SPLITS)
+        splits = min(gemm.splits_for(T, weight), ROW_PARALLEL_MAX_SPLITS)
         part = self.part_buf[: splits * T * N].view(splits, T, N)
         gemm.linear_partials(x, weight, splits, partials=part)
         C().fused_allreduce_add_rmsnorm(self.part_ptrs, self.out_ptrs, self.res_ptrs, self.flag_ptrs,

@@ -60,3 +60,20 @@ def test_awq_engine_matches_reference_backend(tmp_path):
         llm.exit()
         del llm
     assert outs[0] == outs[1]
+
+
+@pytest.mark.parametrize("splits", [2, 4, 8])
+def test_awq_partials_sum(splits):
+    """Split-K fp32 partials of the W4A16 kernel (consumed by the fused QKV / add+RMSNorm reducers)."""
+    from llmserve_b200.ops import gemm
+    g = torch.Generator().manual_seed(splits)
+    w = torch.randn(512, 2048, generator=g) * 0.05
+    qw, qz, sc = awq_quantize_dense(w)
+    sc = sc.bfloat16()
+    dense = dequantize_awq_gemm(qw, qz, sc, group_size=128).float()
+    packed = awq_ops.prepare_awq_weights(qw.to(DEV), qz.to(DEV), sc.to(DEV), 128)
+    x = torch.randn(48, 2048, generator=g).bfloat16()
+    parts = gemm.linear_partials(x.to(DEV), packed, splits)
+    torch.cuda.synchronize()
+    assert parts.shape == (splits, 48, 512)
+    assert rel_err(parts.sum(0).cpu(), x.float() @ dense) < 1e-3
