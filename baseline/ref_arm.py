@@ -109,6 +109,14 @@ def run(args, metric: str):
         raise RuntimeError("reference package did not resolve to baseline/_ref")
     import random
     world = args.gpus
+    # The reference spawns its own workers and rendezvouses over its tcp:// init method.  Under
+    # torchrun the launcher's variables (TORCHELASTIC_USE_AGENT_STORE in particular, which turns a
+    # tcp:// rendezvous into a client of a store nobody serves) would leak into it: drop them so
+    # the reference runs exactly as it does when started on its own.
+    for key in [k for k in os.environ if k.startswith(("TORCHELASTIC_", "TORCH_ELASTIC_"))] + [
+            "RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK", "ROLE_WORLD_SIZE",
+            "GROUP_WORLD_SIZE", "ROLE_NAME", "MASTER_ADDR", "MASTER_PORT"]:
+        os.environ.pop(key, None)
     llm = LLM(path, tensor_parallel_size=world, enforce_eager=args.eager,
               max_model_len=args.input_len + args.output_len + 16,
               max_num_batched_tokens=max(16384, args.concurrency * args.input_len), max_num_seqs=args.concurrency,

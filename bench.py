@@ -206,16 +206,25 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+REF_TP_UNAVAILABLE = (
+    "reference tensor parallelism fails in its stock code path: Sequence.__getstate__ does not ship seq_id "
+    "(llmserve/engine/sequence.py:91-93) but ModelRunner.prepare_prefill reads seq.seq_id on every rank "
+    "(llmserve/engine/model_runner.py:277-281), so worker ranks raise AttributeError on the first prefill "
+    "and rank 0 waits in an NCCL all-reduce until the 600 s watchdog")
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", 0))
     ref = os.path.join(ROOT, "baseline", "_ref")
-    if rank == 0:
-        why = None
-        if not os.path.isdir(os.path.join(ref, "llmserve")):
-            why = "reference build not installed under baseline/_ref"
-        if why:
+    why = None
+    if not os.path.isdir(os.path.join(ref, "llmserve")):
+        why = "reference build not installed under baseline/_ref"
+    elif args.gpus > 1:
+        why = REF_TP_UNAVAILABLE
+    if why:
+        if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
-            return
+        return
     sys.path.insert(0, os.path.join(ROOT, "baseline"))
     from ref_arm import run as ref_run  # noqa: E402
     ref_run(args, METRIC)

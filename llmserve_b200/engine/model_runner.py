@@ -15,6 +15,7 @@ sizing ``:186-229``, metadata ``:258-338``, graphs ``:383-418``).  Differences b
 * decode CUDA graphs also hold the LM head, so one replay yields the logit shard.
 """
 import os
+import time
 
 import numpy as np
 import torch
@@ -71,6 +72,7 @@ class ModelRunner:
         self.enforce_eager = config.enforce_eager
         self.world_size = config.tensor_parallel_size
         self.rank = rank
+        self.step_profile = {} if os.environ.get("LLMSERVE_STEP_PROFILE") == "1" else None
         self.is_cuda = config.device == "cuda"
         if self.is_cuda:
             self.device = torch.device("cuda", config.device_offset + rank)
@@ -148,6 +150,10 @@ class ModelRunner:
 
     # ---- control plane -----------------------------------------------------------------------
     def exit(self):
+        if self.step_profile:
+            import sys
+            print(f"[llmserve_b200 rank {self.rank}] step profile: "
+                  + ", ".join(f"{k}={v:.4f}" for k, v in sorted(self.step_profile.items())), file=sys.stderr)
         if self.channel is not None and self.rank == 0:
             try:
                 self.channel.wait_acks(self.config.comm_timeout_s)
@@ -178,19 +184,29 @@ class ModelRunner:
             gc.collect()
             torch.cuda.empty_cache()
 
+    def _prof(self, key: str, dt: float):
+        p = self.step_profile
+        p[key] = p.get(key, 0.0) + dt
+
     def loop(self):
         worker = self.rank - 1
         while True:
+            t0 = time.perf_counter()
             try:
                 method, args = self.channel.recv(worker, idle_timeout_s=5.0, parent_pid=self._parent_pid)
             except RpcTimeout:
                 break
+            if self.step_profile is not None and method == "run":
+                self._prof("worker_recv_wait_s", time.perf_counter() - t0)
             if method == "exit":
                 self.channel.ack(worker, True)
                 self.exit()
                 break
             try:
+                t1 = time.perf_counter()
                 getattr(self, method)(*args)
+                if self.step_profile is not None and method == "run":
+                    self._prof("run_s", time.perf_counter() - t1)
                 self.channel.ack(worker, True)
             except Exception as e:
                 self.channel.ack(worker, False, f"{type(e).__name__}: {e}")
@@ -200,7 +216,16 @@ class ModelRunner:
         if self.channel is not None and self.rank == 0:
             self.channel.check_workers()
             self.channel.send(method, *args)
+        if self.step_profile is not None and method == "run":
+            t1 = time.perf_counter()
+            out = getattr(self, method)(*args)
+            self._prof("run_s", time.perf_counter() - t1)
+            return out
         return getattr(self, method)(*args)
+
+    def get_step_profile(self) -> dict:
+        """Host-side phase totals recorded when ``LLMSERVE_STEP_PROFILE=1`` (diagnostics)."""
+        return dict(self.step_profile or {})
 
     # ---- memory ------------------------------------------------------------------------------
     def _kv_block_bytes(self) -> int:
@@ -420,14 +445,21 @@ class ModelRunner:
         if self.draft_model is not None and not warmup:
             self.spec.note_plain_step(decodes)
         if self._use_graph(decodes, is_prefill):
+            t_run = time.perf_counter()
             logits, vals, idx = self._decode_graph_step(decodes)
             if getattr(self.sampler, "is_greedy", False):
                 tokens = tp.vocab_parallel_argmax(vals, idx, self.model.lm_head.vocab_start)
             else:
                 tokens = self.sample_tokens(logits, self.prepare_sample(seqs))
             host = self.graph_tokens_host[:len(decodes)]
+            t_sync = time.perf_counter()
             host.copy_(tokens)
             token_list = host.tolist()
+            if self.step_profile is not None:
+                now = time.perf_counter()
+                self._prof("decode_launch_s", t_sync - t_run)
+                self._prof("decode_sync_wait_s", now - t_sync)
+                self._prof("decode_steps", 1)
             self.d2h_bytes += 8 * len(token_list)
             return token_list if self.rank == 0 else None
         input_ids, positions = self.prepare_prefill(seqs, decodes) if is_prefill else self.prepare_decode(decodes)

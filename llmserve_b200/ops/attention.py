@@ -116,7 +116,7 @@ def tma_partition(batch: int, kv_heads: int) -> int:
     if _TMA_PARTITION:
         return _TMA_PARTITION
     pairs = batch * kv_heads
-    return 128 if pairs < NUM_SMS else 256 if pairs < 2 * NUM_SMS else 512
+    return 128 if pairs < NUM_SMS // 2 else 256 if pairs < NUM_SMS else 512
 
 
 def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, workspace=None):
