@@ -45,6 +45,9 @@ def parse():
     p.add_argument("--awq", action="store_true",
                    help="AutoAWQ 4-bit g128 Qwen3-8B (random codes/zeros, |N(0,1)|*0.01 scales) on the W4A16 kernel")
     p.add_argument("--nccl-only", action="store_true", help="disable the fused NVLink collectives")
+    p.add_argument("--mem-util", type=float, default=0.85, help="gpu_memory_utilization (KV pool sizing)")
+    p.add_argument("--profile-range", action="store_true",
+                   help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     return p.parse_args()
 
 
@@ -130,7 +133,7 @@ def run_ours(args):
     kwargs = dict(load_format="dummy", tensor_parallel_size=world, enforce_eager=args.eager,
                   max_model_len=args.input_len + args.output_len + 16,
                   max_num_batched_tokens=max(16384, args.concurrency * args.input_len),
-                  max_num_seqs=args.concurrency, kvcache_block_size=256, gpu_memory_utilization=0.85,
+                  max_num_seqs=args.concurrency, kvcache_block_size=256, gpu_memory_utilization=args.mem_util,
                   fused_collectives=not args.nccl_only, comm_timeout_s=300.0)
     if world > 1:
         kwargs.update(distributed_launcher="external", distributed_init_method="env://",
@@ -165,6 +168,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     tok0 = tokens_so_far()
     h2d0, d2h0 = runner.h2d_bytes, runner.d2h_bytes
+    if args.profile_range:
+        torch.cuda.profiler.start()
     with ClockSampler(visible_indices(world)) as clocks:
         t0 = time.perf_counter()
         for _ in range(args.steps):
@@ -174,6 +179,8 @@ def run_ours(args):
         runner.call("mark_event", "bench_end")
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
+    if args.profile_range:
+        torch.cuda.profiler.stop()
     per_rank = runner.call("gather_elapsed", "bench_start", "bench_end")
     tokens = tokens_so_far() - tok0
     dev_ms = max(r[0] for r in per_rank)

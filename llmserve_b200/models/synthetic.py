@@ -174,3 +174,17 @@ def write_eagle3_checkpoint(path: str, target_config: dict, draft_vocab: int, se
         sd["embed_tokens.weight"] = rnd(V, H)
     save_file(sd, os.path.join(path, "model.safetensors"))
     return path
+
+
+def write_word_tokenizer(path: str, vocab_size: int, eos_token_id: int) -> str:
+    """A word-level HF fast tokenizer whose words are ``t0 .. t{vocab-1}`` (``t{i}`` -> id ``i``);
+    calibration and evaluation text for synthetic checkpoints is written in those words."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    os.makedirs(path, exist_ok=True)
+    tok = Tokenizer(models.WordLevel(vocab={f"t{i}": i for i in range(vocab_size)}, unk_token="t0"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    tok.save(os.path.join(path, "tokenizer.json"))
+    with open(os.path.join(path, "tokenizer_config.json"), "w") as f:
+        json.dump({"tokenizer_class": "PreTrainedTokenizerFast", "eos_token": f"t{eos_token_id}",
+                   "unk_token": "t0", "model_max_length": 1 << 20}, f)
+    return path

@@ -17,7 +17,7 @@
 //                    commits free the ring stage and the operand buffer.
 //   warps 2..9     : epilogue (tcgen05.ld), bf16 output or fp32 split-K partials.
 // Every wait is bounded (a timeout records an error code and the roles drain and return).
-// No TMA multicast is used.
+// Every CTA issues its own TMA loads.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>

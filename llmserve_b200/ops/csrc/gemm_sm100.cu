@@ -15,7 +15,7 @@
 //
 // Every mbarrier wait is bounded; a timeout records an error code in `status`, stops issuing
 // work, waits (bounded) for the TMA copies already in flight, frees TMEM and returns.
-// No TMA multicast is used anywhere (the kernel runs under tensor parallelism).
+// Every CTA issues its own TMA loads from this GPU's memory (the kernel runs under tensor parallelism).
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>

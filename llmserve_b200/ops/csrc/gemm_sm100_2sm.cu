@@ -20,10 +20,10 @@
 // reads TMEM lanes 32*(w%4)..+31, the restriction tcgen05.ld places on a warp).
 // Both CTAs' TMA loads complete on the even CTA's "full" barrier (the cta_group::2 form of the
 // bulk tensor copy addresses a barrier in the peer CTA); the MMA thread's commits arrive on the
-// "empty" and "accumulator full" barriers of both CTAs (one commit per CTA, no multicast).  Every
+// "empty" and "accumulator full" barriers of both CTAs (one plain commit per CTA).  Every
 // wait is bounded: a timeout records an error code, stops the role, and both CTAs still meet at
-// the final cluster barrier before TMEM is released.  No TMA multicast is used (the kernel runs
-// under tensor parallelism).
+// the final cluster barrier before TMEM is released.  Every CTA loads its own tiles from
+// this GPU's memory (the kernel runs under tensor parallelism).
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
