@@ -46,6 +46,8 @@ def parse():
                    help="AutoAWQ 4-bit g128 Qwen3-8B (random codes/zeros, |N(0,1)|*0.01 scales) on the W4A16 kernel")
     p.add_argument("--nccl-only", action="store_true", help="disable the fused NVLink collectives")
     p.add_argument("--mem-util", type=float, default=0.85, help="gpu_memory_utilization (KV pool sizing)")
+    p.add_argument("--no-overlap", action="store_true",
+                   help="synchronous decode loop (no launch of step N+1 before step N's tokens are read)")
     p.add_argument("--profile-range", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     return p.parse_args()
@@ -134,7 +136,7 @@ def run_ours(args):
                   max_model_len=args.input_len + args.output_len + 16,
                   max_num_batched_tokens=max(16384, args.concurrency * args.input_len),
                   max_num_seqs=args.concurrency, kvcache_block_size=256, gpu_memory_utilization=args.mem_util,
-                  fused_collectives=not args.nccl_only, comm_timeout_s=300.0)
+                  fused_collectives=not args.nccl_only, comm_timeout_s=300.0, overlap_decode=not args.no_overlap)
     if world > 1:
         kwargs.update(distributed_launcher="external", distributed_init_method="env://",
                       rpc_channel=f"llmserve_b200_bench_{os.environ.get('MASTER_PORT', '0')}")
@@ -200,6 +202,7 @@ def run_ours(args):
                    "parallelism": f"tp{world}", "workload": f"closed-loop {args.input_len} in / {args.output_len} out, "
                    f"concurrency {args.concurrency}, greedy", "cuda_graphs": not args.eager,
                    "collectives": "nccl" if args.nccl_only or world == 1 else "fused-nvlink",
+                   "overlapped_decode": not args.no_overlap,
                    "l2": "inputs larger than L2: every step streams all 16 GB of weights"},
         "e2e": {"value": round(tokens / wall, 2), "unit": "tok/s", "h2d_bytes_per_step": round(h2d),
                 "d2h_bytes_per_step": round(d2h)},

@@ -99,6 +99,7 @@ class Config:
     max_kvcache_blocks: int = -1
     distributed_launcher: str = "spawn"
     rpc_channel: str | None = None
+    overlap_decode: bool = True
 
     def __post_init__(self):
         if not os.path.isdir(self.model):

@@ -14,6 +14,7 @@ import os
 from dataclasses import fields
 from time import perf_counter
 
+import numpy as np
 import torch.multiprocessing as mp
 from tqdm.auto import tqdm
 
@@ -94,6 +95,8 @@ class LLMEngine:
         self.speculative_batch_calls = 0
         self.speculative_batch_sequences = 0
         self.speculative_max_batch_size = 0
+        self._inflight: list[Sequence] | None = None
+        self.overlapped_launches = 0
         self._exited = False
         atexit.register(self.exit)
 
@@ -102,6 +105,12 @@ class LLMEngine:
         if self._exited:
             return
         self._exited = True
+        try:
+            if self._inflight is not None:
+                self._inflight = None
+                self.model_runner.drain_decode()
+        except Exception:
+            pass
         try:
             self.model_runner.call("exit")
         finally:
@@ -167,6 +176,8 @@ class LLMEngine:
         }
 
     def step(self):
+        if self._inflight is not None:
+            return self._overlapped_step()
         step_start = perf_counter()
         out = self.scheduler.schedule()
         seqs = out.scheduled_seqs
@@ -183,6 +194,8 @@ class LLMEngine:
                     results = self.model_runner.call("run_speculative_batch", seqs)
                 return self._postprocess_speculative_step(seqs, results, step_start)
 
+        if self._can_overlap(out):
+            return self._start_overlap(out, step_start)
         before = {s.seq_id: s.num_completion_tokens for s in seqs}
         token_ids = self.model_runner.call("run", out)
         self.scheduler.postprocess(out, token_ids)
@@ -194,6 +207,97 @@ class LLMEngine:
                 self._record_emission(s, metric, s.num_completion_tokens - before[s.seq_id], step_end, events)
         self.last_step_events = events
         return [(s.seq_id, s.completion_token_ids) for s in seqs if s.is_finished], out.num_batched_tokens
+
+    # ---- overlapped decode ---------------------------------------------------------------------
+    # In a run of pure-decode steps with greedy sampling, step N+1 is launched before step N's
+    # tokens reach the host: its input ids are taken from step N's output on the device, its
+    # positions and block slots only depend on sequence lengths, and the host work of a step
+    # (reading tokens, postprocessing, metrics, scheduling, packing the next launch) runs while the
+    # GPU computes the next one.  A sequence that stops on EOS is computed one extra step and
+    # that token is dropped; its KV write lands in its own unsealed tail block.  Anything else --
+    # a waiting request, a full pool, a batch the graphs do not cover -- drains the pipeline and
+    # the scheduler takes over again.
+    def _can_overlap(self, out) -> bool:
+        r = self.model_runner
+        return (self.config.overlap_decode and not out.prefill_seqs and bool(out.decode_seqs)
+                and r.can_overlap()
+                and r.overlap_fits(len(out.decode_seqs), max(len(s.block_table) for s in out.decode_seqs) + 1))
+
+    def _start_overlap(self, out, step_start):
+        seqs = list(out.decode_seqs)
+        pos = np.fromiter((len(s) - 1 for s in seqs), dtype=np.int32, count=len(seqs))
+        ids = np.fromiter((s.last_token for s in seqs), dtype=np.int32, count=len(seqs))
+        self.model_runner.overlap_launch(seqs, pos, ids, -1, False)
+        self.overlapped_launches += 1
+        self._inflight = seqs
+        self.last_step_events = self._base_events(step_start, perf_counter(), seqs, [], len(seqs))
+        return [], len(seqs)
+
+    def _plan_next(self, prev: list[Sequence]):
+        """Sequences, positions and feed rows of the step after ``prev``; None to drain."""
+        sched = self.scheduler
+        if sched.waiting:
+            return None
+        live = [s for s in prev if not s.is_finished]
+        if len(live) != len(sched.running):
+            return None
+        bm, bsz = sched.block_manager, sched.block_manager.block_size
+        rows, seqs = [], []
+        need = 0
+        for i, s in enumerate(prev):
+            if s.is_finished or s.num_completion_tokens + 1 >= s.max_tokens:
+                continue          # done, or the in-flight token is its last
+            L = len(s)            # the in-flight token sits at position L
+            if L % bsz == 0 and len(s.block_table) <= L // bsz:
+                need += 1
+            rows.append(i)
+            seqs.append(s)
+        if not seqs or need > len(bm.free_block_ids):
+            return None
+        if not self.model_runner.overlap_fits(len(seqs), max(len(s.block_table) for s in seqs) + 1):
+            return None
+        for s in seqs:
+            L = len(s)
+            if L % bsz == 0:
+                bm._seal(s, L // bsz - 1)            # every token of that block is known now
+                if len(s.block_table) <= L // bsz:
+                    s.block_table.append(bm._take_next_free().block_id)
+        pos = np.fromiter((len(s) for s in seqs), dtype=np.int32, count=len(seqs))
+        return seqs, pos, np.asarray(rows, dtype=np.int32)
+
+    def _overlapped_step(self):
+        step_start = perf_counter()
+        prev = self._inflight
+        plan = self._plan_next(prev)
+        runner = self.model_runner
+        if plan is None:
+            self._inflight = None
+            tokens = runner.drain_decode()
+            launched = 0
+        else:
+            seqs, pos, feed = plan
+            runner.overlap_launch(seqs, pos, 0, feed, True)
+            self.overlapped_launches += 1
+            tokens = runner.collect_decode()
+            self._inflight = seqs
+            launched = len(seqs)
+        step_end = perf_counter()
+        events = self._base_events(step_start, step_end, prev, [], launched)
+        done = []
+        bm = self.scheduler.block_manager
+        for s, t in zip(prev, tokens):
+            if s.is_finished:
+                continue          # stopped on EOS one step earlier: this token is dropped
+            self.scheduler._postprocess_sequence(s, t, is_prefill=False)
+            if not s.is_finished and len(s) % bm.block_size == 0:
+                bm._seal(s, len(s) // bm.block_size - 1)   # as the synchronous may_append would
+            metric = self.request_metrics.get(s.seq_id)
+            if metric is not None:
+                self._record_emission(s, metric, 1, step_end, events)
+            if s.is_finished:
+                done.append((s.seq_id, s.completion_token_ids))
+        self.last_step_events = events
+        return done, launched
 
     def _postprocess_speculative_step(self, seqs, results, step_start):
         if len(seqs) != len(results):

@@ -118,6 +118,14 @@ class ModelRunner:
         self.graphs = {}
         self.graph_pool = None
         self.decode_workspace = None
+        # decode step staging: [ids | positions | slots | lengths | feed rows | block tables]
+        self.pack_max_bs = min(config.max_num_seqs, 512)
+        self.graph_W = -(-(config.max_model_len + config.speculative_gamma + 2) // self.block_size)
+        n = self.pack_max_bs * (5 + self.graph_W)
+        self.graph_pack_nps = [np.zeros(n, dtype=np.int32) for _ in range(2)]
+        self.graph_pack_hosts = [None, None]
+        self.graph_pack_turn = 0
+        self.inflight_bs = 0
         self.warmup_model()
         self.allocate_kv_cache()
         if self.is_cuda and not self.enforce_eager:
@@ -317,7 +325,9 @@ class ModelRunner:
             self.draft_v_cache = torch.zeros(dshape, dtype=self.dtype, device=self.device)
         self._bind_pools(self.k_cache, self.v_cache, self.draft_k_cache, self.draft_v_cache)
         if self.is_cuda:
-            max_ctx = cfg.max_model_len + cfg.speculative_gamma + 16
+            # the block tables the decode graphs pass cover whole blocks: size the split-KV
+            # workspace for that capacity so the graph never builds a fresh one
+            max_ctx = -(-(cfg.max_model_len + cfg.speculative_gamma + 16) // self.block_size) * self.block_size
             heads = max(hf.num_attention_heads // self.world_size,
                         self.draft_model.num_heads if self.draft_model is not None else 0)
             self.decode_workspace = attn_ops.DecodeWorkspace(
@@ -483,31 +493,37 @@ class ModelRunner:
     @torch.inference_mode()
     def capture_cudagraph(self):
         """Decode graphs per batch bucket.  All step inputs live in ONE packed int32 device buffer
-        (ids, positions, slots, context lengths, block tables) filled by one host-to-device copy
-        from a pinned staging buffer; the graph also holds the LM head and the greedy argmax."""
-        cfg = self.config
-        max_bs = min(cfg.max_num_seqs, 512)
-        W = -(-(cfg.max_model_len + cfg.speculative_gamma + 2) // self.block_size)
+        (ids, positions, slots, context lengths, feed rows, block tables) filled by one
+        host-to-device copy from a pinned staging buffer (two of them, used alternately, so the
+        host can fill one while the other's copy is still queued); the graph also holds the LM
+        head and the greedy argmax.  ``feed[i] >= 0`` makes row i take the token the previous
+        step sampled for row ``feed[i]`` straight from the device (overlapped decode)."""
+        max_bs, W = self.pack_max_bs, self.graph_W
         d = self.device
-        n = max_bs * (4 + W)                       # ids, pos, slots, lens, tables (int32 each)
+        n = max_bs * (5 + W)                       # ids, pos, slots, lens, feed, tables (int32 each)
         self.graph_pack = torch.zeros(n, dtype=torch.int32, device=d)
-        self.graph_pack_host = torch.zeros(n, dtype=torch.int32, pin_memory=True)
-        self.graph_pack_np = self.graph_pack_host.numpy()
+        self.graph_pack_hosts = [torch.zeros(n, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self.graph_pack_nps = [h.numpy() for h in self.graph_pack_hosts]
         self.graph_tokens_host = torch.zeros(max_bs, dtype=torch.int64, pin_memory=True)
         pk = self.graph_pack
         v = {
             "ids32": pk[0:max_bs], "pos32": pk[max_bs:2 * max_bs],
             "slot_mapping": pk[2 * max_bs:3 * max_bs], "context_lens": pk[3 * max_bs:4 * max_bs],
-            "block_tables": pk[4 * max_bs:].view(max_bs, W),
+            "feed32": pk[4 * max_bs:5 * max_bs],
+            "block_tables": pk[5 * max_bs:].view(max_bs, W),
             "logits": torch.zeros(max_bs, self.model.lm_head.shard_size, dtype=self.dtype, device=d),
             "tok_val": torch.zeros(max_bs, dtype=torch.float32, device=d),
             "tok_idx": torch.zeros(max_bs, dtype=torch.int64, device=d),
         }
-        self.graph_W = W
+        # the sampled global ids of the last decode step: the argmax itself at TP = 1, a copy of
+        # the vocab-parallel reduction at TP > 1
+        v["feed_src"] = v["tok_idx"] if self.world_size == 1 else torch.zeros(max_bs, dtype=torch.int64, device=d)
         self.graph_bs = [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
         self.graphs, self.graph_pool, self.graph_launches = {}, None, {}
         self.graph_vars = v
+        self._tokens_event = None
         v["context_lens"].fill_(1)
+        v["feed32"].fill_(-1)
         for bs in reversed(self.graph_bs):
             g = torch.cuda.CUDAGraph()
             self._graph_body(bs)                   # warm-up outside capture
@@ -525,26 +541,30 @@ class ModelRunner:
         v = self.graph_vars
         set_context(False, slot_mapping=v["slot_mapping"][:bs], context_lens=v["context_lens"][:bs],
                     block_tables=v["block_tables"][:bs], decode_workspace=self.decode_workspace)
-        ids = v["ids32"][:bs].long()
+        ids = sampling_ops.feed_ids(v["ids32"][:bs], v["feed32"][:bs], v["feed_src"])
         pos = v["pos32"][:bs].long()
         v["logits"][:bs] = self.model.compute_logits(self.model(ids, pos))
         sampling_ops.local_argmax_into(v["logits"][:bs], v["tok_val"][:bs], v["tok_idx"][:bs])
 
-    def _decode_graph_step(self, seqs: list[Sequence]):
-        """Pack the step inputs, one H2D copy, replay; returns the logits shard view and the
-        per-shard argmax (value, index) views of the graph outputs."""
+    def _next_pack(self):
+        """The pinned staging buffer to fill next (alternating)."""
+        self.graph_pack_turn ^= 1
+        return self.graph_pack_hosts[self.graph_pack_turn], self.graph_pack_nps[self.graph_pack_turn]
+
+    def fill_decode_pack(self, a: np.ndarray, seqs: list[Sequence], positions: np.ndarray, ids, feed) -> tuple[int, int]:
+        """Write one decode step into staging array ``a``: row i runs token ``ids[i]`` (or the
+        previous step's row ``feed[i]``) at ``positions[i]`` of ``seqs[i]``.  Returns (bs, graph bs)."""
         bs = len(seqs)
-        gbs = next(x for x in self.graph_bs if x >= bs)
-        max_bs, W = self.graph_vars["ids32"].shape[0], self.graph_W
-        a = self.graph_pack_np
-        bsz = self.block_size
-        lens = np.fromiter((len(s) for s in seqs), dtype=np.int32, count=bs)
-        a[0:bs] = [s.last_token for s in seqs]
-        a[max_bs:max_bs + bs] = lens - 1
-        last_blocks = np.fromiter((s.block_table[(len(s) - 1) // bsz] for s in seqs), dtype=np.int32, count=bs)
-        a[2 * max_bs:2 * max_bs + bs] = last_blocks * bsz + (lens - 1) % bsz
-        a[3 * max_bs:3 * max_bs + bs] = lens
-        tables = a[4 * max_bs:].reshape(max_bs, W)
+        gbs = next(x for x in self.graph_bs if x >= bs) if self.graphs else bs
+        max_bs, W, bsz = self.pack_max_bs, self.graph_W, self.block_size
+        a[0:bs] = ids
+        a[max_bs:max_bs + bs] = positions
+        blocks = np.fromiter((s.block_table[p // bsz] for s, p in zip(seqs, positions.tolist())), dtype=np.int32,
+                             count=bs)
+        a[2 * max_bs:2 * max_bs + bs] = blocks * bsz + positions % bsz
+        a[3 * max_bs:3 * max_bs + bs] = positions + 1
+        a[4 * max_bs:4 * max_bs + bs] = feed
+        tables = a[5 * max_bs:].reshape(max_bs, W)
         for i, s in enumerate(seqs):
             t = s.block_table
             tables[i, :len(t)] = t
@@ -553,13 +573,125 @@ class ModelRunner:
             a[max_bs + bs:max_bs + gbs] = 0
             a[2 * max_bs + bs:2 * max_bs + gbs] = -1
             a[3 * max_bs + bs:3 * max_bs + gbs] = 1
-        nbytes = (4 * max_bs + gbs * W) * 4
-        self.h2d_bytes += nbytes
-        self.graph_pack[: 4 * max_bs + gbs * W].copy_(self.graph_pack_host[: 4 * max_bs + gbs * W], non_blocking=True)
+            a[4 * max_bs + bs:4 * max_bs + gbs] = -1
+        return bs, gbs
+
+    def _replay(self, host: torch.Tensor, bs: int, gbs: int):
+        max_bs, W = self.pack_max_bs, self.graph_W
+        n = 5 * max_bs + gbs * W
+        self.h2d_bytes += n * 4
+        self.graph_pack[:n].copy_(host[:n], non_blocking=True)
+        self.graphs[gbs].replay()
+        LaunchCounter.launches += self.graph_launches[gbs]
+        v = self.graph_vars
+        if self.world_size > 1:
+            tokens = tp.vocab_parallel_argmax(v["tok_val"][:bs], v["tok_idx"][:bs], self.model.lm_head.vocab_start)
+            v["feed_src"][:bs].copy_(tokens)
+
+    def _decode_graph_step(self, seqs: list[Sequence]):
+        """Pack the step inputs, one H2D copy, replay; returns the logits shard view and the
+        per-shard argmax (value, index) views of the graph outputs."""
+        host, a = self._next_pack()
+        lens = np.fromiter((len(s) for s in seqs), dtype=np.int32, count=len(seqs))
+        ids = np.fromiter((s.last_token for s in seqs), dtype=np.int32, count=len(seqs))
+        bs, gbs = self.fill_decode_pack(a, seqs, lens - 1, ids, -1)
+        max_bs, W = self.pack_max_bs, self.graph_W
+        n = 5 * max_bs + gbs * W
+        self.h2d_bytes += n * 4
+        self.graph_pack[:n].copy_(host[:n], non_blocking=True)
         self.graphs[gbs].replay()
         LaunchCounter.launches += self.graph_launches[gbs]
         v = self.graph_vars
         return v["logits"][:bs], v["tok_val"][:bs], v["tok_idx"][:bs]
+
+    # ---- overlapped decode: step N+1 is launched before step N's tokens reach the host -----------
+    def can_overlap(self) -> bool:
+        """Greedy decode through CUDA graphs (or the CPU tier's eager emulation), no draft model."""
+        return (getattr(self.sampler, "is_greedy", False) and self.draft_model is None
+                and (bool(self.graphs) or not self.is_cuda))
+
+    def overlap_fits(self, bs: int, max_blocks: int) -> bool:
+        if not self.is_cuda:
+            return True
+        return bool(self.graphs) and bs <= self.graph_bs[-1] and max_blocks <= self.graph_W
+
+    def overlap_launch(self, seqs: list[Sequence], positions: np.ndarray, ids, feed, read_previous: bool) -> int:
+        """Rank 0: stage one overlapped decode step of ``seqs`` and launch it on every rank."""
+        host, a = self._next_pack()
+        bs, gbs = self.fill_decode_pack(a, seqs, positions, ids, feed)
+        if self.channel is not None:
+            n = 5 * self.pack_max_bs + gbs * self.graph_W
+            self.channel.check_workers()
+            self.channel.send("launch_decode", a[:n].copy(), bs, gbs, read_previous)
+        self.launch_decode(None, bs, gbs, read_previous)
+        return bs
+
+    @torch.inference_mode()
+    def launch_decode(self, pack: np.ndarray | None, bs: int, gbs: int, read_previous: bool):
+        """Run one overlapped decode step.  Rank 0 fills ``pack`` itself (``None`` is passed to it)
+        and sends its used prefix to the workers.  With ``read_previous`` rank 0 first queues the
+        device->host copy of the in-flight step's tokens (so it lands before this step overwrites
+        them); :meth:`collect_decode` waits for it."""
+        if not self.is_cuda:
+            if pack is not None:
+                _, a = self._next_pack()
+                a[:pack.shape[0]] = pack
+            return self._launch_decode_cpu(bs, read_previous)
+        if pack is None:
+            host = self.graph_pack_hosts[self.graph_pack_turn]
+        else:
+            host, a = self._next_pack()
+            a[:pack.shape[0]] = pack
+        v = self.graph_vars
+        if read_previous and self.rank == 0:
+            nb = self.inflight_bs
+            self.graph_tokens_host[:nb].copy_(v["feed_src"][:nb], non_blocking=True)
+            self.d2h_bytes += 8 * nb
+            self._tokens_event = torch.cuda.Event()
+            self._tokens_event.record()
+            self._tokens_bs = nb
+        self._replay(host, bs, gbs)
+        self.inflight_bs = bs
+
+    def collect_decode(self) -> list[int]:
+        """Rank 0: the previous in-flight step's tokens (queued by :meth:`launch_decode`)."""
+        if not self.is_cuda:
+            return self._cpu_collected
+        self._tokens_event.synchronize()
+        return self.graph_tokens_host[:self._tokens_bs].tolist()
+
+    @torch.inference_mode()
+    def drain_decode(self) -> list[int]:
+        """Rank 0: the current in-flight step's tokens; nothing is in flight afterwards."""
+        nb = self.inflight_bs
+        self.inflight_bs = 0
+        if not self.is_cuda:
+            return self._cpu_next.tolist()
+        host = self.graph_tokens_host[:nb]
+        host.copy_(self.graph_vars["feed_src"][:nb])
+        self.d2h_bytes += 8 * nb
+        return host.tolist()
+
+    def _launch_decode_cpu(self, bs, read_previous):
+        """CPU tier: the same protocol computed eagerly (the tokens stay in a tensor until read)."""
+        a = self.graph_pack_nps[self.graph_pack_turn]
+        max_bs, W = self.pack_max_bs, self.graph_W
+        ids, pos = a[0:bs].astype(np.int64), a[max_bs:max_bs + bs].astype(np.int64)
+        slots, lens, feed = a[2 * max_bs:2 * max_bs + bs], a[3 * max_bs:3 * max_bs + bs], a[4 * max_bs:4 * max_bs + bs]
+        tables = a[5 * max_bs:].reshape(max_bs, W)[:bs]
+        prev = getattr(self, "_cpu_next", None)
+        if read_previous:
+            self._cpu_collected = prev.tolist()
+        ids_t = torch.as_tensor(ids)
+        fed = torch.as_tensor(feed) >= 0
+        if bool(fed.any()):
+            ids_t[fed] = prev[torch.as_tensor(feed)[fed].long()]
+        set_context(False, slot_mapping=torch.as_tensor(slots), context_lens=torch.as_tensor(lens),
+                    block_tables=torch.as_tensor(np.ascontiguousarray(tables)), decode_workspace=None)
+        logits = self.model.compute_logits(self.model(ids_t, torch.as_tensor(pos)))
+        reset_context()
+        self._cpu_next = self.sample_tokens(logits, None).cpu()
+        self.inflight_bs = bs
 
     # ---- device timing (benchmarks): every rank records, rank 0 gathers -------------------------
     def mark_event(self, tag: str):

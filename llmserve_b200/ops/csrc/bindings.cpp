@@ -45,6 +45,13 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
 bool decode_tma_supported(int64_t block_size, int64_t head_dim);
 void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, at::Tensor partials,
               int64_t splits, at::Tensor status);
+void gemm_bf16_streamk(at::Tensor partials, at::Tensor x, at::Tensor w, int64_t n, int64_t grid, int64_t stages,
+                       at::Tensor status);
+int64_t streamk_slots(int64_t m_tiles, int64_t k_tiles, int64_t grid);
+void splitk_silu_halves(at::Tensor out, at::Tensor partials);
+void feed_ids(at::Tensor out, at::Tensor ids, at::Tensor feed, at::Tensor prev, at::Tensor status);
+void kv_push(at::Tensor src_k, at::Tensor src_v, at::Tensor dst_k, at::Tensor dst_v, at::Tensor src_ids,
+             at::Tensor dst_ids, at::Tensor status);
 }  // namespace lsb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -77,6 +84,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_allreduce_add_rmsnorm", &lsb::fused_allreduce_add_rmsnorm);
   m.def("gemm_bf16_silu", &lsb::gemm_bf16_silu);
   m.def("splitk_silu", &lsb::splitk_silu);
+  m.def("splitk_silu_halves", &lsb::splitk_silu_halves);
+  m.def("gemm_bf16_streamk", &lsb::gemm_bf16_streamk);
+  m.def("streamk_slots", &lsb::streamk_slots);
+  m.def("kv_push", &lsb::kv_push);
+  m.def("feed_ids", &lsb::feed_ids);
   m.def("gemm_bf16", &lsb::gemm_bf16, py::arg("out"), py::arg("x"), py::arg("w"), py::arg("partials"),
         py::arg("splits"), py::arg("status"), py::arg("max_stages") = 0);
 }

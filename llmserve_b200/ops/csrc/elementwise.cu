@@ -368,7 +368,9 @@ __global__ void __launch_bounds__(512) splitk_add_rmsnorm_kernel(bf16* __restric
   }
 }
 
-// split-K reduction of an interleaved gate/up projection + SiLU-mul -> bf16 [T, N/2]
+// split-K reduction of a gate/up projection + SiLU-mul -> bf16 [T, N/2].  INTERLEAVED: rows
+// interleaved per 64 (g0..g63, u0..u63, g64, ...); otherwise [gate (N/2) | up (N/2)].
+template <bool INTERLEAVED>
 __global__ void splitk_silu_kernel(bf16* __restrict__ out, const float* __restrict__ part, int S, int T, int N) {
   pdl_trigger();
   pdl_wait();
@@ -378,15 +380,35 @@ __global__ void splitk_silu_kernel(bf16* __restrict__ out, const float* __restri
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i / half;
     const int j = (int)(i % half);
-    const int64_t gidx = t * N + (j / 64) * 128 + (j % 64);
+    const int64_t gidx = INTERLEAVED ? t * N + (j / 64) * 128 + (j % 64) : t * N + j;
+    const int64_t uoff = INTERLEAVED ? 64 : half;
     float g = 0.f, u = 0.f;
     for (int s = 0; s < S; ++s) {
       g += __ldcg(part + s * TN + gidx);
-      u += __ldcg(part + s * TN + gidx + 64);
+      u += __ldcg(part + s * TN + gidx + uoff);
     }
     g = to_f(to_b(g));
     u = to_f(to_b(u));
     out[i] = to_b(g / (1.f + expf(-g)) * u);
+  }
+}
+
+// Decode-step input ids for the overlapped (one step ahead) decode loop: row i takes the token
+// the previous step sampled for its row feed[i] (still on the device), or the host-supplied id
+// when feed[i] < 0.  Replaces the int32 -> int64 widening of the ids at the head of the step.
+__global__ void feed_ids_kernel(int64_t* __restrict__ out, const int* __restrict__ ids,
+                                const int* __restrict__ feed, const int64_t* __restrict__ prev, int n, int n_prev,
+                                int* status) {
+  pdl_trigger();
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int f = feed[i];
+    int64_t v = ids[i];
+    if (f >= 0) {
+      if (f < n_prev) v = prev[f];
+      else if (status != nullptr) record_error(status, kBadIndex);
+    }
+    out[i] = v;
   }
 }
 
@@ -539,6 +561,19 @@ void silu_and_mul(at::Tensor out, at::Tensor x) {
   launch_pdl(silu_mul_kernel, grid_for(vec, 256), 256, 0, stream(), (bf16*)out.data_ptr(), (const bf16*)x.data_ptr(), I, vec);
 }
 
+void feed_ids(at::Tensor out, at::Tensor ids, at::Tensor feed, at::Tensor prev, at::Tensor status) {
+  LSB_CHECK(out.scalar_type() == at::kLong && ids.scalar_type() == at::kInt && feed.scalar_type() == at::kInt &&
+                prev.scalar_type() == at::kLong, "feed_ids: out int64, ids/feed int32, prev int64");
+  LSB_CHECK(out.is_contiguous() && ids.is_contiguous() && feed.is_contiguous() && prev.is_contiguous(),
+            "feed_ids: contiguous tensors");
+  const int n = out.numel();
+  LSB_CHECK(ids.numel() == n && feed.numel() == n, "feed_ids: length mismatch");
+  if (n == 0) return;
+  const at::cuda::CUDAGuard g(out.device());
+  launch_pdl(feed_ids_kernel, 1, 256, 0, stream(), out.data_ptr<int64_t>(), ids.data_ptr<int>(), feed.data_ptr<int>(),
+             prev.data_ptr<int64_t>(), n, (int)prev.numel(), status_ptr(status));
+}
+
 void embedding(at::Tensor out, at::Tensor ids, at::Tensor table, at::Tensor status) {
   check_bf16(table, "table");
   check_bf16(out, "out");
@@ -561,7 +596,7 @@ void qkv_rope(at::Tensor q_out, at::Tensor k_out, at::Tensor qkv, at::Tensor pos
   if (from_partials) {
     LSB_CHECK(qkv.dim() == 3 && qkv.is_contiguous(), "qkv partials must be contiguous [S, T, W]");
     S = qkv.size(0);
-    LSB_CHECK(S == 1 || S == 2 || S == 4 || S == 8, "qkv partial count must be 1, 2, 4 or 8");
+    LSB_CHECK(S >= 1 && S <= 8, "qkv partial count must be 1..8");
     LSB_CHECK(store, "partials input needs the paged-store variant");
     qkv = qkv.view({S * qkv.size(1), qkv.size(2)});
   } else {
@@ -605,7 +640,11 @@ void qkv_rope(at::Tensor q_out, at::Tensor k_out, at::Tensor qkv, at::Tensor pos
     case 0: LSB_ROPE(P, true, 0); break;    \
     case 1: LSB_ROPE(P, true, 1); break;    \
     case 2: LSB_ROPE(P, true, 2); break;    \
+    case 3: LSB_ROPE(P, true, 3); break;    \
     case 4: LSB_ROPE(P, true, 4); break;    \
+    case 5: LSB_ROPE(P, true, 5); break;    \
+    case 6: LSB_ROPE(P, true, 6); break;    \
+    case 7: LSB_ROPE(P, true, 7); break;    \
     default: LSB_ROPE(P, true, 8); break;   \
   }
   if (hd == 128) {
@@ -680,7 +719,11 @@ void splitk_reduce_add_rmsnorm(at::Tensor out, at::Tensor res_out, at::Tensor pa
   switch (S) {
     case 1: go(splitk_add_rmsnorm_kernel<1>); break;
     case 2: go(splitk_add_rmsnorm_kernel<2>); break;
+    case 3: go(splitk_add_rmsnorm_kernel<3>); break;
     case 4: go(splitk_add_rmsnorm_kernel<4>); break;
+    case 5: go(splitk_add_rmsnorm_kernel<5>); break;
+    case 6: go(splitk_add_rmsnorm_kernel<6>); break;
+    case 7: go(splitk_add_rmsnorm_kernel<7>); break;
     case 8: go(splitk_add_rmsnorm_kernel<8>); break;
     default: go(splitk_add_rmsnorm_kernel<0>); break;
   }
@@ -693,7 +736,19 @@ void splitk_silu(at::Tensor out, at::Tensor partials) {
   LSB_CHECK(N % 128 == 0 && out.numel() == (int64_t)T * (N / 2), "interleaved gate/up shape mismatch");
   if (T == 0) return;
   const at::cuda::CUDAGuard g(out.device());
-  launch_pdl(splitk_silu_kernel, grid_for((int64_t)T * N / 2, 256), 256, 0, stream(), (bf16*)out.data_ptr(),
+  launch_pdl(splitk_silu_kernel<true>, grid_for((int64_t)T * N / 2, 256), 256, 0, stream(), (bf16*)out.data_ptr(),
+             partials.data_ptr<float>(), S, T, N);
+}
+
+// Same for a [gate | up] projection (the layout the checkpoint loader writes).
+void splitk_silu_halves(at::Tensor out, at::Tensor partials) {
+  check_bf16(out, "out");
+  LSB_CHECK(partials.scalar_type() == at::kFloat && partials.is_contiguous() && partials.dim() == 3, "bad partials");
+  const int S = partials.size(0), T = partials.size(1), N = partials.size(2);
+  LSB_CHECK(N % 2 == 0 && out.numel() == (int64_t)T * (N / 2), "gate/up shape mismatch");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard g(out.device());
+  launch_pdl(splitk_silu_kernel<false>, grid_for((int64_t)T * N / 2, 256), 256, 0, stream(), (bf16*)out.data_ptr(),
              partials.data_ptr<float>(), S, T, N);
 }
 

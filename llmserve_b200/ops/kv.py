@@ -5,6 +5,8 @@
   store into the QK-norm/RoPE kernel; this standalone op serves tests and utilities.
 * ``commit_tree_kv``  -- copy the accepted EAGLE3 tree nodes' K/V of every layer into their
   paged slots in one launch (``llmserve/speculative/tree_kv.py:13-76``).
+* ``push_blocks``     -- copy whole paged blocks (every layer, K and V) from one pool into another,
+  on another GPU over NVLink by peer stores (prefill/decode disaggregation).
 * ``embedding``       -- row gather from a replicated embedding table.
 """
 import torch
@@ -51,3 +53,24 @@ def embedding(ids: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
     out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
     C().embedding(out, ids.contiguous(), table, status(table.device))
     return out
+
+
+def push_blocks(src_k, src_v, dst_k, dst_v, src_ids, dst_ids):
+    """Copy blocks ``src_ids`` of the pools ``src_k/src_v [L, Bs, kvh, bs, hd]`` into blocks
+    ``dst_ids`` of ``dst_k/dst_v [L, Bd, kvh, bs, hd]``.  On CUDA the copy is one kernel on the
+    source GPU's current stream whose stores go straight to the destination GPU (peer access is
+    enabled on first use); the caller orders the destination's readers after it (an event)."""
+    if len(src_ids) != len(dst_ids):
+        raise ValueError("source and destination block lists differ in length")
+    if not len(src_ids):
+        return
+    if not src_k.is_cuda:
+        si = torch.as_tensor(src_ids, dtype=torch.long)
+        di = torch.as_tensor(dst_ids, dtype=torch.long)
+        dst_k[:, di] = src_k[:, si].to(dst_k.device)
+        dst_v[:, di] = src_v[:, si].to(dst_v.device)
+        return
+    dev = src_k.device
+    si = torch.as_tensor(src_ids, dtype=torch.int32).to(dev, non_blocking=True)
+    di = torch.as_tensor(dst_ids, dtype=torch.int32).to(dev, non_blocking=True)
+    C().kv_push(src_k, src_v, dst_k, dst_v, si, di, status(dev))

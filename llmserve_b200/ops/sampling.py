@@ -12,7 +12,7 @@
 import numpy as np
 import torch
 
-from llmserve_b200.ops._ext import C
+from llmserve_b200.ops._ext import C, status
 
 
 def argmax(logits: torch.Tensor) -> torch.Tensor:
@@ -33,6 +33,19 @@ def local_argmax(logits: torch.Tensor):
     vals = torch.empty(logits.shape[0], dtype=torch.float32, device=logits.device)
     C().argmax_rows(out, vals, logits.contiguous())
     return vals, out
+
+
+def feed_ids(ids32: torch.Tensor, feed32: torch.Tensor, prev: torch.Tensor) -> torch.Tensor:
+    """int64 step ids: ``prev[feed[i]]`` where ``feed[i] >= 0`` (the previous step's token, still on
+    the device), else ``ids32[i]``."""
+    if not ids32.is_cuda:
+        out = ids32.long()
+        m = feed32 >= 0
+        out[m] = prev[feed32[m].long()]
+        return out
+    out = torch.empty(ids32.shape[0], dtype=torch.int64, device=ids32.device)
+    C().feed_ids(out, ids32, feed32, prev, status(ids32.device))
+    return out
 
 
 def local_argmax_into(logits: torch.Tensor, values: torch.Tensor, indices: torch.Tensor) -> None:

@@ -95,9 +95,10 @@ class FusedComm:
         T, K = x.shape
         N = weight.shape[0]
         from llmserve_b200.parallel.fused import ROW_PARALLEL_MAX_SPLITS
-        splits = min(gemm.splits_for(T, weight), ROW_PARALLEL_MAX_SPLITS)
+        # plain K splits: every partial plane crosses NVLink, so the fewer the better here
+        splits = min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS)
         part = self.part_buf[: splits * T * N].view(splits, T, N)
-        gemm.linear_partials(x, weight, splits, partials=part)
+        gemm.linear_partials(x, weight, splits, partials=part, streamk=False)
         C().fused_allreduce_add_rmsnorm(self.part_ptrs, self.out_ptrs, self.res_ptrs, self.flag_ptrs,
                                         residual.contiguous(), norm_weight, self.rank, splits, T, N, float(eps),
                                         status(x.device))

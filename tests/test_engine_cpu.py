@@ -141,3 +141,43 @@ def test_dummy_load_format_and_reset_metrics(tmp_path):
     llm.reset_metrics()
     assert llm.get_metrics()["summary"]["num_requests"] == 0
     llm.exit()
+
+
+def _run_overlap(path, prompts, overlap, eos=None, max_tokens=(20,), **kw):
+    llm = LLM(path, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256,
+              num_kvcache_blocks=kw.pop("num_kvcache_blocks", 64), overlap_decode=overlap, **kw)
+    llm.model_runner.sampler = GreedySampler()
+    if eos is not None:
+        llm.scheduler.eos = eos
+    ids = [llm.add_request(p, SamplingParams(temperature=0.5, max_tokens=max_tokens[i % len(max_tokens)],
+                                             ignore_eos=eos is None)) for i, p in enumerate(prompts)]
+    outs, steps, launched = {}, 0, 0
+    while not llm.is_finished():
+        done, n = llm.step()
+        steps += 1
+        outs.update(dict(done))
+    m = llm.get_metrics()["summary"]
+    llm.exit()
+    return [outs[i] for i in ids], m, llm.overlapped_launches
+
+
+def test_overlapped_decode_matches_synchronous(ckpts):
+    """The one-step-ahead decode loop (input ids fed from the device, host work overlapped) emits
+    exactly the synchronous loop's tokens: mixed max_tokens, block boundaries (block 16), EOS
+    stops found one step late, and a pool small enough that the pipeline has to drain."""
+    tgt, _ = ckpts
+    prompts = _prompts(6, seed=3)
+    base, mb, n0 = _run_overlap(tgt, prompts, False, max_tokens=(20, 7, 33))
+    over, mo, n1 = _run_overlap(tgt, prompts, True, max_tokens=(20, 7, 33))
+    assert n0 == 0 and n1 > 20
+    assert over == base
+    assert mo["total_output_tokens"] == mb["total_output_tokens"] and mo["num_finished"] == 6
+    # EOS: stop on a token that the synchronous run emits mid-sequence
+    eos = base[0][4]
+    b2, _, _ = _run_overlap(tgt, prompts, False, eos=eos, max_tokens=(30,))
+    o2, m2, _ = _run_overlap(tgt, prompts, True, eos=eos, max_tokens=(30,))
+    assert o2 == b2 and len(o2[0]) == 5 and o2[0][-1] == eos
+    # tight pool: preemption / drain path
+    b3, _, _ = _run_overlap(tgt, prompts, False, max_tokens=(40,), num_kvcache_blocks=14)
+    o3, _, n3 = _run_overlap(tgt, prompts, True, max_tokens=(40,), num_kvcache_blocks=14)
+    assert o3 == b3 and n3 > 0

@@ -280,7 +280,7 @@ def test_argmax_and_sampling():
     assert (got.cpu() == want).float().mean() >= 8 / 9
 
 
-@pytest.mark.parametrize("S", [2, 4, 8])
+@pytest.mark.parametrize("S", [2, 3, 4, 5, 6, 7, 8])
 def test_qkv_rope_from_splitk_partials(S):
     T, nh, nkv, hd, bs, nblk = 9, 8, 2, 128, 256, 2
     W = (nh + 2 * nkv) * hd
@@ -314,3 +314,30 @@ def test_gate_up_silu_fused_epilogue(T, I, K):
     o3 = torch.empty(T, I, device=DEV, dtype=torch.bfloat16)
     C().splitk_silu(o3, parts)
     assert rel_err(o3, ref) < 1e-2
+
+
+def test_kv_push_blocks_same_gpu_and_bad_ids():
+    L, nkv, bs, hd = 3, 2, 16, 64
+    src_k = torch.randn(L, 10, nkv, bs, hd, device=DEV).bfloat16()
+    src_v = torch.randn_like(src_k)
+    dst_k = torch.zeros(L, 7, nkv, bs, hd, device=DEV, dtype=torch.bfloat16)
+    dst_v = torch.zeros_like(dst_k)
+    kv.push_blocks(src_k, src_v, dst_k, dst_v, [4, 0, 9], [6, 2, 3])
+    torch.cuda.synchronize()
+    for s, d in ((4, 6), (0, 2), (9, 3)):
+        assert torch.equal(dst_k[:, d], src_k[:, s]) and torch.equal(dst_v[:, d], src_v[:, s])
+    assert not dst_k[:, [0, 1, 4, 5]].any()
+    kv.push_blocks(src_k, src_v, dst_k, dst_v, [1], [7])        # destination id out of range: skipped
+    with pytest.raises(RuntimeError, match="out-of-range"):
+        check_status(torch.device(DEV))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_kv_push_blocks_to_peer_gpu():
+    src_k = torch.randn(2, 6, 8, 256, 128, device="cuda:0").bfloat16()
+    src_v = torch.randn_like(src_k)
+    dst_k = torch.zeros(2, 5, 8, 256, 128, device="cuda:1", dtype=torch.bfloat16)
+    dst_v = torch.zeros_like(dst_k)
+    kv.push_blocks(src_k, src_v, dst_k, dst_v, [5, 2], [0, 4])
+    torch.cuda.synchronize(0)
+    assert torch.equal(dst_k[:, 0].cpu(), src_k[:, 5].cpu()) and torch.equal(dst_v[:, 4].cpu(), src_v[:, 2].cpu())
