@@ -134,7 +134,7 @@ class ModelRunner:
         if self.world_size > 1:
             name = channel_name or "llmserve_b200"
             if rank == 0:
-                self.channel = RpcChannel(name, self.world_size - 1, create=True)
+                self.channel = RpcChannel(name, self.world_size - 1, create=True, ack_timeout_s=config.comm_timeout_s)
                 tp.barrier()
             else:
                 tp.barrier()

@@ -8,7 +8,8 @@ handling the reference lacks:
   still alive and exits if it is gone (no orphaned GPU processes);
 * workers acknowledge each call and report exceptions through their status slot, so rank 0 can
   raise a clear error instead of blocking;
-* the wait is a spin-then-sleep poll on a sequence counter (tens of microseconds per call).
+* the wait is a spin-then-sleep poll on a sequence counter (tens of microseconds per call);
+* a call is published only after every worker acknowledged the previous one (one payload slot).
 
 Layout of the segment: ``[0:8)`` call sequence number, ``[8:16)`` payload length,
 ``[64 + 16*w, +16)`` worker ``w``'s (acknowledged sequence, status), error text of worker ``w``
@@ -30,8 +31,9 @@ class RpcTimeout(RuntimeError):
 
 class RpcChannel:
 
-    def __init__(self, name: str, num_workers: int, create: bool, size: int = 1 << 22):
+    def __init__(self, name: str, num_workers: int, create: bool, size: int = 1 << 22, ack_timeout_s: float = 120.0):
         self.name = name
+        self.ack_timeout_s = ack_timeout_s
         self.num_workers = num_workers
         if create:
             try:
@@ -49,6 +51,13 @@ class RpcChannel:
 
     # ---- rank 0 ------------------------------------------------------------------------------
     def send(self, method: str, *args):
+        """Publish one call.  The payload area is single-slot, so the previous call must have been
+        taken by every worker first: without this wait a worker that is still busy (or asleep in
+        its poll back-off) when two calls are sent in a row would skip the earlier one, and the
+        ranks' collective sequences would diverge.  Rank 0 runs its own part of every call it
+        sends before sending the next, so the wait cannot deadlock."""
+        if self.seq:
+            self.wait_acks(self.ack_timeout_s)
         data = pickle.dumps((method, args), protocol=pickle.HIGHEST_PROTOCOL)
         if HEADER + len(data) > self.shm.size:
             raise ValueError(f"RPC payload of {len(data)} bytes exceeds the channel size")
@@ -83,7 +92,9 @@ class RpcChannel:
 
     # ---- workers -----------------------------------------------------------------------------
     def recv(self, worker: int, idle_timeout_s: float, parent_pid: int):
-        spin_until = time.monotonic() + 0.002
+        # busy-poll while calls are likely to follow (a decode step is a few milliseconds), then
+        # back off to short sleeps
+        spin_until = time.monotonic() + 0.05
         sleep_s = 0.00002
         last_check = time.monotonic()
         while True:
@@ -96,7 +107,7 @@ class RpcChannel:
             now = time.monotonic()
             if now > spin_until:
                 time.sleep(sleep_s)
-                sleep_s = min(sleep_s * 2, 0.001)
+                sleep_s = min(sleep_s * 2, 0.0002)
             if now - last_check > idle_timeout_s:
                 last_check = now
                 if not _alive(parent_pid):

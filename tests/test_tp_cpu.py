@@ -103,6 +103,35 @@ def test_orphaned_worker_exits_on_its_own():
     assert waited < 5 and p.exitcode == 0
 
 
+def _counting_worker(name, n, q):
+    ch = RpcChannel(name, 1, create=False)
+    seen = []
+    for _ in range(n):
+        method, args = ch.recv(0, idle_timeout_s=5.0, parent_pid=os.getppid())
+        seen.append(args[0])
+        if args[0] % 7 == 0:
+            time.sleep(0.003)        # a slow call: the next send must wait for it
+        ch.ack(0, True)
+    q.put(seen)
+    ch.close()
+
+
+def test_back_to_back_calls_are_never_skipped():
+    """Calls that rank 0 publishes without waiting in between (the overlapped decode launches, the
+    sampler mirror) all reach the worker, in order."""
+    name = f"lsb_test_{os.getpid()}_d"
+    ch = RpcChannel(name, 1, create=True, ack_timeout_s=30)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_counting_worker, args=(name, 60, q))
+    p.start()
+    for i in range(60):
+        ch.send("call", i)
+    assert q.get(timeout=60) == list(range(60))
+    p.join(10)
+    ch.close()
+
+
 def test_ack_wait_is_bounded():
     ch = RpcChannel(f"lsb_test_{os.getpid()}_c", 1, create=True)
     ch.send("noop")

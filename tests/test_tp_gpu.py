@@ -59,6 +59,7 @@ def _fused_worker(rank, world, port, q):
 
 
 @needs2
+@pytest.mark.timeout(600)
 @pytest.mark.parametrize("world", [w for w in (2, 4, 8) if w <= NGPU])
 def test_fused_allreduce_add_rmsnorm_matches_nccl(world):
     ctx = mp.get_context("spawn")
@@ -76,6 +77,7 @@ def test_fused_allreduce_add_rmsnorm_matches_nccl(world):
 
 
 @needs2
+@pytest.mark.timeout(600)
 def test_engine_tp2_matches_tp1_first_logits(tmp_path):
     from llmserve_b200 import LLM, SamplingParams
     from llmserve_b200.engine.model_runner import GreedySampler
@@ -97,3 +99,31 @@ def test_engine_tp2_matches_tp1_first_logits(tmp_path):
     # random weights: the first tokens agree; later ones may flip on near-ties after bf16 reassociation
     assert [o[0] for o in outs[1]] == [o[0] for o in outs[2]]
     assert all(len(o) == 6 for o in outs[2])
+
+
+@needs2
+@pytest.mark.timeout(600)
+def test_engine_tp2_graphs_overlapped_decode_matches_synchronous(tmp_path):
+    """TP=2 with CUDA graphs and the fused NVLink collective: the overlapped decode loop (ids fed
+    from the device, vocab-parallel argmax copied into the feed buffer) emits the synchronous
+    loop's tokens exactly (same kernels, same batch shapes)."""
+    from llmserve_b200 import LLM, SamplingParams
+    from llmserve_b200.engine.model_runner import GreedySampler
+    from llmserve_b200.models.synthetic import TINY, write_qwen3_checkpoint
+    cfg = dict(TINY, torch_dtype="bfloat16", hidden_size=512, num_attention_heads=8, num_key_value_heads=4,
+               intermediate_size=1024, head_dim=64, num_hidden_layers=4)
+    path = write_qwen3_checkpoint(str(tmp_path / "m"), cfg)
+    prompts = [[5, 6, 7, 8, 9, 10, 11], [100, 200, 300], list(range(40, 90))]
+    outs = {}
+    for overlap in (False, True):
+        llm = LLM(path, tensor_parallel_size=2, enforce_eager=False, max_model_len=256, kvcache_block_size=16,
+                  max_num_batched_tokens=512, max_num_seqs=8, gpu_memory_utilization=0.3, overlap_decode=overlap,
+                  distributed_init_method=f"tcp://127.0.0.1:{_port()}")
+        llm.model_runner.sampler = GreedySampler()
+        sps = [SamplingParams(max_tokens=n, ignore_eos=True) for n in (40, 17, 29)]
+        outs[overlap] = [o["token_ids"] for o in llm.generate(prompts, sps, use_tqdm=False)]
+        launched = llm.overlapped_launches
+        llm.exit()
+        del llm
+        assert (launched > 10) == overlap
+    assert outs[True] == outs[False]
