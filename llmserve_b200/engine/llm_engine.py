@@ -70,6 +70,12 @@ def _diffs(times):
 
 class LLMEngine:
 
+    def __new__(cls, model=None, **kwargs):
+        if kwargs.get("pd_disaggregation"):
+            from llmserve_b200.engine.pd_engine import PDEngine
+            return PDEngine(model, **kwargs)
+        return super().__new__(cls)
+
     def __init__(self, model, **kwargs):
         names = {f.name for f in fields(Config)}
         config = Config(model, **{k: v for k, v in kwargs.items() if k in names})

@@ -181,3 +181,25 @@ def test_overlapped_decode_matches_synchronous(ckpts):
     b3, _, _ = _run_overlap(tgt, prompts, False, max_tokens=(40,), num_kvcache_blocks=14)
     o3, _, n3 = _run_overlap(tgt, prompts, True, max_tokens=(40,), num_kvcache_blocks=14)
     assert o3 == b3 and n3 > 0
+
+
+def test_pd_disaggregation_matches_single_engine(ckpts):
+    """Prefill on one engine, decode on another (both on the CPU tier here), KV blocks pushed
+    between their pools: the tokens equal a single engine's; prefix hits in the decode pool are
+    reused instead of copied; a small decode pool makes requests wait (parked) without loss."""
+    tgt, _ = ckpts
+    prompts = _prompts(6, seed=5)
+    prompts.append(list(prompts[0]))          # identical prompt: decode-side prefix hit
+    base, _ = _run(tgt, prompts, max_tokens=24)
+    for blocks in (64, 14):
+        llm = LLM(tgt, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256,
+                  num_kvcache_blocks=blocks, pd_disaggregation=True, pd_prefill_devices=(0,), pd_decode_devices=(0,))
+        llm.model_runner.sampler = GreedySampler()
+        assert llm.prefill.model_runner.sampler.is_greedy
+        out = llm.generate(prompts, SamplingParams(temperature=0.5, max_tokens=24, ignore_eos=True))
+        m = llm.get_metrics()["summary"]
+        llm.exit()
+        assert [o["token_ids"] for o in out] == base
+        assert m["pd"]["handoffs"] == 7 and m["pd"]["blocks_pushed"] > 0 and m["num_finished"] == 7
+        if blocks == 64:
+            assert m["pd"]["blocks_reused"] >= 1
