@@ -69,7 +69,7 @@ class LinearBase(nn.Module):
         pre-swizzled) and release the row-major copy.  The tile image is kept as a buffer so
         memory accounting still sees it."""
         if (os.environ.get("LLMSERVE_PACK_WEIGHTS", "1") == "0" or self.quant_method is not None
-                or not self.weight.is_cuda or getattr(self, "interleaved", False) or self.packed_weight is not None):
+                or not self.weight.is_cuda or self.packed_weight is not None):
             return
         pw = gemm.pack_weight(self.weight.data)
         self.register_buffer("weight_tiles", pw.data, persistent=False)
@@ -135,7 +135,7 @@ class MergedColumnParallelLinear(ColumnParallelLinear):
 
     def forward_silu(self, x):
         if self.interleaved:
-            return gemm.linear_silu(x, self.weight)
+            return gemm.linear_silu(x, self.gemm_weight)
         if x.is_cuda and self.quant_method is None and self.bias is None:
             y = gemm.gate_up_silu(x, self.gemm_weight)
             if y is not None:

@@ -37,6 +37,9 @@ void fused_allreduce_add_rmsnorm(std::vector<int64_t> part, std::vector<int64_t>
                                  int64_t T, int64_t N, double eps, at::Tensor status);
 void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages);
 void splitk_silu(at::Tensor out, at::Tensor partials);
+void silu_and_mul_interleaved(at::Tensor out, at::Tensor x);
+void gemm_bf16_silu_packed(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, at::Tensor status,
+                           int64_t max_stages);
 void gemm_bf16_packed(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, at::Tensor partials, int64_t splits,
                       at::Tensor status, int64_t max_stages);
 void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
@@ -84,6 +87,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_allreduce_add_rmsnorm", &lsb::fused_allreduce_add_rmsnorm);
   m.def("gemm_bf16_silu", &lsb::gemm_bf16_silu);
   m.def("splitk_silu", &lsb::splitk_silu);
+  m.def("silu_and_mul_interleaved", &lsb::silu_and_mul_interleaved);
+  m.def("gemm_bf16_silu_packed", &lsb::gemm_bf16_silu_packed);
   m.def("splitk_silu_halves", &lsb::splitk_silu_halves);
   m.def("gemm_bf16_streamk", &lsb::gemm_bf16_streamk);
   m.def("streamk_slots", &lsb::streamk_slots);

@@ -8,6 +8,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <cooperative_groups.h>
 #include <cstdlib>
 #include <tuple>
 
@@ -81,6 +82,9 @@ int norm_threads(int H) {
 // ------------------------------------------------------------------------------------------
 // SiLU-mul: out[t, i] = bf16(silu(x[t, i]) * x[t, I + i])
 // ------------------------------------------------------------------------------------------
+// INTERLEAVED: the input row holds gate/up in alternating 64-column chunks (g0..g63, u0..u63, ...)
+// instead of [gate (I) | up (I)].
+template <bool INTERLEAVED>
 __global__ void silu_mul_kernel(bf16* __restrict__ out, const bf16* __restrict__ x, int I, int64_t total_vec) {
   pdl_trigger();
   pdl_wait();
@@ -89,8 +93,10 @@ __global__ void silu_mul_kernel(bf16* __restrict__ out, const bf16* __restrict__
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total_vec; v += stride) {
     const int64_t row = v / vec_per_row;
     const int col = (int)(v % vec_per_row) * 8;
-    Vec8 g = *reinterpret_cast<const Vec8*>(x + row * 2 * I + col);
-    Vec8 u = *reinterpret_cast<const Vec8*>(x + row * 2 * I + I + col);
+    const int64_t gcol = INTERLEAVED ? (col / 64) * 128 + col % 64 : col;
+    const int64_t ucol = INTERLEAVED ? gcol + 64 : I + col;
+    Vec8 g = *reinterpret_cast<const Vec8*>(x + row * 2 * I + gcol);
+    Vec8 u = *reinterpret_cast<const Vec8*>(x + row * 2 * I + ucol);
     Vec8 o;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -368,6 +374,97 @@ __global__ void __launch_bounds__(512) splitk_add_rmsnorm_kernel(bf16* __restric
   }
 }
 
+// Same operation with a row spread over a cluster of CL CTAs (each owns N / CL columns): a decode
+// step has few rows (T = 64 at C = 64), so one CTA per row leaves most SMs idle and serialises
+// every row's partial reads in one SM.  Each CTA issues all S partial loads of its columns at
+// once, and the CTAs of a row add their sums of squares through distributed shared memory.
+template <int S, int CL, int kPer>
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(256)
+    splitk_add_rmsnorm_cluster_kernel(bf16* __restrict__ out, bf16* __restrict__ res_out,
+                                      const float* __restrict__ part, const bf16* __restrict__ residual,
+                                      const bf16* __restrict__ w, int T, int N, float eps) {
+  namespace cg = cooperative_groups;
+  // kPer float4 chunks per thread: N = CL * 256 * 4 * kPer
+  pdl_trigger();
+  pdl_wait();
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float red[8];
+  __shared__ float cta_ss;
+  const int row = blockIdx.y;
+  const int cols = N / CL;
+  const int c0 = (int)cluster.block_rank() * cols;
+  const int64_t TN = (int64_t)T * N;
+  float4 v[kPer];
+  float ss = 0.f;
+  float4 p[kPer][S];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int col = c0 + (threadIdx.x + k * 256) * 4;
+    if (col < c0 + cols) {
+      const int64_t off = (int64_t)row * N + col;
+#pragma unroll
+      for (int s2 = 0; s2 < S; ++s2) p[k][s2] = __ldcg(reinterpret_cast<const float4*>(part + s2 * TN + off));
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int col = c0 + (threadIdx.x + k * 256) * 4;
+    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (col >= c0 + cols) continue;
+    const int64_t off = (int64_t)row * N + col;
+    float4 acc = p[k][0];
+#pragma unroll
+    for (int s2 = 1; s2 < S; ++s2) {
+      acc.x += p[k][s2].x; acc.y += p[k][s2].y; acc.z += p[k][s2].z; acc.w += p[k][s2].w;
+    }
+    const uint2 rr = *reinterpret_cast<const uint2*>(residual + off);
+    const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
+    const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
+    v[k].x = to_f(to_b(acc.x)) + __low2float(r01);
+    v[k].y = to_f(to_b(acc.y)) + __high2float(r01);
+    v[k].z = to_f(to_b(acc.z)) + __low2float(r23);
+    v[k].w = to_f(to_b(acc.w)) + __high2float(r23);
+    const __nv_bfloat162 o01 = __floats2bfloat162_rn(v[k].x, v[k].y), o23 = __floats2bfloat162_rn(v[k].z, v[k].w);
+    uint2 oraw;
+    oraw.x = *reinterpret_cast<const uint32_t*>(&o01);
+    oraw.y = *reinterpret_cast<const uint32_t*>(&o23);
+    *reinterpret_cast<uint2*>(res_out + off) = oraw;
+    ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i];
+    cta_ss = t;
+  }
+  cluster.sync();
+  float total = 0.f;
+#pragma unroll
+  for (int c = 0; c < CL; ++c) total += *cluster.map_shared_rank(&cta_ss, c);
+  cluster.sync();                                  // keep cta_ss alive until every CTA has read it
+  const float inv = rsqrtf(total / N + eps);
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int col = c0 + (threadIdx.x + k * 256) * 4;
+    if (col >= c0 + cols) continue;
+    const uint2 wraw = *reinterpret_cast<const uint2*>(w + col);
+    const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wraw.x);
+    const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wraw.y);
+    const float o0 = to_f(to_b(to_f(to_b(v[k].x * inv)) * __low2float(w01)));
+    const float o1 = to_f(to_b(to_f(to_b(v[k].y * inv)) * __high2float(w01)));
+    const float o2 = to_f(to_b(to_f(to_b(v[k].z * inv)) * __low2float(w23)));
+    const float o3 = to_f(to_b(to_f(to_b(v[k].w * inv)) * __high2float(w23)));
+    const __nv_bfloat162 q01 = __floats2bfloat162_rn(o0, o1), q23 = __floats2bfloat162_rn(o2, o3);
+    uint2 oraw;
+    oraw.x = *reinterpret_cast<const uint32_t*>(&q01);
+    oraw.y = *reinterpret_cast<const uint32_t*>(&q23);
+    *reinterpret_cast<uint2*>(out + (int64_t)row * N + col) = oraw;
+  }
+}
+
 // split-K reduction of a gate/up projection + SiLU-mul -> bf16 [T, N/2].  INTERLEAVED: rows
 // interleaved per 64 (g0..g63, u0..u63, g64, ...); otherwise [gate (N/2) | up (N/2)].
 template <bool INTERLEAVED>
@@ -558,7 +655,20 @@ void silu_and_mul(at::Tensor out, at::Tensor x) {
   const int64_t vec = out.numel() / 8;
   if (vec == 0) return;
   const at::cuda::CUDAGuard g(x.device());
-  launch_pdl(silu_mul_kernel, grid_for(vec, 256), 256, 0, stream(), (bf16*)out.data_ptr(), (const bf16*)x.data_ptr(), I, vec);
+  launch_pdl(silu_mul_kernel<false>, grid_for(vec, 256), 256, 0, stream(), (bf16*)out.data_ptr(),
+             (const bf16*)x.data_ptr(), I, vec);
+}
+
+void silu_and_mul_interleaved(at::Tensor out, at::Tensor x) {
+  check_bf16(x, "x");
+  check_bf16(out, "out");
+  const int I = out.size(-1);
+  LSB_CHECK(x.size(-1) == 2 * I && I % 64 == 0, "interleaved silu_and_mul expects [T, 2I] -> [T, I], I % 64 == 0");
+  const int64_t vec = out.numel() / 8;
+  if (vec == 0) return;
+  const at::cuda::CUDAGuard g(x.device());
+  launch_pdl(silu_mul_kernel<true>, grid_for(vec, 256), 256, 0, stream(), (bf16*)out.data_ptr(),
+             (const bf16*)x.data_ptr(), I, vec);
 }
 
 void feed_ids(at::Tensor out, at::Tensor ids, at::Tensor feed, at::Tensor prev, at::Tensor status) {
@@ -713,6 +823,28 @@ void splitk_reduce_add_rmsnorm(at::Tensor out, at::Tensor res_out, at::Tensor pa
   int threads = std::min(512, std::max(32, ((N / 4 + 31) / 32) * 32));
   auto args = std::make_tuple((bf16*)out.data_ptr(), (bf16*)res_out.data_ptr(), partials.data_ptr<float>(),
                               (const bf16*)residual.data_ptr(), (const bf16*)w.data_ptr(), S, T, N, (float)eps);
+  if ((N == 4096 || N == 8192) && S >= 1 && S <= 8 && std::getenv("LLMSERVE_NORM_ROW_CTA") == nullptr) {
+    // a cluster of 4 CTAs per row: one (N = 4096) or two float4 per thread and split
+    auto cargs = std::make_tuple((bf16*)out.data_ptr(), (bf16*)res_out.data_ptr(), partials.data_ptr<float>(),
+                                 (const bf16*)residual.data_ptr(), (const bf16*)w.data_ptr(), T, N, (float)eps);
+    auto cgo = [&](auto kern) {
+      std::apply([&](auto... a) { launch_pdl(kern, dim3(4, T), 256, 0, stream(), a...); }, cargs);
+    };
+#define LSB_NORM_CL(KP)                                                   \
+    switch (S) {                                                          \
+      case 1: cgo(splitk_add_rmsnorm_cluster_kernel<1, 4, KP>); break;    \
+      case 2: cgo(splitk_add_rmsnorm_cluster_kernel<2, 4, KP>); break;    \
+      case 3: cgo(splitk_add_rmsnorm_cluster_kernel<3, 4, KP>); break;    \
+      case 4: cgo(splitk_add_rmsnorm_cluster_kernel<4, 4, KP>); break;    \
+      case 5: cgo(splitk_add_rmsnorm_cluster_kernel<5, 4, KP>); break;    \
+      case 6: cgo(splitk_add_rmsnorm_cluster_kernel<6, 4, KP>); break;    \
+      case 7: cgo(splitk_add_rmsnorm_cluster_kernel<7, 4, KP>); break;    \
+      default: cgo(splitk_add_rmsnorm_cluster_kernel<8, 4, KP>); break;   \
+    }
+    if (N == 4096) { LSB_NORM_CL(1) } else { LSB_NORM_CL(2) }
+#undef LSB_NORM_CL
+    return;
+  }
   auto go = [&](auto kern) {
     std::apply([&](auto... a) { launch_pdl(kern, T, threads, N * sizeof(float), stream(), a...); }, args);
   };

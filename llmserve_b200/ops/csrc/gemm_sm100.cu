@@ -423,13 +423,19 @@ static int pair_min_tokens() {
 
 // SiLU-gated projection with an interleaved gate/up weight [N, K] (N = 2 * I, interleaved per 64
 // rows): out = silu(gate) * up as bf16 [T, I], in the GEMM epilogue (no split-K).
-void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages) {
+static void gemm_silu_dispatch(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, bool packed, at::Tensor status,
+                               int64_t max_stages) {
   LSB_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
             "gemm operands must be bf16 CUDA tensors");
-  LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1) && x.stride(1) == 1 && w.stride(1) == 1,
-            "gemm shape mismatch");
-  LSB_CHECK(w.size(0) % BM == 0, "interleaved gate/up weight must have a multiple of 128 rows");
-  const int T = x.size(0), N = w.size(0);
+  LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1, "gemm shape mismatch");
+  if (packed) {
+    const int64_t kt = (x.size(1) + BK - 1) / BK, mt = (n + 255) / 256 * 2;
+    LSB_CHECK(w.size(1) == BK && w.is_contiguous() && w.size(0) == mt * kt * BM, "packed weight shape mismatch");
+  } else {
+    LSB_CHECK(x.size(1) == w.size(1) && w.size(0) == n, "gemm shape mismatch");
+  }
+  LSB_CHECK(n % BM == 0, "interleaved gate/up weight must have a multiple of 128 rows");
+  const int T = x.size(0), N = (int)n;
   LSB_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)T * (N / 2),
             "bad out");
   if (T == 0) return;
@@ -439,15 +445,26 @@ void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor statu
   const bool shallow = max_stages > 0 && max_stages <= 4;
 #define LSB_SILU(BNV)                                                                  \
   do {                                                                                 \
-    if (shallow) launch<BNV, 4, 1>(x, w, N, false, o, nullptr, 1, st);                 \
-    else launch<BNV, stages_for<BNV>(), 1>(x, w, N, false, o, nullptr, 1, st);         \
+    if (shallow) launch<BNV, 4, 1>(x, w, N, packed, o, nullptr, 1, st);                \
+    else launch<BNV, stages_for<BNV>(), 1>(x, w, N, packed, o, nullptr, 1, st);        \
   } while (0)
   if (T <= 16) LSB_SILU(16);
   else if (T <= 32) LSB_SILU(32);
   else if (T <= 64) LSB_SILU(64);
-  else if (T <= 128) launch<128, stages_for<128>(), 1>(x, w, N, false, o, nullptr, 1, st);
-  else launch<256, stages_for<256>(), 1>(x, w, N, false, o, nullptr, 1, st);
+  else if (T <= 128) launch<128, stages_for<128>(), 1>(x, w, N, packed, o, nullptr, 1, st);
+  else launch<256, stages_for<256>(), 1>(x, w, N, packed, o, nullptr, 1, st);
 #undef LSB_SILU
+}
+
+void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages) {
+  LSB_CHECK(w.dim() == 2, "gemm weight must be 2-D");
+  gemm_silu_dispatch(out, x, w, w.size(0), false, status, max_stages);
+}
+
+// Same with the tile-packed image (gemm.pack_weight) of an interleaved gate/up weight of n rows.
+void gemm_bf16_silu_packed(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, at::Tensor status,
+                           int64_t max_stages) {
+  gemm_silu_dispatch(out, x, w, n, true, status, max_stages);
 }
 
 void gemm_bf16_pair(void* out, bool out_f32, const at::Tensor& x, const at::Tensor& w, int N, bool packed, int* status);

@@ -264,6 +264,9 @@ def interleave_gate_up(w: torch.Tensor) -> torch.Tensor:
     return torch.stack([g, u], dim=1).reshape(2 * I, -1).contiguous()
 
 
+SILU_EPILOGUE_MAX_T = 128     # above this the projection runs on the 2-SM kernel and SiLU-mul separately
+
+
 def linear_silu(x: torch.Tensor, w_interleaved: torch.Tensor, max_splits: int = 8) -> torch.Tensor:
     """``silu(x @ gate^T) * (x @ up^T)`` for an interleaved gate/up weight, fused in the GEMM
     epilogue (or in the split-K reduction when K is split)."""
@@ -273,8 +276,15 @@ def linear_silu(x: torch.Tensor, w_interleaved: torch.Tensor, max_splits: int = 
     out = torch.empty(T, N // 2, dtype=x.dtype, device=x.device)
     if T == 0:
         return out
+    if T > SILU_EPILOGUE_MAX_T:
+        # prefill-sized: the 2-SM GEMM writes the interleaved projection, then one SiLU-mul pass
+        y = linear(x2, w_interleaved)
+        C().silu_and_mul_interleaved(out, y)
+        return out
     splits = min(choose_splits(T, N, K), max_splits)
-    if splits == 1:
+    if splits == 1 and isinstance(w_interleaved, PackedWeight):
+        C().gemm_bf16_silu_packed(out, x2, w_interleaved.data, w_interleaved.n, status(x.device), _stages(T))
+    elif splits == 1:
         C().gemm_bf16_silu(out, x2, w_interleaved, status(x.device), _stages(T))
     else:
         partials = linear_partials(x2, w_interleaved, splits)

@@ -314,6 +314,22 @@ def test_gate_up_silu_fused_epilogue(T, I, K):
     o3 = torch.empty(T, I, device=DEV, dtype=torch.bfloat16)
     C().splitk_silu(o3, parts)
     assert rel_err(o3, ref) < 1e-2
+    # tile-packed interleaved weight (the engine's layout): fused epilogue and split-K paths
+    pw = gemm.pack_weight(wi)
+    assert rel_err(gemm.linear_silu(x, pw), ref) < 1e-2
+    assert rel_err(gemm.linear_silu(x, pw, max_splits=1), ref) < 1e-2
+
+
+@pytest.mark.parametrize("T", [300, 1024])
+def test_gate_up_silu_prefill_sized_interleaved(T):
+    """Above the epilogue's token range the interleaved projection runs on the 2-SM kernel and the
+    interleaved SiLU-mul kernel."""
+    I, K = 1536, 1024
+    x = torch.randn(T, K, device=DEV).bfloat16()
+    w = (torch.randn(2 * I, K, device=DEV) * 0.05).bfloat16()
+    ref = activation.silu_and_mul_ref((x.float() @ w.float().t()).bfloat16().cpu()).to(DEV)
+    pw = gemm.pack_weight(gemm.interleave_gate_up(w))
+    assert rel_err(gemm.linear_silu(x, pw), ref) < 1e-2
 
 
 def test_kv_push_blocks_same_gpu_and_bad_ids():
