@@ -59,3 +59,12 @@ def test_profilers_measure_on_gpu():
                                            num_attention_heads=8, num_key_value_heads=2))[1]
     r = awqp.measure_projection_cuda(p, num_tokens=8, group_size=128, device=dev, warmup=2, repeats=5)
     assert all(r[s] > 0 for s in awqp.STAGES)
+
+
+def test_step_timeline_exclusive_time_and_gaps():
+    from benchmarks.step_timeline import exclusive_times, short_name
+    rows = [("a", 0.0, 10.0), ("b", 5.0, 12.0), ("a", 20.0, 25.0), ("c", 21.0, 23.0)]
+    excl, cnt, idle = exclusive_times(rows)
+    assert excl == {"a": 15.0, "b": 2.0, "c": 0.0} and cnt["a"] == 2 and idle == 8.0
+    assert short_name("void lsb::(anonymous namespace)::gemm_bf16_kernel<64, 4, 0>(CUtensorMap_st, int)") == \
+        "gemm_bf16_kernel<64, 4, 0>"
