@@ -45,6 +45,9 @@ def parse():
     p.add_argument("--awq", action="store_true",
                    help="AutoAWQ 4-bit g128 Qwen3-8B (random codes/zeros, |N(0,1)|*0.01 scales) on the W4A16 kernel")
     p.add_argument("--nccl-only", action="store_true", help="disable the fused NVLink collectives")
+    p.add_argument("--eagle3", action="store_true",
+                   help="EAGLE3 speculative decoding, gamma 3, with a random-init Qwen3-8B speculator (1 layer, "
+                        "fc 12288->4096, draft vocab 32000); acceptance is not meaningful with random weights")
     p.add_argument("--mem-util", type=float, default=0.85, help="gpu_memory_utilization (KV pool sizing)")
     p.add_argument("--no-overlap", action="store_true",
                    help="synchronous decode loop (no launch of step N+1 before step N's tokens are read)")
@@ -141,6 +144,10 @@ def run_ours(args):
         kwargs.update(distributed_launcher="external", distributed_init_method="env://",
                       rpc_channel=f"llmserve_b200_bench_{os.environ.get('MASTER_PORT', '0')}")
     path = model_dir(args.layers, args.awq)
+    if args.eagle3:
+        from llmserve_b200.models.synthetic import EAGLE3_8B, write_config_only
+        kwargs.update(speculative_model=write_config_only(os.path.join(tempfile.gettempdir(), "llmserve_b200_eagle3_8b"),
+                                                          EAGLE3_8B), speculative_gamma=3)
     if rank > 0:
         run_worker(path, rank, **kwargs)
         return
@@ -197,7 +204,8 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init Qwen3-8B weights N(0,0.02), prompt ids uniform over the vocab",
-        "config": {"model": ("Qwen3-8B" if args.layers == 36 else f"Qwen3-8B-{args.layers}L") + ("-AWQ" if args.awq else ""),
+        "config": {"model": ("Qwen3-8B" if args.layers == 36 else f"Qwen3-8B-{args.layers}L") + ("-AWQ" if args.awq else "")
+                   + ("+EAGLE3" if args.eagle3 else ""),
                    "global_batch": args.concurrency, "seq_len": args.input_len + args.output_len,
                    "parallelism": f"tp{world}", "workload": f"closed-loop {args.input_len} in / {args.output_len} out, "
                    f"concurrency {args.concurrency}, greedy", "cuda_graphs": not args.eager,
@@ -210,6 +218,10 @@ def run_ours(args):
         "latency": {"ttft_p99_ms": None if m["ttft"]["p99"] is None else round(m["ttft"]["p99"] * 1e3, 2),
                     "tpot_p99_ms": None if m["tpot"]["p99"] is None else round(m["tpot"]["p99"] * 1e3, 3)},
         "per_rank_device_ms": [round(r[0], 3) for r in per_rank],
+        "speculative": None if not args.eagle3 else {
+            k: m["speculative"].get(k) for k in ("steps", "acceptance_rate", "acceptance_length", "mean_batch_size")}
+        | {"step_latency_p50_ms": None if m["speculative_step_latency"]["p50"] is None
+           else round(m["speculative_step_latency"]["p50"] * 1e3, 3)},
         "clocks": clocks.summary(),
         "impl": "ours",
     }
