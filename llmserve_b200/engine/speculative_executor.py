@@ -27,7 +27,7 @@ from llmserve_b200.models.eagle3 import Eagle3Speculator
 from llmserve_b200.ops import kv as kv_ops
 from llmserve_b200.ops import sampling as sampling_ops
 from llmserve_b200.parallel import state as tp
-from llmserve_b200.speculative.sampling import greedy_accept_batch, speculative_accept_reject_from_logits
+from llmserve_b200.speculative.sampling import greedy_accept_packed, speculative_accept_reject_from_logits
 from llmserve_b200.speculative.tree import build_fixed_tree_topology, select_greedy_tree_path
 from llmserve_b200.speculative.types import SpeculativeDecodeOutput
 from llmserve_b200.utils.context import reset_context, set_context
@@ -248,9 +248,9 @@ class SpeculativeExecutor:
         t = perf_counter()
         if greedy:
             target_ids = self._target_ids(logits).view(B, n)
-            num_acc, final = greedy_accept_batch(target_ids, draft_tokens)
-            host = torch.cat([num_acc.unsqueeze(1).long(), final.unsqueeze(1), start_ids.unsqueeze(1),
-                              draft_tokens], 1).tolist()
+            packed = greedy_accept_packed(target_ids, draft_tokens, start_ids)
+            num_acc = packed[:, 0]
+            host = packed.tolist()
             r.d2h_bytes += 8 * B * (g + 3)
             accepts = [(row[0], row[1], row[3:], row[0] == g) for row in host]
             starts = [row[2] for row in host]

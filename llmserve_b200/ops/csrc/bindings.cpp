@@ -52,6 +52,7 @@ void gemm_bf16_streamk(at::Tensor partials, at::Tensor x, at::Tensor w, int64_t 
                        at::Tensor status);
 int64_t streamk_slots(int64_t m_tiles, int64_t k_tiles, int64_t grid);
 void splitk_silu_halves(at::Tensor out, at::Tensor partials);
+void greedy_accept(at::Tensor out, at::Tensor target, at::Tensor draft, at::Tensor start);
 void feed_ids(at::Tensor out, at::Tensor ids, at::Tensor feed, at::Tensor prev, at::Tensor status);
 void kv_push(at::Tensor src_k, at::Tensor src_v, at::Tensor dst_k, at::Tensor dst_v, at::Tensor src_ids,
              at::Tensor dst_ids, at::Tensor status);
@@ -94,6 +95,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("streamk_slots", &lsb::streamk_slots);
   m.def("kv_push", &lsb::kv_push);
   m.def("feed_ids", &lsb::feed_ids);
+  m.def("greedy_accept", &lsb::greedy_accept);
   m.def("gemm_bf16", &lsb::gemm_bf16, py::arg("out"), py::arg("x"), py::arg("w"), py::arg("partials"),
         py::arg("splits"), py::arg("status"), py::arg("max_stages") = 0);
 }

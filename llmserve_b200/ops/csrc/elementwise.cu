@@ -509,6 +509,28 @@ __global__ void feed_ids_kernel(int64_t* __restrict__ out, const int* __restrict
   }
 }
 
+// Greedy speculative acceptance for a batch, packed for one host copy: row b of `out` is
+// [accepted count a, final token (target id at row a: the correction, or the bonus when a == g),
+//  start token, the g draft tokens].  Draft j is accepted while it equals the target's argmax at
+// verify row j, for every j before it.
+__global__ void greedy_accept_kernel(int64_t* __restrict__ out, const int64_t* __restrict__ target,
+                                     const int64_t* __restrict__ draft, const int64_t* __restrict__ start, int B,
+                                     int g) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int64_t* t = target + (int64_t)b * (g + 1);
+  const int64_t* d = draft + (int64_t)b * g;
+  int64_t* o = out + (int64_t)b * (g + 3);
+  int a = 0;
+  while (a < g && d[a] == t[a]) ++a;
+  o[0] = a;
+  o[1] = t[a];
+  o[2] = start[b];
+  for (int j = 0; j < g; ++j) o[3 + j] = d[j];
+}
+
 // ------------------------------------------------------------------------------------------
 // Row argmax (lowest index on ties) and exponential-race sampling
 // ------------------------------------------------------------------------------------------
@@ -669,6 +691,20 @@ void silu_and_mul_interleaved(at::Tensor out, at::Tensor x) {
   const at::cuda::CUDAGuard g(x.device());
   launch_pdl(silu_mul_kernel<true>, grid_for(vec, 256), 256, 0, stream(), (bf16*)out.data_ptr(),
              (const bf16*)x.data_ptr(), I, vec);
+}
+
+void greedy_accept(at::Tensor out, at::Tensor target, at::Tensor draft, at::Tensor start) {
+  LSB_CHECK(out.scalar_type() == at::kLong && target.scalar_type() == at::kLong && draft.scalar_type() == at::kLong &&
+                start.scalar_type() == at::kLong, "greedy_accept: int64 tensors");
+  LSB_CHECK(out.is_contiguous() && target.is_contiguous() && draft.is_contiguous() && start.is_contiguous(),
+            "greedy_accept: contiguous tensors");
+  const int B = draft.size(0), g = draft.size(1);
+  LSB_CHECK(target.size(0) == B && target.size(1) == g + 1 && start.numel() == B && out.size(0) == B &&
+                out.size(1) == g + 3, "greedy_accept: shapes [B, g+1], [B, g], [B] -> [B, g+3]");
+  if (B == 0) return;
+  const at::cuda::CUDAGuard guard(out.device());
+  launch_pdl(greedy_accept_kernel, (B + 127) / 128, 128, 0, stream(), out.data_ptr<int64_t>(),
+             target.data_ptr<int64_t>(), draft.data_ptr<int64_t>(), start.data_ptr<int64_t>(), B, g);
 }
 
 void feed_ids(at::Tensor out, at::Tensor ids, at::Tensor feed, at::Tensor prev, at::Tensor status) {

@@ -5,8 +5,9 @@
 * rejection sampling (Leviathan et al., 2023): accept ``x`` with ``min(1, p(x)/q(x))``; on reject
   sample from ``norm(max(p - q, 0))``; after full acceptance sample the bonus from ``p``.
 
-``greedy_accept_batch`` is the batched device form used by the executor: one comparison, a
-cumulative product and a gather for the whole batch, with a single host copy of the result.
+``greedy_accept_batch`` is the batched tensor form (one comparison, a cumulative product and a
+gather for the whole batch); ``greedy_accept_packed`` is what the executor uses: one sm_100a
+kernel that also packs the start and draft tokens, so the step needs a single host copy.
 """
 import torch
 
@@ -85,3 +86,18 @@ def greedy_accept_batch(target_ids: torch.Tensor, draft_ids: torch.Tensor):
     num_acc = torch.cumprod(match, dim=1).sum(dim=1)
     final = target_ids.gather(1, num_acc.unsqueeze(1).long()).squeeze(1)
     return num_acc, final
+
+
+def greedy_accept_packed(target_ids: torch.Tensor, draft_ids: torch.Tensor, start_ids: torch.Tensor) -> torch.Tensor:
+    """``[B, g + 3]`` int64 rows ``[accepted, final, start, drafts...]`` for one host copy (one
+    sm_100a kernel on CUDA; the batched torch form on the host)."""
+    B, g = draft_ids.shape
+    if not target_ids.is_cuda:
+        num_acc, final = greedy_accept_batch(target_ids, draft_ids)
+        return torch.cat([num_acc.unsqueeze(1).long(), final.unsqueeze(1).long(), start_ids.view(B, 1).long(),
+                          draft_ids.long()], 1)
+    from llmserve_b200.ops._ext import C
+    out = torch.empty(B, g + 3, dtype=torch.int64, device=target_ids.device)
+    C().greedy_accept(out, target_ids.long().contiguous(), draft_ids.long().contiguous(),
+                      start_ids.long().contiguous().view(-1))
+    return out

@@ -208,3 +208,16 @@ def test_streamk_schedule_slots_match_brute_force():
         assert 1 <= slots <= gemm.STREAMK_MAX_SLOTS and 1 <= grid <= 2 * 148 and stages in (4, 8)
     assert gemm.streamk_schedule(151936, 4096) is None          # LM head: plain tiles
     assert gemm.streamk_plan(300, 4096, 4096) is None           # prefill-sized T
+
+
+def test_packed_greedy_accept_matches_per_sequence_rule():
+    from llmserve_b200.speculative.sampling import greedy_accept_packed
+    g = torch.Generator().manual_seed(4)
+    draft = torch.randint(0, 4, (50, 3), generator=g)
+    target = torch.randint(0, 4, (50, 4), generator=g)
+    start = torch.arange(50)
+    packed = greedy_accept_packed(target, draft, start)
+    for i in range(50):
+        r = greedy_accept_from_ids(target[i].tolist(), draft[i].tolist())
+        assert packed[i, 0] == r.num_accepted and packed[i, 1] == r.final_token_id
+        assert packed[i, 2] == i and packed[i, 3:].tolist() == draft[i].tolist()

@@ -357,3 +357,17 @@ def test_kv_push_blocks_to_peer_gpu():
     kv.push_blocks(src_k, src_v, dst_k, dst_v, [5, 2], [0, 4])
     torch.cuda.synchronize(0)
     assert torch.equal(dst_k[:, 0].cpu(), src_k[:, 5].cpu()) and torch.equal(dst_v[:, 4].cpu(), src_v[:, 2].cpu())
+
+
+def test_greedy_accept_kernel_matches_batched_reference():
+    from llmserve_b200.speculative.sampling import greedy_accept_packed
+    g = torch.Generator().manual_seed(9)
+    B, gam = 37, 3
+    draft = torch.randint(0, 5, (B, gam), generator=g)
+    target = torch.randint(0, 5, (B, gam + 1), generator=g)
+    target[:8, :gam] = draft[:8]                   # full acceptance rows: the bonus token is final
+    start = torch.randint(0, 1000, (B,), generator=g)
+    want = greedy_accept_packed(target, draft, start)
+    got = greedy_accept_packed(target.to(DEV), draft.to(DEV), start.to(DEV))
+    assert torch.equal(got.cpu(), want)
+    assert (want[:8, 0] == gam).all() and torch.equal(want[:8, 1], target[:8, gam])
