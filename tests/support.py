@@ -5,7 +5,8 @@ import sys
 
 import pytest
 
-_REF_CANDIDATES = [os.environ.get("LLMSERVE_REFERENCE_PATH", ""), "/root/reference",
+# the reference checkout named by LLMSERVE_REFERENCE_PATH, else its package installed under baseline/_ref
+_REF_CANDIDATES = [os.environ.get("LLMSERVE_REFERENCE_PATH", ""),
                    os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")]
 
 
