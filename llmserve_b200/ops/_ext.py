@@ -78,7 +78,10 @@ def status(device):
     key = str(d)
     t = _STATUS.get(key)
     if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=d)
+        # a normal tensor even when first asked for inside inference mode: check_status resets it
+        # in place from ordinary code
+        with torch.inference_mode(False):
+            t = torch.zeros(1, dtype=torch.int32, device=d)
         _STATUS[key] = t
     return t
 

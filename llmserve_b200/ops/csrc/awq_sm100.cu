@@ -332,11 +332,7 @@ void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz,
   const int kps = (k_tiles + splits - 1) / splits;
   const CUtensorMap mx = activation_map(x, BN);
   auto kern = awq_gemm_kernel<BN, ST, WB>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    configured = true;
-  }
+  ensure_dynamic_smem((const void*)kern, L::kBytes);
   dim3 grid(((N + QBM - 1) / QBM) * ((T + BN - 1) / BN), 1, splits);
   launch_pdl(kern, grid, dim3(kQThreads), L::kBytes, at::cuda::getCurrentCUDAStream(), mx,
              (const uint32_t*)qt.data_ptr(), (const uint2*)sz.data_ptr(), out, partials, T, N, k_tiles, kps, status);

@@ -115,6 +115,11 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 bool pdl_enabled();
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) applies to the CURRENT device only: one process
+// that drives several GPUs (prefill/decode disaggregation, tests) must set it on each of them.
+// Sets it for the current device the first time `bytes` exceeds what was set there.
+void ensure_dynamic_smem(const void* func, int bytes);
+
 // cudaLaunchKernelEx with the PDL attribute (when enabled).
 template <typename... KArgs, typename... Args>
 inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

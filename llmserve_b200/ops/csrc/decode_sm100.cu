@@ -487,11 +487,7 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
 #define LSB_DEC_TMA(HD)                                                                                             \
   do {                                                                                                              \
     const int smem = DecLayout<HD>::smem_bytes(G);                                                                  \
-    static int configured_smem = 0;                                                                                 \
-    if (smem > configured_smem) {                                                                                   \
-      cudaFuncSetAttribute(decode_tma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);              \
-      configured_smem = smem;                                                                                       \
-    }                                                                                                               \
+    ensure_dynamic_smem((const void*)decode_tma_kernel<HD>, smem);                                                \
     int per_sm = 1;                                                                                                 \
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_tma_kernel<HD>, kDecThreads, smem);               \
     const int grid = (int)std::min<int64_t>(n_items, (int64_t)sm_count() * std::max(per_sm, 1));                   \

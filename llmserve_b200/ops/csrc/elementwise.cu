@@ -10,7 +10,10 @@
 
 #include <cooperative_groups.h>
 #include <cstdlib>
+#include <map>
+#include <mutex>
 #include <tuple>
+#include <utility>
 
 #include "common.cuh"
 
@@ -629,6 +632,19 @@ int grid_for(int64_t work, int threads) {
 }
 
 }  // namespace
+
+void ensure_dynamic_smem(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = done[{func, dev}];
+  if (bytes > have) {
+    cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    have = bytes;
+  }
+}
 
 bool pdl_enabled() {
   static const bool on = [] {

@@ -384,11 +384,7 @@ void launch(const at::Tensor& x, const at::Tensor& w, int N, bool packed, bf16* 
   const CUtensorMap mx = make_map(x.data_ptr(), T, K, x.stride(0), BN);
   const CUtensorMap& mw = weight_map(w, packed);
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    configured = true;
-  }
+  ensure_dynamic_smem((const void*)kern, L::kBytes);
   dim3 grid(((N + BM - 1) / BM) * ((T + BN - 1) / BN), 1, splits);
   launch_pdl(kern, grid, dim3(128), L::kBytes, at::cuda::getCurrentCUDAStream(), mw, mx, out, partials, T, N, k_tiles,
              kps, (int)packed, status);

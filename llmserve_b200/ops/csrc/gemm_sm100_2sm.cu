@@ -375,8 +375,8 @@ int max_pairs_resident() {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     pairs = sms / 2;
-    cudaFuncSetAttribute(gemm_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    cudaFuncSetAttribute(gemm_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    ensure_dynamic_smem((const void*)gemm_pair_kernel<false>, kSmemBytes);
+    ensure_dynamic_smem((const void*)gemm_pair_kernel<true>, kSmemBytes);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
     cfg.blockDim = dim3(kThreads);
@@ -408,6 +408,9 @@ void gemm_bf16_pair(void* out, bool out_f32, const at::Tensor& x, const at::Tens
   const int k_tiles = (K + kBK - 1) / kBK;
   const int tiles = ((N + kTileN - 1) / kTileN) * ((T + kTileT - 1) / kTileT);
   const int pairs = std::min(tiles, max_pairs_resident());
+  // the occupancy query above ran on the first device only; the attribute is per device
+  ensure_dynamic_smem((const void*)gemm_pair_kernel<false>, kSmemBytes);
+  ensure_dynamic_smem((const void*)gemm_pair_kernel<true>, kSmemBytes);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kThreads);

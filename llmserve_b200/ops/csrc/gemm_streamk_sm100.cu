@@ -301,11 +301,7 @@ void launch_streamk(float* part, const at::Tensor& x, const at::Tensor& w, int N
   const CUtensorMap mx = activation_map(x, BN);
   const CUtensorMap& mw = weight_map(w, true);
   auto kern = gemm_streamk_kernel<BN, STAGES>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    configured = true;
-  }
+  ensure_dynamic_smem((const void*)kern, L::kBytes);
   launch_pdl(kern, dim3(grid), dim3(kThreadsSK), L::kBytes, at::cuda::getCurrentCUDAStream(), mw, mx, part,
              (int)x.size(0), N, k_tiles, m_tiles, S, status);
 }
