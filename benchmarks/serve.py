@@ -84,7 +84,8 @@ ENGINE_KEYS = {
     "enable_kv_capacity_admission": False, "max_num_seqs": 512, "gpu_memory_utilization": 0.9,
     "speculative_gamma": 3, "speculative_tree_nodes": 0, "speculative_accept_mode": "greedy",
     "speculative_trace": False, "tensor_parallel_size": 1, "load_format": "auto", "fused_collectives": True,
-    "kvcache_block_size": 256,
+    "kvcache_block_size": 256, "overlap_decode": True, "pd_disaggregation": False, "pd_prefill_devices": (),
+    "pd_decode_devices": (),
 }
 
 

@@ -207,3 +207,29 @@ def test_compact_record_units():
                                       finish_time=2.5, output_tokens=3, prompt_tokens=4, success=True,
                                       token_times=[1.5, 2.0, 2.5], output_event_times=[1.5, 2.5]))
     assert rec["ttft_ms"] == 500 and rec["tpot_ms"] == 500 and rec["e2e_ms"] == 1500
+
+
+def test_run_point_with_real_cpu_engines_plain_and_disaggregated(tmp_path):
+    """A closed-loop point through benchmarks.serve with the engine itself (CPU tier): the plain
+    engine and the prefill/decode-disaggregated variant both complete and emit tokens."""
+    from llmserve_b200 import LLM
+    from llmserve_b200.models.synthetic import TINY, write_qwen3_checkpoint
+    path = write_qwen3_checkpoint(str(tmp_path / "m"), TINY)
+    suite = {"schema_version": 1, "name": "cpu-pd", "runs": 1,
+             "profiles": {"p": {"classes": [{"name": "c", "weight": 1, "input_len": 24, "output_len": 12}],
+                                "prompt_id_high": 1000}},
+             "experiments": [{"name": "e", "arrival": "closed-loop", "profile": "p", "max_concurrencies": [3],
+                              "warmup_seconds": 0.2, "measurement_seconds": 1.0,
+                              "variants": [{"name": "baseline"},
+                                           {"name": "pd", "pd_disaggregation": True, "pd_prefill_devices": [0],
+                                            "pd_decode_devices": [0]}],
+                              "runtime": {"argmax_sampler": True, "max_model_len": 128,
+                                          "max_num_batched_tokens": 256, "kvcache_block_size": 16}}]}
+
+    def factory(model, **kw):
+        return LLM(model, device="cpu", num_kvcache_blocks=64, **kw)
+
+    for point in expand_suite(suite):
+        result = run_point(point, path, engine_factory=factory, metadata={"git_commit": "abc"})
+        assert result["complete"], point["variant"]
+        assert result["metrics"]["throughput"]["output_tokens_per_second"] > 0
