@@ -32,6 +32,7 @@ void comm_free(int64_t p);
 at::Tensor comm_ipc_handle(int64_t p);
 int64_t comm_open_handle(at::Tensor handle);
 void comm_close_handle(int64_t p);
+void comm_set_spin_limit(int64_t polls);
 void fused_allreduce_add_rmsnorm(std::vector<int64_t> part, std::vector<int64_t> out, std::vector<int64_t> res,
                                  std::vector<int64_t> flags, at::Tensor res_in, at::Tensor w, int64_t rank, int64_t S,
                                  int64_t T, int64_t N, double eps, at::Tensor status);
@@ -85,6 +86,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_ipc_handle", &lsb::comm_ipc_handle);
   m.def("comm_open_handle", &lsb::comm_open_handle);
   m.def("comm_close_handle", &lsb::comm_close_handle);
+  m.def("comm_set_spin_limit", &lsb::comm_set_spin_limit);
   m.def("fused_allreduce_add_rmsnorm", &lsb::fused_allreduce_add_rmsnorm);
   m.def("gemm_bf16_silu", &lsb::gemm_bf16_silu);
   m.def("splitk_silu", &lsb::splitk_silu);

@@ -14,7 +14,8 @@
 //   5. the last CTA of the rank signals phase 2 to every peer and waits (bounded) for all of them,
 //      so when the kernel ends every rank holds all rows.
 // `epoch` lives in device memory and is advanced by the kernel itself, so the launch can be
-// captured in a CUDA graph.  Every wait gives up after kSpinLimit polls, records
+// captured in a CUDA graph.  Every wait gives up after a bounded number of polls (kSpinLimit unless
+// lowered for a test), records
 // kTimeoutPeerFlag in the status word and lets the kernel finish (no hang, no trap).
 //
 // One buffer of each kind suffices: a rank can only overwrite a peer's buffers after that peer
@@ -57,11 +58,16 @@ __device__ __forceinline__ void st_v2(bf16* p, uint2 v) {
   asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
 }
 
+// Polls before a peer-flag wait gives up (kSpinLimit unless lowered by comm_set_spin_limit, which
+// the failure-detection test uses to make a wait on a flag nothing sets end in milliseconds).
+__device__ uint32_t g_flag_spin_limit = kSpinLimit;
+
 __device__ bool wait_flags(const uint32_t* flags, int W, uint32_t epoch, int* status) {
+  const uint32_t limit = *((volatile uint32_t*)&g_flag_spin_limit);
   for (int r = 0; r < W; ++r) {
     uint32_t i = 0;
     while ((int32_t)(ld_acquire_sys(flags + r) - epoch) < 0) {
-      if (++i > kSpinLimit) {
+      if (++i > limit) {
         record_error(status, kTimeoutPeerFlag);
         return false;
       }
@@ -222,6 +228,13 @@ int64_t comm_open_handle(at::Tensor handle) {
 }
 
 void comm_close_handle(int64_t p) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(p)); }
+
+// Spin limit of the peer-flag waits on the current device, clamped to [1024, kSpinLimit].
+void comm_set_spin_limit(int64_t polls) {
+  uint32_t v = (uint32_t)std::min<int64_t>(std::max<int64_t>(polls, 1024), (int64_t)kSpinLimit);
+  auto e = cudaMemcpyToSymbol(g_flag_spin_limit, &v, sizeof(v));
+  LSB_CHECK(e == cudaSuccess, std::string("setting the spin limit failed: ") + cudaGetErrorString(e));
+}
 
 // part/out/res/flags: W base addresses each (this rank's mapping of every rank's buffers)
 void fused_allreduce_add_rmsnorm(std::vector<int64_t> part, std::vector<int64_t> out, std::vector<int64_t> res,

@@ -371,3 +371,34 @@ def test_greedy_accept_kernel_matches_batched_reference():
     got = greedy_accept_packed(target.to(DEV), draft.to(DEV), start.to(DEV))
     assert torch.equal(got.cpu(), want)
     assert (want[:8, 0] == gam).all() and torch.equal(want[:8, 1], target[:8, gam])
+
+
+def test_fused_collective_wait_on_unset_flag_returns_error_status():
+    """Failure detection on the device without a fault: a two-rank fused collective whose second
+    rank never runs (its buffer is local memory that nothing signals).  Rank 0's waits for the
+    peer's flags give up after the (lowered) spin limit, record the error in the status word and
+    let the kernel finish; the host raises, and the context stays usable."""
+    from llmserve_b200.parallel.comm import FLAG_BYTES, FusedComm
+    hidden, T, cap = 4096, 4, 64
+    nbytes = FusedComm.buffer_bytes(hidden, cap)
+    bufs = [C().comm_alloc(nbytes) for _ in range(2)]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    try:
+        out_b = cap * hidden * 2
+        outs = [b + FLAG_BYTES for b in bufs]
+        res = [b + FLAG_BYTES + out_b for b in bufs]
+        parts = [b + FLAG_BYTES + 2 * out_b for b in bufs]
+        res_in = torch.randn(T, hidden, device=dev).bfloat16()
+        w = torch.ones(hidden, device=dev).bfloat16()
+        C().comm_set_spin_limit(1 << 16)
+        C().fused_allreduce_add_rmsnorm(parts, outs, res, bufs, res_in, w, 0, 1, T, hidden, 1e-6, status(dev))
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="peer flag wait timed out"):
+            check_status(dev)
+        x = torch.randn(64, 64, device=dev)
+        assert torch.isfinite(x @ x).all()
+    finally:
+        C().comm_set_spin_limit(1 << 40)           # back to the default (clamped to the compile-time limit)
+        torch.cuda.synchronize()
+        for b in bufs:
+            C().comm_free(b)
