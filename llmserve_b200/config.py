@@ -100,6 +100,7 @@ class Config:
     distributed_launcher: str = "spawn"
     rpc_channel: str | None = None
     overlap_decode: bool = True
+    pd_role: str = ""          # internal: "decode" exports its KV pools to the prefill ranks
 
     def __post_init__(self):
         if not os.path.isdir(self.model):

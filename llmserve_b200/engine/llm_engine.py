@@ -134,19 +134,23 @@ class LLMEngine:
         self.scheduler.reset_metrics()
 
     # ---- requests ----------------------------------------------------------------------------
-    def add_request(self, prompt: str | list[int], sampling_params: SamplingParams) -> int:
-        if isinstance(prompt, str):
-            prompt = self.tokenizer.encode(prompt)
-        seq = Sequence(list(prompt), sampling_params)
-        self.request_metrics[seq.seq_id] = {
-            "seq_id": seq.seq_id, "arrival_time": perf_counter(), "first_token_time": None,
+    @staticmethod
+    def new_request_metric(seq_id: int, prompt_tokens: int) -> dict:
+        return {
+            "seq_id": seq_id, "arrival_time": perf_counter(), "first_token_time": None,
             "token_times": [], "output_event_times": [], "speculative_step_latencies": [],
-            "finish_time": None, "prompt_tokens": len(prompt), "output_tokens": 0, "success": False,
+            "finish_time": None, "prompt_tokens": prompt_tokens, "output_tokens": 0, "success": False,
             "failure_reason": None, "speculative_steps": 0, "speculative_draft_tokens": 0,
             "speculative_accepted_tokens": 0, "speculative_emitted_tokens": 0,
             "speculative_accept_all_count": 0, "speculative_gamma_counts": {}, "speculative_trace": [],
             "speculative_timing": {},
         }
+
+    def add_request(self, prompt: str | list[int], sampling_params: SamplingParams) -> int:
+        if isinstance(prompt, str):
+            prompt = self.tokenizer.encode(prompt)
+        seq = Sequence(list(prompt), sampling_params)
+        self.request_metrics[seq.seq_id] = self.new_request_metric(seq.seq_id, len(prompt))
         self.scheduler.add(seq)
         return seq.seq_id
 

@@ -182,7 +182,9 @@ class ModelRunner:
         # release device memory so another engine can be built in this process
         self._bind_pools(None, None)
         self.k_cache = self.v_cache = self.draft_k_cache = self.draft_v_cache = None
+        self.peer_k = self.peer_v = None
         self.decode_workspace = None
+        self._release_pd()
         self.graph_vars = None
         if self.is_cuda:
             import gc
@@ -315,8 +317,11 @@ class ModelRunner:
         cfg.num_kvcache_blocks = blocks
         nkv = hf.num_key_value_heads // self.world_size
         shape = (hf.num_hidden_layers, blocks, nkv, self.block_size, hf.head_dim)
-        self.k_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
-        self.v_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        if cfg.pd_role == "decode":
+            self.k_cache, self.v_cache = self._exportable_pools(shape)
+        else:
+            self.k_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
+            self.v_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
         self.draft_k_cache = self.draft_v_cache = None
         if self.draft_model is not None:
             d = self.draft_model
@@ -332,6 +337,86 @@ class ModelRunner:
                         self.draft_model.num_heads if self.draft_model is not None else 0)
             self.decode_workspace = attn_ops.DecodeWorkspace(
                 max(cfg.max_num_seqs, 16), heads, hf.head_dim, max_ctx, self.device)
+
+    # ---- prefill/decode disaggregation: KV pools shared across processes ---------------------
+    def _exportable_pools(self, shape):
+        """K and V pools another process can map: ordinary device tensors shared through CUDA IPC
+        (torch's tensor reduction) on the GPU, a named shared-memory segment on the CPU tier."""
+        if self.is_cuda:
+            from torch.multiprocessing.reductions import reduce_tensor
+            pools = torch.zeros((2, *shape), dtype=self.dtype, device=self.device)
+            self._pd_desc = {"kind": "cuda", "ipc": reduce_tensor(pools)}
+        else:
+            from multiprocessing.shared_memory import SharedMemory
+            esize = torch.tensor([], dtype=self.dtype).element_size()
+            nbytes = 2 * esize
+            for d in shape:
+                nbytes *= d
+            self._pd_shm = SharedMemory(create=True, size=nbytes)
+            raw = torch.frombuffer(self._pd_shm.buf, dtype=torch.uint8)
+            raw.zero_()
+            pools = raw.view(self.dtype).view(2, *shape)
+            self._pd_desc = {"kind": "shm", "name": self._pd_shm.name}
+        self._pd_desc.update(shape=tuple(shape), dtype=str(self.dtype).replace("torch.", ""))
+        self._pd_pools = pools
+        return pools[0], pools[1]
+
+    def export_kv(self):
+        """Every rank's pool descriptor, gathered on rank 0 (the decode side of a disaggregated pair)."""
+        mine = getattr(self, "_pd_desc", None)
+        if self.world_size == 1:
+            return [mine]
+        out = [None] * self.world_size
+        torch.distributed.all_gather_object(out, mine)
+        return out
+
+    def open_peer_kv(self, descs):
+        """Prefill side: map the decode rank with this rank's index (same KV-head shard).  On the
+        GPU the mapping is a tensor on the decode GPU; the push kernel stores into it over NVLink."""
+        d = descs[self.rank]
+        if d["kind"] == "cuda":
+            fn, args = d["ipc"]
+            pools = fn(*args)
+        else:
+            from multiprocessing import resource_tracker
+            from multiprocessing.shared_memory import SharedMemory
+            self._peer_shm = SharedMemory(name=d["name"])
+            try:     # the decode process owns (and unlinks) the segment, not this one
+                resource_tracker.unregister(self._peer_shm._name, "shared_memory")
+            except Exception:
+                pass
+            raw = torch.frombuffer(self._peer_shm.buf, dtype=torch.uint8)
+            pools = raw.view(getattr(torch, d["dtype"])).view(2, *d["shape"])
+        if tuple(pools.shape[3:]) != tuple(self.k_cache.shape[2:]) or pools.shape[1] != self.k_cache.shape[0]:
+            raise ValueError("prefill and decode KV pools have different block shapes")
+        self._peer_pools = pools
+        self.peer_k, self.peer_v = pools[0], pools[1]
+
+    def push_kv(self, src_ids, dst_ids):
+        """Copy blocks of this rank's pool into the mapped decode pool; returns when they landed."""
+        from llmserve_b200.ops import kv as kv_ops
+        kv_ops.push_blocks(self.k_cache, self.v_cache, self.peer_k, self.peer_v, src_ids, dst_ids)
+        if self.is_cuda:
+            torch.cuda.current_stream(self.device).synchronize()
+
+    def _release_pd(self):
+        import gc
+        self._peer_pools = self._pd_pools = None
+        gc.collect()                       # drop the tensors that view the shared segments
+        for name, unlink in (("_peer_shm", False), ("_pd_shm", True)):
+            shm = getattr(self, name, None)
+            if shm is None:
+                continue
+            try:
+                shm.close()
+            except BufferError:            # a view is still alive; the OS reclaims it at exit
+                pass
+            if unlink:
+                try:
+                    shm.unlink()
+                except FileNotFoundError:
+                    pass
+            setattr(self, name, None)
 
     def get_memory_metrics(self) -> dict:
         seen, model_bytes = set(), 0

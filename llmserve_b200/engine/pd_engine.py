@@ -17,9 +17,19 @@ pd_disaggregation=True, pd_prefill_devices=(a,), pd_decode_devices=(b,))`` build
 * A sequence that finds no room in the decode pool waits (parked) until decode blocks free up;
   the prefill engine never decodes it.
 
-Scope: one GPU per side (``tensor_parallel_size=1``), no speculative draft; both engines live in
-this process (the same device for both sides is allowed and runs the same protocol).
+With one GPU per side both engines live in this process (the same device for both sides is
+allowed and runs the same protocol).  With ``tensor_parallel_size = p > 1`` each side is a
+tensor-parallel group of ``p`` consecutive GPUs (``pd_prefill_devices=(0, 1, 2, 3)``,
+``pd_decode_devices=(4, 5, 6, 7)``): the prefill engine's rank 0 runs here, the decode engine runs
+in a child process (its own rank 0 and workers, its own process group) that this process drives
+through a pipe.  Decode rank r exports its pools to prefill rank r (CUDA IPC; both hold the same
+KV-head shard), and every prefill rank pushes its shard of each handed-off block with the same
+kernel; the push returns once the blocks landed, before the decode side admits the sequences.
+No speculative draft in either mode.
 """
+import os
+import socket
+import traceback
 from time import perf_counter
 
 import torch
@@ -45,6 +55,141 @@ class _RunnerPair:
         setattr(self._dec, name, value)
 
 
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+class _DecodeServer:
+    """The decode engine of a tensor-parallel disaggregated pair, in its own process."""
+
+    def __init__(self, engine):
+        self.eng = engine
+        self.pending = {}
+
+    def reserve(self, items):
+        """Allocate decode blocks for handed-off sequences, in order, until the pool is full.
+        Returns ``(seq_id, block_table, prefix-hit blocks)`` for each sequence that fits."""
+        from llmserve_b200.engine.sequence import Sequence
+        from llmserve_b200.sampling_params import SamplingParams
+        bm = self.eng.scheduler.block_manager
+        out = []
+        for seq_id, token_ids, n_prompt, max_tokens, ignore_eos, temperature in items:
+            seq = Sequence(list(token_ids), SamplingParams(temperature=temperature, max_tokens=max_tokens,
+                                                           ignore_eos=ignore_eos))
+            seq.seq_id, seq.num_prompt_tokens = seq_id, n_prompt
+            if not bm.can_allocate(seq):
+                break
+            bm.allocate(seq)
+            hits = seq.num_cached_tokens // bm.block_size
+            seq.num_cached_tokens = seq.num_tokens
+            self.pending[seq_id] = seq
+            out.append((seq_id, list(seq.block_table), hits))
+        return out
+
+    def admit(self, seq_ids):
+        from llmserve_b200.engine.sequence import SequenceStatus
+        for sid in seq_ids:
+            s = self.pending.pop(sid)
+            s.status = SequenceStatus.RUNNING
+            self.eng.request_metrics[sid] = self.eng.new_request_metric(sid, s.num_prompt_tokens)
+            self.eng.scheduler.running.append(s)
+
+    def step(self):
+        if self.eng.is_finished():
+            return [], [], 0
+        done, n = self.eng.step()
+        for sid, _ in done:
+            self.eng.request_metrics.pop(sid, None)
+        return done, list(self.eng.last_step_events.get("decode_seq_ids", [])), n
+
+    def set_sampler(self, sampler):
+        self.eng.model_runner.sampler = sampler
+
+    def kv_metrics(self):
+        return self.eng.scheduler.kv_capacity_metrics()
+
+
+def _decode_server_main(model, kwargs, conn):
+    from llmserve_b200.engine.llm_engine import LLMEngine
+    try:
+        eng = LLMEngine(model, **kwargs)
+        conn.send(("ok", (eng.model_runner.call("export_kv"), eng.config.num_kvcache_blocks)))
+    except Exception as e:  # reported to the parent, which raises
+        conn.send(("error", f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
+        return
+    server = _DecodeServer(eng)
+    while True:
+        try:
+            cmd, args = conn.recv()
+        except EOFError:             # the parent is gone
+            eng.exit()
+            return
+        if cmd == "exit":
+            eng.exit()
+            conn.send(("ok", None))
+            return
+        try:
+            conn.send(("ok", getattr(server, cmd)(*args)))
+        except Exception as e:
+            conn.send(("error", f"{type(e).__name__}: {e}\n{traceback.format_exc()}"))
+
+
+class _RemoteDecode:
+    """Parent side of the decode server: synchronous calls with a bounded wait."""
+
+    def __init__(self, model, kwargs, timeout_s: float):
+        import torch.multiprocessing as mp
+        ctx = mp.get_context("spawn")
+        self.conn, child = ctx.Pipe()
+        self.proc = ctx.Process(target=_decode_server_main, args=(model, kwargs, child), daemon=False)
+        self.proc.start()
+        self.timeout_s = timeout_s
+        self.ready = self._reply(max(timeout_s, 600.0))
+
+    def _reply(self, timeout_s):
+        if not self.conn.poll(timeout_s):
+            raise TimeoutError(f"decode server did not answer within {timeout_s:.0f}s")
+        status, value = self.conn.recv()
+        if status != "ok":
+            raise RuntimeError(f"decode server failed: {value}")
+        return value
+
+    def call(self, cmd, *args):
+        if not self.proc.is_alive():
+            raise RuntimeError("decode server exited")
+        self.conn.send((cmd, args))
+        return self._reply(self.timeout_s)
+
+    def close(self):
+        try:
+            if self.proc.is_alive():
+                self.call("exit")
+        finally:
+            self.proc.join(timeout=self.timeout_s)
+            if self.proc.is_alive():
+                self.proc.terminate()
+
+
+class _RemoteRunnerPair:
+    """``llm.model_runner`` of the tensor-parallel pair: the sampler goes to both sides."""
+
+    def __init__(self, prefill_runner, remote):
+        object.__setattr__(self, "_pre", prefill_runner)
+        object.__setattr__(self, "_remote", remote)
+
+    def __getattr__(self, name):
+        return getattr(self._pre, name)
+
+    def __setattr__(self, name, value):
+        if name == "sampler":
+            self._remote.call("set_sampler", value)
+        setattr(self._pre, name, value)
+
+
 class PDEngine:
 
     def __init__(self, model, **kwargs):
@@ -54,12 +199,20 @@ class PDEngine:
         kwargs.pop("pd_disaggregation", None)
         kwargs.pop("device_offset", None)
         kwargs.pop("overlap_decode", None)
-        if len(pre) != 1 or len(dec) != 1:
-            raise ValueError("pd_disaggregation takes one prefill device and one decode device")
-        if kwargs.get("tensor_parallel_size", 1) != 1:
-            raise ValueError("pd_disaggregation runs each side on one GPU (tensor_parallel_size=1)")
+        kwargs.pop("pd_role", None)
+        tp = kwargs.get("tensor_parallel_size", 1)
+        if len(pre) != tp or len(dec) != tp:
+            raise ValueError("pd_disaggregation needs tensor_parallel_size devices on each side")
         if kwargs.get("speculative_model"):
             raise ValueError("pd_disaggregation does not support a speculative draft model")
+        self.pd_stats = {"handoffs": 0, "blocks_pushed": 0, "blocks_reused": 0, "bytes_pushed": 0,
+                         "parked_steps": 0}
+        self._parked: list[Sequence] = []
+        self.last_step_events: dict = {}
+        self.remote = None
+        if tp > 1:
+            self._init_tensor_parallel(model, kwargs, pre, dec)
+            return
         self.prefill = LLMEngine(model, **kwargs, device_offset=pre[0], overlap_decode=False)
         self.decode = LLMEngine(model, **kwargs, device_offset=dec[0])
         self.decode.request_metrics = self.prefill.request_metrics
@@ -67,20 +220,45 @@ class PDEngine:
         self.tokenizer = self.prefill.tokenizer
         self.model_runner = _RunnerPair(self.prefill.model_runner, self.decode.model_runner)
         self.request_metrics = self.prefill.request_metrics
-        self.last_step_events: dict = {}
-        self._parked: list[Sequence] = []
-        self.pd_stats = {"handoffs": 0, "blocks_pushed": 0, "blocks_reused": 0, "bytes_pushed": 0,
-                         "parked_steps": 0}
         pr, dr = self.prefill.model_runner, self.decode.model_runner
         self._cuda = pr.is_cuda
         if pr.k_cache.shape[0] != dr.k_cache.shape[0] or pr.k_cache.shape[2:] != dr.k_cache.shape[2:]:
             raise ValueError("prefill and decode KV pools have different block shapes")
+
+    def _init_tensor_parallel(self, model, kwargs, pre, dec):
+        from llmserve_b200.engine.llm_engine import LLMEngine
+        p = len(pre)
+        if pre != tuple(range(pre[0], pre[0] + p)) or dec != tuple(range(dec[0], dec[0] + p)):
+            raise ValueError("each side of a tensor-parallel pair takes consecutive GPUs")
+        timeout = float(kwargs.get("comm_timeout_s", 120.0))
+        tag = f"{os.getpid()}_{id(self)}"
+        dkw = dict(kwargs, device_offset=dec[0], pd_role="decode", rpc_channel=f"llmserve_b200_pdd_{tag}",
+                   distributed_init_method=f"tcp://127.0.0.1:{_free_port()}")
+        self.remote = _RemoteDecode(model, dkw, timeout)
+        descs, self.decode_blocks = self.remote.ready
+        try:
+            self.prefill = LLMEngine(model, **dict(kwargs, rpc_channel=f"llmserve_b200_pdp_{tag}",
+                                                   distributed_init_method=f"tcp://127.0.0.1:{_free_port()}"),
+                                     device_offset=pre[0], overlap_decode=False)
+            self.prefill.model_runner.call("open_peer_kv", descs)
+        except Exception:
+            self.remote.close()
+            raise
+        self.decode = None
+        self.config = self.prefill.config
+        self.tokenizer = self.prefill.tokenizer
+        self.request_metrics = self.prefill.request_metrics
+        self.model_runner = _RemoteRunnerPair(self.prefill.model_runner, self.remote)
+        self._remote_seqs: dict = {}
+        self._cuda = self.prefill.model_runner.is_cuda
 
     # ---- API --------------------------------------------------------------------------------
     def add_request(self, prompt, sampling_params) -> int:
         return self.prefill.add_request(prompt, sampling_params)
 
     def is_finished(self) -> bool:
+        if self.remote is not None:
+            return self.prefill.is_finished() and not self._parked and not self._remote_seqs
         return self.prefill.is_finished() and self.decode.is_finished() and not self._parked
 
     def _on(self, engine):
@@ -96,6 +274,8 @@ class PDEngine:
             outputs += done
             tokens += n
             self._park_new_first_tokens()
+        if self.remote is not None:
+            return self._remote_step(t0, outputs, tokens)
         self._handoff()
         if not self.decode.is_finished():
             with self._on(self.decode):
@@ -120,19 +300,88 @@ class PDEngine:
         return [{"text": self.tokenizer.decode(done[k]), "token_ids": done[k]} for k in sorted(done)]
 
     def get_metrics(self) -> dict:
-        m = self.decode.get_metrics()
-        m["summary"]["kv_cache_prefill"] = self.prefill.get_metrics()["summary"]["kv_cache"]
+        if self.remote is not None:
+            m = self.prefill.get_metrics()
+            m["summary"]["kv_cache_prefill"] = m["summary"]["kv_cache"]
+            m["summary"]["kv_cache"] = self.remote.call("kv_metrics")
+        else:
+            m = self.decode.get_metrics()
+            m["summary"]["kv_cache_prefill"] = self.prefill.get_metrics()["summary"]["kv_cache"]
         m["summary"]["pd"] = dict(self.pd_stats, parked=len(self._parked))
         return m
 
     def reset_metrics(self):
         self.prefill.reset_metrics()
-        self.decode.reset_metrics()
+        if self.decode is not None:
+            self.decode.reset_metrics()
         self.pd_stats = dict.fromkeys(self.pd_stats, 0)
 
     def exit(self):
+        if self.remote is not None:
+            try:
+                self.remote.close()
+            finally:
+                self.prefill.exit()
+            return
         self.decode.exit()
         self.prefill.exit()
+
+    # ---- tensor-parallel pair ---------------------------------------------------------------
+    def _remote_step(self, t0, outputs, tokens):
+        self._remote_handoff()
+        if self._remote_seqs:
+            done, emitted, n = self.remote.call("step")
+            t = perf_counter()
+            tokens += n
+            for sid in emitted:
+                m = self.request_metrics.get(sid)
+                if m is not None:
+                    m["token_times"].append(t)
+                    m["output_event_times"].append(t)
+                    m["output_tokens"] += 1
+            for sid, toks in done:
+                m = self.request_metrics.get(sid)
+                if m is not None:
+                    m["finish_time"], m["success"], m["output_tokens"] = t, True, len(toks)
+                self._remote_seqs.pop(sid, None)
+                outputs.append((sid, toks))
+        self.last_step_events = {"step_start": t0, "step_end": perf_counter(), "num_tokens": tokens,
+                                 "prefill": self.prefill.last_step_events, "parked": len(self._parked),
+                                 "decoding": len(self._remote_seqs)}
+        return outputs, tokens
+
+    def _remote_handoff(self):
+        if not self._parked:
+            return
+        items = [(s.seq_id, list(s.token_ids), s.num_prompt_tokens, s.max_tokens, s.ignore_eos, s.temperature)
+                 for s in self._parked]
+        reserved = self.remote.call("reserve", items)
+        if not reserved:
+            self.pd_stats["parked_steps"] += 1
+            return
+        pre_r = self.prefill.model_runner
+        bs = self.prefill.scheduler.block_manager.block_size
+        src, dst, moved = [], [], []
+        for (sid, table, hits), s in zip(reserved, list(self._parked)):
+            n_kv_blocks = -(-(len(s) - 1) // bs)
+            src += s.block_table[hits:n_kv_blocks]
+            dst += table[hits:n_kv_blocks]
+            self.pd_stats["blocks_reused"] += min(hits, n_kv_blocks)
+            moved.append(s)
+        if src:
+            pre_r.call("push_kv", src, dst)          # every prefill rank pushes its KV-head shard
+            if pre_r.channel is not None:
+                pre_r.channel.wait_acks(self.remote.timeout_s)
+        bm = self.prefill.scheduler.block_manager
+        for s in moved:
+            bm.deallocate(s)                          # after every rank's copy landed
+            self._parked.remove(s)
+            self._remote_seqs[s.seq_id] = s
+        self.remote.call("admit", [s.seq_id for s in moved])
+        per_block = 2 * pre_r.k_cache[:, 0].numel() * pre_r.k_cache.element_size() * pre_r.world_size
+        self.pd_stats["handoffs"] += len(moved)
+        self.pd_stats["blocks_pushed"] += len(src)
+        self.pd_stats["bytes_pushed"] += len(src) * per_block
 
     # ---- handoff ----------------------------------------------------------------------------
     def _park_new_first_tokens(self):

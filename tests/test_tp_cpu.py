@@ -52,6 +52,28 @@ def test_tp2_gloo_matches_tp1_with_and_without_speculation(ckpts):
     assert _gen(tgt, 2, draft) == ref
 
 
+def test_disaggregated_tp2_prefill_tp2_decode_over_gloo(ckpts):
+    """Prefill TP=2 (this process + a worker) and decode TP=2 (a server process + its worker), KV
+    blocks pushed rank to rank into the decode pools (shared segments on the CPU tier): the tokens
+    equal a single TP=1 engine's."""
+    tgt, _ = ckpts
+    ref = _gen(tgt, 1)
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, 1024, (int(n),), generator=g).tolist() for n in (9, 33, 17, 50)]
+    llm = LLM(tgt, device="cpu", enforce_eager=True, num_kvcache_blocks=64, kvcache_block_size=16, max_model_len=256,
+              tensor_parallel_size=2, comm_timeout_s=60, pd_disaggregation=True, pd_prefill_devices=(0, 1),
+              pd_decode_devices=(2, 3))
+    try:
+        llm.model_runner.sampler = GreedySampler()
+        out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=12, ignore_eos=True))]
+        m = llm.get_metrics()["summary"]
+    finally:
+        llm.exit()
+    assert out == ref
+    assert m["pd"]["handoffs"] == 4 and m["pd"]["blocks_pushed"] > 0 and m["num_finished"] == 4
+    assert m["total_output_tokens"] == 48
+
+
 def test_tp2_gloo_temperature_sampling_is_rank_consistent(ckpts):
     tgt, _ = ckpts
     llm = LLM(tgt, device="cpu", enforce_eager=True, num_kvcache_blocks=64, kvcache_block_size=16, max_model_len=256,
