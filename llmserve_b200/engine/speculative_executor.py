@@ -196,11 +196,13 @@ class SpeculativeExecutor:
             sel = torch.tensor(fresh, dtype=torch.int64, device=dev)
             start_ids[sel] = toks
             start_aux[sel] = aux
-        for i in range(B):
-            if merged[i]:
-                tok, a = self.prev_correction[seqs[i].seq_id]
-                start_ids[i] = tok
-                start_aux[i] = a
+        carried = [i for i in range(B) if merged[i]]
+        if carried:
+            # one gather for every carried correction token and aux row (not two copies per sequence)
+            prev = [self.prev_correction[seqs[i].seq_id] for i in carried]
+            sel = torch.tensor(carried, dtype=torch.int64, device=dev)
+            start_ids[sel] = torch.tensor([p[0] for p in prev], dtype=torch.int64, device=dev)
+            start_aux[sel] = torch.stack([p[1] for p in prev]).to(start_aux.dtype)
         target_decode_time = perf_counter() - t
 
         kv0 = [self.draft_kv_len.get(s.seq_id, len(s)) for s in seqs]
