@@ -23,6 +23,7 @@ from llmserve_b200.engine.model_runner import ModelRunner
 from llmserve_b200.engine.scheduler import Scheduler
 from llmserve_b200.engine.sequence import Sequence
 from llmserve_b200.sampling_params import SamplingParams
+from llmserve_b200.utils.nvtx import nvtx_range
 from llmserve_b200.utils.tokenizer import load_tokenizer
 
 _engine_ids = itertools.count()
@@ -186,10 +187,15 @@ class LLMEngine:
         }
 
     def step(self):
+        with nvtx_range("llmserve.step"):
+            return self._step()
+
+    def _step(self):
         if self._inflight is not None:
             return self._overlapped_step()
         step_start = perf_counter()
-        out = self.scheduler.schedule()
+        with nvtx_range("schedule"):
+            out = self.scheduler.schedule()
         seqs = out.scheduled_seqs
         if self._can_run_speculative_step(out):
             reserve = self.model_runner.speculative_gamma + 2

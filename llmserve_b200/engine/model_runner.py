@@ -444,6 +444,34 @@ class ModelRunner:
         return out
 
     # ---- step metadata -----------------------------------------------------------------------
+    def check_bounds(self, seqs: list[Sequence], positions, slots):
+        """``Config.debug_bounds_checks``: validate a step's metadata on the host before any
+        kernel sees it -- every block id inside the pool, every position inside the sequence's
+        blocks, every slot either -1 (skip) or inside the pool and equal to the block-table slot of
+        its position.  Raises ValueError naming the sequence; a no-op when the option is off."""
+        if not self.config.debug_bounds_checks:
+            return
+        nb, bsz = self.config.num_kvcache_blocks, self.block_size
+        positions = np.asarray(positions, dtype=np.int64).reshape(-1)
+        slots = np.asarray(slots, dtype=np.int64).reshape(-1)
+        if positions.shape != slots.shape:
+            raise ValueError("bounds check: positions and slots differ in length")
+        per = len(positions) // max(len(seqs), 1) if len(seqs) and len(positions) % len(seqs) == 0 else None
+        for s in seqs:
+            bad = [b for b in s.block_table if not 0 <= b < nb]
+            if bad:
+                raise ValueError(f"bounds check: sequence {s.seq_id} holds block ids {bad} outside 0..{nb - 1}")
+        if ((slots < -1) | (slots >= nb * bsz)).any():
+            raise ValueError(f"bounds check: slot outside the pool of {nb * bsz} slots: {slots.min()}..{slots.max()}")
+        if per is not None:
+            for i, s in enumerate(seqs):
+                for p, sl in zip(positions[i * per:(i + 1) * per], slots[i * per:(i + 1) * per]):
+                    if p < 0 or p // bsz >= len(s.block_table):
+                        raise ValueError(f"bounds check: sequence {s.seq_id} position {p} beyond its "
+                                         f"{len(s.block_table)} blocks")
+                    if sl >= 0 and sl != s.block_table[p // bsz] * bsz + p % bsz:
+                        raise ValueError(f"bounds check: sequence {s.seq_id} position {p} maps to slot {sl}")
+
     def prepare_block_tables(self, seqs: list[Sequence]) -> torch.Tensor:
         width = max(1, max(len(s.block_table) for s in seqs))
         rows = np.zeros((len(seqs), width), dtype=np.int32)
@@ -478,6 +506,9 @@ class ModelRunner:
             max_q, max_k = max(max_q, q), max(max_k, end)
         d = self.device
         slot_arr = np.concatenate(slots)
+        if self.config.debug_bounds_checks:
+            for s, sl, end in zip(seqs, slots, lens_k):
+                self.check_bounds([s], np.arange(end - len(sl), end), sl)
         self.h2d_bytes += 16 * len(ids) + 4 * len(slot_arr) + 16 * len(seqs) + 8
         set_context(
             True,
@@ -503,6 +534,7 @@ class ModelRunner:
             ids[i], pos[i], lens[i] = s.last_token, L - 1, L
             slots[i] = s.block_table[(L - 1) // self.block_size] * self.block_size + (L - 1) % self.block_size
         d = self.device
+        self.check_bounds(seqs, pos, slots)
         self.h2d_bytes += ids.nbytes + pos.nbytes + slots.nbytes + lens.nbytes
         set_context(False, slot_mapping=_to_device(slots, torch.int32, d), context_lens=_to_device(lens, torch.int32, d),
                     block_tables=self.prepare_block_tables(seqs), decode_workspace=self.decode_workspace)
@@ -647,6 +679,7 @@ class ModelRunner:
         blocks = np.fromiter((s.block_table[p // bsz] for s, p in zip(seqs, positions.tolist())), dtype=np.int32,
                              count=bs)
         a[2 * max_bs:2 * max_bs + bs] = blocks * bsz + positions % bsz
+        self.check_bounds(seqs, positions, a[2 * max_bs:2 * max_bs + bs])
         a[3 * max_bs:3 * max_bs + bs] = positions + 1
         a[4 * max_bs:4 * max_bs + bs] = feed
         tables = a[5 * max_bs:].reshape(max_bs, W)

@@ -32,6 +32,7 @@ from llmserve_b200.speculative.tree import build_fixed_tree_topology, select_gre
 from llmserve_b200.speculative.types import SpeculativeDecodeOutput
 from llmserve_b200.utils.context import reset_context, set_context
 from llmserve_b200.utils.loader import seed_for
+from llmserve_b200.utils.nvtx import nvtx_range
 
 
 def _mask_bits(mask: torch.Tensor) -> torch.Tensor:
@@ -214,7 +215,8 @@ class SpeculativeExecutor:
         temps = torch.tensor([s.temperature for s in seqs], device=dev).unsqueeze(1)
         for depth in range(g):
             ts = perf_counter()
-            hidden, logits = self._draft_decode(seqs, cur_ids, cur_in, [k + depth for k in kv0])
+            with nvtx_range(f"draft.{depth}"):
+                hidden, logits = self._draft_decode(seqs, cur_ids, cur_in, [k + depth for k in kv0])
             fwd_time += perf_counter() - ts
             ts = perf_counter()
             if greedy:
@@ -241,8 +243,9 @@ class SpeculativeExecutor:
                     block_tables=r.prepare_block_tables(seqs),
                     seqlens_k=torch.tensor([b + n for b in base], dtype=torch.int32, device=dev))
         try:
-            hidden, aux = r.model.forward_with_eagle3_aux(vin, vpos)
-            logits = r.model.compute_logits(hidden, all_tokens=True)
+            with nvtx_range("verify"):
+                hidden, aux = r.model.forward_with_eagle3_aux(vin, vpos)
+                logits = r.model.compute_logits(hidden, all_tokens=True)
         finally:
             reset_context()
         verify_time = perf_counter() - t

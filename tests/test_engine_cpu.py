@@ -203,3 +203,28 @@ def test_pd_disaggregation_matches_single_engine(ckpts):
         assert m["pd"]["handoffs"] == 7 and m["pd"]["blocks_pushed"] > 0 and m["num_finished"] == 7
         if blocks == 64:
             assert m["pd"]["blocks_reused"] >= 1
+
+
+def test_debug_bounds_checks_catch_bad_metadata(ckpts):
+    """``debug_bounds_checks``: a block id outside the pool or a slot that disagrees with the
+    block table is reported on the host before any kernel runs; the same run without corruption
+    passes the checks and matches the unchecked run."""
+    tgt, _ = ckpts
+    prompts = _prompts(3, seed=9)
+    base, _ = _run(tgt, prompts, max_tokens=10)
+    checked, _ = _run(tgt, prompts, max_tokens=10, debug_bounds_checks=True)
+    assert checked == base
+    llm = LLM(tgt, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=64,
+              debug_bounds_checks=True)
+    llm.model_runner.sampler = GreedySampler()
+    llm.add_request(prompts[0], SamplingParams(max_tokens=10, ignore_eos=True))
+    llm.step()                                   # prefill
+    seq = llm.scheduler.running[0]
+    seq.block_table[0] = 64                      # one past the pool
+    with pytest.raises(ValueError, match="outside"):
+        llm.step()
+    seq.block_table[0] = 0
+    r = llm.model_runner
+    with pytest.raises(ValueError, match="maps to slot"):
+        r.check_bounds([seq], [len(seq) - 1], [5])
+    llm.exit()

@@ -221,3 +221,12 @@ def test_packed_greedy_accept_matches_per_sequence_rule():
         r = greedy_accept_from_ids(target[i].tolist(), draft[i].tolist())
         assert packed[i, 0] == r.num_accepted and packed[i, 1] == r.final_token_id
         assert packed[i, 2] == i and packed[i, 3:].tolist() == draft[i].tolist()
+
+
+def test_nvtx_ranges_are_noops_when_disabled_or_without_cuda(monkeypatch):
+    from llmserve_b200.utils import nvtx
+    with nvtx.nvtx_range("x"):
+        pass
+    monkeypatch.setattr(nvtx, "ENABLED", True)
+    with nvtx.nvtx_range("x"):          # no CUDA here: still a no-op
+        pass
