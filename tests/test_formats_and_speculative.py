@@ -230,3 +230,18 @@ def test_nvtx_ranges_are_noops_when_disabled_or_without_cuda(monkeypatch):
     monkeypatch.setattr(nvtx, "ENABLED", True)
     with nvtx.nvtx_range("x"):          # no CUDA here: still a no-op
         pass
+
+
+def test_engine_imports_without_triton_flash_attn_or_vllm():
+    """The engine never needs Triton, flash-attn, FlashInfer or vLLM (reference test:
+    ``tests/test_optional_dependencies.py``)."""
+    import subprocess
+    import sys
+    code = ("import sys\n"
+            "for m in ('triton', 'flash_attn', 'flashinfer', 'vllm'): sys.modules[m] = None\n"
+            "import llmserve_b200, llmserve_b200.engine.llm_engine, llmserve_b200.engine.pd_engine\n"
+            "import llmserve_b200.quantization.awq_calibration, benchmarks.serve\n"
+            "from llmserve_b200 import LLM, SamplingParams\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
