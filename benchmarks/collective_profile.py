@@ -1,0 +1,118 @@
+"""Row-parallel projection + TP reduction + residual + RMSNorm: fused NVLink kernel vs NCCL.
+
+``torchrun --nproc-per-node N -m benchmarks.collective_profile [--tokens 1,16,64] [--hidden 4096]
+[--inner 4096] [--iters 50]``  (N = 2..8, one process per GPU, NCCL for set-up)
+
+For each token count T every rank runs the o_proj-shaped step of one decoder layer on its shard
+(x [T, inner / N] @ W [hidden, inner / N]^T) followed by the reduction over ranks, the residual
+add and the RMSNorm:
+
+* ``fused``   -- the engine's path: tcgen05 GEMM writing split-K partials into the peer-mapped
+  buffer, then ``fused_allreduce_add_rmsnorm`` (reduce-scatter over NVLink peer loads, norm,
+  all-gather by peer stores) -- ``FusedComm.row_parallel_add_norm``;
+* ``nccl``    -- the baseline: the same GEMM (bf16 output), ``dist.all_reduce``, add+RMSNorm kernel;
+* ``gemm``    -- the GEMM alone, to separate the collective's share.
+
+Times are CUDA events on each rank around ``--iters`` back-to-back calls (after warm-up), the max
+over ranks is reported.  The roofline of the fused step is the slowest of its weight bytes at the
+measured HBM bandwidth, its FLOPs at the measured bf16 peak, and the bytes that cross NVLink per
+rank at the measured 770 GB/s per direction (``roofline_us``); ``fraction`` = roofline / achieved.
+"""
+import argparse
+import json
+import os
+
+NVLINK_GBS = 770.0           # measured peer copy, per direction per GPU
+
+
+def fused_roofline_us(T: int, hidden: int, inner_shard: int, world: int, splits: int, hbm_gbs: float,
+                      bf16_tflops: float, nvlink_gbs: float = NVLINK_GBS) -> dict:
+    """Lower bound of one fused row-parallel step on one rank (µs) and its three terms."""
+    rows = -(-T // world)
+    weight_bytes = hidden * inner_shard * 2
+    flops = 2.0 * T * hidden * inner_shard
+    # reads the other ranks' fp32 partial planes of its rows, pushes its finished rows (normed
+    # output + residual, bf16) to the other ranks
+    link_bytes = (world - 1) * rows * hidden * (4 * splits + 2 * 2)
+    terms = {"hbm_us": weight_bytes / (hbm_gbs * 1e3), "compute_us": flops / (bf16_tflops * 1e6),
+             "nvlink_us": link_bytes / (nvlink_gbs * 1e3)}
+    return dict(terms, roofline_us=max(terms.values()), nvlink_bytes=link_bytes, weight_bytes=weight_bytes)
+
+
+def _peaks():
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0
+
+
+def main(argv=None):
+    import torch
+    import torch.distributed as dist
+
+    from llmserve_b200.ops import gemm, norm as norm_ops
+    from llmserve_b200.parallel import state as tp
+    from llmserve_b200.parallel.comm import FusedComm
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--tokens", default="1,16,64")
+    p.add_argument("--hidden", type=int, default=4096)
+    p.add_argument("--inner", type=int, default=4096)
+    p.add_argument("--iters", type=int, default=50)
+    args = p.parse_args(argv)
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    tp.init_tensor_parallel(rank, world, "env://", dev, 120.0)
+    tokens = [int(t) for t in args.tokens.split(",")]
+    comm = FusedComm.create(dev, args.hidden, max(tokens))
+    hbm, peak = _peaks()
+    k = args.inner // world
+    g = torch.Generator(device=dev).manual_seed(rank)
+    w = gemm.pack_weight((torch.randn(args.hidden, k, device=dev, generator=g) * 0.02).bfloat16())
+    nw = torch.ones(args.hidden, device=dev).bfloat16()
+
+    def timed(fn):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) * 1e3 / args.iters], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t)
+
+    with torch.inference_mode():
+        for T in tokens:
+            x = torch.randn(T, k, device=dev, generator=g).bfloat16()
+            res = torch.randn(T, args.hidden, device=dev, generator=g).bfloat16()
+            splits = min(gemm.splits_for(T, w, streamk=False), 8)
+            row = {"tokens": T, "world": world, "hidden": args.hidden, "inner_shard": k, "splits": splits}
+            if comm is not None and comm.can_handle(T, args.hidden):
+                row["fused_us"] = timed(lambda: comm.row_parallel_add_norm(x, w, res, nw, 1e-6))
+            row["gemm_us"] = timed(lambda: gemm.linear_partials(x, w, splits, streamk=False))
+
+            def nccl():
+                y = gemm.linear(x, w)
+                dist.all_reduce(y)
+                norm_ops.add_rms_norm(y, res, nw, 1e-6)
+            row["nccl_us"] = timed(nccl)
+            row.update(fused_roofline_us(T, args.hidden, k, world, splits, hbm, peak))
+            if "fused_us" in row:
+                row["fraction_of_roofline"] = row["roofline_us"] / row["fused_us"]
+            if rank == 0:
+                print(json.dumps(row), flush=True)
+    if comm is not None:
+        comm.close()
+    tp.destroy_tensor_parallel()
+
+
+if __name__ == "__main__":
+    main()
