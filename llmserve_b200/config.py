@@ -16,6 +16,10 @@ are grouped at the end:
 * ``distributed_launcher`` -- ``"spawn"``: rank 0 starts the TP workers itself (reference
                               behaviour); ``"external"``: ranks were started by torchrun and
                               ranks > 0 call :func:`llmserve_b200.engine.llm_engine.run_worker`.
+* ``overlap_decode``       -- launch decode step N+1 from device-resident tokens before step N is
+                              read on the host (greedy, graph decode); on by default.
+
+``awq_backend="triton"`` is accepted for compatibility and runs the sm_100a W4A16 kernel.
 """
 import json
 import os
@@ -120,8 +124,11 @@ class Config:
                 raise ValueError("tree speculation requires gamma=3 and greedy acceptance")
             if self.speculative_model is None:
                 raise ValueError("tree speculation requires a speculative_model")
-        if self.awq_backend not in ("reference", "cuda"):
-            raise ValueError("awq_backend must be 'reference' or 'cuda'")
+        if self.awq_backend not in ("reference", "triton", "cuda"):
+            raise ValueError("awq_backend must be 'reference', 'triton', or 'cuda'")
+        if self.awq_backend == "triton":
+            # the reference's Triton W4A16 kernels are replaced by the sm_100a kernel here
+            self.awq_backend = "cuda"
         if self.device not in ("cuda", "cpu"):
             raise ValueError("device must be 'cuda' or 'cpu'")
         if self.distributed_launcher not in ("spawn", "external"):
