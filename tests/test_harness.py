@@ -233,3 +233,24 @@ def test_run_point_with_real_cpu_engines_plain_and_disaggregated(tmp_path):
         result = run_point(point, path, engine_factory=factory, metadata={"git_commit": "abc"})
         assert result["complete"], point["variant"]
         assert result["metrics"]["throughput"]["output_tokens_per_second"] > 0
+
+
+def test_b200_suite_pd_variant_reaches_the_engine_factory():
+    """The disaggregated variant of the B200 suite passes its device split and the overlapped-loop
+    default through ``run_point`` to the engine constructor."""
+    suite = json.load(open("benchmarks/suites/b200-serving.json"))
+    points = [p for p in expand_suite(suite) if p["experiment"] == "pd-closed-loop-1p1d"]
+    assert {p["variant"] for p in points} == {"baseline", "pd"}
+    seen = {}
+    clock = FakeClock()
+
+    def factory(model, **kw):
+        seen[kw.get("pd_disaggregation")] = kw
+        return FakeEngine(clock)
+
+    for p in points[:2]:
+        p = dict(p, warmup_seconds=0.05, measurement_seconds=0.1)
+        run_point(p, "/models/tiny", engine_factory=factory, make_sampling_params=_sp, clock=clock, sleep=clock.sleep,
+                  metadata={"git_commit": "abc"})
+    assert seen[True]["pd_prefill_devices"] == [0] and seen[True]["pd_decode_devices"] == [1]
+    assert seen[False]["overlap_decode"] is True and seen[False]["pd_disaggregation"] is False
