@@ -194,3 +194,34 @@ def test_process_group_timeout_ends_collective_after_rank_loss():
         p.join(30)
     assert res[1] == "left"
     assert res[0].startswith("error")
+
+
+def test_disaggregated_decode_server_loss_surfaces_as_an_error(ckpts):
+    """Host fault injection: the decode side of a tensor-parallel disaggregated pair dies between
+    steps (its server process is killed); the next step raises a clear error instead of hanging,
+    and the decode server's own worker exits on its own (orphan check)."""
+    tgt, _ = ckpts
+    llm = LLM(tgt, device="cpu", enforce_eager=True, num_kvcache_blocks=64, kvcache_block_size=16, max_model_len=256,
+              tensor_parallel_size=2, comm_timeout_s=20, pd_disaggregation=True, pd_prefill_devices=(0, 1),
+              pd_decode_devices=(2, 3))
+    try:
+        llm.model_runner.sampler = GreedySampler()
+        llm.add_request(list(range(5, 30)), SamplingParams(max_tokens=8, ignore_eos=True))
+        llm.step()                                # prefill + handoff + first decode step
+        import psutil
+        workers = psutil.Process(llm.remote.proc.pid).children(recursive=True)
+        llm.remote.proc.kill()                    # the server process this engine started
+        llm.remote.proc.join(timeout=30)
+        t0 = time.monotonic()
+        with pytest.raises((RuntimeError, TimeoutError, EOFError, BrokenPipeError, ConnectionError)):
+            while not llm.is_finished():
+                llm.step()
+        assert time.monotonic() - t0 < 60
+        # the server's tensor-parallel worker notices its parent is gone and leaves by itself
+        _, alive = psutil.wait_procs(workers, timeout=60)
+        assert not alive, [w.pid for w in alive]
+    finally:
+        try:
+            llm.prefill.exit()
+        except Exception:
+            pass
