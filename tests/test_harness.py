@@ -180,9 +180,15 @@ def test_suite_expansion_ids_and_aggregate():
 
 def test_suite_expansion_matches_reference():
     ref = _ref_bench("suite")
-    for name in ("smoke", "formal-closed-loop", "formal-poisson"):
+    import os
+    ref_suites = os.path.join(os.path.dirname(os.path.dirname(ref.__file__)), "benchmarks", "suites")
+    for name in ("smoke", "formal-closed-loop", "formal-poisson", "pilot", "awq-capacity-confirm"):
         suite = json.load(open(f"benchmarks/suites/{name}.json"))
         assert expand_suite(suite) == ref.expand_suite(suite)
+        # the experiment definitions behind the published numbers are the same
+        if name != "smoke" and os.path.exists(os.path.join(ref_suites, f"{name}.json")):
+            with open(os.path.join(ref_suites, f"{name}.json")) as f:
+                assert json.load(f) == suite, name
 
 
 def test_execute_suite_records_failures_and_continues(tmp_path):
