@@ -26,7 +26,13 @@ from llmserve_b200.ops import attention as attn_ops
 from llmserve_b200.ops import norm as norm_ops
 from llmserve_b200.ops import rope as rope_ops
 from llmserve_b200.ops.rope import build_cos_sin_cache
-from llmserve_b200.utils.context import get_context
+from llmserve_b200.speculative.draft import (  # noqa: F401  (offline API, importable from here as in the reference)
+    DraftKVPool, DraftKVRef, generate_eagle3_draft_tokens, generate_eagle3_draft_tokens_batched,
+    run_eagle3_offline_step, run_eagle3_speculative_cycle, run_eagle3_target_verify)
+from llmserve_b200.speculative.sampling import (  # noqa: F401
+    sample_from_logits, speculative_accept_greedy_from_logits, speculative_accept_reject_from_logits)
+from llmserve_b200.speculative.types import Eagle3DraftOutput
+from llmserve_b200.utils.context import get_context, reset_context, set_context
 
 
 def normalize_eagle3_config(config: dict) -> dict:
@@ -258,6 +264,48 @@ class Eagle3Speculator(nn.Module):
         fused = aux_hidden if aux_hidden.shape[-1] == self.hidden_size else self.fc(aux_hidden)
         hidden = self.midlayer(embeds, fused, positions)
         return hidden, self.lm_head(self.norm(hidden))
+
+    @torch.inference_mode()
+    def propose(self, input_ids, aux_hidden, positions, temperature: float, past_kv=None, kv_valid_lens=None):
+        """One offline draft step for B requests (``llmserve/models/eagle3.py:345-364`` of the
+        reference): ids and positions ``[B, 1]``, ``aux_hidden`` ``[B, 1, 3*Ht or H]``.
+
+        The step's K/V goes to a paged :class:`DraftKVPool` (a new one when ``past_kv`` is None;
+        otherwise the rows of the given :class:`DraftKVRef`, first cut to ``kv_valid_lens`` when
+        given), and attention runs through the same store and decode-attention kernels as the
+        engine's draft.  The engine's own pool binding is restored afterwards.  Tokens are sampled
+        from the target-vocabulary logits at ``temperature`` (draft argmax when it is 0)."""
+        ids = input_ids.reshape(-1).long()
+        B = ids.numel()
+        dev = ids.device
+        if past_kv is None:
+            pool = DraftKVPool.for_model(self, dev)
+            past_kv = DraftKVRef(pool, pool.new_rows(B))
+        pool, rows = past_kv.pool, list(past_kv.rows)
+        if len(rows) != B:
+            raise ValueError(f"{B} draft inputs for {len(rows)} K/V rows")
+        if kv_valid_lens is not None:
+            for r, n in zip(rows, kv_valid_lens.reshape(-1).tolist()):
+                pool.set_length(r, int(n))
+        slots = pool.append_slots(rows)
+        attn = self.midlayer.self_attn
+        bound = attn.k_cache, attn.v_cache
+        attn.k_cache, attn.v_cache = pool.k, pool.v
+        set_context(False, slot_mapping=torch.tensor(slots, dtype=torch.int32, device=dev),
+                    context_lens=torch.tensor(past_kv.lengths, dtype=torch.int32, device=dev),
+                    block_tables=pool.block_table(rows, dev))
+        try:
+            hidden, logits = self(ids, aux_hidden.reshape(B, -1), positions.reshape(-1).long())
+        finally:
+            reset_context()
+            attn.k_cache, attn.v_cache = bound
+        target_logits = self.map_draft_logits(logits)
+        if temperature > 1e-10:
+            token_ids = sample_from_logits(target_logits, temperature)
+        else:
+            token_ids = self.greedy_sample(logits)
+        return Eagle3DraftOutput(hidden.unsqueeze(1), logits.unsqueeze(1), target_logits.unsqueeze(1),
+                                 token_ids.view(B, 1), DraftKVRef(pool, rows))
 
     def map_draft_logits(self, draft_logits: torch.Tensor) -> torch.Tensor:
         """Scatter draft-vocab logits into a -inf target-vocab row (rejection sampling)."""

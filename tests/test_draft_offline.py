@@ -1,0 +1,189 @@
+"""Offline EAGLE3 drafting API: the paged draft K/V pool, serial vs batched drafting with per-request
+gammas, contiguous-K/V draft models, one speculative cycle and one offline step."""
+import pytest
+import torch
+
+from llmserve_b200.models.eagle3 import Eagle3Speculator
+from llmserve_b200.models.synthetic import TINY, write_eagle3_checkpoint, write_qwen3_checkpoint
+from llmserve_b200.speculative.draft import (STAGES, DraftKVPool, DraftKVRef, generate_eagle3_draft_tokens,
+                                             generate_eagle3_draft_tokens_batched, run_eagle3_offline_step,
+                                             run_eagle3_speculative_cycle)
+from llmserve_b200.speculative.types import Eagle3DraftOutput
+from llmserve_b200.utils.context import reset_context, set_context
+
+
+@pytest.fixture(scope="module")
+def draft(tmp_path_factory):
+    root = tmp_path_factory.mktemp("draft")
+    tgt = write_qwen3_checkpoint(str(root / "t"), TINY)
+    model = Eagle3Speculator.from_pretrained(write_eagle3_checkpoint(str(root / "d"), TINY, 512), target_model_path=tgt)
+    model.prepare()
+    return model
+
+
+def _aux(batch, width, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(batch, 1, width, generator=g)
+
+
+def test_pool_slots_growth_trim_and_release():
+    pool = DraftKVPool(2, 8, block_size=4, num_blocks=1)
+    a, b = pool.new_rows(2)
+    slots = []
+    for _ in range(6):
+        slots += pool.append_slots([a, b])
+    assert pool.k.shape[0] >= 4 and len(set(slots)) == 12          # grew, no slot reused
+    assert pool.lengths[a] == pool.lengths[b] == 6
+    table = pool.block_table([a, b])
+    assert table.shape == (2, 2) and table.dtype == torch.int32
+    for r, row_slots in ((a, slots[0::2]), (b, slots[1::2])):
+        assert row_slots == [pool.blocks[r][p // 4] * 4 + p % 4 for p in range(6)]
+    free0 = len(pool.free)
+    pool.set_length(a, 3)
+    assert len(pool.blocks[a]) == 1 and len(pool.free) == free0 + 1
+    with pytest.raises(ValueError):
+        pool.set_length(a, 5)
+    pool.release(b)
+    assert b not in pool.blocks and len(pool.free) == free0 + 3
+
+
+def test_serial_draft_matches_one_causal_pass(draft):
+    """The paged decode steps give the same hidden states as one causal prefill over the same inputs."""
+    width = 3 * TINY["hidden_size"]
+    pool = DraftKVPool.for_model(draft, "cpu", block_size=2, num_blocks=1)      # forces growth
+    ref = DraftKVRef(pool, pool.new_rows(1))
+    start_aux = _aux(1, width, 0)
+    seq = generate_eagle3_draft_tokens(draft, 17, start_aux, 9, 4, 0.0, past_kv=ref, draft_sampling_mode="greedy")
+    assert len(seq.draft_token_ids) == 4 and seq.draft_target_logits.shape == (4, TINY["vocab_size"])
+    assert set(seq.proposal_timing) == set(STAGES)
+    assert seq.past_kv.lengths == [4]
+    # replay the four steps as one prefill: inputs are the start token and the drafted tokens, the
+    # start aux row then the draft's own hidden states
+    hs, toks = [], []
+    ids, aux, pos, past = torch.tensor([[17]]), start_aux, torch.tensor([[9]]), None
+    for _ in range(4):
+        out = draft.propose(ids, aux, pos, 0.0, past_kv=past)
+        hs.append(out.hidden_states[0, 0])
+        toks.append(int(out.token_ids))
+        ids, aux, pos, past = out.token_ids, out.hidden_states, pos + 1, out.past_kv
+    assert toks == seq.draft_token_ids
+    pool2 = DraftKVPool.for_model(draft, "cpu")
+    (row,) = pool2.new_rows(1)
+    slots = [pool2.append_slots([row])[0] for _ in range(4)]
+    fc_in = torch.cat([draft.fc(start_aux.reshape(1, -1)), torch.stack(hs[:3])])
+    attn = draft.midlayer.self_attn
+    bound = attn.k_cache, attn.v_cache
+    attn.k_cache, attn.v_cache = pool2.k, pool2.v
+    set_context(True, cu_seqlens_q=torch.tensor([0, 4], dtype=torch.int32), max_seqlen_q=4,
+                slot_mapping=torch.tensor(slots, dtype=torch.int32), seqlens_k=torch.tensor([4], dtype=torch.int32),
+                block_tables=pool2.block_table([row]))
+    try:
+        tokens = torch.tensor([17, *seq.draft_token_ids[:3]])
+        hidden, _ = draft(tokens, fc_in, torch.arange(9, 13))
+    finally:
+        reset_context()
+        attn.k_cache, attn.v_cache = bound
+    torch.testing.assert_close(hidden, torch.stack(hs), atol=1e-4, rtol=1e-4)
+    k_serial, _ = pool.gather(ref.rows[0])
+    k_prefill, _ = pool2.gather(row)
+    torch.testing.assert_close(k_serial, k_prefill, atol=1e-4, rtol=1e-4)
+
+
+def test_batched_equals_serial_with_per_request_gammas(draft):
+    width = 3 * TINY["hidden_size"]
+    aux = _aux(3, width, 1)
+    starts, positions, gammas = [5, 300, 77], [4, 11, 30], [3, 1, 2]
+    batch = generate_eagle3_draft_tokens_batched(draft, starts, aux, positions, 3, 0.0,
+                                                 draft_sampling_mode="greedy", gammas=gammas)
+    for i in range(3):
+        one = generate_eagle3_draft_tokens(draft, starts[i], aux[i:i + 1], positions[i], gammas[i], 0.0,
+                                           draft_sampling_mode="greedy")
+        assert batch[i].draft_token_ids == one.draft_token_ids
+        torch.testing.assert_close(batch[i].draft_target_logits, one.draft_target_logits, atol=1e-4, rtol=1e-4)
+        assert batch[i].past_kv.lengths == [gammas[i]]
+        assert set(batch[i].proposal_timing) == set(STAGES)
+    pools = {id(s.past_kv.pool) for s in batch}
+    assert len(pools) == 1                                         # one pool, one row per request
+    # a second round continues from the returned rows
+    more = generate_eagle3_draft_tokens_batched(draft, [s.draft_token_ids[-1] for s in batch], aux, positions, 1,
+                                                0.0, past_kv=[s.past_kv for s in batch],
+                                                draft_sampling_mode="greedy")
+    assert [m.past_kv.lengths[0] for m in more] == [g + 1 for g in gammas]
+    with pytest.raises(ValueError):
+        generate_eagle3_draft_tokens_batched(draft, [1, 2], aux[:2], [0, 0], 2, 0.0, gammas=[1, 0])
+
+
+class _ContiguousDraft:
+    """A test double with the reference's contiguous K/V: each step appends one position whose
+    value is the input token id; logits peak at ``input + 1``."""
+    vocab = 64
+
+    def __init__(self):
+        self.calls = []
+
+    def propose(self, input_ids, aux_hidden, positions, temperature, past_kv=None, kv_valid_lens=None):
+        self.calls.append((input_ids.reshape(-1).tolist(), aux_hidden.shape[-1],
+                           None if kv_valid_lens is None else kv_valid_lens.tolist(),
+                           None if past_kv is None else past_kv[0].shape[2]))
+        B = input_ids.shape[0]
+        new = input_ids.float().view(B, 1, 1, 1).expand(B, 1, 1, 2)
+        past = new.clone() if past_kv is None else torch.cat([past_kv[0], new], dim=2)
+        logits = torch.full((B, 1, self.vocab), -50.0)
+        logits[torch.arange(B), 0, (input_ids.reshape(-1) + 1) % self.vocab] = 50.0
+        return Eagle3DraftOutput(torch.ones(B, 1, 4), logits, logits, logits.argmax(-1), (past, past.clone()))
+
+    def greedy_sample(self, draft_logits):
+        return draft_logits.argmax(-1)
+
+
+def test_contiguous_kv_is_padded_and_split_per_request():
+    model = _ContiguousDraft()
+    past = [(torch.full((1, 1, 2, 2), 7.0),) * 2, None, (torch.full((1, 1, 5, 2), 9.0),) * 2]
+    out = generate_eagle3_draft_tokens_batched(model, [1, 10, 20], torch.zeros(3, 1, 12), [0, 0, 0], 2, 1.0,
+                                               past_kv=past, gammas=[2, 1, 2])
+    assert [o.draft_token_ids for o in out] == [[2, 3], [11], [21, 22]]
+    assert model.calls[0] == ([1, 10, 20], 12, [2, 0, 5], 5)        # padded to the longest, valid lengths
+    assert model.calls[1] == ([2, 21], 4, [3, 6], 6)                # request 1 has finished
+    k0 = out[0].past_kv[0][0, 0, :, 0].tolist()
+    assert k0 == [7.0, 7.0, 1.0, 2.0]                               # valid prefix + one new position per step
+    assert out[1].past_kv[0][0, 0, :, 0].tolist() == [10.0]
+    assert out[2].past_kv[0][0, 0, :, 0].tolist() == [9.0] * 5 + [20.0, 21.0]
+
+
+def test_offline_step_and_cycle(draft):
+    width = 3 * TINY["hidden_size"]
+    V = TINY["vocab_size"]
+
+    class Target:
+        """Verify logits that peak at the next input token, and at 7 after the last one."""
+
+        def __init__(self):
+            self.inputs = None
+
+        def parameters(self):
+            return iter([torch.zeros(1)])
+
+        def forward_with_eagle3_aux(self, input_ids, positions):
+            self.inputs = (input_ids.tolist(), positions.tolist())
+            return input_ids, torch.zeros(input_ids.numel(), width)
+
+        def compute_logits(self, hidden):
+            nxt = hidden.tolist()[1:] + [7]
+            logits = torch.full((len(nxt), V), -100.0)
+            logits[torch.arange(len(nxt)), torch.tensor(nxt)] = 100.0
+            return logits
+
+    target = Target()
+    torch.manual_seed(0)
+    res = run_eagle3_offline_step(target, draft, 3, _aux(1, width, 2), 20, 3, 1.0, random_values=torch.zeros(3))
+    assert target.inputs == ([3, *res.draft_token_ids], [20, 21, 22, 23])
+    assert res.sample_result.accepted_token_ids == res.draft_token_ids
+    assert res.sample_result.token_ids == res.draft_token_ids + [7]
+    assert res.past_kv.lengths == [3]
+
+    cyc = run_eagle3_speculative_cycle(draft, 3, _aux(1, width, 2), 20, torch.zeros(4, V), 3, 1.0,
+                                       random_values=torch.zeros(3))
+    assert cyc.sample_result.accepted_all and cyc.sample_result.num_accepted == 3
+    assert cyc.draft_target_logits.shape == (3, V)
+    with pytest.raises(ValueError):
+        run_eagle3_speculative_cycle(draft, 3, _aux(1, width, 2), 20, torch.zeros(3, V), 3, 1.0)
