@@ -29,6 +29,7 @@ from llmserve_b200.ops import sampling as sampling_ops
 from llmserve_b200.parallel import state as tp
 from llmserve_b200.speculative.sampling import greedy_accept_packed, speculative_accept_reject_from_logits
 from llmserve_b200.speculative.tree import build_fixed_tree_topology, select_greedy_tree_path
+from llmserve_b200.speculative.tree_kv import TreeKVCacheManager
 from llmserve_b200.speculative.types import SpeculativeDecodeOutput
 from llmserve_b200.utils.context import reset_context, set_context
 from llmserve_b200.utils.loader import seed_for
@@ -395,14 +396,11 @@ class SpeculativeExecutor:
         accept_time = perf_counter() - t
 
         t = perf_counter()
-        layers = [layer.self_attn.attn for layer in r.model.model.layers]
-        tk = torch.stack([a.tree_k for a in layers], 0)
-        tv = torch.stack([a.tree_v for a in layers], 0)
-        commit = res.commit_node_indices
+        manager = TreeKVCacheManager([layer.self_attn.attn for layer in r.model.model.layers],
+                                     k_cache=r.k_cache, v_cache=r.v_cache)
+        commit = [int(i) for i in res.commit_node_indices]
         slots = torch.tensor([seq.slot(base + j) for j in range(len(commit))], dtype=torch.int32, device=dev)
-        kv_ops.commit_tree_kv(tk, tv, r.k_cache, r.v_cache, torch.tensor(commit, dtype=torch.int32, device=dev), slots)
-        for a in layers:
-            a.tree_k = a.tree_v = torch.tensor([])
+        manager.commit(commit, slots)
         commit_time = perf_counter() - t
 
         t = perf_counter()

@@ -245,3 +245,43 @@ def test_engine_imports_without_triton_flash_attn_or_vllm():
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-2000:]
+
+
+# ---- tree K/V commit manager -------------------------------------------------------------------
+class _TreeLayer:
+    def __init__(self, values):
+        self.tree_k = torch.tensor(values, dtype=torch.float32).view(-1, 1, 1)
+        self.tree_v = self.tree_k + 10
+
+
+def test_tree_kv_manager_validates_and_always_clears():
+    from llmserve_b200.speculative.tree_kv import TreeKVCacheManager
+    layers = [_TreeLayer([1, 2, 3]), _TreeLayer([4, 5])]
+    with pytest.raises(ValueError, match="same shape"):
+        TreeKVCacheManager(layers).commit([0], torch.tensor([4], dtype=torch.int32))
+    assert all(layer.tree_k.numel() == 0 and layer.tree_v.numel() == 0 for layer in layers)
+    layer = _TreeLayer([1, 2, 3])
+    manager = TreeKVCacheManager([layer])
+    with pytest.raises(ValueError, match="slot count"):
+        manager.commit([0, 2], torch.tensor([4], dtype=torch.int32))
+    layer.tree_k = torch.tensor([1.0, 2.0, 3.0]).view(-1, 1, 1)
+    layer.tree_v = layer.tree_k + 10
+    with pytest.raises(ValueError, match="node index"):
+        manager.commit([0, 3], torch.tensor([4, 5], dtype=torch.int32))
+    assert layer.tree_k.numel() == 0
+    with pytest.raises(ValueError, match="capture"):
+        manager.commit([0], torch.tensor([4], dtype=torch.int32))
+    with pytest.raises(ValueError):
+        TreeKVCacheManager([])
+
+
+def test_tree_kv_manager_commits_selected_nodes_of_every_layer():
+    from llmserve_b200.speculative.tree_kv import TreeKVCacheManager
+    layers = [_TreeLayer([1, 2, 3]), _TreeLayer([4, 5, 6])]
+    k_cache = torch.zeros(2, 2, 1, 4, 1)                 # [layers, blocks, kv_heads, block_size, head_dim]
+    v_cache = torch.zeros_like(k_cache)
+    TreeKVCacheManager(layers, k_cache=k_cache, v_cache=v_cache).commit([0, 2], torch.tensor([5, 6], dtype=torch.int32))
+    assert k_cache[:, 1, 0, 1:3, 0].tolist() == [[1.0, 3.0], [4.0, 6.0]]
+    assert v_cache[:, 1, 0, 1:3, 0].tolist() == [[11.0, 13.0], [14.0, 16.0]]
+    assert k_cache[:, 0].abs().sum() == 0
+    assert all(layer.tree_k.numel() == 0 for layer in layers)
