@@ -285,3 +285,41 @@ def test_tree_kv_manager_commits_selected_nodes_of_every_layer():
     assert v_cache[:, 1, 0, 1:3, 0].tolist() == [[11.0, 13.0], [14.0, 16.0]]
     assert k_cache[:, 0].abs().sum() == 0
     assert all(layer.tree_k.numel() == 0 for layer in layers)
+
+
+# ---- Qwen3 auxiliary hidden states for EAGLE3 ----------------------------------------------------
+def test_eagle3_aux_layers_are_the_residual_streams_entering_the_chosen_layers():
+    from torch import nn
+
+    from llmserve_b200.models.qwen3 import Qwen3Model, get_eagle3_aux_layer_ids
+    assert get_eagle3_aux_layer_ids(36) == (2, 18, 33)
+    assert get_eagle3_aux_layer_ids(2) == (0, 1, 1)
+
+    class Norm(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.weight, self.eps = nn.Parameter(torch.ones(4), requires_grad=False), 1e-6
+
+    class Layer(nn.Module):
+        def __init__(self, i):
+            super().__init__()
+            self.i, self.input_layernorm = i, Norm()
+
+        def forward_fused(self, positions, h, residual, next_norm):
+            stream = residual + (self.i + 1)              # layer i adds i + 1 to the stream
+            return h * 0 + self.i, stream
+
+    model = Qwen3Model.__new__(Qwen3Model)
+    nn.Module.__init__(model)
+    model.embed_tokens = lambda ids: torch.full((ids.numel(), 4), 100.0)
+    model.layers = nn.ModuleList(Layer(i) for i in range(8))
+    model.norm = Norm()
+    ids, pos = torch.tensor([1, 2, 3]), torch.tensor([0, 1, 2])
+    plain = model(ids, pos)
+    hidden, aux = model(ids, pos, aux_layer_ids=(2, 5, 5))
+    assert torch.equal(hidden, plain)
+    entering = {i: 100.0 + sum(k + 1 for k in range(i)) for i in range(8)}
+    expected = torch.cat([torch.full((3, 4), entering[i]) for i in (2, 5, 5)], dim=-1)
+    assert torch.equal(aux, expected)                      # concatenation order kept, duplicates kept
+    with pytest.raises(ValueError, match="aux_layer_ids"):
+        model(ids, pos, aux_layer_ids=(2, 5, 9))
