@@ -207,3 +207,36 @@ def test_sequence_pickle_ships_minimal_state():
     w = pickle.loads(pickle.dumps(s))
     assert w.token_ids == [] and w.last_token == 9 and len(w) == 6 and w.seq_id == s.seq_id
     assert w.temperature == 0.5 and w.status == SequenceStatus.RUNNING
+
+
+def _running(sched, prompt, max_tokens, ignore_eos=False):
+    seq = Sequence(prompt, SamplingParams(max_tokens=max_tokens, ignore_eos=ignore_eos))
+    sched.add(seq)
+    out = sched.schedule()
+    sched.postprocess(out, [7] * len(out.scheduled_seqs))          # prefill samples its first token
+    return seq
+
+
+def test_postprocess_speculative_appends_stops_at_eos_and_max_tokens():
+    sched = Scheduler(_cfg(enable_kv_capacity_admission=True))
+    bm = sched.block_manager
+    a = _running(sched, list(range(3, 18)), 10)                      # 15 prompt + 1 sampled = 16 tokens
+    assert bm.ensure_slots(a, 6)                                     # reserves a second block
+    sched.postprocess_speculative(a, [11, 12, 13])
+    assert a.token_ids[-3:] == [11, 12, 13] and a.num_cached_tokens == len(a) and not a.is_finished
+    assert len(a.block_table) == a.num_blocks                         # unused reserved blocks released
+    assert bm.blocks[a.block_table[0]].hash != -1                      # the full block got its hash
+    # tokens after an EOS are dropped and the sequence retires (its reservation too)
+    assert bm.ensure_slots(a, 4)
+    sched.postprocess_speculative(a, [14, 2, 15])
+    assert a.token_ids[-2:] == [14, 2] and a.is_finished and a.seq_id not in sched._reserved_blocks
+    # max_tokens caps what is appended
+    b = _running(sched, list(range(3, 10)), 3)
+    assert bm.ensure_slots(b, 4)
+    sched.postprocess_speculative(b, [20, 21, 22, 23])
+    assert b.num_completion_tokens == 3 and b.token_ids[-2:] == [20, 21] and b.is_finished
+    # ignore_eos keeps going through an EOS
+    c = _running(sched, list(range(3, 10)), 8, ignore_eos=True)
+    assert bm.ensure_slots(c, 4)
+    sched.postprocess_speculative(c, [2, 2, 30])
+    assert c.token_ids[-3:] == [2, 2, 30] and not c.is_finished
