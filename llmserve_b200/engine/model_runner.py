@@ -14,6 +14,7 @@ sizing ``:186-229``, metadata ``:258-338``, graphs ``:383-418``).  Differences b
   workers through the RPC channel;
 * decode CUDA graphs also hold the LM head, so one replay yields the logit shard.
 """
+import dataclasses
 import os
 import time
 
@@ -89,10 +90,14 @@ class ModelRunner:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
 
+        quant_config = config.quant_config
+        if quant_config is not None and not self.is_cuda:
+            # the fp32 host path dequantises AWQ weights with fp32 scales (loaded from bf16)
+            quant_config = dataclasses.replace(quant_config, activation_dtype=self.dtype)
         prev_dtype = torch.get_default_dtype()
         torch.set_default_dtype(self.dtype)
         with torch.device(self.device):
-            self.model = Qwen3ForCausalLM(hf, quant_config=config.quant_config)
+            self.model = Qwen3ForCausalLM(hf, quant_config=quant_config)
         torch.set_default_dtype(prev_dtype)
         if config.load_format == "dummy":
             init_dummy_weights(self.model, seed=config.seed)

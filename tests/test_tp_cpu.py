@@ -225,3 +225,37 @@ def test_disaggregated_decode_server_loss_surfaces_as_an_error(ckpts):
             llm.prefill.exit()
         except Exception:
             pass
+
+
+def test_awq_engine_on_the_host_matches_dequantized_dense_and_shards_over_gloo(tmp_path):
+    """AutoAWQ GEMM g128 checkpoint on the fp32 host path: the same tokens as a dense checkpoint
+    holding the dequantised weights, and TP=2 (packed qweight/qzeros/scales sliced per rank) equal
+    to TP=1."""
+    import json
+
+    from safetensors import safe_open
+    from safetensors.torch import save_file
+
+    from llmserve_b200.models.synthetic import write_awq_checkpoint
+    from llmserve_b200.quantization.awq import dequantize_awq_gemm
+    awq = write_awq_checkpoint(str(tmp_path / "awq"), TINY, seed=3)
+    dense_dir = tmp_path / "dense"
+    dense_dir.mkdir()
+    cfg = json.load(open(os.path.join(awq, "config.json")))
+    cfg.pop("quantization_config")
+    cfg["torch_dtype"] = "float32"
+    json.dump(cfg, open(dense_dir / "config.json", "w"))
+    tensors = {}
+    with safe_open(os.path.join(awq, "model.safetensors"), "pt") as f:
+        for name in f.keys():
+            if name.endswith(".qweight"):
+                base = name[: -len(".qweight")]
+                w = dequantize_awq_gemm(f.get_tensor(name), f.get_tensor(base + ".qzeros"),
+                                        f.get_tensor(base + ".scales").float(), group_size=128)
+                tensors[base + ".weight"] = w.t().contiguous()
+            elif not name.endswith((".qzeros", ".scales")):
+                tensors[name] = f.get_tensor(name).float()
+    save_file(tensors, str(dense_dir / "model.safetensors"))
+    ref = _gen(str(dense_dir), 1)
+    assert _gen(awq, 1) == ref
+    assert _gen(awq, 2) == ref
