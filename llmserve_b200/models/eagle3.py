@@ -307,6 +307,11 @@ class Eagle3Speculator(nn.Module):
         return Eagle3DraftOutput(hidden.unsqueeze(1), logits.unsqueeze(1), target_logits.unsqueeze(1),
                                  token_ids.view(B, 1), DraftKVRef(pool, rows))
 
+    def compute_logits(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        """Draft logits of ``hidden_states`` scattered into the target vocabulary (``-inf`` outside
+        the draft vocabulary), as ``llmserve/models/eagle3.py:330-332`` of the reference."""
+        return self.map_draft_logits(self.lm_head(self.norm(hidden_states)))
+
     def map_draft_logits(self, draft_logits: torch.Tensor) -> torch.Tensor:
         """Scatter draft-vocab logits into a -inf target-vocab row (rejection sampling)."""
         idx = torch.arange(self.draft_vocab_size, device=draft_logits.device) + self.d2t

@@ -187,3 +187,11 @@ def test_offline_step_and_cycle(draft):
     assert cyc.draft_target_logits.shape == (3, V)
     with pytest.raises(ValueError):
         run_eagle3_speculative_cycle(draft, 3, _aux(1, width, 2), 20, torch.zeros(3, V), 3, 1.0)
+
+
+def test_compute_logits_maps_the_draft_head_into_the_target_vocab(draft):
+    width = 3 * TINY["hidden_size"]
+    out = draft.propose(torch.tensor([[5]]), _aux(1, width, 4), torch.tensor([[3]]), 0.0)
+    mapped = draft.compute_logits(out.hidden_states[:, 0])
+    torch.testing.assert_close(mapped, out.target_logits[:, 0])
+    assert torch.isinf(mapped).sum() == TINY["vocab_size"] - 512
