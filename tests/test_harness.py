@@ -260,3 +260,74 @@ def test_b200_suite_pd_variant_reaches_the_engine_factory():
                   metadata={"git_commit": "abc"})
     assert seen[True]["pd_prefill_devices"] == [0] and seen[True]["pd_decode_devices"] == [1]
     assert seen[False]["overlap_decode"] is True and seen[False]["pd_disaggregation"] is False
+
+
+def _point_result(point, commit, tps, complete=True):
+    return {"schema_version": 2, "complete": complete, "point_id": point["point_id"], "git_commit": commit,
+            "config": point, "metrics": {"throughput": {"output_tokens_per_second": tps}}}
+
+
+def test_execute_suite_resume_start_failure_timeout_and_bad_exit(tmp_path):
+    import subprocess
+
+    from benchmarks.environment import atomic_write_json
+    suite = json.load(open("benchmarks/suites/smoke.json"))
+    points = expand_suite(suite)
+    assert len(points) == 4
+    runs = tmp_path / "runs"
+    runs.mkdir()
+    atomic_write_json(runs / f"{points[0]['point_id']}.json", _point_result(points[0], "c1", 10.0))   # resumable
+    atomic_write_json(runs / f"{points[1]['point_id']}.json", _point_result(points[1], "c0", 11.0))   # old commit
+    seen = []
+
+    def runner(cmd, **kw):
+        pid = next(p["point_id"] for p in points if p["point_id"] in cmd[cmd.index("--point-config") + 1])
+        seen.append(pid)
+        out = cmd[cmd.index("--output") + 1]
+        if pid == points[1]["point_id"]:
+            raise OSError("exec format error")
+        if pid == points[2]["point_id"]:
+            raise subprocess.TimeoutExpired(cmd, 5)
+        point = next(p for p in points if p["point_id"] == pid)
+        atomic_write_json(out, _point_result(point, "c1", 12.0))            # complete, but the worker failed
+        return SimpleNamespace(returncode=3, stderr="late crash")
+
+    rc = execute_suite(suite, tmp_path, "/m/model", None, {"git_commit": "c1"}, resume=True, timeout_seconds=5,
+                       command_runner=runner)
+    assert rc == 1
+    assert seen == [p["point_id"] for p in points[1:]]                  # the matching result was resumed
+    res = {p["point_id"]: json.loads((runs / f"{p['point_id']}.json").read_text()) for p in points}
+    assert res[points[0]["point_id"]]["complete"] is True
+    assert res[points[1]["point_id"]]["error"]["type"] == "WorkerStartError"
+    assert "timed out" in res[points[2]["point_id"]]["error"]["message"]
+    assert res[points[3]["point_id"]]["complete"] is False
+    manifest = json.loads((tmp_path / "manifest.json").read_text())
+    assert manifest["completed_points"] == 1 and manifest["failed_points"] == 3 and not manifest["complete"]
+
+
+def test_summary_rows_and_aggregates_match_reference_on_sparse_results():
+    ref = _ref_bench("suite")
+    suite = json.load(open("benchmarks/suites/formal-closed-loop.json"))
+    points = expand_suite(suite)[:6]
+    results = []
+    for i, p in enumerate(points):
+        r = _point_result(p, "c", None if i == 2 else 100.0 + 7 * i, complete=i != 4)
+        r["metrics"]["latency"] = {"overall": {"ttft": {"p50": 0.01 * i, "p99": 0.02 * i}}}
+        if i == 1:
+            r["metrics"]["speculative"] = {"acceptance_rate": 0.5, "acceptance_length": 2.5}
+        results.append(r)
+    assert build_summary_rows(results) == ref.build_summary_rows(results)
+    for path, kw in (("metrics.throughput.output_tokens_per_second", {}),
+                     ("metrics.latency.overall.ttft.p99", {"scale": 1000.0, "unit": "ms"})):
+        assert aggregate_results(results, path, **kw) == ref.aggregate_results(results, path, **kw)
+
+
+def test_expand_suite_rejects_unknown_profile_like_the_reference():
+    ref = _ref_bench("suite")
+    suite = json.load(open("benchmarks/suites/smoke.json"))
+    suite["experiments"][0]["profile"] = "no-such-profile"
+    with pytest.raises(Exception) as ours:
+        expand_suite(suite)
+    with pytest.raises(Exception) as theirs:
+        ref.expand_suite(suite)
+    assert type(ours.value) is type(theirs.value)
