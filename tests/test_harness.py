@@ -331,3 +331,24 @@ def test_expand_suite_rejects_unknown_profile_like_the_reference():
     with pytest.raises(Exception) as theirs:
         ref.expand_suite(suite)
     assert type(ours.value) is type(theirs.value)
+
+
+def test_run_point_result_equals_reference_with_the_same_fake_engine():
+    """Poisson and closed-loop points through both harnesses with one fake engine and fake clock:
+    the result documents (config, metrics, per-request records, KV summary) are identical."""
+    ref = _ref_bench("serve")
+
+    def run(fn, point):
+        clock = FakeClock()
+        return fn(point, "/models/tiny", speculative_model="/models/draft",
+                  engine_factory=lambda m, **kw: FakeEngine(clock), make_sampling_params=_sp, clock=clock,
+                  sleep=clock.sleep, metadata={"git_commit": "abc"})
+
+    for name in ("smoke", "formal-closed-loop"):
+        for point in expand_suite(json.load(open(f"benchmarks/suites/{name}.json")))[:3]:
+            if point["arrival"] == "closed-loop":
+                point = dict(point, warmup_seconds=0.05, measurement_seconds=0.5)
+            ours, theirs = run(run_point, point), run(ref.run_point, point)
+            ours.pop("environment", None)
+            theirs.pop("environment", None)
+            assert ours == theirs, point["point_id"]
