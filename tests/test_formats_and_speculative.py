@@ -323,3 +323,25 @@ def test_eagle3_aux_layers_are_the_residual_streams_entering_the_chosen_layers()
     assert torch.equal(aux, expected)                      # concatenation order kept, duplicates kept
     with pytest.raises(ValueError, match="aux_layer_ids"):
         model(ids, pos, aux_layer_ids=(2, 5, 9))
+
+
+def test_config_fields_and_defaults_cover_the_reference():
+    """Every ``Config`` field of the reference exists here with the same default, so the same
+    ``LLM(model, **kwargs)`` calls work.  The one deliberate difference: the default rendezvous
+    address is 127.0.0.1 instead of ``localhost`` (a container's host name may not resolve)."""
+    import dataclasses
+
+    from llmserve_b200.config import Config
+    ref = reference_module("llmserve.config")
+    ours = {f.name: f for f in dataclasses.fields(Config)}
+    for f in dataclasses.fields(ref.Config):
+        assert f.name in ours, f.name
+        if f.name in ("hf_config", "quant_config"):
+            continue
+        want = f.default if f.default is not dataclasses.MISSING else None
+        got = ours[f.name].default if ours[f.name].default is not dataclasses.MISSING else None
+        if f.name == "distributed_init_method":
+            assert want == "tcp://localhost:2333" and got == "tcp://127.0.0.1:2333"
+            continue
+        assert got == want, f.name
+        assert ours[f.name].init == f.init, f.name
