@@ -195,3 +195,48 @@ def test_compute_logits_maps_the_draft_head_into_the_target_vocab(draft):
     mapped = draft.compute_logits(out.hidden_states[:, 0])
     torch.testing.assert_close(mapped, out.target_logits[:, 0])
     assert torch.isinf(mapped).sum() == TINY["vocab_size"] - 512
+
+
+@pytest.mark.parametrize("norm_before_residual", [False, True])
+def test_drafts_equal_the_reference_speculator(tmp_path, norm_before_residual):
+    """The same EAGLE3 checkpoint (random norm weights too) in both implementations: serial greedy
+    drafts give the same tokens and target-vocabulary logits, and so do batched drafts with
+    per-request gammas (paged draft K/V here, padded contiguous K/V in the reference)."""
+    import json
+    import os
+
+    from safetensors.torch import load_file, save_file
+
+    from tests.support import reference_module
+    ref_eagle = reference_module("llmserve.models.eagle3")
+    target_cfg = dict(TINY, num_hidden_layers=6)          # the reference wants >= 6 target layers
+    tgt = write_qwen3_checkpoint(str(tmp_path / "t"), target_cfg)
+    d = write_eagle3_checkpoint(str(tmp_path / "d"), target_cfg, 512, seed=5)
+    cfg = json.load(open(os.path.join(d, "config.json")))
+    cfg["norm_before_residual"] = norm_before_residual
+    json.dump(cfg, open(os.path.join(d, "config.json"), "w"))
+    sd = load_file(os.path.join(d, "model.safetensors"))
+    g = torch.Generator().manual_seed(9)
+    for k in sd:
+        if k.endswith("norm.weight"):
+            sd[k] = 1 + 0.1 * torch.randn(sd[k].shape, generator=g)
+    save_file(sd, os.path.join(d, "model.safetensors"))
+    ours = Eagle3Speculator.from_pretrained(d, target_model_path=tgt)
+    ours.prepare()
+    theirs = ref_eagle.Eagle3Speculator.from_pretrained(d, target_model_path=tgt).eval()
+    width = 3 * TINY["hidden_size"]
+    aux = _aux(3, width, 6)
+    with torch.no_grad():
+        a = generate_eagle3_draft_tokens(ours, 11, aux[:1], 7, 4, 1.0, draft_sampling_mode="greedy")
+        b = ref_eagle.generate_eagle3_draft_tokens(theirs, 11, aux[:1], 7, 4, 1.0, draft_sampling_mode="greedy")
+        assert a.draft_token_ids == b.draft_token_ids
+        torch.testing.assert_close(a.draft_target_logits, b.draft_target_logits, atol=2e-4, rtol=2e-4)
+        gammas = [3, 1, 2]
+        xs = generate_eagle3_draft_tokens_batched(ours, [4, 99, 500], aux, [2, 9, 30], 3, 1.0,
+                                                  draft_sampling_mode="greedy", gammas=gammas)
+        ys = ref_eagle.generate_eagle3_draft_tokens_batched(theirs, [4, 99, 500], aux, [2, 9, 30], 3, 1.0,
+                                                            draft_sampling_mode="greedy", gammas=gammas)
+    for x, y in zip(xs, ys):
+        assert x.draft_token_ids == y.draft_token_ids
+        torch.testing.assert_close(x.draft_target_logits, y.draft_target_logits, atol=2e-4, rtol=2e-4)
+        assert x.past_kv.lengths[0] == y.past_kv[0].shape[2]
