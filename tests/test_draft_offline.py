@@ -240,3 +240,57 @@ def test_drafts_equal_the_reference_speculator(tmp_path, norm_before_residual):
         assert x.draft_token_ids == y.draft_token_ids
         torch.testing.assert_close(x.draft_target_logits, y.draft_target_logits, atol=2e-4, rtol=2e-4)
         assert x.past_kv.lengths[0] == y.past_kv[0].shape[2]
+
+
+class _FakeTarget:
+    """Verify logits over 8 tokens: row j is uniform-ish with a bump at ``(input_j * 3) % 8``."""
+
+    def forward_with_eagle3_aux(self, input_ids, positions):
+        h = input_ids.float().unsqueeze(-1).repeat(1, 4)
+        return h, torch.cat([h + 1, h + 2, h + 3], -1)
+
+    def compute_logits(self, hidden):
+        logits = torch.zeros(hidden.shape[0], 8)
+        logits[torch.arange(hidden.shape[0]), (hidden[:, 0].long() * 3) % 8] = 1.5
+        return logits
+
+
+class _FakeDraft:
+    """Deterministic draft over 8 tokens whose target-vocabulary logits favour ``step + 2``."""
+    hidden_size = 4
+
+    def __init__(self, out_type):
+        self.out_type, self.step = out_type, 0
+
+    def propose(self, input_ids, aux_hidden_states, positions, temperature, past_kv=None, kv_valid_lens=None):
+        s = self.step
+        self.step += 1
+        logits = torch.zeros(1, 1, 8)
+        logits[0, 0, (s + 2) % 8] = 1.0
+        past = (torch.zeros(1, 1, s + 1, 1), torch.zeros(1, 1, s + 1, 1))
+        return self.out_type(torch.full((1, 1, 4), float(s)), logits, logits, torch.tensor([[(s + 2) % 8]]), past)
+
+
+def test_offline_step_and_cycle_equal_the_reference():
+    from tests.support import reference_module
+    ref_eagle = reference_module("llmserve.models.eagle3")
+    for seed in range(6):
+        rv = torch.rand(3, generator=torch.Generator().manual_seed(seed))
+        torch.manual_seed(seed)
+        ours = run_eagle3_offline_step(_FakeTarget(), _FakeDraft(Eagle3DraftOutput), 5, torch.zeros(1, 1, 12), 4, 3,
+                                       1.0, random_values=rv)
+        torch.manual_seed(seed)
+        theirs = ref_eagle.run_eagle3_offline_step(_FakeTarget(), _FakeDraft(ref_eagle.Eagle3DraftOutput), 5,
+                                                   torch.zeros(1, 1, 12), 4, 3, 1.0, random_values=rv)
+        assert ours.draft_token_ids == theirs.draft_token_ids
+        torch.testing.assert_close(ours.verify_output.target_logits, theirs.verify_output.target_logits)
+        for f in ("token_ids", "accepted_token_ids", "final_token_id", "num_accepted", "accepted_all"):
+            assert getattr(ours.sample_result, f) == getattr(theirs.sample_result, f), (seed, f)
+        logits = torch.randn(4, 8, generator=torch.Generator().manual_seed(100 + seed))
+        torch.manual_seed(seed)
+        a = run_eagle3_speculative_cycle(_FakeDraft(Eagle3DraftOutput), 5, torch.zeros(1, 1, 12), 4, logits, 3, 1.0,
+                                         random_values=rv)
+        torch.manual_seed(seed)
+        b = ref_eagle.run_eagle3_speculative_cycle(_FakeDraft(ref_eagle.Eagle3DraftOutput), 5, torch.zeros(1, 1, 12),
+                                                   4, logits, 3, 1.0, random_values=rv)
+        assert (a.draft_token_ids, a.sample_result.token_ids) == (b.draft_token_ids, b.sample_result.token_ids)
