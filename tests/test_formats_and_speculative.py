@@ -345,3 +345,40 @@ def test_config_fields_and_defaults_cover_the_reference():
             continue
         assert got == want, f.name
         assert ours[f.name].init == f.init, f.name
+
+
+@pytest.mark.parametrize("nodes", [6, 10])
+def test_tree_attention_equals_reference_tree_path(nodes):
+    """Prefix in a paged pool (shuffled blocks) + tree nodes under the ancestor mask: the host
+    reference of the tree-attention kernel equals the reference engine's masked-SDPA tree path."""
+    from llmserve_b200.ops.attention import tree_attention_ref
+    ref_attn = reference_module("llmserve.layers.attention")
+    ref_ctx = reference_module("llmserve.utils.context")
+    topo = build_fixed_tree_topology(nodes)
+    n, nh, nkv, hd, bs, P = len(topo.parents), 8, 2, 16, 16, 37
+    g = torch.Generator().manual_seed(nodes)
+    pk, pv = torch.randn(P, nkv, hd, generator=g), torch.randn(P, nkv, hd, generator=g)
+    q = torch.randn(n, nh, hd, generator=g)
+    tk, tv = torch.randn(n, nkv, hd, generator=g), torch.randn(n, nkv, hd, generator=g)
+    nblocks = 6
+    table = torch.tensor([4, 1, 3], dtype=torch.int32)
+    ours_k = torch.zeros(nblocks, nkv, bs, hd)
+    ours_v = torch.zeros_like(ours_k)
+    theirs_k = torch.zeros(nblocks, bs, nkv, hd)
+    theirs_v = torch.zeros_like(theirs_k)
+    slots = []
+    for p in range(P):
+        b, o = int(table[p // bs]), p % bs
+        ours_k[b, :, o], ours_v[b, :, o] = pk[p], pv[p]
+        theirs_k[b, o], theirs_v[b, o] = pk[p], pv[p]
+        slots.append(b * bs + o)
+    mask = topo.attention_mask()
+    ours = tree_attention_ref(q, ours_k, ours_v, table, P, tk, tv, mask, hd ** -0.5)
+    layer = ref_attn.Attention(nh, hd, hd ** -0.5, nkv)
+    layer.k_cache, layer.v_cache = theirs_k, theirs_v
+    ref_ctx.set_context(True, tree_prefix_slots=torch.tensor(slots), tree_attention_mask=mask)
+    try:
+        theirs = layer(q, tk, tv)
+    finally:
+        ref_ctx.reset_context()
+    torch.testing.assert_close(ours, theirs, atol=1e-5, rtol=1e-5)
