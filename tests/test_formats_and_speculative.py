@@ -382,3 +382,51 @@ def test_tree_attention_equals_reference_tree_path(nodes):
     finally:
         ref_ctx.reset_context()
     torch.testing.assert_close(ours, theirs, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_norm_rope_and_silu_host_references_equal_the_reference_layers(dtype):
+    """The host references that the sm_100a kernels are tested against compute what the reference's
+    layers compute (RMSNorm, fused add + RMSNorm with the bf16 residual, neox RoPE from the
+    cos/sin cache, SiLU-mul), run here with the reference's ``torch.compile`` switched off."""
+    import torch._dynamo
+
+    from llmserve_b200.ops.activation import silu_and_mul_ref
+    from llmserve_b200.ops.norm import add_rms_norm_ref, rms_norm_ref
+    from llmserve_b200.ops.rope import apply_rope_ref, build_cos_sin_cache
+    ln = reference_module("llmserve.layers.layernorm")
+    rope = reference_module("llmserve.layers.rotary_embedding")
+    act = reference_module("llmserve.layers.activation")
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(5, 64, generator=g).to(dtype)
+    res = torch.randn(5, 64, generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(64, generator=g)).to(dtype)
+    norm = ln.RMSNorm(64, eps=1e-6).to(dtype)
+    norm.weight.data.copy_(w)
+    pos = torch.tensor([0, 3, 17, 200, 4095])
+    q = torch.randn(5, 4, 128, generator=g).to(dtype)
+    k = torch.randn(5, 2, 128, generator=g).to(dtype)
+    emb = rope.RotaryEmbedding(128, 128, 4096, 1000000.0)
+    cs = build_cos_sin_cache(128, 4096, 1000000.0)
+    gate_up = torch.randn(5, 2 * 96, generator=g).to(dtype)
+    saved = torch._dynamo.config.disable
+    torch._dynamo.config.disable = True
+    try:
+        with torch.no_grad():
+            ref_n = norm(x.clone())
+            ref_an, ref_res = norm(x.clone(), res.clone())
+            ref_q, ref_k = emb(pos, q, k)
+            ref_act = act.SiluAndMul()(gate_up)
+    finally:
+        torch._dynamo.config.disable = saved
+    tol = dict(atol=1e-5, rtol=1e-5) if dtype == torch.float32 else dict(atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(rms_norm_ref(x, w, 1e-6), ref_n, **tol)
+    an, r = add_rms_norm_ref(x, res, w, 1e-6)
+    torch.testing.assert_close(an, ref_an, **tol)
+    if dtype == torch.bfloat16:
+        # (with fp32 activations the reference's in-place ops alias its returned residual with the
+        # normalised output -- ``x.float()`` is ``x`` itself -- so only the bf16 residual compares)
+        torch.testing.assert_close(r, ref_res, **tol)
+    torch.testing.assert_close(apply_rope_ref(q, pos, cs), ref_q, **tol)
+    torch.testing.assert_close(apply_rope_ref(k, pos, cs), ref_k, **tol)
+    torch.testing.assert_close(silu_and_mul_ref(gate_up), ref_act, **tol)
