@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--eagle3", action="store_true",
                    help="EAGLE3 speculative decoding, gamma 3, with a random-init Qwen3-8B speculator (1 layer, "
                         "fc 12288->4096, draft vocab 32000); acceptance is not meaningful with random weights")
+    p.add_argument("--spec-graphs", action="store_true",
+                   help="with --eagle3: run the greedy speculative step through its CUDA graphs")
     p.add_argument("--mem-util", type=float, default=0.85, help="gpu_memory_utilization (KV pool sizing)")
     p.add_argument("--no-overlap", action="store_true",
                    help="synchronous decode loop (no launch of step N+1 before step N's tokens are read)")
@@ -147,7 +149,8 @@ def run_ours(args):
     if args.eagle3:
         from llmserve_b200.models.synthetic import EAGLE3_8B, write_config_only
         kwargs.update(speculative_model=write_config_only(os.path.join(tempfile.gettempdir(), "llmserve_b200_eagle3_8b"),
-                                                          EAGLE3_8B), speculative_gamma=3)
+                                                          EAGLE3_8B), speculative_gamma=3,
+                      speculative_cuda_graphs=args.spec_graphs)
     if rank > 0:
         run_worker(path, rank, **kwargs)
         return
@@ -211,6 +214,7 @@ def run_ours(args):
                    f"concurrency {args.concurrency}, greedy", "cuda_graphs": not args.eager,
                    "collectives": "nccl" if args.nccl_only or world == 1 else "fused-nvlink",
                    "overlapped_decode": not args.no_overlap,
+                   "speculative_graphs": bool(args.eagle3 and args.spec_graphs),
                    "l2": "inputs larger than L2: every step streams all 16 GB of weights"},
         "e2e": {"value": round(tokens / wall, 2), "unit": "tok/s", "h2d_bytes_per_step": round(h2d),
                 "d2h_bytes_per_step": round(d2h)},

@@ -18,6 +18,8 @@ are grouped at the end:
                               ranks > 0 call :func:`llmserve_b200.engine.llm_engine.run_worker`.
 * ``overlap_decode``       -- launch decode step N+1 from device-resident tokens before step N is
                               read on the host (greedy, graph decode); on by default.
+* ``speculative_cuda_graphs`` -- capture the greedy EAGLE3 chain step (drafts, packed verify,
+                              acceptance) in CUDA graphs per batch bucket (TP = 1); off by default.
 
 ``awq_backend="triton"`` is accepted for compatibility and runs the sm_100a W4A16 kernel.
 """
@@ -104,6 +106,7 @@ class Config:
     distributed_launcher: str = "spawn"
     rpc_channel: str | None = None
     overlap_decode: bool = True
+    speculative_cuda_graphs: bool = False
     pd_role: str = ""          # internal: "decode" exports its KV pools to the prefill ranks
 
     def __post_init__(self):

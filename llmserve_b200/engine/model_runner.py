@@ -135,6 +135,7 @@ class ModelRunner:
         self.allocate_kv_cache()
         if self.is_cuda and not self.enforce_eager:
             self.capture_cudagraph()
+        self.spec.setup_graphs()
 
         if self.world_size > 1:
             name = channel_name or "llmserve_b200"
@@ -174,6 +175,7 @@ class ModelRunner:
                 pass
         self.graphs = {}
         self.graph_pool = None
+        self.spec.graphs = None
         if self.is_cuda:
             torch.cuda.synchronize()
         if self.world_size > 1:

@@ -47,6 +47,7 @@ class SpeculativeExecutor:
         self.r = runner
         self.draft_kv_len: dict[int, int] = {}
         self.prev_correction: dict[int, tuple[int, torch.Tensor]] = {}
+        self.graphs = None          # SpeculativeGraphs when Config.speculative_cuda_graphs applies
 
     # ---- set-up ------------------------------------------------------------------------------
     def load_draft_model(self):
@@ -85,6 +86,21 @@ class SpeculativeExecutor:
         draft.d2t.copy_(ids - torch.arange(draft.draft_vocab_size))
         draft.t2d.zero_()
         draft.t2d[ids] = True
+
+    def setup_graphs(self):
+        """Graphs (host tier: static-buffer emulation) of the greedy chain step, when enabled and
+        in scope: TP = 1, greedy acceptance, no tree."""
+        r = self.r
+        cfg = r.config
+        if (not getattr(cfg, "speculative_cuda_graphs", False) or r.draft_model is None or r.world_size != 1
+                or r.speculative_accept_mode != "greedy" or r.speculative_tree_nodes
+                or (r.is_cuda and r.enforce_eager)):
+            return
+        from llmserve_b200.engine.speculative_graphs import SpeculativeGraphs
+        graphs = SpeculativeGraphs(self, min(cfg.max_num_seqs, 64))
+        if r.is_cuda:
+            graphs.capture()
+        self.graphs = graphs
 
     def clear_all(self):
         self.draft_kv_len.clear()
@@ -208,6 +224,22 @@ class SpeculativeExecutor:
         target_decode_time = perf_counter() - t
 
         kv0 = [self.draft_kv_len.get(s.seq_id, len(s)) for s in seqs]
+        base = [len(s) - (1 if m else 0) for s, m in zip(seqs, merged)]
+        sg = self.graphs
+        if sg is not None and greedy and not r.speculative_trace and sg.fits(seqs):
+            t = perf_counter()
+            sg.ids[:B].copy_(start_ids)
+            sg.aux[:B].copy_(start_aux)
+            sg.fill(seqs, kv0, base)
+            with nvtx_range("speculative.graph"):
+                host = sg.run(B)
+            graph_time = perf_counter() - t
+            accepts = [(row[0], row[1], row[3:], row[0] == g) for row in host]
+            starts = [row[2] for row in host]
+            timing = {"target_decode_time": target_decode_time, "fresh": len(fresh), "draft_time": 0.0,
+                      "verify_time": graph_time, "accept_time": 0.0, "fwd_time": 0.0, "sample_time": 0.0}
+            return self._finish(seqs, merged, accepts, starts, sg.corr_aux[:B].clone(), kv0, None, n_or=g + 1,
+                                timing=timing, t_total=t_total)
         t = perf_counter()
         draft_tokens = torch.empty(B, g, dtype=torch.int64, device=dev)
         mapped_logits = []
@@ -233,7 +265,6 @@ class SpeculativeExecutor:
         draft_time = perf_counter() - t
 
         t = perf_counter()
-        base = [len(s) - (1 if m else 0) for s, m in zip(seqs, merged)]
         n = g + 1
         vin = torch.cat([start_ids.unsqueeze(1), draft_tokens], 1).reshape(-1)
         vpos = torch.tensor([b + j for b in base for j in range(n)], dtype=torch.int64, device=dev)
@@ -276,7 +307,17 @@ class SpeculativeExecutor:
             num_acc = torch.tensor([a[0] for a in accepts], device=dev)
         corr_aux = aux.view(B, n, -1)[torch.arange(B, device=dev), num_acc.long()]
         accept_time = perf_counter() - t
+        timing = {"target_decode_time": target_decode_time, "fresh": len(fresh), "draft_time": draft_time,
+                  "verify_time": verify_time, "accept_time": accept_time, "fwd_time": fwd_time,
+                  "sample_time": sample_time}
+        return self._finish(seqs, merged, accepts, starts, corr_aux, kv0, logits, n_or=n, timing=timing,
+                            t_total=t_total)
 
+    def _finish(self, seqs, merged, accepts, starts, corr_aux, kv0, logits, *, n_or, timing, t_total):
+        """Per-sequence outputs of a chain step and the state the next step starts from: the
+        correction token with its auxiliary hidden state, and the kept draft K/V length."""
+        r = self.r
+        B, g = len(seqs), r.speculative_gamma
         t = perf_counter()
         outputs = []
         for i, s in enumerate(seqs):
@@ -285,23 +326,24 @@ class SpeculativeExecutor:
             self.prev_correction[s.seq_id] = (fin, corr_aux[i])
             self.draft_kv_len[s.seq_id] = kv0[i] + min(acc + 1, g)
             debug = None
-            if r.speculative_trace:
-                debug = self._debug(logits, i, n, starts[i], list(drafts), tokens, acc, all_ok, kv0[i])
+            if r.speculative_trace and logits is not None:
+                debug = self._debug(logits, i, n_or, starts[i], list(drafts), tokens, acc, all_ok, kv0[i])
             outputs.append(SpeculativeDecodeOutput(tokens, g, acc, bool(all_ok), len(tokens), None, debug))
         kv_time = perf_counter() - t
         total = perf_counter() - t_total
+        fresh = timing["fresh"]
         for i, o in enumerate(outputs):
             o.timing = {
-                "target_decode_time": (target_decode_time / len(fresh)) if not merged[i] else 0.0,
-                "draft_proposal_time": draft_time / B,
-                "target_verify_time": verify_time / B,
-                "accept_time": accept_time / B,
+                "target_decode_time": (timing["target_decode_time"] / fresh) if not merged[i] else 0.0,
+                "draft_proposal_time": timing["draft_time"] / B,
+                "target_verify_time": timing["verify_time"] / B,
+                "accept_time": timing["accept_time"] / B,
                 "kv_update_time": kv_time / B,
                 "trace_time": 0.0,
                 "total_time": total / B,
                 "draft_pack_time": 0.0,
-                "draft_forward_time": fwd_time / B,
-                "draft_sample_time": sample_time / B,
+                "draft_forward_time": timing["fwd_time"] / B,
+                "draft_sample_time": timing["sample_time"] / B,
                 "draft_compact_time": 0.0,
             }
         return outputs

@@ -228,3 +228,22 @@ def test_debug_bounds_checks_catch_bad_metadata(ckpts):
     with pytest.raises(ValueError, match="maps to slot"):
         r.check_bounds([seq], [len(seq) - 1], [5])
     llm.exit()
+
+
+def test_speculative_graph_step_layout_equals_eager_and_baseline(ckpts):
+    """The static-buffer step of the EAGLE3 graphs (run as its host emulation here): the same
+    tokens as the eager speculative step and as plain decoding, with batches that leave padded
+    rows in their bucket and sequences that cross block boundaries."""
+    tgt, draft = ckpts
+    prompts = _prompts(5, seed=8)
+    base, _ = _run(tgt, prompts, max_tokens=40)
+    eager, _ = _run(tgt, prompts, max_tokens=40, speculative_model=draft)
+    llm = LLM(tgt, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=64,
+              speculative_model=draft, speculative_cuda_graphs=True, debug_bounds_checks=True)
+    llm.model_runner.sampler = GreedySampler()
+    out = llm.generate(prompts, SamplingParams(temperature=0.5, max_tokens=40, ignore_eos=True), use_tqdm=False)
+    sg = llm.model_runner.spec.graphs
+    assert sg is not None and sg.steps > 0
+    llm.exit()
+    graphed = [o["token_ids"] for o in out]
+    assert graphed == eager == base
