@@ -30,7 +30,7 @@ from llmserve_b200.ops import attention as attn_ops
 from llmserve_b200.ops import sampling as sampling_ops
 from llmserve_b200.ops._ext import LaunchCounter
 from llmserve_b200.parallel import state as tp
-from llmserve_b200.utils.context import get_context, reset_context, set_context
+from llmserve_b200.utils.context import reset_context, set_context
 from llmserve_b200.utils.loader import init_dummy_weights, load_model
 
 

@@ -18,7 +18,6 @@ from llmserve_b200.layers.attention import Attention
 from llmserve_b200.layers.embed_head import ParallelLMHead, ReplicatedEmbedding
 from llmserve_b200.layers.linear import MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear
 from llmserve_b200.layers.norm import RMSNorm
-from llmserve_b200.ops import activation
 from llmserve_b200.ops import norm as norm_ops
 from llmserve_b200.ops.rope import build_cos_sin_cache
 from llmserve_b200.parallel import state as tp

@@ -9,7 +9,7 @@ import torch
 
 from llmserve_b200.models.eagle3 import (Eagle3Speculator, normalize_eagle3_config, normalize_eagle3_weight_name,
                                          validate_eagle3_target_config)
-from llmserve_b200.models.synthetic import TINY, awq_quantize_dense, write_awq_checkpoint, write_eagle3_checkpoint
+from llmserve_b200.models.synthetic import TINY, awq_quantize_dense, write_eagle3_checkpoint
 from llmserve_b200.quantization.awq import (AWQRuntimeConfig, awq_reference_linear, dequantize_awq_gemm,
                                             pack_awq_int4, unpack_awq_int4)
 from llmserve_b200.speculative.sampling import (greedy_accept_batch, greedy_accept_from_ids,
@@ -53,7 +53,7 @@ def test_awq_config_validation():
 
 def test_awq_checkpoint_loads_with_tp_slicing_on_cpu(tmp_path):
     """AutoAWQ checkpoint through the engine loader; TP=2 shards of a packed layer concatenate back."""
-    from llmserve_b200.layers.linear import MergedColumnParallelLinear, RowParallelLinear
+    from llmserve_b200.layers.linear import RowParallelLinear
     from llmserve_b200.parallel import state as tp
     cfg = AWQRuntimeConfig(4, 128, True, "gemm", "autoawq", torch.bfloat16)
     w = torch.randn(512, 256) * 0.02
