@@ -6,7 +6,7 @@ independent of torch's own arch list.
 import glob
 import os
 
-from setuptools import setup
+from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -17,6 +17,10 @@ sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "b
 
 setup(
     name="llmserve_b200",
+    version="0.1.0",
+    python_requires=">=3.10",
+    packages=find_packages(include=["llmserve_b200", "llmserve_b200.*", "benchmarks"]),
+    package_data={"benchmarks": ["suites/*.json"]},
     ext_modules=[
         CUDAExtension(
             name="llmserve_b200._C",
