@@ -85,7 +85,7 @@ ENGINE_KEYS = {
     "speculative_gamma": 3, "speculative_tree_nodes": 0, "speculative_accept_mode": "greedy",
     "speculative_trace": False, "tensor_parallel_size": 1, "load_format": "auto", "fused_collectives": True,
     "kvcache_block_size": 256, "overlap_decode": True, "pd_disaggregation": False, "pd_prefill_devices": (),
-    "pd_decode_devices": (), "speculative_cuda_graphs": False,
+    "pd_decode_devices": (), "speculative_cuda_graphs": False, "device": "cuda", "num_kvcache_blocks": -1,
 }
 
 

@@ -233,7 +233,7 @@ def test_run_point_with_real_cpu_engines_plain_and_disaggregated(tmp_path):
                                           "max_num_batched_tokens": 256, "kvcache_block_size": 16}}]}
 
     def factory(model, **kw):
-        return LLM(model, device="cpu", num_kvcache_blocks=64, **kw)
+        return LLM(model, **dict(kw, device="cpu", num_kvcache_blocks=64))
 
     for point in expand_suite(suite):
         result = run_point(point, path, engine_factory=factory, metadata={"git_commit": "abc"})
@@ -352,3 +352,34 @@ def test_run_point_result_equals_reference_with_the_same_fake_engine():
             ours.pop("environment", None)
             theirs.pop("environment", None)
             assert ours == theirs, point["point_id"]
+
+
+def test_run_suite_command_line_end_to_end_on_the_host_tier(tmp_path):
+    """``python -m benchmarks.run_suite`` exactly as a user runs it: one subprocess per point
+    (``benchmarks.serve``), a real engine on the host tier, manifest and CSVs written."""
+    import csv
+    import os
+    import subprocess
+    import sys
+
+    from llmserve_b200.models.synthetic import TINY, write_qwen3_checkpoint
+    path = write_qwen3_checkpoint(str(tmp_path / "m"), TINY)
+    suite = {"schema_version": 1, "name": "cpu-cli", "runs": 1,
+             "profiles": {"p": {"classes": [{"name": "c", "weight": 1, "input_len": 20, "output_len": 8}],
+                                "prompt_id_high": 1000}},
+             "experiments": [{"name": "e", "arrival": "closed-loop", "profile": "p", "max_concurrencies": [2],
+                              "warmup_seconds": 0.2, "measurement_seconds": 1.0,
+                              "variants": [{"name": "baseline"}, {"name": "chunked", "enable_chunked_prefill": True}],
+                              "runtime": {"argmax_sampler": True, "max_model_len": 128, "max_num_batched_tokens": 256,
+                                          "kvcache_block_size": 16, "device": "cpu", "num_kvcache_blocks": 64}}]}
+    (tmp_path / "suite.json").write_text(json.dumps(suite))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    proc = subprocess.run([sys.executable, "-m", "benchmarks.run_suite", "--suite", str(tmp_path / "suite.json"),
+                           "--output-dir", str(tmp_path / "out"), "--model", path, "--allow-dirty",
+                           "--timeout-seconds", "300"], cwd=root, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stdout[-2000:] + proc.stderr[-2000:]
+    manifest = json.loads((tmp_path / "out" / "manifest.json").read_text())
+    assert manifest["complete"] and manifest["completed_points"] == 2
+    rows = list(csv.DictReader(open(tmp_path / "out" / "summary.csv")))
+    assert len(rows) == 2 and all(float(r["output_throughput_tps"]) > 0 for r in rows)
+    assert str(tmp_path) not in (tmp_path / "out" / "runs" / f"{rows[0]['point_id']}.json").read_text()
