@@ -247,3 +247,24 @@ def test_speculative_graph_step_layout_equals_eager_and_baseline(ckpts):
     llm.exit()
     graphed = [o["token_ids"] for o in out]
     assert graphed == eager == base
+
+
+def test_get_metrics_equals_the_reference_summary_of_the_same_run(ckpts):
+    """The reference engine's own ``get_metrics`` applied to this engine's request records,
+    scheduler and runner (speculation and capacity admission on) returns exactly our metrics."""
+    from tests.support import reference_module
+    ref_engine = reference_module("llmserve.engine.llm_engine")
+    tgt, draft = ckpts
+    llm = LLM(tgt, device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=64,
+              speculative_model=draft, enable_kv_capacity_admission=True)
+    llm.model_runner.sampler = GreedySampler()
+    llm.generate(_prompts(3, seed=2), SamplingParams(max_tokens=12, ignore_eos=True), use_tqdm=False)
+    ours = llm.get_metrics()
+    proxy = ref_engine.LLMEngine.__new__(ref_engine.LLMEngine)
+    for k in ("request_metrics", "scheduler", "model_runner", "speculative_batch_calls",
+              "speculative_batch_sequences", "speculative_max_batch_size", "last_step_events"):
+        object.__setattr__(proxy, k, getattr(llm, k))
+    theirs = ref_engine.LLMEngine.get_metrics(proxy)
+    llm.exit()
+    assert ours["summary"]["speculative"]["steps"] > 0
+    assert ours == theirs
