@@ -268,3 +268,53 @@ def test_get_metrics_equals_the_reference_summary_of_the_same_run(ckpts):
     llm.exit()
     assert ours["summary"]["speculative"]["steps"] > 0
     assert ours == theirs
+
+
+@pytest.mark.parametrize("speculative", [False, True])
+def test_step_is_lockstep_with_the_reference_engine_step(ckpts, speculative):
+    """Two engines with the same requests: one steps with ``LLMEngine.step``, the other with the
+    reference engine's ``step`` driving its scheduler and runner.  Every step returns the same
+    outputs and the same events (timestamps aside), and the request records end identical."""
+    from tests.support import reference_module
+    ref_engine = reference_module("llmserve.engine.llm_engine")
+    tgt, draft = ckpts
+    kw = dict(device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=64,
+              enable_chunked_prefill=True, max_num_batched_tokens=40, overlap_decode=False,
+              speculative_model=draft if speculative else None)
+    ours, driven = LLM(tgt, **kw), LLM(tgt, **kw)
+    for e in (ours, driven):
+        e.model_runner.sampler = GreedySampler()
+    proxy = ref_engine.LLMEngine.__new__(ref_engine.LLMEngine)
+    for k in ("request_metrics", "scheduler", "model_runner", "last_step_events"):
+        object.__setattr__(proxy, k, getattr(driven, k))
+    for k in ("speculative_batch_calls", "speculative_batch_sequences", "speculative_max_batch_size"):
+        object.__setattr__(proxy, k, 0)
+    sp = SamplingParams(max_tokens=10, ignore_eos=True)
+    for p in _prompts(4, seed=5):
+        ours.add_request(p, sp)
+        driven.add_request(p, sp)
+    # sequence ids come from one process-wide counter: compare them by arrival order
+    order_ours = {sid: i for i, sid in enumerate(ours.request_metrics)}
+    order_driven = {sid: i for i, sid in enumerate(driven.request_metrics)}
+
+    def norm(events, order):
+        return {k: ([order[x] for x in v] if k.endswith("seq_ids") else v) for k, v in events.items()
+                if k not in ("step_start", "step_end", "speculative_debug", "speculative_debug_by_seq")}
+
+    steps = 0
+    while not ours.is_finished():
+        a, b = ours.step(), ref_engine.LLMEngine.step(proxy)
+        assert a[1] == b[1] and [t for _, t in a[0]] == [t for _, t in b[0]], steps
+        assert norm(ours.last_step_events, order_ours) == norm(proxy.last_step_events, order_driven), steps
+        steps += 1
+    assert driven.is_finished() and steps > 3
+    fields = ("output_tokens", "prompt_tokens", "success", "speculative_steps", "speculative_draft_tokens",
+              "speculative_accepted_tokens", "speculative_emitted_tokens", "speculative_accept_all_count",
+              "speculative_gamma_counts")
+    rec = [[m[f] for f in fields] + [len(m["token_times"]), len(m["output_event_times"])]
+           for m in ours.request_metrics.values()]
+    assert rec == [[m[f] for f in fields] + [len(m["token_times"]), len(m["output_event_times"])]
+                   for m in driven.request_metrics.values()]
+    assert ours.speculative_batch_calls == proxy.speculative_batch_calls
+    ours.exit()
+    driven.exit()
