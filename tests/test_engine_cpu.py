@@ -270,7 +270,7 @@ def test_get_metrics_equals_the_reference_summary_of_the_same_run(ckpts):
     assert ours == theirs
 
 
-@pytest.mark.parametrize("speculative", [False, True])
+@pytest.mark.parametrize("speculative", [False, True, "tree"])
 def test_step_is_lockstep_with_the_reference_engine_step(ckpts, speculative):
     """Two engines with the same requests: one steps with ``LLMEngine.step``, the other with the
     reference engine's ``step`` driving its scheduler and runner.  Every step returns the same
@@ -280,7 +280,8 @@ def test_step_is_lockstep_with_the_reference_engine_step(ckpts, speculative):
     tgt, draft = ckpts
     kw = dict(device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=64,
               enable_chunked_prefill=True, max_num_batched_tokens=40, overlap_decode=False,
-              speculative_model=draft if speculative else None)
+              speculative_model=draft if speculative else None,
+              speculative_tree_nodes=10 if speculative == "tree" else 0)
     ours, driven = LLM(tgt, **kw), LLM(tgt, **kw)
     for e in (ours, driven):
         e.model_runner.sampler = GreedySampler()
@@ -290,7 +291,7 @@ def test_step_is_lockstep_with_the_reference_engine_step(ckpts, speculative):
     for k in ("speculative_batch_calls", "speculative_batch_sequences", "speculative_max_batch_size"):
         object.__setattr__(proxy, k, 0)
     sp = SamplingParams(max_tokens=10, ignore_eos=True)
-    for p in _prompts(4, seed=5):
+    for p in _prompts(1 if speculative == "tree" else 4, seed=5):
         ours.add_request(p, sp)
         driven.add_request(p, sp)
     # sequence ids come from one process-wide counter: compare them by arrival order
