@@ -180,3 +180,28 @@ def test_quantizer_cli_exports_autoawq_and_resumes(tmp_path):
     assert base["mode"] == "bf16"
     # quantisation error on a random model is small: mean NLL within 2% of the bf16 model
     assert abs(res["perplexity"]["mean_nll"] - base["perplexity"]["mean_nll"]) < 0.02 * base["perplexity"]["mean_nll"]
+
+
+def test_layer_calibration_is_as_accurate_as_the_reference_pipeline():
+    """The same HF Qwen3 layer and calibration activations through both pipelines: the error of the
+    quantised layer's output (relative to its residual update) is within 2% of the reference's
+    (this pipeline evaluates its searches in fp32 on an evenly spaced token subsample)."""
+    from transformers import Qwen3ForCausalLM
+
+    from llmserve_b200.quantization.qwen3_awq import calibrate_qwen3_layer
+    from llmserve_b200.quantization.quantize_qwen3 import capture_first_layer_input
+    ref = reference_module("llmserve.quantization.qwen3_awq")
+    torch.manual_seed(1)
+    model = Qwen3ForCausalLM(_tiny_hf_config()).eval()
+    enc = {"input_ids": torch.randint(0, 512, (2, 64)), "attention_mask": torch.ones(2, 64, dtype=torch.long)}
+    hidden, kwargs = capture_first_layer_input(model, enc, torch.device("cpu"))
+    layer = model.model.layers[0]
+    with torch.no_grad():
+        dense = layer(hidden, **kwargs)
+        dense = dense[0] if isinstance(dense, tuple) else dense
+    ours = calibrate_qwen3_layer(copy.deepcopy(layer), hidden, forward_kwargs=kwargs, n_grid=10, max_tokens=128)
+    theirs = ref.calibrate_qwen3_layer(copy.deepcopy(layer), hidden, forward_kwargs=kwargs, n_grid=10, max_tokens=128)
+    upd = (dense - hidden).norm()
+    err_ours = float((ours.hidden_states - dense).norm() / upd)
+    err_ref = float((theirs.hidden_states - dense).norm() / upd)
+    assert err_ours <= 1.02 * err_ref, (err_ours, err_ref)
