@@ -181,6 +181,15 @@ def test_quantizer_cli_exports_autoawq_and_resumes(tmp_path):
     # quantisation error on a random model is small: mean NLL within 2% of the bf16 model
     assert abs(res["perplexity"]["mean_nll"] - base["perplexity"]["mean_nll"]) < 0.02 * base["perplexity"]["mean_nll"]
 
+    # the reference runtime accepts the export and dequantises it to the same weights
+    ref_awq = reference_module("llmserve.layers.quantization.awq")
+    from transformers import AutoConfig
+    ref_awq.AWQRuntimeConfig.from_hf_config(AutoConfig.from_pretrained(str(tmp_path / "awq")))
+    base_name = "model.layers.1.self_attn.o_proj"
+    tensors = [sd[f"{base_name}.{t}"] for t in ("qweight", "qzeros", "scales")]
+    torch.testing.assert_close(ref_awq.dequantize_awq_gemm(*tensors, group_size=128),
+                               dequantize_awq_gemm(*tensors, group_size=128), rtol=0, atol=0)
+
 
 def test_layer_calibration_is_as_accurate_as_the_reference_pipeline():
     """The same HF Qwen3 layer and calibration activations through both pipelines: the error of the
