@@ -25,7 +25,11 @@ in a child process (its own rank 0 and workers, its own process group) that this
 through a pipe.  Decode rank r exports its pools to prefill rank r (CUDA IPC; both hold the same
 KV-head shard), and every prefill rank pushes its shard of each handed-off block with the same
 kernel; the push returns once the blocks landed, before the decode side admits the sequences.
-No speculative draft in either mode.
+
+An EAGLE3 draft is supported with one GPU per side: the prefill engine also runs the draft's
+prefill, the same block ids of the draft pools are pushed with the target's, and the draft K/V
+length (host state of the speculative executor) moves with the sequence, so the decode engine
+drafts exactly as a single speculative engine would.  Tensor-parallel sides take no draft.
 """
 import os
 import socket
@@ -203,8 +207,8 @@ class PDEngine:
         tp = kwargs.get("tensor_parallel_size", 1)
         if len(pre) != tp or len(dec) != tp:
             raise ValueError("pd_disaggregation needs tensor_parallel_size devices on each side")
-        if kwargs.get("speculative_model"):
-            raise ValueError("pd_disaggregation does not support a speculative draft model")
+        if kwargs.get("speculative_model") and tp > 1:
+            raise ValueError("pd_disaggregation with a speculative draft model needs one GPU per side")
         self.pd_stats = {"handoffs": 0, "blocks_pushed": 0, "blocks_reused": 0, "bytes_pushed": 0,
                          "parked_steps": 0}
         self._parked: list[Sequence] = []
@@ -418,9 +422,21 @@ class PDEngine:
         if not moved:
             self.pd_stats["parked_steps"] += 1
             return
+        draft = pre_r.draft_model is not None
+        if draft:
+            # the draft's prompt K/V lives in the same block ids of the draft pools; the length of
+            # the draft K/V (host state of the speculative executor) moves with the sequence
+            for s in moved:
+                n = pre_r.spec.draft_kv_len.pop(s.seq_id, None)
+                if n is not None:
+                    dec_r.spec.draft_kv_len[s.seq_id] = n
+                pre_r.spec.prev_correction.pop(s.seq_id, None)
         if src:
             with self._on(self.prefill):
                 kv_ops.push_blocks(pre_r.k_cache, pre_r.v_cache, dec_r.k_cache, dec_r.v_cache, src, dst)
+                if draft:
+                    kv_ops.push_blocks(pre_r.draft_k_cache.unsqueeze(0), pre_r.draft_v_cache.unsqueeze(0),
+                                       dec_r.draft_k_cache.unsqueeze(0), dec_r.draft_v_cache.unsqueeze(0), src, dst)
                 if self._cuda:
                     ev = torch.cuda.Event()
                     ev.record()
@@ -428,6 +444,8 @@ class PDEngine:
                 with self._on(self.decode):
                     torch.cuda.current_stream().wait_event(ev)
         per_block = 2 * pre_r.k_cache[:, 0].numel() * pre_r.k_cache.element_size()
+        if draft:
+            per_block += 2 * pre_r.draft_k_cache[0].numel() * pre_r.draft_k_cache.element_size()
         self.pd_stats["handoffs"] += len(moved)
         self.pd_stats["blocks_pushed"] += len(src)
         self.pd_stats["bytes_pushed"] += len(src) * per_block

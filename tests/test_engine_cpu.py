@@ -319,3 +319,28 @@ def test_step_is_lockstep_with_the_reference_engine_step(ckpts, speculative):
     assert ours.speculative_batch_calls == proxy.speculative_batch_calls
     ours.exit()
     driven.exit()
+
+
+def test_pd_disaggregation_with_eagle3_keeps_the_draft_state(ckpts):
+    """Prefill/decode disaggregation with an EAGLE3 draft: the draft's prompt K/V and its length move
+    with each sequence, so the decode side drafts exactly what a single speculative engine drafts
+    (same draft tokens step by step) and the output equals plain decoding."""
+    tgt, draft = ckpts
+    prompts = _prompts(4, seed=9)
+    base, _ = _run(tgt, prompts, max_tokens=16)
+    kw = dict(device="cpu", enforce_eager=True, kvcache_block_size=16, max_model_len=256, num_kvcache_blocks=64,
+              speculative_model=draft, speculative_trace=True)
+    runs = []
+    for pd in (False, True):
+        extra = dict(pd_disaggregation=True, pd_prefill_devices=(0,), pd_decode_devices=(0,)) if pd else {}
+        llm = LLM(tgt, **kw, **extra)
+        llm.model_runner.sampler = GreedySampler()
+        out = llm.generate(prompts, SamplingParams(temperature=0.5, max_tokens=16, ignore_eos=True), use_tqdm=False)
+        m = llm.get_metrics()
+        llm.exit()
+        drafts = [[e["draft_token_ids"] for e in r["speculative_trace"]] for r in m["requests"]]
+        runs.append(([o["token_ids"] for o in out], drafts, m["summary"]))
+    (single, d_single, _), (pd_out, d_pd, summary) = runs
+    assert single == base and pd_out == base
+    assert d_pd == d_single and any(d_single)
+    assert summary["pd"]["handoffs"] == 4 and summary["speculative"]["steps"] > 0
