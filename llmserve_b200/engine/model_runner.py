@@ -189,7 +189,7 @@ class ModelRunner:
         # release device memory so another engine can be built in this process
         self._bind_pools(None, None)
         self.k_cache = self.v_cache = self.draft_k_cache = self.draft_v_cache = None
-        self.peer_k = self.peer_v = None
+        self.peer_k = self.peer_v = self.peer_dk = self.peer_dv = None
         self.decode_workspace = None
         self._release_pd()
         self.graph_vars = None
@@ -325,7 +325,7 @@ class ModelRunner:
         nkv = hf.num_key_value_heads // self.world_size
         shape = (hf.num_hidden_layers, blocks, nkv, self.block_size, hf.head_dim)
         if cfg.pd_role == "decode":
-            self.k_cache, self.v_cache = self._exportable_pools(shape)
+            self.k_cache, self.v_cache = self._exportable_pools(shape, "kv")
         else:
             self.k_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
             self.v_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
@@ -333,8 +333,11 @@ class ModelRunner:
         if self.draft_model is not None:
             d = self.draft_model
             dshape = (blocks, d.num_kv_heads, self.block_size, d.head_dim)
-            self.draft_k_cache = torch.zeros(dshape, dtype=self.dtype, device=self.device)
-            self.draft_v_cache = torch.zeros(dshape, dtype=self.dtype, device=self.device)
+            if cfg.pd_role == "decode":
+                self.draft_k_cache, self.draft_v_cache = self._exportable_pools(dshape, "draft")
+            else:
+                self.draft_k_cache = torch.zeros(dshape, dtype=self.dtype, device=self.device)
+                self.draft_v_cache = torch.zeros(dshape, dtype=self.dtype, device=self.device)
         self._bind_pools(self.k_cache, self.v_cache, self.draft_k_cache, self.draft_v_cache)
         if self.is_cuda:
             # the block tables the decode graphs pass cover whole blocks: size the split-KV
@@ -346,84 +349,112 @@ class ModelRunner:
                 max(cfg.max_num_seqs, 16), heads, hf.head_dim, max_ctx, self.device)
 
     # ---- prefill/decode disaggregation: KV pools shared across processes ---------------------
-    def _exportable_pools(self, shape):
+    def _exportable_pools(self, shape, key: str):
         """K and V pools another process can map: ordinary device tensors shared through CUDA IPC
-        (torch's tensor reduction) on the GPU, a named shared-memory segment on the CPU tier."""
+        (torch's tensor reduction) on the GPU, a named shared-memory segment on the CPU tier.
+        ``key`` names the pair in the descriptor (``"kv"`` target, ``"draft"`` EAGLE3 draft)."""
+        if not hasattr(self, "_pd_descs"):
+            self._pd_descs, self._pd_pools, self._pd_shms = {}, [], []
         if self.is_cuda:
             from torch.multiprocessing.reductions import reduce_tensor
             pools = torch.zeros((2, *shape), dtype=self.dtype, device=self.device)
-            self._pd_desc = {"kind": "cuda", "ipc": reduce_tensor(pools)}
+            desc = {"kind": "cuda", "ipc": reduce_tensor(pools)}
         else:
             from multiprocessing.shared_memory import SharedMemory
             esize = torch.tensor([], dtype=self.dtype).element_size()
             nbytes = 2 * esize
             for d in shape:
                 nbytes *= d
-            self._pd_shm = SharedMemory(create=True, size=nbytes)
-            raw = torch.frombuffer(self._pd_shm.buf, dtype=torch.uint8)
+            shm = SharedMemory(create=True, size=nbytes)
+            self._pd_shms.append(shm)
+            raw = torch.frombuffer(shm.buf, dtype=torch.uint8)
             raw.zero_()
             pools = raw.view(self.dtype).view(2, *shape)
-            self._pd_desc = {"kind": "shm", "name": self._pd_shm.name}
-        self._pd_desc.update(shape=tuple(shape), dtype=str(self.dtype).replace("torch.", ""))
-        self._pd_pools = pools
+            desc = {"kind": "shm", "name": shm.name}
+        desc.update(shape=tuple(shape), dtype=str(self.dtype).replace("torch.", ""))
+        self._pd_descs[key] = desc
+        self._pd_pools.append(pools)
         return pools[0], pools[1]
 
     def export_kv(self):
-        """Every rank's pool descriptor, gathered on rank 0 (the decode side of a disaggregated pair)."""
-        mine = getattr(self, "_pd_desc", None)
+        """Every rank's pool descriptors (``{"kv": ..., "draft": ...}``), gathered on rank 0 (the
+        decode side of a disaggregated pair)."""
+        mine = getattr(self, "_pd_descs", None)
         if self.world_size == 1:
             return [mine]
         out = [None] * self.world_size
         torch.distributed.all_gather_object(out, mine)
         return out
 
-    def open_peer_kv(self, descs):
-        """Prefill side: map the decode rank with this rank's index (same KV-head shard).  On the
-        GPU the mapping is a tensor on the decode GPU; the push kernel stores into it over NVLink."""
-        d = descs[self.rank]
+    def _map_pools(self, d):
         if d["kind"] == "cuda":
             fn, args = d["ipc"]
-            pools = fn(*args)
-        else:
-            from multiprocessing import resource_tracker
-            from multiprocessing.shared_memory import SharedMemory
-            self._peer_shm = SharedMemory(name=d["name"])
-            try:     # the decode process owns (and unlinks) the segment, not this one
-                resource_tracker.unregister(self._peer_shm._name, "shared_memory")
-            except Exception:
-                pass
-            raw = torch.frombuffer(self._peer_shm.buf, dtype=torch.uint8)
-            pools = raw.view(getattr(torch, d["dtype"])).view(2, *d["shape"])
+            return fn(*args)
+        from multiprocessing import resource_tracker
+        from multiprocessing.shared_memory import SharedMemory
+        shm = SharedMemory(name=d["name"])
+        try:     # the decode process owns (and unlinks) the segment, not this one
+            resource_tracker.unregister(shm._name, "shared_memory")
+        except Exception:
+            pass
+        self._peer_shms.append(shm)
+        raw = torch.frombuffer(shm.buf, dtype=torch.uint8)
+        return raw.view(getattr(torch, d["dtype"])).view(2, *d["shape"])
+
+    def open_peer_kv(self, descs):
+        """Prefill side: map the decode rank with this rank's index (same KV-head shard; the draft's
+        pools are replicated).  On the GPU a mapping is a tensor on the decode GPU; the push kernel
+        stores into it over NVLink."""
+        d = descs[self.rank]
+        self._peer_shms, self._peer_pools = [], []
+        pools = self._map_pools(d["kv"])
         if tuple(pools.shape[3:]) != tuple(self.k_cache.shape[2:]) or pools.shape[1] != self.k_cache.shape[0]:
             raise ValueError("prefill and decode KV pools have different block shapes")
-        self._peer_pools = pools
+        self._peer_pools.append(pools)
         self.peer_k, self.peer_v = pools[0], pools[1]
+        self.peer_dk = self.peer_dv = None
+        if self.draft_model is not None:
+            if "draft" not in d:
+                raise ValueError("the decode side has no draft pools")
+            dpools = self._map_pools(d["draft"])
+            if tuple(dpools.shape[2:]) != tuple(self.draft_k_cache.shape[1:]):
+                raise ValueError("prefill and decode draft pools have different block shapes")
+            self._peer_pools.append(dpools)
+            self.peer_dk, self.peer_dv = dpools[0], dpools[1]
 
     def push_kv(self, src_ids, dst_ids):
-        """Copy blocks of this rank's pool into the mapped decode pool; returns when they landed."""
+        """Copy blocks of this rank's pools (target, and draft when present) into the mapped decode
+        pools; returns when they landed."""
         from llmserve_b200.ops import kv as kv_ops
         kv_ops.push_blocks(self.k_cache, self.v_cache, self.peer_k, self.peer_v, src_ids, dst_ids)
+        if getattr(self, "peer_dk", None) is not None:
+            kv_ops.push_blocks(self.draft_k_cache.unsqueeze(0), self.draft_v_cache.unsqueeze(0),
+                               self.peer_dk.unsqueeze(0), self.peer_dv.unsqueeze(0), src_ids, dst_ids)
         if self.is_cuda:
             torch.cuda.current_stream(self.device).synchronize()
+
+    def set_draft_lengths(self, lengths: dict):
+        """Decode side of a disaggregated pair: the draft K/V length of each handed-off sequence."""
+        self.spec.draft_kv_len.update(lengths)
 
     def _release_pd(self):
         import gc
         self._peer_pools = self._pd_pools = None
+        self.peer_k = self.peer_v = self.peer_dk = self.peer_dv = None
         gc.collect()                       # drop the tensors that view the shared segments
-        for name, unlink in (("_peer_shm", False), ("_pd_shm", True)):
-            shm = getattr(self, name, None)
-            if shm is None:
-                continue
-            try:
-                shm.close()
-            except BufferError:            # a view is still alive; the OS reclaims it at exit
-                pass
-            if unlink:
+        for shms, unlink in ((getattr(self, "_peer_shms", None) or [], False),
+                             (getattr(self, "_pd_shms", None) or [], True)):
+            for shm in shms:
                 try:
-                    shm.unlink()
-                except FileNotFoundError:
+                    shm.close()
+                except BufferError:        # a view is still alive; the OS reclaims it at exit
                     pass
-            setattr(self, name, None)
+                if unlink:
+                    try:
+                        shm.unlink()
+                    except FileNotFoundError:
+                        pass
+        self._peer_shms, self._pd_shms = [], []
 
     def get_memory_metrics(self) -> dict:
         seen, model_bytes = set(), 0

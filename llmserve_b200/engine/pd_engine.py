@@ -26,10 +26,10 @@ through a pipe.  Decode rank r exports its pools to prefill rank r (CUDA IPC; bo
 KV-head shard), and every prefill rank pushes its shard of each handed-off block with the same
 kernel; the push returns once the blocks landed, before the decode side admits the sequences.
 
-An EAGLE3 draft is supported with one GPU per side: the prefill engine also runs the draft's
-prefill, the same block ids of the draft pools are pushed with the target's, and the draft K/V
-length (host state of the speculative executor) moves with the sequence, so the decode engine
-drafts exactly as a single speculative engine would.  Tensor-parallel sides take no draft.
+With an EAGLE3 draft the prefill engine also runs the draft's prefill, the same block ids of the
+draft pools are pushed with the target's (every rank holds the whole draft pool), and the draft
+K/V length (host state of the speculative executor) moves with the sequence, so the decode engine
+drafts exactly as a single speculative engine would.
 """
 import os
 import socket
@@ -94,8 +94,10 @@ class _DecodeServer:
             out.append((seq_id, list(seq.block_table), hits))
         return out
 
-    def admit(self, seq_ids):
+    def admit(self, seq_ids, draft_lengths=None):
         from llmserve_b200.engine.sequence import SequenceStatus
+        if draft_lengths:
+            self.eng.model_runner.call("set_draft_lengths", draft_lengths)     # every decode rank
         for sid in seq_ids:
             s = self.pending.pop(sid)
             s.status = SequenceStatus.RUNNING
@@ -103,12 +105,16 @@ class _DecodeServer:
             self.eng.scheduler.running.append(s)
 
     def step(self):
+        """One decode step: finished sequences, sequences that emitted, tokens, and the speculative
+        counters of the finished sequences' records (the parent keeps the request table)."""
         if self.eng.is_finished():
-            return [], [], 0
+            return [], [], 0, {}
         done, n = self.eng.step()
+        spec = {}
         for sid, _ in done:
-            self.eng.request_metrics.pop(sid, None)
-        return done, list(self.eng.last_step_events.get("decode_seq_ids", [])), n
+            m = self.eng.request_metrics.pop(sid, None) or {}
+            spec[sid] = {k: v for k, v in m.items() if k.startswith("speculative_")}
+        return done, list(self.eng.last_step_events.get("decode_seq_ids", [])), n, spec
 
     def set_sampler(self, sampler):
         self.eng.model_runner.sampler = sampler
@@ -207,8 +213,6 @@ class PDEngine:
         tp = kwargs.get("tensor_parallel_size", 1)
         if len(pre) != tp or len(dec) != tp:
             raise ValueError("pd_disaggregation needs tensor_parallel_size devices on each side")
-        if kwargs.get("speculative_model") and tp > 1:
-            raise ValueError("pd_disaggregation with a speculative draft model needs one GPU per side")
         self.pd_stats = {"handoffs": 0, "blocks_pushed": 0, "blocks_reused": 0, "bytes_pushed": 0,
                          "parked_steps": 0}
         self._parked: list[Sequence] = []
@@ -334,7 +338,7 @@ class PDEngine:
     def _remote_step(self, t0, outputs, tokens):
         self._remote_handoff()
         if self._remote_seqs:
-            done, emitted, n = self.remote.call("step")
+            done, emitted, n, spec = self.remote.call("step")
             t = perf_counter()
             tokens += n
             for sid in emitted:
@@ -347,6 +351,7 @@ class PDEngine:
                 m = self.request_metrics.get(sid)
                 if m is not None:
                     m["finish_time"], m["success"], m["output_tokens"] = t, True, len(toks)
+                    m.update(spec.get(sid, {}))
                 self._remote_seqs.pop(sid, None)
                 outputs.append((sid, toks))
         self.last_step_events = {"step_start": t0, "step_end": perf_counter(), "num_tokens": tokens,
@@ -381,8 +386,15 @@ class PDEngine:
             bm.deallocate(s)                          # after every rank's copy landed
             self._parked.remove(s)
             self._remote_seqs[s.seq_id] = s
-        self.remote.call("admit", [s.seq_id for s in moved])
+        ids = [s.seq_id for s in moved]
+        lengths = None
+        if pre_r.draft_model is not None:
+            lengths = {sid: pre_r.spec.draft_kv_len[sid] for sid in ids if sid in pre_r.spec.draft_kv_len}
+            pre_r.call("clear_speculative_state", ids)                        # every prefill rank
+        self.remote.call("admit", ids, lengths)
         per_block = 2 * pre_r.k_cache[:, 0].numel() * pre_r.k_cache.element_size() * pre_r.world_size
+        if pre_r.draft_model is not None:
+            per_block += 2 * pre_r.draft_k_cache[0].numel() * pre_r.draft_k_cache.element_size() * pre_r.world_size
         self.pd_stats["handoffs"] += len(moved)
         self.pd_stats["blocks_pushed"] += len(src)
         self.pd_stats["bytes_pushed"] += len(src) * per_block

@@ -52,26 +52,43 @@ def test_tp2_gloo_matches_tp1_with_and_without_speculation(ckpts):
     assert _gen(tgt, 2, draft) == ref
 
 
-def test_disaggregated_tp2_prefill_tp2_decode_over_gloo(ckpts):
+@pytest.mark.parametrize("speculative", [False, True])
+def test_disaggregated_tp2_prefill_tp2_decode_over_gloo(ckpts, speculative):
     """Prefill TP=2 (this process + a worker) and decode TP=2 (a server process + its worker), KV
     blocks pushed rank to rank into the decode pools (shared segments on the CPU tier): the tokens
-    equal a single TP=1 engine's."""
-    tgt, _ = ckpts
+    equal a single TP=1 engine's.  With an EAGLE3 draft the draft pools and lengths move too: the
+    decode side drafts the same tokens, step by step, as a single TP=2 speculative engine."""
+    tgt, draft = ckpts
     ref = _gen(tgt, 1)
     g = torch.Generator().manual_seed(11)
     prompts = [torch.randint(0, 1024, (int(n),), generator=g).tolist() for n in (9, 33, 17, 50)]
-    llm = LLM(tgt, device="cpu", enforce_eager=True, num_kvcache_blocks=64, kvcache_block_size=16, max_model_len=256,
-              tensor_parallel_size=2, comm_timeout_s=60, pd_disaggregation=True, pd_prefill_devices=(0, 1),
-              pd_decode_devices=(2, 3))
-    try:
-        llm.model_runner.sampler = GreedySampler()
-        out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=12, ignore_eos=True))]
-        m = llm.get_metrics()["summary"]
-    finally:
-        llm.exit()
+    kw = dict(device="cpu", enforce_eager=True, num_kvcache_blocks=64, kvcache_block_size=16, max_model_len=256,
+              tensor_parallel_size=2, comm_timeout_s=60)
+    if speculative:
+        kw.update(speculative_model=draft, speculative_trace=True)
+    runs = []
+    for pd in ((True, False) if speculative else (True,)):
+        extra = dict(pd_disaggregation=True, pd_prefill_devices=(0, 1), pd_decode_devices=(2, 3)) if pd else \
+            dict(distributed_init_method=f"tcp://127.0.0.1:{_port()}")
+        llm = LLM(tgt, **kw, **extra)
+        try:
+            llm.model_runner.sampler = GreedySampler()
+            out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=12, ignore_eos=True),
+                                                        use_tqdm=False)]
+            met = llm.get_metrics()
+        finally:
+            llm.exit()
+        runs.append((out, met))
+    out, met = runs[0]
+    m = met["summary"]
     assert out == ref
     assert m["pd"]["handoffs"] == 4 and m["pd"]["blocks_pushed"] > 0 and m["num_finished"] == 4
     assert m["total_output_tokens"] == 48
+    if speculative:
+        def drafts(metrics):
+            return [[e["draft_token_ids"] for e in r["speculative_trace"]] for r in metrics["requests"]]
+        assert m["speculative"]["steps"] > 0
+        assert drafts(met) == drafts(runs[1][1]) and any(drafts(met))
 
 
 def test_tp2_gloo_temperature_sampling_is_rank_consistent(ckpts):
