@@ -1,0 +1,48 @@
+"""The parts of ``bench.py`` that run without a GPU: the clock sampler's summary of nvidia-smi
+samples (median SM clock, throttle reasons that invalidate a run) and the reference arm's
+``unavailable`` line for tensor-parallel runs."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+
+
+def test_clock_summary_takes_the_median_and_collects_active_reasons(tmp_path):
+    s = bench.ClockSampler([0])
+    s.path = str(tmp_path / "clocks.csv")
+    rows = [
+        "0, 1965, 1965, 700.5, 0x0, Not Active, Not Active, Not Active, Not Active",
+        "0, 1800, 1965, 990.1, 0x4, Not Active, Not Active, Not Active, Active",
+        "0, 1890, 1965, 985.0, 0x4, Not Active, Not Active, Not Active, Active",
+        "garbage line",
+    ]
+    (tmp_path / "clocks.csv").write_text("\n".join(rows) + "\n")
+    out = s.summary()
+    assert out["sm_mhz"] == 1890 and out["sm_max_mhz"] == 1965 and out["samples"] == 3
+    assert out["reasons"] == ["sw_power_cap"] and out["power_w_max"] == 990.1
+
+
+def test_clock_summary_without_samples_says_so(tmp_path):
+    s = bench.ClockSampler([0])
+    s.path = str(tmp_path / "missing.csv")
+    assert s.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+
+def test_visible_indices_follow_cuda_visible_devices(monkeypatch):
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "3,5,6")
+    assert bench.visible_indices(2) == [3, 5]
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert bench.visible_indices(4) == [0, 1, 2, 3]
+
+
+def test_reference_arm_at_tp2_prints_its_unavailable_line():
+    proc = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--gpus", "2"], cwd=ROOT,
+                          capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    line = json.loads(proc.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "unavailable" in line
