@@ -238,8 +238,8 @@ class SpeculativeExecutor:
             starts = [row[2] for row in host]
             timing = {"target_decode_time": target_decode_time, "fresh": len(fresh), "draft_time": 0.0,
                       "verify_time": graph_time, "accept_time": 0.0, "fwd_time": 0.0, "sample_time": 0.0}
-            return self._finish(seqs, merged, accepts, starts, sg.corr_aux[:B].clone(), kv0, None, n_or=g + 1,
-                                timing=timing, t_total=t_total)
+            return self._finish(seqs, merged, accepts, starts, sg.corr_aux[:B].clone(), kv0, None,
+                                verify_width=g + 1, timing=timing, t_total=t_total)
         t = perf_counter()
         draft_tokens = torch.empty(B, g, dtype=torch.int64, device=dev)
         mapped_logits = []
@@ -310,10 +310,10 @@ class SpeculativeExecutor:
         timing = {"target_decode_time": target_decode_time, "fresh": len(fresh), "draft_time": draft_time,
                   "verify_time": verify_time, "accept_time": accept_time, "fwd_time": fwd_time,
                   "sample_time": sample_time}
-        return self._finish(seqs, merged, accepts, starts, corr_aux, kv0, logits, n_or=n, timing=timing,
+        return self._finish(seqs, merged, accepts, starts, corr_aux, kv0, logits, verify_width=n, timing=timing,
                             t_total=t_total)
 
-    def _finish(self, seqs, merged, accepts, starts, corr_aux, kv0, logits, *, n_or, timing, t_total):
+    def _finish(self, seqs, merged, accepts, starts, corr_aux, kv0, logits, *, verify_width, timing, t_total):
         """Per-sequence outputs of a chain step and the state the next step starts from: the
         correction token with its auxiliary hidden state, and the kept draft K/V length."""
         r = self.r
@@ -327,7 +327,7 @@ class SpeculativeExecutor:
             self.draft_kv_len[s.seq_id] = kv0[i] + min(acc + 1, g)
             debug = None
             if r.speculative_trace and logits is not None:
-                debug = self._debug(logits, i, n_or, starts[i], list(drafts), tokens, acc, all_ok, kv0[i])
+                debug = self._debug(logits, i, verify_width, starts[i], list(drafts), tokens, acc, all_ok, kv0[i])
             outputs.append(SpeculativeDecodeOutput(tokens, g, acc, bool(all_ok), len(tokens), None, debug))
         kv_time = perf_counter() - t
         total = perf_counter() - t_total
