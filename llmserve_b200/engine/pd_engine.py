@@ -295,16 +295,22 @@ class PDEngine:
                                  "parked": len(self._parked)}
         return outputs, tokens
 
-    def generate(self, prompts, sampling_params, use_tqdm: bool = False):
+    def generate(self, prompts, sampling_params, use_tqdm: bool = True):
+        from tqdm.auto import tqdm
+        bar = tqdm(total=len(prompts), desc="Generating", dynamic_ncols=True, disable=not use_tqdm)
         if not isinstance(sampling_params, list):
             sampling_params = [sampling_params] * len(prompts)
         for p, sp in zip(prompts, sampling_params):
             self.add_request(p, sp)
         done = {}
         while not self.is_finished():
-            out, _ = self.step()
+            t = perf_counter()
+            out, n = self.step()
+            bar.set_postfix({"tok/s": f"{int(n / max(perf_counter() - t, 1e-9))}"})
             for sid, toks in out:
                 done[sid] = toks
+                bar.update(1)
+        bar.close()
         return [{"text": self.tokenizer.decode(done[k]), "token_ids": done[k]} for k in sorted(done)]
 
     def get_metrics(self) -> dict:
