@@ -19,7 +19,7 @@ are grouped at the end:
 * ``overlap_decode``       -- launch decode step N+1 from device-resident tokens before step N is
                               read on the host (greedy, graph decode); on by default.
 * ``speculative_cuda_graphs`` -- capture the greedy EAGLE3 chain step (drafts, packed verify,
-                              acceptance) in CUDA graphs per batch bucket (TP = 1); off by default.
+                              acceptance) in CUDA graphs per batch bucket; off by default.
 
 ``awq_backend="triton"`` is accepted for compatibility and runs the sm_100a W4A16 kernel.
 """

@@ -89,10 +89,10 @@ class SpeculativeExecutor:
 
     def setup_graphs(self):
         """Graphs (host tier: static-buffer emulation) of the greedy chain step, when enabled and
-        in scope: TP = 1, greedy acceptance, no tree."""
+        in scope: greedy acceptance, no tree.  Every rank captures its own (same order)."""
         r = self.r
         cfg = r.config
-        if (not getattr(cfg, "speculative_cuda_graphs", False) or r.draft_model is None or r.world_size != 1
+        if (not getattr(cfg, "speculative_cuda_graphs", False) or r.draft_model is None
                 or r.speculative_accept_mode != "greedy" or r.speculative_tree_nodes
                 or (r.is_cuda and r.enforce_eager)):
             return

@@ -18,8 +18,9 @@ into static device buffers by the executor (the fresh ones come from the target 
 carried ones from the previous step's correction).  Padded rows of a bucket store nothing
 (slot -1) and their results are ignored.
 
-Scope: tensor parallelism 1, greedy acceptance, chain drafting (no tree), no per-step trace.
-Other steps run eagerly.  It is opt-in (``Config.speculative_cuda_graphs``).  On the host tier
+Scope: greedy acceptance, chain drafting (no tree), no per-step trace; every tensor-parallel
+rank captures and replays its own graphs (the verify's vocab-parallel argmax is a collective
+inside them, and the draft is replicated).  Other steps run eagerly.  It is opt-in (``Config.speculative_cuda_graphs``).  On the host tier
 (``device="cpu"``) the same body runs eagerly over the same static buffers, which is how the
 buffer layout and the step logic are tested without a GPU.
 """

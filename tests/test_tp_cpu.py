@@ -50,6 +50,7 @@ def test_tp2_gloo_matches_tp1_with_and_without_speculation(ckpts):
     ref = _gen(tgt, 1)
     assert _gen(tgt, 2) == ref
     assert _gen(tgt, 2, draft) == ref
+    assert _gen(tgt, 2, draft, speculative_cuda_graphs=True) == ref      # graph step layout, every rank
 
 
 @pytest.mark.parametrize("speculative", [False, True])
