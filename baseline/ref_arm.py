@@ -94,6 +94,19 @@ def make_checkpoint(layers: int) -> str:
     return path
 
 
+def make_eagle3_checkpoint() -> str:
+    """A random-init EAGLE3 speculator for the Qwen3-8B shape in the RedHat layout (one decoder
+    layer, fc 3 x 4096 -> 4096, draft vocabulary 32000 with d2t / t2d); data only."""
+    sys.path.insert(0, ROOT)
+    from llmserve_b200.models.synthetic import QWEN3_8B, write_eagle3_checkpoint
+    path = os.path.join(tempfile.gettempdir(), "lsb_ref_eagle3_qwen3_8b")
+    done = os.path.join(path, ".complete")
+    if not os.path.exists(done):
+        write_eagle3_checkpoint(path, QWEN3_8B, draft_vocab=32000, nested=True, include_embedding=False)
+        open(done, "w").close()
+    return path
+
+
 def run(args, metric: str):
     rank = int(os.environ.get("RANK", 0))
     if rank > 0:
@@ -117,10 +130,13 @@ def run(args, metric: str):
             "RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK", "ROLE_WORLD_SIZE",
             "GROUP_WORLD_SIZE", "ROLE_NAME", "MASTER_ADDR", "MASTER_PORT"]:
         os.environ.pop(key, None)
-    llm = LLM(path, tensor_parallel_size=world, enforce_eager=args.eager,
+    eagle3 = bool(getattr(args, "eagle3", False))
+    # the reference speculates only in eager mode (its llm_engine.py:359-368), so --eagle3 runs eager
+    extra = dict(speculative_model=make_eagle3_checkpoint(), speculative_gamma=3) if eagle3 else {}
+    llm = LLM(path, tensor_parallel_size=world, enforce_eager=args.eager or eagle3,
               max_model_len=args.input_len + args.output_len + 16,
               max_num_batched_tokens=max(16384, args.concurrency * args.input_len), max_num_seqs=args.concurrency,
-              distributed_init_method=f"tcp://127.0.0.1:{_free_port()}")
+              distributed_init_method=f"tcp://127.0.0.1:{_free_port()}", **extra)
 
     class ArgmaxSampler:            # the reference benchmark's sampler (benchmarks/serve.py)
         def __call__(self, logits, temperatures):
@@ -167,12 +183,15 @@ def run(args, metric: str):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: random-init Qwen3-8B weights N(0,0.02) written as HF safetensors, prompt ids uniform over the vocab",
-        "config": {"model": "Qwen3-8B" if args.layers == 36 else f"Qwen3-8B-{args.layers}L",
+        "config": {"model": ("Qwen3-8B" if args.layers == 36 else f"Qwen3-8B-{args.layers}L")
+                   + ("+EAGLE3" if eagle3 else ""),
                    "global_batch": args.concurrency, "seq_len": args.input_len + args.output_len,
-                   "parallelism": f"tp{world}", "cuda_graphs": not args.eager,
+                   "parallelism": f"tp{world}", "cuda_graphs": not (args.eager or eagle3),
                    "workload": f"closed-loop {args.input_len} in / {args.output_len} out, concurrency {args.concurrency}, greedy"},
         "e2e": {"value": round(n / wall, 2), "unit": "tok/s"},
         "latency": {"ttft_p99_ms": None if m["ttft"]["p99"] is None else round(m["ttft"]["p99"] * 1e3, 2),
                     "tpot_p99_ms": None if m["tpot"]["p99"] is None else round(m["tpot"]["p99"] * 1e3, 3)},
+        "speculative": None if not eagle3 else {k: (m.get("speculative") or {}).get(k) for k in
+                                                ("steps", "acceptance_rate", "acceptance_length")},
         "timing": "CUDA events on the reference's rank-0 device", "checkpoint_write_s": round(t_ckpt, 1),
     }), flush=True)
