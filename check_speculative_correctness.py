@@ -77,6 +77,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--speculative-tree-nodes", type=int, choices=[0, 6, 10], default=0)
     p.add_argument("--speculative-accept-mode", choices=["greedy", "rejection"], default="greedy")
     p.add_argument("--speculative-trace", action="store_true")
+    p.add_argument("--speculative-cuda-graphs", action="store_true",
+                   help="run the speculative engine's greedy chain step through its CUDA graphs")
     p.add_argument("--argmax-sampler", action="store_true")
     p.add_argument("--max-model-len", type=int, default=64)
     p.add_argument("--max-num-batched-tokens", type=int, default=64)
@@ -120,12 +122,14 @@ class Checker:
         import torch
         torch.manual_seed(self.args.seed)
         a = self.args
-        return self.factory(self.model, enforce_eager=True, tensor_parallel_size=1, max_model_len=a.max_model_len,
-                            max_num_batched_tokens=a.max_num_batched_tokens,
+        graphs = speculative and getattr(a, "speculative_cuda_graphs", False)
+        extra = {"speculative_cuda_graphs": True} if graphs else {}
+        return self.factory(self.model, enforce_eager=not graphs, tensor_parallel_size=1,
+                            max_model_len=a.max_model_len, max_num_batched_tokens=a.max_num_batched_tokens,
                             speculative_model=self.draft if speculative else None,
                             speculative_gamma=a.speculative_gamma, speculative_tree_nodes=tree_nodes,
                             speculative_accept_mode=accept_mode, speculative_trace=trace, device=a.device,
-                            load_format=a.load_format, seed=a.seed)
+                            load_format=a.load_format, seed=a.seed, **extra)
 
     def _drain(self, engine, outputs, events, limit):
         steps = 0

@@ -57,3 +57,17 @@ def test_check_logic_flags_bad_metrics():
     assert csc.parse_batch_sizes("4,2,2") == [2, 4]
     with pytest.raises(ValueError):
         csc.parse_token_ids(" , ")
+
+
+def test_graphed_speculative_step_tokens_match_on_cpu(ckpts, tmp_path):
+    """``--speculative-cuda-graphs``: the speculative engine takes the graphed chain step (its
+    static-buffer emulation on the CPU tier) and still matches plain decoding token for token."""
+    tgt, draft = ckpts
+    out = tmp_path / "g.json"
+    rc = csc.main(["--model", tgt, "--speculative-model", draft, "--device", "cpu", "--argmax-sampler",
+                   "--speculative-cuda-graphs", "--prompt-token-ids", "8,19,301,44,2,70,5", "--output-len", "14",
+                   "--max-model-len", "128", "--require-token-match", "--output-json", str(out)],
+                  engine_factory=_factory)
+    report = json.loads(out.read_text())
+    assert rc == 0, report["checks"]
+    assert report["checks"]["token_ids_match"] and len(report["baseline"]["token_ids"]) == 14
