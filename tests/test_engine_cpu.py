@@ -344,3 +344,15 @@ def test_pd_disaggregation_with_eagle3_keeps_the_draft_state(ckpts):
     assert single == base and pd_out == base
     assert d_pd == d_single and any(d_single)
     assert summary["pd"]["handoffs"] == 4 and summary["speculative"]["steps"] > 0
+
+
+def test_awq_target_with_eagle3_equals_awq_plain_decoding(tmp_path, ckpts):
+    """An AutoAWQ W4A16 target with an EAGLE3 draft (the reference runs AWQ eager, TP 1, and its
+    speculation separately): speculative output equals the AWQ target's plain decoding."""
+    from llmserve_b200.models.synthetic import write_awq_checkpoint
+    _, draft = ckpts
+    awq = write_awq_checkpoint(str(tmp_path / "awq"), TINY, seed=3)
+    prompts = _prompts(3, seed=1)
+    base, _ = _run(awq, prompts, max_tokens=12)
+    spec, m = _run(awq, prompts, max_tokens=12, speculative_model=draft)
+    assert spec == base and m["summary"]["speculative"]["steps"] > 0
