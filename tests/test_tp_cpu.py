@@ -245,10 +245,10 @@ def test_disaggregated_decode_server_loss_surfaces_as_an_error(ckpts):
             pass
 
 
-def test_awq_engine_on_the_host_matches_dequantized_dense_and_shards_over_gloo(tmp_path):
+def test_awq_engine_on_the_host_matches_dequantized_dense_and_shards_over_gloo(tmp_path, ckpts):
     """AutoAWQ GEMM g128 checkpoint on the fp32 host path: the same tokens as a dense checkpoint
-    holding the dequantised weights, and TP=2 (packed qweight/qzeros/scales sliced per rank) equal
-    to TP=1."""
+    holding the dequantised weights, and TP=2 (packed qweight/qzeros/scales sliced per rank, with
+    and without an EAGLE3 draft) equal to TP=1."""
     import json
 
     from safetensors import safe_open
@@ -277,3 +277,4 @@ def test_awq_engine_on_the_host_matches_dequantized_dense_and_shards_over_gloo(t
     ref = _gen(str(dense_dir), 1)
     assert _gen(awq, 1) == ref
     assert _gen(awq, 2) == ref
+    assert _gen(awq, 2, ckpts[1]) == ref          # with an EAGLE3 draft, tensor parallel
