@@ -21,14 +21,12 @@ class WorkloadClass:
     output_len: int
 
     def __post_init__(self):
+        bad = [f"{field}={getattr(self, field)!r}" for field in ("weight", "input_len", "output_len")
+               if not getattr(self, field) > 0]
         if not self.name:
-            raise ValueError("workload class name cannot be empty")
-        if self.weight <= 0:
-            raise ValueError("workload class weight must be positive")
-        if self.input_len <= 0:
-            raise ValueError("input_len must be positive")
-        if self.output_len <= 0:
-            raise ValueError("output_len must be positive")
+            bad.insert(0, "name is empty")
+        if bad:
+            raise ValueError(f"invalid request class {self.name!r}: " + ", ".join(bad) + " (lengths and weight must be > 0)")
 
 
 @dataclass(frozen=True)
@@ -55,6 +53,11 @@ def class_counts(classes: Sequence[WorkloadClass], total: int) -> list[int]:
 _class_counts = class_counts
 
 
+def _need_classes(classes):
+    if not classes:
+        raise ValueError("a workload profile needs at least one request class")
+
+
 def _assignments(classes, counts):
     out = []
     for c, n in zip(classes, counts):
@@ -64,10 +67,9 @@ def _assignments(classes, counts):
 
 def build_request_specs(classes: Sequence[WorkloadClass], num_requests: int, seed: int,
                         prompt_id_high: int = DEFAULT_PROMPT_ID_HIGH) -> list[RequestSpec]:
-    if not classes:
-        raise ValueError("classes cannot be empty")
+    _need_classes(classes)
     if num_requests < 0:
-        raise ValueError("num_requests must be non-negative")
+        raise ValueError(f"num_requests={num_requests}: a workload cannot have a negative size")
     rng = Random(seed)
     picks = _assignments(classes, class_counts(classes, num_requests))
     rng.shuffle(picks)
@@ -78,10 +80,9 @@ def build_request_specs(classes: Sequence[WorkloadClass], num_requests: int, see
 
 def iter_request_specs(classes: Sequence[WorkloadClass], seed: int, cycle_size: int = 100,
                        prompt_id_high: int = DEFAULT_PROMPT_ID_HIGH):
-    if not classes:
-        raise ValueError("classes cannot be empty")
+    _need_classes(classes)
     if cycle_size <= 0:
-        raise ValueError("cycle_size must be positive")
+        raise ValueError(f"cycle_size={cycle_size}: each cycle must hold at least one request")
     rng = Random(seed)
     counts = class_counts(classes, cycle_size)
     request_id = 0

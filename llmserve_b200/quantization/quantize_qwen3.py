@@ -16,11 +16,15 @@ Unlike the reference, ``--device cpu`` is accepted (small models, tests); the de
 """
 import argparse
 import hashlib
+import itertools
 import json
+import os
+import tempfile
 import time
 from pathlib import Path
 
 import torch
+from torch.utils._pytree import tree_map
 
 from llmserve_b200.quantization.qwen3_awq import (apply_qwen3_layer_cache, calibrate_qwen3_layer,
                                                    export_qwen3_awq_checkpoint, load_qwen3_layer_cache,
@@ -49,55 +53,49 @@ def build_parser() -> argparse.ArgumentParser:
 
 
 def load_calibration_texts(path: Path, *, max_samples: int) -> list:
-    if max_samples <= 0:
-        raise ValueError("max_samples must be positive")
-    if not path.is_file():
-        raise FileNotFoundError(f"calibration file does not exist: {path}")
-    texts = []
-    with path.open("r", encoding="utf-8") as f:
-        for line in f:
-            if line.strip():
-                texts.append(line.strip())
-                if len(texts) == max_samples:
-                    break
-    if not texts:
-        raise ValueError("calibration file contains no nonempty samples")
-    return texts
+    """The first ``max_samples`` non-blank lines of ``path`` (stripped), one calibration sample
+    each."""
+    if max_samples < 1:
+        raise ValueError(f"max_samples={max_samples}: at least one calibration sample is needed")
+    try:
+        with open(path, encoding="utf-8") as f:
+            samples = list(itertools.islice((ln.strip() for ln in f if ln.strip()), max_samples))
+    except (FileNotFoundError, IsADirectoryError) as e:
+        raise FileNotFoundError(f"no calibration text file at {path}") from e
+    if not samples:
+        raise ValueError(f"{path} holds only blank lines; nothing to calibrate on")
+    return samples
 
 
 def _sha256(path: Path) -> str:
-    h = hashlib.sha256()
-    with path.open("rb") as f:
-        for block in iter(lambda: f.read(1 << 20), b""):
-            h.update(block)
-    return h.hexdigest()
+    with open(path, "rb") as f:
+        return hashlib.file_digest(f, "sha256").hexdigest()
 
 
 def atomic_write_json(path: Path, payload: dict) -> None:
+    """The progress record, sorted and UTF-8, replaced atomically (a resumed run never reads half a file)."""
+    text = json.dumps(payload, indent=2, ensure_ascii=False, sort_keys=True) + "\n"
     path.parent.mkdir(parents=True, exist_ok=True)
-    tmp = path.with_suffix(path.suffix + ".tmp")
-    tmp.write_text(json.dumps(payload, indent=2, ensure_ascii=False, sort_keys=True) + "\n", encoding="utf-8")
-    tmp.replace(path)
+    fd, tmp = tempfile.mkstemp(dir=path.parent, suffix=".partial")
+    with os.fdopen(fd, "w", encoding="utf-8") as f:
+        f.write(text)
+    os.replace(tmp, path)
 
 
 def _to(value, device):
-    if isinstance(value, torch.Tensor):
-        return value.to(device)
-    if isinstance(value, (tuple, list)):
-        return type(value)(_to(v, device) for v in value)
-    if isinstance(value, dict):
-        return {k: _to(v, device) for k, v in value.items()}
-    return value
+    """Every tensor inside a (nested) argument structure moved to ``device``."""
+    return tree_map(lambda v: v.to(device) if isinstance(v, torch.Tensor) else v, value)
 
 
 def validate_args(args) -> None:
+    problems = [f"--{n.replace('_', '-')} must be >= 1" for n in ("max_calib_samples", "max_seq_len", "search_tokens",
+                                                                  "n_grid") if getattr(args, n) < 1]
     if args.group_size != 128:
-        raise ValueError("the llmserve_b200 AWQ runtime requires group_size=128")
-    for name in ("max_calib_samples", "max_seq_len", "search_tokens", "n_grid"):
-        if getattr(args, name) <= 0:
-            raise ValueError(f"{name} must be positive")
+        problems.append(f"--group-size {args.group_size}: the W4A16 kernels take groups of 128 only")
     if args.model.resolve() == args.output.resolve():
-        raise ValueError("output directory must differ from the BF16 source model")
+        problems.append("--output would overwrite the BF16 source checkpoint")
+    if problems:
+        raise ValueError("; ".join(problems))
 
 
 @torch.no_grad()
