@@ -135,7 +135,7 @@ def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, wor
     part = decode_partition(B, k_cache.shape[1])
     C().decode_attention(out, q.contiguous(), k_cache, v_cache, block_tables, context_lens, float(scale),
                          workspace.partial_out, workspace.partial_ml, workspace.counters,
-                         -(-workspace.max_splits * 128 // part), part)
+                         -(-workspace.max_splits * 128 // part), part, 0, status(q.device))
     return out
 
 
@@ -144,7 +144,7 @@ def prefill_attention(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables
         return prefill_attention_ref(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, scale)
     out = torch.empty_like(q)
     C().prefill_attention(out, q.contiguous(), k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables,
-                          float(scale), int(max_seqlen_q))
+                          float(scale), int(max_seqlen_q), status(q.device))
     return out
 
 
@@ -161,7 +161,7 @@ def tree_attention(q, k_cache, v_cache, block_table, prefix_len, tree_k, tree_v,
         mask_bits = (tree_mask.to(q.device).long() * w).sum(1).to(torch.int32)
     out = torch.empty_like(q)
     C().tree_attention(out, q.contiguous(), k_cache, v_cache, block_table.to(torch.int32), int(prefix_len),
-                       tree_k.contiguous(), tree_v.contiguous(), mask_bits, float(scale))
+                       tree_k.contiguous(), tree_v.contiguous(), mask_bits, float(scale), status(q.device))
     return out
 
 

@@ -33,7 +33,7 @@ template <int HD>
 __global__ void __launch_bounds__(NTHREADS) prefill_kernel(
     bf16* __restrict__ out, const bf16* __restrict__ q, const bf16* __restrict__ kc, const bf16* __restrict__ vc,
     const int* __restrict__ cu_q, const int* __restrict__ seqlens_k, const int* __restrict__ block_tables,
-    int bt_stride, float scale_log2, int nh, int nkv, int bs, int tiles_per_seq) {
+    int bt_stride, float scale_log2, int nh, int nkv, int bs, int tiles_per_seq, int nblk, int* __restrict__ status) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(128) char smem[];
@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(NTHREADS) prefill_kernel(
   const int kend = min(k_len, shift + last_row + 1);
   const int ntiles = (kend + KT - 1) / KT;
   if (ntiles > 0) {
-    load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, 0, kend, kvh, nkv, bs);
+    load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, 0, kend, kvh, nkv, bs, nblk, status);
     cp_async_commit();
     cp_async_wait<1>();
   } else {
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(NTHREADS) prefill_kernel(
   const int qpos[2] = {shift + row_a, shift + row_a + 8};
   for (int t = 0; t < ntiles; ++t) {
     if (t + 1 < ntiles) {
-      load_kv_tile<HD>(sk[(t + 1) & 1], sv[(t + 1) & 1], kc, vc, bt, (t + 1) * KT, kend, kvh, nkv, bs);
+      load_kv_tile<HD>(sk[(t + 1) & 1], sv[(t + 1) & 1], kc, vc, bt, (t + 1) * KT, kend, kvh, nkv, bs, nblk, status);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -132,7 +132,8 @@ template <int HD>
 __global__ void tree_kernel(bf16* __restrict__ out, const bf16* __restrict__ q, const bf16* __restrict__ kc,
                             const bf16* __restrict__ vc, const int* __restrict__ bt, int prefix_len,
                             const bf16* __restrict__ tk, const bf16* __restrict__ tv, int n_tree,
-                            const int* __restrict__ mask_bits, float scale_log2, int nh, int nkv, int bs) {
+                            const int* __restrict__ mask_bits, float scale_log2, int nh, int nkv, int bs, int nblk,
+                            int* __restrict__ status) {
   pdl_trigger();
   pdl_wait();
   constexpr int PER = HD / 32;
@@ -148,7 +149,12 @@ __global__ void tree_kernel(bf16* __restrict__ out, const bf16* __restrict__ q, 
   for (int key = warp; key < total; key += 4) {
     const bf16 *kp, *vp;
     if (key < prefix_len) {
-      const size_t off = (((size_t)bt[key / bs] * nkv + kvh) * bs + key % bs) * HD;
+      const int blk = bt[key / bs];
+      if ((unsigned)blk >= (unsigned)nblk) {   // never dereferenced: the key is skipped
+        if (lane == 0) record_error(status, kBadIndex);
+        continue;
+      }
+      const size_t off = (((size_t)blk * nkv + kvh) * bs + key % bs) * HD;
       kp = kc + off;
       vp = vc + off;
     } else {
@@ -198,10 +204,11 @@ void check_pool(const at::Tensor& kc, const at::Tensor& vc) {
 
 }  // namespace
 
+int* status_ptr(const at::Tensor& status);
 
 void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
                       at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, at::Tensor counters,
-                      int64_t max_splits, int64_t partition, int64_t grid_z) {
+                      int64_t max_splits, int64_t partition, int64_t grid_z, at::Tensor status) {
   check_pool(kc, vc);
   LSB_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q must be bf16 [B, nh, hd]");
   LSB_CHECK(block_tables.scalar_type() == at::kInt && block_tables.is_contiguous(), "block_tables must be int32");
@@ -228,7 +235,8 @@ void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc
     launch_pdl(decode_kernel<HD>, grid, NTHREADS, smem, stream(), (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), \
                (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(), block_tables.data_ptr<int>(),               \
                (int)block_tables.size(1), context_lens.data_ptr<int>(), sl, part_o.data_ptr<float>(),             \
-               part_ml.data_ptr<float>(), counters.data_ptr<int>(), (int)max_splits, (int)partition, nh, nkv, bs); \
+               part_ml.data_ptr<float>(), counters.data_ptr<int>(), (int)max_splits, (int)partition, nh, nkv, bs,   \
+               (int)kc.size(0), status_ptr(status));                                                               \
   } while (0)
   if (hd == 128) LSB_DEC(128);
   else if (hd == 64) LSB_DEC(64);
@@ -237,7 +245,8 @@ void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc
 }
 
 void prefill_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,
-                       at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_seqlen_q) {
+                       at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_seqlen_q,
+                       at::Tensor status) {
   check_pool(kc, vc);
   LSB_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q must be bf16 [T, nh, hd]");
   LSB_CHECK(cu_q.scalar_type() == at::kInt && seqlens_k.scalar_type() == at::kInt, "cu_seqlens / seqlens_k int32");
@@ -255,7 +264,7 @@ void prefill_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor v
     launch_pdl(prefill_kernel<HD>, grid, NTHREADS, smem, stream(),                                                        \
         (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(),  \
         cu_q.data_ptr<int>(), seqlens_k.data_ptr<int>(), block_tables.data_ptr<int>(), block_tables.size(1), sl,   \
-        nh, nkv, bs, tiles);                                                                                      \
+        nh, nkv, bs, tiles, (int)kc.size(0), status_ptr(status));                                                  \
   } while (0)
   if (hd == 128) LSB_PRE(128);
   else if (hd == 64) LSB_PRE(64);
@@ -264,7 +273,7 @@ void prefill_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor v
 }
 
 void tree_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bt, int64_t prefix_len,
-                    at::Tensor tk, at::Tensor tv, at::Tensor mask_bits, double scale) {
+                    at::Tensor tk, at::Tensor tv, at::Tensor mask_bits, double scale, at::Tensor status) {
   check_pool(kc, vc);
   const int n = q.size(0), nh = q.size(1), hd = q.size(2), nkv = kc.size(1), bs = kc.size(2);
   LSB_CHECK(tk.size(0) <= 32, "at most 32 tree nodes");
@@ -276,12 +285,12 @@ void tree_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, 
     launch_pdl(tree_kernel<128>, dim3(n, nh), 128, 0, stream(), 
         (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(),
         bt.data_ptr<int>(), prefix_len, (const bf16*)tk.data_ptr(), (const bf16*)tv.data_ptr(), tk.size(0),
-        mask_bits.data_ptr<int>(), sl, nh, nkv, bs);
+        mask_bits.data_ptr<int>(), sl, nh, nkv, bs, (int)kc.size(0), status_ptr(status));
   else if (hd == 64)
     launch_pdl(tree_kernel<64>, dim3(n, nh), 128, 0, stream(), 
         (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), (const bf16*)kc.data_ptr(), (const bf16*)vc.data_ptr(),
         bt.data_ptr<int>(), prefix_len, (const bf16*)tk.data_ptr(), (const bf16*)tv.data_ptr(), tk.size(0),
-        mask_bits.data_ptr<int>(), sl, nh, nkv, bs);
+        mask_bits.data_ptr<int>(), sl, nh, nkv, bs, (int)kc.size(0), status_ptr(status));
   else
     LSB_CHECK(false, "head_dim must be 64 or 128");
 }

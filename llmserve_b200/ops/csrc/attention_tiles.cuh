@@ -44,19 +44,26 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
   return (uint32_t)(r * HD * 2 + ((c ^ (r & 7)) << 4));
 }
 
-// Stage KT keys [kstart, kstart+KT) of one KV head (rows >= kend are zero-filled).
+// Stage KT keys [kstart, kstart+KT) of one KV head (rows >= kend are zero-filled).  A block id
+// outside [0, nblk) is never dereferenced: its rows are zero-filled and kBadIndex is recorded
+// (status may be null).
 template <int HD>
 __device__ __forceinline__ void load_kv_tile(bf16* sk, bf16* sv, const bf16* kc, const bf16* vc, const int* bt,
-                                             int kstart, int kend, int kvh, int nkv, int bs) {
+                                             int kstart, int kend, int kvh, int nkv, int bs, int nblk, int* status) {
   constexpr int CH = HD / 8;   // 16-byte chunks per row
   for (int q = threadIdx.x; q < KT * CH; q += NTHREADS) {
     const int r = q / CH, c = q % CH;
     const int pos = kstart + r;
-    const bool ok = pos < kend;
+    bool ok = pos < kend;
     size_t off = 0;
     if (ok) {
       const int blk = bt[pos / bs];
-      off = (((size_t)blk * nkv + kvh) * bs + pos % bs) * HD + c * 8;
+      if ((unsigned)blk < (unsigned)nblk) {
+        off = (((size_t)blk * nkv + kvh) * bs + pos % bs) * HD + c * 8;
+      } else {
+        ok = false;
+        if (c == 0) record_error(status, kBadIndex);
+      }
     }
     cp_async16(reinterpret_cast<char*>(sk) + swz<HD>(r, c), kc + off, ok);
     cp_async16(reinterpret_cast<char*>(sv) + swz<HD>(r, c), vc + off, ok);
@@ -142,7 +149,7 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(
     bf16* __restrict__ out, const bf16* __restrict__ q, const bf16* __restrict__ kc, const bf16* __restrict__ vc,
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ context_lens, float scale_log2,
     float* __restrict__ part_o, float* __restrict__ part_ml, int* __restrict__ counters, int max_splits,
-    int partition, int nh, int nkv, int bs) {
+    int partition, int nh, int nkv, int bs, int nblk, int* __restrict__ status) {
   pdl_trigger();
   extern __shared__ __align__(128) char smem[];
   __shared__ int is_last;
@@ -155,7 +162,9 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(
   // only the newest position's K/V (ctx - 1) is written by the kernel just before this one.  So
   // the first tile, when it ends before that position, is streamed before waiting on the
   // predecessor (programmatic dependent launch), overlapping it with the QKV projection.
-  const int ctx = context_lens[b];
+  // a context longer than the block table row is clamped to it: every block-table read and every
+  // split slot (b, h, split < max_splits) then stays inside what the caller sized
+  const int ctx = max(0, min(context_lens[b], bt_stride * bs));
   const int nsplits = (ctx + partition - 1) / partition;
   const int* bt = block_tables + (size_t)b * bt_stride;
   bool prefetched = false;
@@ -163,7 +172,7 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(
     const int ks = blockIdx.z * partition;
     const int ke = min(ks + partition, ctx);
     if (min(ks + KT, ke) <= ctx - 1) {
-      load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, ks, ke, kvh, nkv, bs);
+      load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, ks, ke, kvh, nkv, bs, nblk, status);
       cp_async_commit();
       prefetched = true;
     }
@@ -205,13 +214,14 @@ __global__ void __launch_bounds__(NTHREADS) decode_kernel(
     float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
     __syncthreads();   // shared memory is reused across splits
     if (!prefetched) {
-      load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, kstart, kend, kvh, nkv, bs);
+      load_kv_tile<HD>(sk[0], sv[0], kc, vc, bt, kstart, kend, kvh, nkv, bs, nblk, status);
       cp_async_commit();
     }
     prefetched = false;
     for (int t = 0; t < ntiles; ++t) {
       if (t + 1 < ntiles) {
-        load_kv_tile<HD>(sk[(t + 1) & 1], sv[(t + 1) & 1], kc, vc, bt, kstart + (t + 1) * KT, kend, kvh, nkv, bs);
+        load_kv_tile<HD>(sk[(t + 1) & 1], sv[(t + 1) & 1], kc, vc, bt, kstart + (t + 1) * KT, kend, kvh, nkv, bs,
+                         nblk, status);
         cp_async_commit();
         cp_async_wait<1>();
       } else {

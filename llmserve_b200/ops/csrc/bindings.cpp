@@ -20,11 +20,12 @@ void argmax_rows(at::Tensor out_idx, at::Tensor out_val, at::Tensor logits);
 void sample_rows(at::Tensor out, at::Tensor logits, at::Tensor temps, int64_t seed);
 void decode_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
                       at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml, at::Tensor counters,
-                      int64_t max_splits, int64_t partition, int64_t grid_z);
+                      int64_t max_splits, int64_t partition, int64_t grid_z, at::Tensor status);
 void prefill_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,
-                       at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_seqlen_q);
+                       at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_seqlen_q,
+                       at::Tensor status);
 void tree_attention(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bt, int64_t prefix_len,
-                    at::Tensor tk, at::Tensor tv, at::Tensor mask_bits, double scale);
+                    at::Tensor tk, at::Tensor tv, at::Tensor mask_bits, double scale, at::Tensor status);
 void gemm_bf16(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor partials, int64_t splits, at::Tensor status,
                int64_t max_stages);
 int64_t comm_alloc(int64_t nbytes);
@@ -78,7 +79,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_tma_supported", &lsb::decode_tma_supported);
   m.def("decode_attention", &lsb::decode_attention, py::arg("out"), py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("context_lens"), py::arg("scale"), py::arg("part_o"), py::arg("part_ml"),
-        py::arg("counters"), py::arg("max_splits"), py::arg("partition"), py::arg("grid_z") = 0);
+        py::arg("counters"), py::arg("max_splits"), py::arg("partition"), py::arg("grid_z"), py::arg("status"));
   m.def("prefill_attention", &lsb::prefill_attention);
   m.def("tree_attention", &lsb::tree_attention);
   m.def("comm_alloc", &lsb::comm_alloc);

@@ -96,12 +96,12 @@ extern "C" int lsb_decode_attention_noalloc(void* out, const void* q, const void
     lsb::launch_pdl(lsb::decode_kernel<128>, grid, dim3(lsb::NTHREADS), (size_t)lsb::decode_smem(128), stream,
                     (lsb::bf16*)out, (const lsb::bf16*)q, (const lsb::bf16*)k_cache, (const lsb::bf16*)v_cache,
                     block_tables, block_table_stride, context_lens, sl, part_o, part_ml, counters, (int)max_splits,
-                    partition, num_heads, num_kv_heads, block_size);
+                    partition, num_heads, num_kv_heads, block_size, num_blocks, (int*)nullptr);
   else
     lsb::launch_pdl(lsb::decode_kernel<64>, grid, dim3(lsb::NTHREADS), (size_t)lsb::decode_smem(64), stream,
                     (lsb::bf16*)out, (const lsb::bf16*)q, (const lsb::bf16*)k_cache, (const lsb::bf16*)v_cache,
                     block_tables, block_table_stride, context_lens, sl, part_o, part_ml, counters, (int)max_splits,
-                    partition, num_heads, num_kv_heads, block_size);
+                    partition, num_heads, num_kv_heads, block_size, num_blocks, (int*)nullptr);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     snprintf(g_error, sizeof(g_error), "kernel launch failed: %s", cudaGetErrorString(e));

@@ -12,7 +12,13 @@
 //   k_cache,
 //   v_cache       bf16 [num_blocks, num_kv_heads, block_size, head_dim]   (16-byte aligned)
 //   block_tables  int32 [batch, block_table_stride]
-//   context_lens  int32 [batch]; context_lens[b] <= block_table_stride * block_size
+//   context_lens  int32 [batch]
+//
+// Inputs the host cannot check without a synchronisation are made safe on the device: a context
+// longer than block_table_stride * block_size is clamped to it (so block-table reads and split
+// slots stay inside what was sized here), and a block id outside [0, num_blocks) is never
+// dereferenced -- its keys and values read as zeros.  Both give a defined result for garbage in,
+// not an error code.  A context of 0 writes zeros.
 //
 // Limits: head_dim 64 or 128; num_heads a multiple of num_kv_heads with at most 16 query heads
 // per KV head; batch * num_kv_heads <= LSB_NOALLOC_MAX_PAIRS; and the split partials

@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
     const bf16* __restrict__ q, const int* __restrict__ block_tables, int bt_stride,
     const int* __restrict__ context_lens, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml,
     int* __restrict__ counters, int max_splits, int partition, int max_chunks, int B, int nh, int nkv, int bs,
-    int box_rows, int* __restrict__ status) {
+    int box_rows, int nblk, int* __restrict__ status) {
   using LY = DecLayout<HD>;
   constexpr int S = LY::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
       for (int item = blockIdx.x; item < n_items && !*aborted; item += gridDim.x) {
         const int chunk = item / pairs, pair = item - chunk * pairs;
         const int b = pair / nkv, kvh = pair - b * nkv;
-        const int ctx = context_lens[b];
+        const int ctx = max(0, min(context_lens[b], bt_stride * bs));   // clamped to the table row
         const int ks = chunk * partition;
         if (ks >= ctx) continue;
         const int ke = min(ks + partition, ctx);
@@ -218,7 +218,14 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
           const uint32_t vt = kt + LY::kTileBytes;
           for (int j = 0; j < nsub; ++j) {
             const int pos = st + j * box_rows;
-            const int row = (bt[pos / bs] * nkv + kvh) * bs + pos % bs;
+            int blk = bt[pos / bs];
+            if ((unsigned)blk >= (unsigned)nblk) {
+              // never dereferenced: a row past the pool is outside the tensor map, so the copy
+              // delivers zeros (and still completes its transaction bytes)
+              record_error(status, kBadIndex);
+              blk = nblk;
+            }
+            const int row = (blk * nkv + kvh) * bs + pos % bs;
 #pragma unroll
             for (int h = 0; h < LY::kHalves; ++h) {
               tma2d(kt + h * LY::kHalfBytes + j * box_rows * 128, &tm_k, &full[s], h * 64, row);
@@ -251,7 +258,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const int chunk = item / pairs, pair = item - chunk * pairs;
     const int b = pair / nkv, kvh = pair - b * nkv;
-    const int ctx = context_lens[b];
+    const int ctx = max(0, min(context_lens[b], bt_stride * bs));
     const int ks = chunk * partition;
     if (ks >= ctx) {
       if (chunk == 0 && warp == 0)   // empty context: defined output
@@ -495,7 +502,7 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
                (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), block_tables.data_ptr<int>(),                      \
                (int)block_tables.size(1), context_lens.data_ptr<int>(), sl, part_o.data_ptr<float>(),               \
                part_ml.data_ptr<float>(), counters.data_ptr<int>(), (int)max_splits, (int)partition, max_chunks, B, \
-               nh, nkv, bs, box_rows, st);                                                                          \
+               nh, nkv, bs, box_rows, (int)kc.size(0), st);                                                          \
   } while (0)
   if (hd == 128) LSB_DEC_TMA(128);
   else LSB_DEC_TMA(64);

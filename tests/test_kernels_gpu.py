@@ -198,9 +198,78 @@ def test_decode_attention_tma_poisoned_pool(B, partition):
     assert int(ws.counters.abs().sum()) == 0
     old = torch.empty_like(q)
     C().decode_attention(old, q, kc, vc, perm, ctx, scale, ws.partial_out, ws.partial_ml, ws.counters,
-                         -(-ws.max_splits * 128 // 256), 256, 0)
+                         -(-ws.max_splits * 128 // 256), 256, 0, status(torch.device(DEV)))
     torch.cuda.synchronize()
     assert torch.isfinite(old.float()).all() and rel_err(out, old) < 5e-3
+
+
+@pytest.mark.parametrize("tma", [True, False])
+def test_decode_attention_out_of_range_blocks_and_long_context(tma):
+    """A block id outside the pool is never read (zeros, kBadIndex recorded) and a context longer
+    than its block-table row is clamped to the row; a correct call afterwards is unaffected."""
+    hd, nh, nkv, bs = 128, 8, 2, 64
+    B, width = 4, 3
+    nblk = B * width
+    kc, vc = _pool(nblk, nkv, bs, hd, seed=11)
+    tables = torch.randperm(nblk, device=DEV)[: B * width].view(B, width).int().contiguous()
+    lens = [100, 150, 192, 30]
+    ctx = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    q = torch.randn(B, nh, hd, device=DEV).bfloat16()
+    scale = 1 / math.sqrt(hd)
+    ws = attention.DecodeWorkspace(B, nh, hd, width * bs, DEV)
+    st = status(torch.device(DEV))
+
+    def run(t, c):
+        out = torch.empty_like(q)
+        if tma:
+            C().decode_attention_tma(out, q, kc, vc, t, c, scale, ws.partial_out, ws.partial_ml, ws.counters,
+                                     ws.max_splits, 128, st)
+        else:
+            C().decode_attention(out, q, kc, vc, t, c, scale, ws.partial_out, ws.partial_ml, ws.counters,
+                                 ws.max_splits, 128, 0, st)
+        torch.cuda.synchronize()
+        return out
+
+    bad = tables.clone()
+    bad[1, 1] = nblk + 1000
+    bad[2, 0] = -7
+    out = run(bad, ctx)
+    assert torch.isfinite(out.float()).all()
+    with pytest.raises(RuntimeError, match="out-of-range"):
+        check_status(torch.device(DEV))
+    # rows whose blocks are all valid are exact
+    ref = attention.decode_attention_ref(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), tables.cpu(),
+                                         ctx.cpu(), scale).to(DEV)
+    for b in (0, 3):
+        assert rel_err(out[b], ref[b]) < 1e-2
+    # a context past the table row (3 blocks = 192 keys) attends to the whole row, nothing more
+    long_ctx = torch.tensor([100, 150, 10_000, 30], dtype=torch.int32, device=DEV)
+    out = run(tables, long_ctx)
+    check_status(torch.device(DEV))
+    assert rel_err(out, ref) < 1e-2          # 192 == the clamp for row 2
+    assert int(ws.counters.abs().sum()) == 0
+    assert rel_err(run(tables, ctx), ref) < 1e-2
+
+
+def test_prefill_and_tree_attention_skip_out_of_range_blocks():
+    hd, nh, nkv, bs = 128, 4, 2, 16
+    kc, vc = _pool(8, nkv, bs, hd, seed=12)
+    tables = torch.tensor([[0, 1, 2, 99]], dtype=torch.int32, device=DEV)
+    q = torch.randn(60, nh, hd, device=DEV).bfloat16()
+    cu = torch.tensor([0, 60], dtype=torch.int32, device=DEV)
+    ks = torch.tensor([60], dtype=torch.int32, device=DEV)
+    out = attention.prefill_attention(q, kc, vc, cu, ks, tables, 0.088, 60)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    with pytest.raises(RuntimeError, match="out-of-range"):
+        check_status(torch.device(DEV))
+    tk = torch.randn(3, nkv, hd, device=DEV).bfloat16()
+    mask = torch.ones(3, 3, dtype=torch.bool, device=DEV).tril()
+    out = attention.tree_attention(q[:3], kc, vc, tables[0], 60, tk, tk, mask, 0.088)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    with pytest.raises(RuntimeError, match="out-of-range"):
+        check_status(torch.device(DEV))
 
 
 @pytest.mark.parametrize("bs", [16, 256])
