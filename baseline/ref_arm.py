@@ -107,7 +107,7 @@ def make_eagle3_checkpoint() -> str:
     return path
 
 
-def run(args, metric: str):
+def run(args, metric: str, window_latency):
     rank = int(os.environ.get("RANK", 0))
     if rank > 0:
         return          # the reference spawns its own tensor-parallel workers from rank 0
@@ -176,6 +176,21 @@ def run(args, metric: str):
     wall = time.perf_counter() - t0
     ms = start.elapsed_time(end)
     n = tokens() - tok0
+    # the same latency window as the llmserve_b200 arm: one full wave of requests admitted after
+    # the timed steps, run to completion
+    seen = set(llm.request_metrics)
+    lat_steps = 0
+    while True:
+        new = [r for k, r in llm.request_metrics.items() if k not in seen]
+        if sum(r["finish_time"] is not None for r in new) >= args.concurrency or lat_steps > 20 * args.output_len:
+            break
+        outs, _ = llm.step()
+        active -= len(outs)
+        refill()
+        lat_steps += 1
+    latency = window_latency([r for k, r in llm.request_metrics.items() if k not in seen])
+    latency["window"] = (f"{lat_steps} steps after the timed ones: the {latency['requests']} requests admitted "
+                         "after the timed steps, once a full wave of them finished")
     m = llm.get_metrics()["summary"]
     llm.exit()
     print(json.dumps({
@@ -189,9 +204,10 @@ def run(args, metric: str):
                    "parallelism": f"tp{world}", "cuda_graphs": not (args.eager or eagle3),
                    "workload": f"closed-loop {args.input_len} in / {args.output_len} out, concurrency {args.concurrency}, greedy"},
         "e2e": {"value": round(n / wall, 2), "unit": "tok/s"},
-        "latency": {"ttft_p99_ms": None if m["ttft"]["p99"] is None else round(m["ttft"]["p99"] * 1e3, 2),
-                    "tpot_p99_ms": None if m["tpot"]["p99"] is None else round(m["tpot"]["p99"] * 1e3, 3)},
+        "latency": latency,
         "speculative": None if not eagle3 else {k: (m.get("speculative") or {}).get(k) for k in
-                                                ("steps", "acceptance_rate", "acceptance_length")},
+                                                ("steps", "acceptance_rate", "acceptance_length")}
+        | {"step_latency_p50_ms": None if (m.get("speculative_step_latency") or {}).get("p50") is None
+           else round(m["speculative_step_latency"]["p50"] * 1e3, 3)},
         "timing": "CUDA events on the reference's rank-0 device", "checkpoint_write_s": round(t_ckpt, 1),
     }), flush=True)

@@ -128,6 +128,22 @@ def request_stream(vocab, n_in, seed=0):
         yield [rng.randrange(vocab) for _ in range(n_in)]
 
 
+def window_latency(metrics: list[dict]) -> dict:
+    """P50 / P99 TTFT and TPOT (the engine's definitions: first token - arrival; (finish - first) /
+    (tokens - 1)) over the finished requests among ``metrics`` (the engine's request records)."""
+    from llmserve_b200.engine.llm_engine import percentile
+    done = [m for m in metrics if m["finish_time"] is not None and m["first_token_time"] is not None]
+    ttft = [m["first_token_time"] - m["arrival_time"] for m in done]
+    tpot = [(m["finish_time"] - m["first_token_time"]) / (m["output_tokens"] - 1) for m in done
+            if m["output_tokens"] > 1]
+
+    def ms(v, q, nd):
+        x = percentile(v, q)
+        return None if x is None else round(x * 1e3, nd)
+    return {"requests": len(done), "ttft_p50_ms": ms(ttft, 50, 2), "ttft_p99_ms": ms(ttft, 99, 2),
+            "tpot_p50_ms": ms(tpot, 50, 3), "tpot_p99_ms": ms(tpot, 99, 3)}
+
+
 def run_ours(args):
     import torch
 
@@ -197,9 +213,25 @@ def run_ours(args):
     tokens = tokens_so_far() - tok0
     dev_ms = max(r[0] for r in per_rank)
     launches = int(per_rank[0][1])
-    m = llm.get_metrics()["summary"]
     h2d = (runner.h2d_bytes - h2d0) / args.steps
     d2h = (runner.d2h_bytes - d2h0) / args.steps
+    # Latency window (after the timed steps, not part of `value`): keep the closed loop running
+    # until one full wave of requests admitted after this point has finished, so P99 TTFT / TPOT
+    # come from complete requests whatever --steps is.
+    seen = set(llm.request_metrics)
+    lat_steps = 0
+    while True:
+        new = [m for k, m in llm.request_metrics.items() if k not in seen]
+        if sum(m["finish_time"] is not None for m in new) >= args.concurrency or lat_steps > 20 * args.output_len:
+            break
+        outs, _ = llm.step()
+        active -= len(outs)
+        refill()
+        lat_steps += 1
+    latency = window_latency([m for k, m in llm.request_metrics.items() if k not in seen])
+    latency["window"] = (f"{lat_steps} steps after the timed ones: the {latency['requests']} requests admitted "
+                         "after the timed steps, once a full wave of them finished")
+    m = llm.get_metrics()["summary"]
     llm.exit()
     value = tokens / (dev_ms / 1e3)
     line = {
@@ -219,8 +251,7 @@ def run_ours(args):
         "e2e": {"value": round(tokens / wall, 2), "unit": "tok/s", "h2d_bytes_per_step": round(h2d),
                 "d2h_bytes_per_step": round(d2h)},
         "gpu_launches": launches,
-        "latency": {"ttft_p99_ms": None if m["ttft"]["p99"] is None else round(m["ttft"]["p99"] * 1e3, 2),
-                    "tpot_p99_ms": None if m["tpot"]["p99"] is None else round(m["tpot"]["p99"] * 1e3, 3)},
+        "latency": latency,
         "per_rank_device_ms": [round(r[0], 3) for r in per_rank],
         "speculative": None if not args.eagle3 else {
             k: m["speculative"].get(k) for k in ("steps", "acceptance_rate", "acceptance_length", "mean_batch_size")}
@@ -253,7 +284,7 @@ def run_reference(args):
         return
     sys.path.insert(0, os.path.join(ROOT, "baseline"))
     from ref_arm import run as ref_run  # noqa: E402
-    ref_run(args, METRIC)
+    ref_run(args, METRIC, window_latency)
 
 
 def main():

@@ -7,9 +7,10 @@ For each token count T every rank runs the o_proj-shaped step of one decoder lay
 (x [T, inner / N] @ W [hidden, inner / N]^T) followed by the reduction over ranks, the residual
 add and the RMSNorm:
 
-* ``fused``   -- the engine's path: tcgen05 GEMM writing split-K partials into the peer-mapped
-  buffer, then ``fused_allreduce_add_rmsnorm`` (reduce-scatter over NVLink peer loads, norm,
-  all-gather by peer stores) -- ``FusedComm.row_parallel_add_norm``;
+* ``fused``   -- the engine's path (``FusedComm.row_parallel_add_norm``): the tcgen05 GEMM's epilogue
+  stores each token row's split-K partials into the inbox of the rank owning the row (peer
+  stores), then ``row_parallel_finish`` reduces the rank's rows from its own inbox, adds the
+  residual, normalises and pushes the finished rows to every rank (peer stores);
 * ``nccl``    -- the baseline: the same GEMM (bf16 output), ``dist.all_reduce``, add+RMSNorm kernel;
 * ``gemm``    -- the GEMM alone, to separate the collective's share.
 
@@ -31,9 +32,9 @@ def fused_roofline_us(T: int, hidden: int, inner_shard: int, world: int, splits:
     rows = -(-T // world)
     weight_bytes = hidden * inner_shard * 2
     flops = 2.0 * T * hidden * inner_shard
-    # reads the other ranks' fp32 partial planes of its rows, pushes its finished rows (normed
-    # output + residual, bf16) to the other ranks
-    link_bytes = (world - 1) * rows * hidden * (4 * splits + 2 * 2)
+    # the GEMM stores the fp32 partial planes of the other ranks' rows into their inboxes, then the
+    # rank pushes its finished rows (normed output + residual, bf16) to the other ranks
+    link_bytes = (T - min(rows, T)) * hidden * 4 * splits + (world - 1) * min(rows, T) * hidden * 2 * 2
     terms = {"hbm_us": weight_bytes / (hbm_gbs * 1e3), "compute_us": flops / (bf16_tflops * 1e6),
              "nvlink_us": link_bytes / (nvlink_gbs * 1e3)}
     return dict(terms, roofline_us=max(terms.values()), nvlink_bytes=link_bytes, weight_bytes=weight_bytes)

@@ -63,6 +63,7 @@ def _to_device(values, dtype, device) -> torch.Tensor:
 
 
 class ModelRunner:
+    _graph_exchanges_argmax = False
 
     def __init__(self, config: Config, rank: int, channel_name: str | None = None, parent_pid: int | None = None):
         self.config = config
@@ -593,11 +594,26 @@ class ModelRunner:
         return (not is_prefill and bool(self.graphs) and len(decodes) <= self.graph_bs[-1]
                 and max(len(s.block_table) for s in decodes) <= self.graph_W)
 
+    def _greedy_from_shards(self, vals: torch.Tensor, idx: torch.Tensor, out: torch.Tensor | None = None):
+        """Global greedy ids from every rank's per-shard (max, local index): the NVLink exchange
+        kernel when the fused collectives are up (no NCCL call, capturable), else NCCL."""
+        fused = tp.get_fused_comm()
+        if self.world_size > 1 and fused is not None and vals.shape[0] <= 512:
+            if out is None:
+                out = torch.empty(vals.shape[0], dtype=torch.int64, device=vals.device)
+            return fused.argmax(vals.contiguous(), idx.to(torch.int64).contiguous(), self.model.lm_head.vocab_start,
+                                out)
+        tokens = tp.vocab_parallel_argmax(vals, idx, self.model.lm_head.vocab_start)
+        if out is not None:
+            out.copy_(tokens)
+            return out
+        return tokens
+
     def sample_tokens(self, logits: torch.Tensor, temperatures: torch.Tensor) -> torch.Tensor:
         """Token ids on every rank from the local logit shard."""
         if getattr(self.sampler, "is_greedy", False):
             vals, idx = sampling_ops.local_argmax(logits)
-            return tp.vocab_parallel_argmax(vals, idx, self.model.lm_head.vocab_start)
+            return self._greedy_from_shards(vals, idx)
         full = tp.gather_logits(logits)
         tokens = self.sampler(full, temperatures).to(torch.int64).reshape(-1)
         return tp.broadcast(tokens.contiguous(), 0)
@@ -613,7 +629,10 @@ class ModelRunner:
             t_run = time.perf_counter()
             logits, vals, idx = self._decode_graph_step(decodes)
             if getattr(self.sampler, "is_greedy", False):
-                tokens = tp.vocab_parallel_argmax(vals, idx, self.model.lm_head.vocab_start)
+                if self._graph_exchanges_argmax:
+                    tokens = self.graph_vars["feed_src"][:len(decodes)]
+                else:
+                    tokens = tp.vocab_parallel_argmax(vals, idx, self.model.lm_head.vocab_start)
             else:
                 tokens = self.sample_tokens(logits, self.prepare_sample(seqs))
             host = self.graph_tokens_host[:len(decodes)]
@@ -676,6 +695,9 @@ class ModelRunner:
         self.graph_bs = [b for b in (1, 2, 4, 8) if b <= max_bs] + list(range(16, max_bs + 1, 16))
         self.graphs, self.graph_pool, self.graph_launches = {}, None, {}
         self.graph_vars = v
+        # at TP > 1 with the fused collectives the graph ends with the vocab-parallel argmax
+        # exchange, writing the global ids straight into feed_src
+        self._graph_exchanges_argmax = self.world_size > 1 and tp.get_fused_comm() is not None
         self._tokens_event = None
         v["context_lens"].fill_(1)
         v["feed32"].fill_(-1)
@@ -700,6 +722,8 @@ class ModelRunner:
         pos = v["pos32"][:bs].long()
         v["logits"][:bs] = self.model.compute_logits(self.model(ids, pos))
         sampling_ops.local_argmax_into(v["logits"][:bs], v["tok_val"][:bs], v["tok_idx"][:bs])
+        if self._graph_exchanges_argmax:
+            self._greedy_from_shards(v["tok_val"][:bs], v["tok_idx"][:bs], v["feed_src"][:bs])
 
     def _next_pack(self):
         """The pinned staging buffer to fill next (alternating)."""
@@ -740,7 +764,7 @@ class ModelRunner:
         self.graphs[gbs].replay()
         LaunchCounter.launches += self.graph_launches[gbs]
         v = self.graph_vars
-        if self.world_size > 1:
+        if self.world_size > 1 and not self._graph_exchanges_argmax:
             tokens = tp.vocab_parallel_argmax(v["tok_val"][:bs], v["tok_idx"][:bs], self.model.lm_head.vocab_start)
             v["feed_src"][:bs].copy_(tokens)
 

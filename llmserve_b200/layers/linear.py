@@ -168,6 +168,8 @@ class QKVParallelLinear(ColumnParallelLinear):
         if x.is_cuda and self.fused_gemm_ok:
             x2 = x.reshape(-1, x.shape[-1])
             w = self.gemm_weight
+            if gemm.use_cluster(x2.shape[0], w):
+                return gemm.linear_reduced(x2.contiguous(), w, plane=True)
             splits = gemm.splits_for(x2.shape[0], w)
             if splits > 1:
                 return gemm.linear_partials(x2.contiguous(), w, splits)

@@ -121,7 +121,7 @@ template <int BN, int STAGES, int WB>
 __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                           const uint32_t* __restrict__ qtiles,
                                                           const uint2* __restrict__ sztiles, bf16* __restrict__ out,
-                                                          float* __restrict__ partials, int T, int N, int k_tiles,
+                                                          const PartDest pd, int T, int N, int k_tiles,
                                                           int k_tiles_per_split, int* __restrict__ status) {
   using L = QSmem<BN, STAGES, WB>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -303,14 +303,15 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
             const int tok = t0 + c0 + j;
             if (tok < T) {
               const float v = __uint_as_float(rr[j]);
-              if (partials != nullptr)
-                partials[((size_t)blockIdx.z * T + tok) * N + feat] = v;
+              if (pd.base[0] != nullptr)
+                *pd.at(blockIdx.z, tok, N, feat) = v;
               else
                 out[(size_t)tok * N + feat] = to_b(v);
             }
           }
         }
       }
+      if (pd.owners > 1) __threadfence_system();   // peer-inbox stores visible before the kernel ends
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -322,8 +323,8 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
 }
 
 template <int BN, int WB>
-void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out, float* partials,
-                int splits, int* status) {
+void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out,
+                const PartDest& pd, int splits, int* status) {
   constexpr int ST = qstages<BN, WB>();
   using L = QSmem<BN, ST, WB>;
   static_assert(L::kStage % 1024 == 0, "stage size must keep 1024-byte alignment");
@@ -335,7 +336,7 @@ void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz,
   ensure_dynamic_smem((const void*)kern, L::kBytes);
   dim3 grid(((N + QBM - 1) / QBM) * ((T + BN - 1) / BN), 1, splits);
   launch_pdl(kern, grid, dim3(kQThreads), L::kBytes, at::cuda::getCurrentCUDAStream(), mx,
-             (const uint32_t*)qt.data_ptr(), (const uint2*)sz.data_ptr(), out, partials, T, N, k_tiles, kps, status);
+             (const uint32_t*)qt.data_ptr(), (const uint2*)sz.data_ptr(), out, pd, T, N, k_tiles, kps, status);
 }
 
 int awq_wbuf() {
@@ -348,11 +349,36 @@ int awq_wbuf() {
 
 template <int BN>
 void awq_launch_any(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out,
-                    float* partials, int splits, int* status) {
+                    const PartDest& pd, int splits, int* status) {
   const int wb = awq_wbuf();
-  if (wb >= 8) awq_launch<BN, 8>(x, qt, sz, N, out, partials, splits, status);
-  else if (wb >= 4) awq_launch<BN, 4>(x, qt, sz, N, out, partials, splits, status);
-  else awq_launch<BN, 2>(x, qt, sz, N, out, partials, splits, status);
+  if (wb >= 8) awq_launch<BN, 8>(x, qt, sz, N, out, pd, splits, status);
+  else if (wb >= 4) awq_launch<BN, 4>(x, qt, sz, N, out, pd, splits, status);
+  else awq_launch<BN, 2>(x, qt, sz, N, out, pd, splits, status);
+}
+
+void awq_dispatch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* o, const PartDest& pd,
+                  int splits, int* st) {
+  const int T = x.size(0);
+  if (T <= 16) awq_launch_any<16>(x, qt, sz, N, o, pd, splits, st);
+  else if (T <= 32) awq_launch_any<32>(x, qt, sz, N, o, pd, splits, st);
+  else if (T <= 64) awq_launch_any<64>(x, qt, sz, N, o, pd, splits, st);
+  else if (T <= 128) awq_launch_any<128>(x, qt, sz, N, o, pd, splits, st);
+  else awq_launch_any<256>(x, qt, sz, N, o, pd, splits, st);
+}
+
+void check_awq_operands(const at::Tensor& x, const at::Tensor& qtiles, const at::Tensor& sztiles, int N) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
+              "llmserve_b200: AWQ GEMM activations must be bf16 [T, K], K-contiguous");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "llmserve_b200: AWQ GEMM activations must be 16-byte aligned");
+  const int K = x.size(1);
+  TORCH_CHECK(K % 128 == 0, "llmserve_b200: AWQ K must be a multiple of the group size 128");
+  const int64_t mt = (N + QBM - 1) / QBM;
+  TORCH_CHECK(qtiles.is_contiguous() && qtiles.scalar_type() == at::kInt && qtiles.numel() == mt * (K / QBK) * QBM * 8,
+              "llmserve_b200: AWQ qtiles shape mismatch");
+  TORCH_CHECK(sztiles.is_contiguous() && sztiles.scalar_type() == at::kInt &&
+                  sztiles.numel() == mt * (K / 128) * QBM * 2,
+              "llmserve_b200: AWQ scale/zero tiles shape mismatch");
 }
 
 }  // namespace
@@ -361,18 +387,8 @@ void awq_launch_any(const at::Tensor& x, const at::Tensor& qt, const at::Tensor&
 // out bf16 [T, N] (splits == 1) or partials fp32 [splits, T, N].
 void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, at::Tensor partials,
               int64_t splits, at::Tensor status) {
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1,
-              "llmserve_b200: AWQ GEMM activations must be bf16 [T, K], K-contiguous");
-  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
-              "llmserve_b200: AWQ GEMM activations must be 16-byte aligned");
-  const int T = x.size(0), K = x.size(1), N = (int)n;
-  TORCH_CHECK(K % 128 == 0, "llmserve_b200: AWQ K must be a multiple of the group size 128");
-  const int64_t mt = (N + QBM - 1) / QBM;
-  TORCH_CHECK(qtiles.is_contiguous() && qtiles.scalar_type() == at::kInt && qtiles.numel() == mt * (K / QBK) * QBM * 8,
-              "llmserve_b200: AWQ qtiles shape mismatch");
-  TORCH_CHECK(sztiles.is_contiguous() && sztiles.scalar_type() == at::kInt &&
-                  sztiles.numel() == mt * (K / 128) * QBM * 2,
-              "llmserve_b200: AWQ scale/zero tiles shape mismatch");
+  const int T = x.size(0), N = (int)n;
+  check_awq_operands(x, qtiles, sztiles, N);
   TORCH_CHECK(splits >= 1 && splits <= 64, "llmserve_b200: splits out of range");
   bf16* o = nullptr;
   float* p = nullptr;
@@ -388,12 +404,27 @@ void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztile
   }
   if (T == 0 || N == 0) return;
   const at::cuda::CUDAGuard g(x.device());
-  int* st = status_ptr(status);
-  if (T <= 16) awq_launch_any<16>(x, qtiles, sztiles, N, o, p, (int)splits, st);
-  else if (T <= 32) awq_launch_any<32>(x, qtiles, sztiles, N, o, p, (int)splits, st);
-  else if (T <= 64) awq_launch_any<64>(x, qtiles, sztiles, N, o, p, (int)splits, st);
-  else if (T <= 128) awq_launch_any<128>(x, qtiles, sztiles, N, o, p, (int)splits, st);
-  else awq_launch_any<256>(x, qtiles, sztiles, N, o, p, (int)splits, st);
+  awq_dispatch(x, qtiles, sztiles, N, o, local_part_dest(p, T, (int)splits), (int)splits, status_ptr(status));
+}
+
+// Row-parallel W4A16 projection under tensor parallelism: partial planes of token row t go to the
+// inbox of the rank owning t (see PartDest), as plain stores from the epilogue.
+void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, std::vector<int64_t> inboxes,
+                        int64_t rank, int64_t rows_per_rank, int64_t splits, at::Tensor status) {
+  const int T = x.size(0), N = (int)n, W = (int)inboxes.size();
+  check_awq_operands(x, qtiles, sztiles, N);
+  TORCH_CHECK(W >= 1 && W <= kMaxOwners && rank >= 0 && rank < W, "llmserve_b200: one inbox per rank (<= 8)");
+  TORCH_CHECK(splits >= 1 && splits <= 64 && rows_per_rank >= 1 && rows_per_rank * W >= T,
+              "llmserve_b200: bad split / row layout");
+  if (T == 0 || N == 0) return;
+  PartDest pd = {};
+  for (int r = 0; r < W; ++r) pd.base[r] = reinterpret_cast<float*>(inboxes[r]);
+  pd.rows = (int)rows_per_rank;
+  pd.slot = (int)rank;
+  pd.planes = (int)splits;
+  pd.owners = W;
+  const at::cuda::CUDAGuard g(x.device());
+  awq_dispatch(x, qtiles, sztiles, N, nullptr, pd, (int)splits, status_ptr(status));
 }
 
 }  // namespace lsb

@@ -25,6 +25,40 @@ enum ErrorCode : int {
 // legitimate wait, and still ends a wait on a flag that is never set.
 constexpr uint32_t kSpinLimit = 1u << 26;
 
+// Where a GEMM writes its fp32 split-K partial planes.  Off tensor parallelism there is one owner
+// (the local [planes, T, N] buffer).  Under tensor parallelism the token rows are dealt to the
+// ranks in blocks of `rows` (rank o owns rows [o*rows, (o+1)*rows)) and base[o] is rank o's inbox
+// (a peer pointer for o != this rank): [source rank][plane][row][N], this rank writing the
+// source-rank slot `slot`.  The owner then reduces every source's planes from its own memory, so
+// the row-parallel reduction crosses NVLink as stores made by the GEMM epilogue, never as loads.
+constexpr int kMaxOwners = 8;
+struct PartDest {
+  float* base[kMaxOwners];
+  int rows;      // token rows per owner (T with one owner)
+  int slot;      // this rank's source slot in every owner's inbox (0 with one owner)
+  int planes;    // split-K planes per source (the GEMM's gridDim.z)
+  int owners;    // 1, or the tensor-parallel size
+  __device__ __forceinline__ float* at(int z, int t, int N, int feat) const {
+    if (owners == 1) return base[0] + ((size_t)z * rows + t) * N + feat;   // local planes: no division
+    const int o = t / rows, r = t - o * rows;
+    float* b = base[0];
+#pragma unroll
+    for (int i = 1; i < kMaxOwners; ++i)   // select without indexing the parameter array dynamically
+      if (i == o) b = base[i];
+    return b + ((size_t)(slot * planes + z) * rows + r) * N + feat;
+  }
+};
+
+inline PartDest local_part_dest(float* partials, int T, int planes) {
+  PartDest d = {};
+  d.base[0] = partials;
+  d.rows = T > 0 ? T : 1;
+  d.slot = 0;
+  d.planes = planes;
+  d.owners = 1;
+  return d;
+}
+
 __device__ __forceinline__ float to_f(bf16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ bf16 to_b(float v) { return __float2bfloat16(v); }
 

@@ -19,13 +19,17 @@
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
+#include <cooperative_groups.h>
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
+#include <map>
 #include <mutex>
 #include <unordered_map>
 
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace lsb {
 namespace {
@@ -36,6 +40,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;   // 64 bf16 = 128 bytes: one 128B swizzle atom per row
 constexpr int kSmemBudget = 200 * 1024;
 constexpr int kGroupT = 8;   // token tiles per raster group
+constexpr int kMaxClusterSplits = 16;   // K splits reduced in one (non-portable) cluster
 
 // ---- descriptors --------------------------------------------------------------------------
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"), K-major, 128B swizzle:
@@ -107,12 +112,20 @@ constexpr int tmem_cols() {
 
 // EPI 0: bf16 output [T, N] or fp32 split-K partials; EPI 1: SiLU-mul of an interleaved gate/up
 // weight (rows 128i..128i+63 gate, +64..+127 up) -> bf16 [T, N/2].
+//
+// cluster_red > 0: the gridDim.z = cluster_red K-split CTAs of one output tile form a thread-block
+// cluster (1, 1, cluster_red) and reduce their accumulators on chip: each CTA parks its fp32 tile
+// [BN tokens][128 features] in its own (now idle) stage memory, the cluster synchronises, and CTA
+// z sums slice z of the tile over every CTA's copy through distributed shared memory, then writes
+// the finished slice once -- bf16 output (or SiLU-mul for EPI 1), or ONE fp32 plane through `pd`
+// (plane 0).  No partial plane touches HBM and, under tensor parallelism, only one plane per rank
+// crosses NVLink.
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                            const __grid_constant__ CUtensorMap tm_x,
-                                                           bf16* __restrict__ out, float* __restrict__ partials,
+                                                           bf16* __restrict__ out, const PartDest pd,
                                                            int T, int N, int k_tiles, int k_tiles_per_split,
-                                                           int packed, int* __restrict__ status) {
+                                                           int packed, int cluster_red, int* __restrict__ status) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -243,7 +256,67 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
   tc_fence_after();
   const int feat = n0 + warp * 32 + lane;
   const uint32_t row_addr = tmem + ((uint32_t)(warp * 32) << 16);
-  if constexpr (EPI == 0) {
+  if (cluster_red > 0) {
+    static_assert(BN * BM * 4 <= STAGES * L::kStage, "reduction tile must fit in the stage memory");
+    cg::cluster_group cluster = cg::this_cluster();
+    float* red = reinterpret_cast<float*>(smem);   // [BN][128] fp32; the stage buffers are idle now
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      if (have) {
+        tc_ld16(row_addr + c0, r);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) r[j] = 0u;
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) red[(c0 + j) * BM + warp * 32 + lane] = __uint_as_float(r[j]);
+    }
+    cluster.sync();   // every K-slice of the tile is parked
+    const int S = cluster_red;
+    const int z = (int)cluster.block_rank();
+    const int nvalid = max(0, min(BN, T - t0));
+    // EPI 0: float4 groups (token j, features 4g..4g+3); EPI 1: (token j, gate/up pair group g < 16)
+    constexpr int kGroups = EPI == 0 ? BM / 4 : BM / 8;
+    const int E = nvalid * kGroups;
+    const int per = (E + S - 1) / S;
+    const int e_end = min(E, (z + 1) * per);
+    for (int e = z * per + (int)threadIdx.x; e < e_end; e += 128) {
+      const int j = e / kGroups, g = e - j * kGroups;
+      const int t = t0 + j;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int src = 0; src < S; ++src) {
+        const float* rs = cluster.map_shared_rank(red, src) + j * BM;
+        const float4 x = *reinterpret_cast<const float4*>(rs + g * 4);
+        a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
+        if constexpr (EPI == 1) {
+          const float4 y = *reinterpret_cast<const float4*>(rs + BM / 2 + g * 4);
+          b.x += y.x; b.y += y.y; b.z += y.z; b.w += y.w;
+        }
+      }
+      const float va[4] = {a.x, a.y, a.z, a.w};
+      if constexpr (EPI == 0) {
+        const int f0 = n0 + g * 4;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (f0 + q >= N) break;
+          if (pd.base[0] != nullptr) *pd.at(0, t, N, f0 + q) = va[q];
+          else out[(size_t)t * N + f0 + q] = to_b(va[q]);
+        }
+      } else {
+        const float vb[4] = {b.x, b.y, b.z, b.w};
+        const int out_n = N / 2, c = m_tile * (BM / 2) + g * 4;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (c + q >= out_n) break;
+          const float gt = to_f(to_b(va[q])), up = to_f(to_b(vb[q]));
+          out[(size_t)t * out_n + c + q] = to_b(gt / (1.f + expf(-gt)) * up);
+        }
+      }
+    }
+    if (pd.owners > 1) __threadfence_system();   // peer-inbox stores visible before the kernel ends
+    cluster.sync();   // keep this CTA's tile alive until every peer CTA has read it
+  } else if constexpr (EPI == 0) {
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       uint32_t r[16];
@@ -259,14 +332,17 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
           const int t = t0 + c0 + j;
           if (t < T) {
             const float v = __uint_as_float(r[j]);
-            if (partials != nullptr)
-              partials[((size_t)blockIdx.z * T + t) * N + feat] = v;
+            if (pd.base[0] != nullptr)
+              *pd.at(blockIdx.z, t, N, feat) = v;
             else
               out[(size_t)t * N + feat] = to_b(v);
           }
         }
       }
     }
+    // stores into peers' inboxes: make them visible system-wide before the kernel ends (the
+    // finishing kernel then publishes them with a release flag)
+    if (pd.owners > 1) __threadfence_system();
   } else {
     // warps 2-3 hold the up rows: hand them to warps 0-1 (same row offset) through shared memory
     float* xch = reinterpret_cast<float*>(smem);            // stage buffers are free now
@@ -373,9 +449,26 @@ const CUtensorMap& weight_map(const at::Tensor& w, bool packed) {
 
 namespace {
 
+// Cluster sizes above 8 need the non-portable opt-in, per kernel and device.
+void allow_large_clusters(const void* func) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, bool> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  bool& d = done[{func, dev}];
+  if (!d) {
+    cudaFuncSetAttribute(func, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    d = true;
+  }
+}
+
+// reduce: the `splits` K-slices of a tile reduce in a cluster (splits <= kMaxClusterSplits) and
+// write bf16 `out` (or SiLU-mul) / one fp32 plane through `pd`; otherwise every slice writes its
+// own fp32 plane through `pd` (or bf16 `out` when splits == 1).
 template <int BN, int STAGES, int EPI = 0>
-void launch(const at::Tensor& x, const at::Tensor& w, int N, bool packed, bf16* out, float* partials, int splits,
-            int* status) {
+void launch(const at::Tensor& x, const at::Tensor& w, int N, bool packed, bf16* out, const PartDest& pd, int splits,
+            int* status, bool reduce = false) {
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kStage % 1024 == 0, "stage size must keep 1024-byte alignment");
   const int T = x.size(0), K = x.size(1);
@@ -386,8 +479,27 @@ void launch(const at::Tensor& x, const at::Tensor& w, int N, bool packed, bf16* 
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
   ensure_dynamic_smem((const void*)kern, L::kBytes);
   dim3 grid(((N + BM - 1) / BM) * ((T + BN - 1) / BN), 1, splits);
-  launch_pdl(kern, grid, dim3(128), L::kBytes, at::cuda::getCurrentCUDAStream(), mw, mx, out, partials, T, N, k_tiles,
-             kps, (int)packed, status);
+  const int cred = reduce && splits > 1 ? splits : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  int nattr = 1;
+  if (cred > 0) {
+    if (cred > 8) allow_large_clusters((const void*)kern);
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = cred;
+    nattr = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  cudaLaunchKernelEx(&cfg, kern, mw, mx, out, pd, T, N, k_tiles, kps, (int)packed, cred, status);
 }
 
 template <int BN>
@@ -420,7 +532,7 @@ static int pair_min_tokens() {
 // SiLU-gated projection with an interleaved gate/up weight [N, K] (N = 2 * I, interleaved per 64
 // rows): out = silu(gate) * up as bf16 [T, I], in the GEMM epilogue (no split-K).
 static void gemm_silu_dispatch(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, bool packed, at::Tensor status,
-                               int64_t max_stages) {
+                               int64_t max_stages, int64_t splits = 1) {
   LSB_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
             "gemm operands must be bf16 CUDA tensors");
   LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1, "gemm shape mismatch");
@@ -439,16 +551,19 @@ static void gemm_silu_dispatch(at::Tensor out, at::Tensor x, at::Tensor w, int64
   bf16* o = (bf16*)out.data_ptr();
   int* st = status_ptr(status);
   const bool shallow = max_stages > 0 && max_stages <= 4;
+  const PartDest nopd = local_part_dest(nullptr, T, 1);
+  LSB_CHECK(splits >= 1 && splits <= kMaxClusterSplits, "SiLU GEMM splits must be 1..16 (cluster reduction)");
+  const int sp = (int)splits;
 #define LSB_SILU(BNV)                                                                  \
   do {                                                                                 \
-    if (shallow) launch<BNV, 4, 1>(x, w, N, packed, o, nullptr, 1, st);                \
-    else launch<BNV, stages_for<BNV>(), 1>(x, w, N, packed, o, nullptr, 1, st);        \
+    if (shallow) launch<BNV, 4, 1>(x, w, N, packed, o, nopd, sp, st, true);            \
+    else launch<BNV, stages_for<BNV>(), 1>(x, w, N, packed, o, nopd, sp, st, true);    \
   } while (0)
   if (T <= 16) LSB_SILU(16);
   else if (T <= 32) LSB_SILU(32);
   else if (T <= 64) LSB_SILU(64);
-  else if (T <= 128) launch<128, stages_for<128>(), 1>(x, w, N, packed, o, nullptr, 1, st);
-  else launch<256, stages_for<256>(), 1>(x, w, N, packed, o, nullptr, 1, st);
+  else if (T <= 128) launch<128, stages_for<128>(), 1>(x, w, N, packed, o, nopd, sp, st, true);
+  else launch<256, stages_for<256>(), 1>(x, w, N, packed, o, nopd, sp, st, true);
 #undef LSB_SILU
 }
 
@@ -463,7 +578,70 @@ void gemm_bf16_silu_packed(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n
   gemm_silu_dispatch(out, x, w, n, true, status, max_stages);
 }
 
+// SiLU-gated projection with K split over `splits` CTAs that reduce in a cluster (no partials).
+void gemm_bf16_silu_reduced(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, bool packed, int64_t splits,
+                            at::Tensor status, int64_t max_stages) {
+  gemm_silu_dispatch(out, x, w, n, packed, status, max_stages, splits);
+}
+
 void gemm_bf16_pair(void* out, bool out_f32, const at::Tensor& x, const at::Tensor& w, int N, bool packed, int* status);
+
+// The one-SM tile kernel for T tokens: a shallow 4-stage ring (two CTAs per SM) for decode-sized
+// T when asked, else the deepest ring that fits.
+static void tile_dispatch(const at::Tensor& x, const at::Tensor& w, int n, bool packed, bf16* o, const PartDest& pd,
+                          int splits, int* st, int64_t max_stages, bool reduce = false) {
+  const int T = x.size(0);
+  if (max_stages > 0 && max_stages <= 4 && T <= 64) {
+    // shallow ring: two CTAs fit on one SM and overlap each other's prologue / epilogue
+    if (T <= 16) launch<16, 4>(x, w, n, packed, o, pd, splits, st, reduce);
+    else if (T <= 32) launch<32, 4>(x, w, n, packed, o, pd, splits, st, reduce);
+    else launch<64, 4>(x, w, n, packed, o, pd, splits, st, reduce);
+    return;
+  }
+  if (T <= 16) launch<16, stages_for<16>()>(x, w, n, packed, o, pd, splits, st, reduce);
+  else if (T <= 32) launch<32, stages_for<32>()>(x, w, n, packed, o, pd, splits, st, reduce);
+  else if (T <= 64) launch<64, stages_for<64>()>(x, w, n, packed, o, pd, splits, st, reduce);
+  else if (T <= 128) launch<128, stages_for<128>()>(x, w, n, packed, o, pd, splits, st, reduce);
+  else launch<256, stages_for<256>()>(x, w, n, packed, o, pd, splits, st, reduce);
+}
+
+static void check_gemm_operands(const at::Tensor& x, const at::Tensor& w, int64_t N, bool packed) {
+  LSB_CHECK(x.is_cuda() && w.is_cuda(), "gemm operands must be CUDA tensors");
+  LSB_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
+  LSB_CHECK(x.dim() == 2 && w.dim() == 2, "gemm operands must be 2-D");
+  LSB_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "gemm operands must be K-contiguous");
+  LSB_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "row strides must be 16-byte multiples");
+  LSB_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+            "gemm operands must be 16-byte aligned");
+  if (packed) {
+    const int64_t kt = (x.size(1) + BK - 1) / BK, mt = (N + 255) / 256 * 2;
+    LSB_CHECK(w.size(1) == BK && w.is_contiguous() && w.size(0) == mt * kt * BM, "packed weight shape mismatch");
+  } else {
+    LSB_CHECK(x.size(1) == w.size(1) && w.size(0) == N, "gemm shape mismatch");
+  }
+}
+
+// K split over `splits` CTAs (1..16) whose accumulators are reduced in a cluster: bf16 out [T, n]
+// when `plane` is empty, else one fp32 plane [T, n].  T < 512 (the tile kernel's range).
+void gemm_bf16_reduced(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, bool packed, at::Tensor plane,
+                       int64_t splits, at::Tensor status, int64_t max_stages) {
+  check_gemm_operands(x, w, n, packed);
+  LSB_CHECK(splits >= 1 && splits <= kMaxClusterSplits, "cluster-reduced splits must be 1..16");
+  const int T = x.size(0);
+  bf16* o = nullptr;
+  float* p = nullptr;
+  if (plane.numel() == 0) {
+    LSB_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)T * n, "bad out");
+    o = (bf16*)out.data_ptr();
+  } else {
+    LSB_CHECK(plane.scalar_type() == at::kFloat && plane.is_contiguous() && plane.numel() == (int64_t)T * n,
+              "bad fp32 plane");
+    p = plane.data_ptr<float>();
+  }
+  if (T == 0 || n == 0) return;
+  const at::cuda::CUDAGuard g(x.device());
+  tile_dispatch(x, w, (int)n, packed, o, local_part_dest(p, T, 1), (int)splits, status_ptr(status), max_stages, true);
+}
 
 // Shared dispatch.  w: row-major [N, K], or (packed) the [rows, 64] pre-swizzled tile image of a
 // weight with N logical rows (rows padded to 256, K to 64).
@@ -502,18 +680,41 @@ static void gemm_dispatch(at::Tensor out, at::Tensor x, at::Tensor w, int64_t N,
     gemm_bf16_pair(o != nullptr ? (void*)o : (void*)p, o == nullptr, x, w, n, packed, st);
     return;
   }
-  if (max_stages > 0 && max_stages <= 4 && T <= 64) {
-    // shallow ring: two CTAs fit on one SM and overlap each other's prologue / epilogue
-    if (T <= 16) launch<16, 4>(x, w, n, packed, o, p, splits, st);
-    else if (T <= 32) launch<32, 4>(x, w, n, packed, o, p, splits, st);
-    else launch<64, 4>(x, w, n, packed, o, p, splits, st);
-    return;
+  tile_dispatch(x, w, n, packed, o, local_part_dest(p, T, (int)splits), (int)splits, st, max_stages);
+}
+
+// Row-parallel projection under tensor parallelism: the fp32 partial planes of token row t go to
+// the inbox of the rank owning t (inboxes[o], a peer pointer for o != rank; see PartDest), as
+// plain stores from the epilogue (no TMA touches peer memory).  w: row-major [n, K], or (packed)
+// the tile image of a weight with n logical rows.
+void gemm_bf16_to_owners(at::Tensor x, at::Tensor w, int64_t n, bool packed, std::vector<int64_t> inboxes,
+                         int64_t rank, int64_t rows_per_rank, int64_t splits, bool reduce, at::Tensor status,
+                         int64_t max_stages) {
+  LSB_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+            "gemm operands must be bf16 CUDA tensors");
+  LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && (x.stride(0) * 2) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "x must be K-contiguous and 16-byte aligned");
+  LSB_CHECK(w.stride(1) == 1 && (w.stride(0) * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+            "w must be K-contiguous and 16-byte aligned");
+  if (packed) {
+    const int64_t kt = (x.size(1) + BK - 1) / BK, mt = (n + 255) / 256 * 2;
+    LSB_CHECK(w.size(1) == BK && w.is_contiguous() && w.size(0) == mt * kt * BM, "packed weight shape mismatch");
+  } else {
+    LSB_CHECK(x.size(1) == w.size(1) && w.size(0) == n, "gemm shape mismatch");
   }
-  if (T <= 16) launch<16, stages_for<16>()>(x, w, n, packed, o, p, splits, st);
-  else if (T <= 32) launch<32, stages_for<32>()>(x, w, n, packed, o, p, splits, st);
-  else if (T <= 64) launch<64, stages_for<64>()>(x, w, n, packed, o, p, splits, st);
-  else if (T <= 128) launch<128, stages_for<128>()>(x, w, n, packed, o, p, splits, st);
-  else launch<256, stages_for<256>()>(x, w, n, packed, o, p, splits, st);
+  const int W = (int)inboxes.size(), T = x.size(0);
+  LSB_CHECK(W >= 1 && W <= kMaxOwners && rank >= 0 && rank < W, "one inbox per rank (<= 8)");
+  LSB_CHECK(splits >= 1 && splits <= 64 && rows_per_rank >= 1 && rows_per_rank * W >= T, "bad split / row layout");
+  if (T == 0) return;
+  PartDest pd = {};
+  for (int r = 0; r < W; ++r) pd.base[r] = reinterpret_cast<float*>(inboxes[r]);
+  LSB_CHECK(!reduce || splits <= kMaxClusterSplits, "cluster-reduced splits must be 1..16");
+  pd.rows = (int)rows_per_rank;
+  pd.slot = (int)rank;
+  pd.planes = reduce ? 1 : (int)splits;   // a cluster-reduced projection sends one plane per rank
+  pd.owners = W;
+  const at::cuda::CUDAGuard g(x.device());
+  tile_dispatch(x, w, (int)n, packed, nullptr, pd, (int)splits, status_ptr(status), max_stages, reduce);
 }
 
 // out: bf16 [T, N] when splits == 1; partials: fp32 [splits, T, N] otherwise.

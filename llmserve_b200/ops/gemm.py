@@ -44,6 +44,11 @@ def _stages(T: int) -> int:
     return 4 if T <= SMALL_T else 0
 
 
+def stages_for_tokens(T: int) -> int:
+    """Pipeline depth the tile GEMM uses for T tokens (4: shallow ring, two CTAs per SM; 0: deepest)."""
+    return _stages(T)
+
+
 class PackedWeight:
     """A weight ``[N, K]`` stored as 128 x 64 tiles in tile order ``(row tile, k tile)``, each tile
     the exact 16 KiB image the GEMM keeps in shared memory (128-byte rows, 16-byte chunks XOR-
@@ -207,6 +212,61 @@ def _empty(device, dtype):
     return _EMPTY[key]
 
 
+# ---- K splits reduced on chip (thread-block cluster + distributed shared memory) -------------
+# With the cluster reduction a K split costs no HBM traffic for partial planes and no reduction
+# kernel, so K is split for parallelism alone: the split count minimises a per-SM cost model
+# (CTAs on the busiest SM x (K tiles per CTA + a fixed per-CTA cost in K tiles)).
+CLUSTER_SPLITK = os.environ.get("LLMSERVE_CLUSTER_SPLITK", "0") == "1"
+CLUSTER_MAX_SPLITS = 16
+CLUSTER_FIXED_KTILES = float(os.environ.get("LLMSERVE_SPLIT_FIXED_KTILES", "4"))
+CLUSTER_MAX_T = 511          # from 512 tokens the persistent 2-SM kernel takes over (one plane)
+
+
+@functools.lru_cache(maxsize=None)
+def cluster_splits(T: int, N: int, K: int, num_sms: int = NUM_SMS) -> int:
+    tiles = (-(-N // TILE_M)) * (-(-T // MAX_TILE_T))
+    k_tiles = -(-K // TILE_K)
+    best, best_cost = 1, float("inf")
+    for s in range(1, min(CLUSTER_MAX_SPLITS, k_tiles) + 1):
+        cost = (-(-tiles * s // num_sms)) * (-(-k_tiles // s) + CLUSTER_FIXED_KTILES)
+        if cost < best_cost - 1e-9:
+            best, best_cost = s, cost
+    return best
+
+
+def _dense(w) -> bool:
+    from llmserve_b200.ops import awq as awq_ops
+    return not isinstance(w, awq_ops.AWQPacked)
+
+
+def use_cluster(T: int, w) -> bool:
+    return CLUSTER_SPLITK and 0 < T <= CLUSTER_MAX_T and _dense(w) and w.device.type == "cuda"
+
+
+def _operand(w):
+    """(tensor, logical rows, packed) for the C entry points."""
+    if isinstance(w, PackedWeight):
+        return w.data, w.n, True
+    return w, w.shape[0], False
+
+
+def linear_reduced(x2: torch.Tensor, w, out: torch.Tensor | None = None, plane: bool = False):
+    """``x2 @ w^T`` with K split over a cluster: bf16 ``[T, N]``, or (``plane``) one fp32 plane
+    ``[1, T, N]`` -- the layout the split-K consumers (QK-norm/RoPE, add+RMSNorm) read."""
+    T, _ = x2.shape
+    data, n, packed = _operand(w)
+    splits = cluster_splits(T, n, x2.shape[1], _num_sms(x2.device))
+    if plane:
+        res = torch.empty(1, T, n, dtype=torch.float32, device=x2.device)
+        C().gemm_bf16_reduced(_empty(x2.device, x2.dtype), x2, data, n, packed, res, splits, status(x2.device),
+                              _stages(T))
+        return res
+    res = out if out is not None else torch.empty(T, n, dtype=x2.dtype, device=x2.device)
+    C().gemm_bf16_reduced(res, x2, data, n, packed, _empty(x2.device, torch.float32), splits, status(x2.device),
+                          _stages(T))
+    return res
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
     if not x.is_cuda:
         return linear_ref(x, w, bias)
@@ -215,6 +275,11 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -
     N = w.shape[0]
     out = torch.empty(T, N, dtype=x.dtype, device=x.device)
     if T == 0:
+        return out.view(*x.shape[:-1], N)
+    if use_cluster(T, w) and _streamk_for(T, w, True) is None:
+        linear_reduced(x2, w, out)
+        if bias is not None:
+            out += bias
         return out.view(*x.shape[:-1], N)
     splits = splits_for(T, w)
     if splits == 1:
@@ -280,6 +345,11 @@ def linear_silu(x: torch.Tensor, w_interleaved: torch.Tensor, max_splits: int = 
         # prefill-sized: the 2-SM GEMM writes the interleaved projection, then one SiLU-mul pass
         y = linear(x2, w_interleaved)
         C().silu_and_mul_interleaved(out, y)
+        return out
+    if use_cluster(T, w_interleaved) and max_splits > 1:
+        data, n, packed = _operand(w_interleaved)
+        C().gemm_bf16_silu_reduced(out, x2, data, n, packed, cluster_splits(T, n, K, _num_sms(x2.device)),
+                                   status(x.device), _stages(T))
         return out
     splits = min(choose_splits(T, N, K), max_splits)
     if splits == 1 and isinstance(w_interleaved, PackedWeight):

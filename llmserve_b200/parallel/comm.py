@@ -1,13 +1,19 @@
 """Peer-mapped buffers and the fused row-parallel collective (``ops/csrc/comm.cu``).
 
-Every rank ``cudaMalloc``s one buffer ``[flags | normed out | residual | split-K partials]``,
-exports its CUDA IPC handle, and maps every peer's buffer (exchange through ``torch.distributed``
-at start-up only).  A row-parallel projection then runs as: sm_100a GEMM writing fp32 split-K
-partials into this rank's buffer, followed by ``fused_allreduce_add_rmsnorm`` which reduces them
-over NVLink, adds the residual, applies RMSNorm and all-gathers the rows into every rank's
-buffers.  The outputs alias the buffers (they are valid until the next fused call), which also
-makes the path CUDA-graph friendly.  Steps with more than ``max_tokens`` tokens (large prefills)
-take the NCCL path; all ranks decide identically from the step shape.
+Every rank ``cudaMalloc``s one buffer ``[control | normed out | residual | inbox]``, exports its
+CUDA IPC handle, and maps every peer's buffer (handles exchanged through ``torch.distributed`` at
+start-up only).  A row-parallel projection then runs as two kernels:
+
+* the sm_100a GEMM (dense or W4A16) whose epilogue stores the fp32 split-K partials of each token
+  row straight into the inbox of the rank that owns the row (peer stores over NVLink);
+* ``row_parallel_finish``: signal, wait, reduce the rank's own rows from its local inbox, add the
+  residual, RMSNorm, push the finished rows into every rank's out/residual buffers, signal, wait.
+
+The outputs alias the buffers (valid until the next fused call), which also makes the path
+CUDA-graph friendly.  The control block also carries the greedy vocab-parallel argmax exchange
+(``argmax``), so a decode step's sampling needs no NCCL call either.  Steps with more than
+``max_tokens`` tokens (large prefills) take the NCCL path; all ranks decide identically from the
+step shape.
 """
 import logging
 
@@ -20,8 +26,12 @@ from llmserve_b200.parallel import state as tp
 
 log = logging.getLogger(__name__)
 
-FLAG_BYTES = 4096
+CTRL_BYTES = 1 << 17          # flag words + argmax slots (ops/csrc/comm.cu), rounded up
 MAX_SPLITS = 8
+
+
+def _rows_per_rank(T: int, world: int) -> int:
+    return max(1, -(-T // world))
 
 
 class FusedComm:
@@ -35,19 +45,18 @@ class FusedComm:
         self.opened = opened
         out_bytes = max_tokens * hidden * 2
         self.flag_ptrs = list(peers)
-        self.out_ptrs = [p + FLAG_BYTES for p in peers]
-        self.res_ptrs = [p + FLAG_BYTES + out_bytes for p in peers]
-        self.part_ptrs = [p + FLAG_BYTES + 2 * out_bytes for p in peers]
-        # local views of the same memory
-        nbytes = FLAG_BYTES + 2 * out_bytes + MAX_SPLITS * max_tokens * hidden * 4
+        self.out_ptrs = [p + CTRL_BYTES for p in peers]
+        self.res_ptrs = [p + CTRL_BYTES + out_bytes for p in peers]
+        self.inbox_ptrs = [p + CTRL_BYTES + 2 * out_bytes for p in peers]
+        nbytes = self.buffer_bytes(hidden, max_tokens, self.world)
         self._local = _wrap(base, nbytes, device)
-        self.out_buf = self._local[FLAG_BYTES:FLAG_BYTES + out_bytes].view(torch.bfloat16)
-        self.res_buf = self._local[FLAG_BYTES + out_bytes:FLAG_BYTES + 2 * out_bytes].view(torch.bfloat16)
-        self.part_buf = self._local[FLAG_BYTES + 2 * out_bytes:].view(torch.float32)
+        self.out_buf = self._local[CTRL_BYTES:CTRL_BYTES + out_bytes].view(torch.bfloat16)
+        self.res_buf = self._local[CTRL_BYTES + out_bytes:CTRL_BYTES + 2 * out_bytes].view(torch.bfloat16)
 
     @staticmethod
-    def buffer_bytes(hidden: int, max_tokens: int) -> int:
-        return FLAG_BYTES + 2 * max_tokens * hidden * 2 + MAX_SPLITS * max_tokens * hidden * 4
+    def buffer_bytes(hidden: int, max_tokens: int, world: int) -> int:
+        inbox = world * MAX_SPLITS * _rows_per_rank(max_tokens, world) * hidden * 4
+        return CTRL_BYTES + 2 * max_tokens * hidden * 2 + inbox
 
     @classmethod
     def create(cls, device, hidden: int, max_tokens: int, timeout_s: float = 120.0):
@@ -55,7 +64,8 @@ class FusedComm:
         max_tokens = min(max_tokens, 512)
         base, opened, peers, ok = 0, [], [], 1
         try:
-            base = C().comm_alloc(cls.buffer_bytes(hidden, max_tokens))
+            assert C().comm_control_bytes() <= CTRL_BYTES
+            base = C().comm_alloc(cls.buffer_bytes(hidden, max_tokens, tp.get_tp_size()))
             handle = C().comm_ipc_handle(base)
         except Exception as e:  # pragma: no cover - depends on the box
             log.warning("fused collectives unavailable (%s); using NCCL", e)
@@ -92,17 +102,37 @@ class FusedComm:
         return 0 < T <= self.max_tokens and N == self.hidden
 
     def row_parallel_add_norm(self, x, weight, residual, norm_weight, eps):
+        from llmserve_b200.ops import awq as awq_ops
+        from llmserve_b200.parallel.fused import ROW_PARALLEL_MAX_SPLITS
         T, K = x.shape
         N = weight.shape[0]
-        from llmserve_b200.parallel.fused import ROW_PARALLEL_MAX_SPLITS
-        # plain K splits: every partial plane crosses NVLink, so the fewer the better here
-        splits = min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS)
-        part = self.part_buf[: splits * T * N].view(splits, T, N)
-        gemm.linear_partials(x, weight, splits, partials=part, streamk=False)
-        C().fused_allreduce_add_rmsnorm(self.part_ptrs, self.out_ptrs, self.res_ptrs, self.flag_ptrs,
-                                        residual.contiguous(), norm_weight, self.rank, splits, T, N, float(eps),
-                                        status(x.device))
+        rows = _rows_per_rank(T, self.world)
+        st = status(x.device)
+        if isinstance(weight, awq_ops.AWQPacked):
+            # W4A16: plain K splits, each plane of a row crosses NVLink once (as the GEMM's stores)
+            splits = min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS)
+            planes = splits
+            C().awq_gemm_to_owners(x, weight.qtiles, weight.sztiles, weight.n, self.inbox_ptrs, self.rank, rows,
+                                   splits, st)
+        else:
+            # dense: the K splits reduce on chip, one fp32 plane per rank crosses NVLink
+            data, n, packed = gemm._operand(weight)
+            reduce = gemm.use_cluster(T, weight)
+            splits = (gemm.cluster_splits(T, n, K) if reduce
+                      else min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS))
+            planes = 1 if reduce else splits
+            C().gemm_bf16_to_owners(x, data, n, packed, self.inbox_ptrs, self.rank, rows, splits, reduce, st,
+                                    gemm.stages_for_tokens(T))
+        C().row_parallel_finish(self.out_ptrs, self.res_ptrs, self.flag_ptrs, self.inbox_ptrs[self.rank],
+                                residual.contiguous(), norm_weight, self.rank, planes, T, N, rows, float(eps), st)
         return self.out_buf[: T * N].view(T, N), self.res_buf[: T * N].view(T, N)
+
+    def argmax(self, values: torch.Tensor, indices: torch.Tensor, shard_offset: int, out: torch.Tensor):
+        """Greedy token ids ``out[int64 rows]`` from every rank's per-shard (max value, local index),
+        exchanged through the control blocks (one kernel, capturable; ties -> lowest global id)."""
+        C().vocab_argmax_exchange(self.flag_ptrs, values, indices, int(shard_offset), out, self.rank,
+                                  status(values.device))
+        return out
 
     def close(self):
         torch.cuda.synchronize(self.device)

@@ -30,8 +30,11 @@ def row_parallel_add_norm(x, weight, residual, norm_weight, eps, fused=None):
     world = tp.get_tp_size()
     if fused is not None and world > 1 and fused.can_handle(T, N):
         return fused.row_parallel_add_norm(x, weight, residual, norm_weight, eps)
-    splits = min(gemm.splits_for(T, weight), ROW_PARALLEL_MAX_SPLITS)
-    partials = gemm.linear_partials(x, weight, splits)
+    if gemm.use_cluster(T, weight):
+        partials = gemm.linear_reduced(x, weight, plane=True)
+    else:
+        splits = min(gemm.splits_for(T, weight), ROW_PARALLEL_MAX_SPLITS)
+        partials = gemm.linear_partials(x, weight, splits)
     if world == 1:
         out = torch.empty(T, N, dtype=x.dtype, device=x.device)
         res_out = torch.empty_like(residual)

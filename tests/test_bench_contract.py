@@ -46,3 +46,16 @@ def test_reference_arm_at_tp2_prints_its_unavailable_line():
     assert proc.returncode == 0, proc.stderr[-2000:]
     line = json.loads(proc.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and "unavailable" in line
+
+
+def test_window_latency_uses_finished_requests_only():
+    recs = [
+        {"arrival_time": 0.0, "first_token_time": 0.1, "finish_time": 1.1, "output_tokens": 11},   # tpot 0.1
+        {"arrival_time": 0.0, "first_token_time": 0.3, "finish_time": 0.5, "output_tokens": 3},    # tpot 0.1
+        {"arrival_time": 0.5, "first_token_time": 0.6, "finish_time": None, "output_tokens": 4},   # unfinished
+    ]
+    lat = bench.window_latency(recs)
+    assert lat["requests"] == 2
+    assert abs(lat["ttft_p50_ms"] - 200.0) < 1e-6 and abs(lat["ttft_p99_ms"] - 298.0) < 1e-6
+    assert abs(lat["tpot_p99_ms"] - 100.0) < 1e-6
+    assert bench.window_latency([])["tpot_p99_ms"] is None

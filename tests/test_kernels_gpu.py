@@ -446,21 +446,29 @@ def test_fused_collective_wait_on_unset_flag_returns_error_status():
     """Failure detection on the device without a fault: a two-rank fused collective whose second
     rank never runs (its buffer is local memory that nothing signals).  Rank 0's waits for the
     peer's flags give up after the (lowered) spin limit, record the error in the status word and
-    let the kernel finish; the host raises, and the context stays usable."""
-    from llmserve_b200.parallel.comm import FLAG_BYTES, FusedComm
-    hidden, T, cap = 4096, 4, 64
-    nbytes = FusedComm.buffer_bytes(hidden, cap)
-    bufs = [C().comm_alloc(nbytes) for _ in range(2)]
+    let the kernel finish; the host raises, and the context stays usable.  The same holds for the
+    vocab-parallel argmax exchange."""
+    from llmserve_b200.parallel.comm import CTRL_BYTES, FusedComm
+    hidden, T, cap, world = 4096, 4, 64, 2
+    nbytes = FusedComm.buffer_bytes(hidden, cap, world)
+    bufs = [C().comm_alloc(nbytes) for _ in range(world)]
     dev = torch.device("cuda", torch.cuda.current_device())
     try:
         out_b = cap * hidden * 2
-        outs = [b + FLAG_BYTES for b in bufs]
-        res = [b + FLAG_BYTES + out_b for b in bufs]
-        parts = [b + FLAG_BYTES + 2 * out_b for b in bufs]
+        outs = [b + CTRL_BYTES for b in bufs]
+        res = [b + CTRL_BYTES + out_b for b in bufs]
+        inbox = bufs[0] + CTRL_BYTES + 2 * out_b
         res_in = torch.randn(T, hidden, device=dev).bfloat16()
         w = torch.ones(hidden, device=dev).bfloat16()
         C().comm_set_spin_limit(1 << 16)
-        C().fused_allreduce_add_rmsnorm(parts, outs, res, bufs, res_in, w, 0, 1, T, hidden, 1e-6, status(dev))
+        C().row_parallel_finish(outs, res, bufs, inbox, res_in, w, 0, 1, T, hidden, 2, 1e-6, status(dev))
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="peer flag wait timed out"):
+            check_status(dev)
+        vals = torch.randn(3, device=dev)
+        idx = torch.arange(3, device=dev)
+        tok = torch.empty(3, dtype=torch.int64, device=dev)
+        C().vocab_argmax_exchange(bufs, vals, idx, 0, tok, 0, status(dev))
         torch.cuda.synchronize()
         with pytest.raises(RuntimeError, match="peer flag wait timed out"):
             check_status(dev)
@@ -471,3 +479,131 @@ def test_fused_collective_wait_on_unset_flag_returns_error_status():
         torch.cuda.synchronize()
         for b in bufs:
             C().comm_free(b)
+
+
+def _wrap_dev(ptr, nbytes, dtype):
+    from llmserve_b200.parallel.comm import _wrap
+    return _wrap(ptr, nbytes, torch.device(DEV)).view(dtype)
+
+
+@pytest.mark.parametrize("reduce", [False, True])
+@pytest.mark.parametrize("world,T,packed", [(1, 5, False), (2, 64, True), (4, 7, True), (4, 64, False)])
+def test_row_parallel_push_layout_single_gpu(world, T, packed, reduce):
+    """The fused row-parallel path's data layout on one GPU: each emulated rank's GEMM stores its
+    partial planes into the owners' inboxes, then each rank's finish kernel runs alone (the peers'
+    arrival flags it would wait for are pre-set, so no kernel waits on another launch) and
+    reduces its rows, normalises them and pushes them to every buffer.  Every buffer must then
+    hold add+RMSNorm of the full fp32 product."""
+    from llmserve_b200.parallel.comm import CTRL_BYTES, FusedComm
+    hidden, K, cap, S = 512, 256, 64, 3
+    nbytes = FusedComm.buffer_bytes(hidden, cap, world)
+    bufs = [C().comm_alloc(nbytes) for _ in range(world)]
+    st = status(torch.device(DEV))
+    try:
+        out_b = cap * hidden * 2
+        outs = [b + CTRL_BYTES for b in bufs]
+        res = [b + CTRL_BYTES + out_b for b in bufs]
+        inboxes = [b + CTRL_BYTES + 2 * out_b for b in bufs]
+        g = torch.Generator(device=DEV).manual_seed(world * 100 + T)
+        xs = [torch.randn(T, K, device=DEV, generator=g).bfloat16() for _ in range(world)]
+        ws = [(torch.randn(hidden, K, device=DEV, generator=g) * 0.05).bfloat16() for _ in range(world)]
+        res_in = torch.randn(T, hidden, device=DEV, generator=g).bfloat16()
+        nw = (1 + 0.1 * torch.randn(hidden, device=DEV, generator=g)).bfloat16()
+        rows = -(-T // world)
+        for r in range(world):
+            w = gemm.pack_weight(ws[r]).data if packed else ws[r]
+            C().gemm_bf16_to_owners(xs[r], w, hidden, packed, inboxes, r, rows, S, reduce, st, 0)
+        # pre-set, in every rank's control block, the arrival flags of the ranks that run later
+        for r in range(world):
+            flags = _wrap_dev(bufs[r], 256, torch.int32)
+            for later in range(r + 1, world):
+                flags[later] = 1
+                flags[world + later] = 1
+        for r in range(world):
+            C().row_parallel_finish(outs, res, bufs, inboxes[r], res_in, nw, r, 1 if reduce else S, T, hidden, rows,
+                                    1e-6, st)
+        torch.cuda.synchronize()
+        y = sum(x.float() @ w.float().t() for x, w in zip(xs, ws)).bfloat16()
+        href, rref = norm.add_rms_norm_ref(y.cpu(), res_in.cpu(), nw.cpu(), 1e-6)
+        for r in range(world):
+            h = _wrap_dev(outs[r], T * hidden * 2, torch.bfloat16).view(T, hidden)
+            rr = _wrap_dev(res[r], T * hidden * 2, torch.bfloat16).view(T, hidden)
+            assert rel_err(h, href.to(DEV)) < 1e-2
+            assert rel_err(rr, rref.to(DEV)) < 1e-2
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            C().comm_free(b)
+
+
+def test_vocab_argmax_exchange_single_gpu():
+    """Two emulated ranks: rank 1's (value, index) pairs are written into rank 0's slots and its
+    arrival flag pre-set, so rank 0's exchange kernel runs alone; ties go to the lower global id."""
+    from llmserve_b200.parallel.comm import FusedComm
+    world, rows, shard = 2, 37, 1000
+    bufs = [C().comm_alloc(FusedComm.buffer_bytes(512, 64, world)) for _ in range(world)]
+    try:
+        g = torch.Generator(device=DEV).manual_seed(3)
+        vals = [torch.randn(rows, device=DEV, generator=g) for _ in range(world)]
+        idx = [torch.randint(0, shard, (rows,), device=DEV, generator=g) for _ in range(world)]
+        vals[1][:5] = vals[0][:5]                       # ties: rank 0's ids are lower
+        slots = _wrap_dev(bufs[0] + 1024, 2 * 8 * 512 * 8, torch.int32).view(2, 8, 512, 2)
+        slots[1, 1, :rows, 0] = vals[1].view(torch.int32)     # epoch 1 -> parity 1
+        slots[1, 1, :rows, 1] = (idx[1] + shard).int()
+        _wrap_dev(bufs[0], 1024, torch.int32)[64 + 1] = 1
+        out = torch.empty(rows, dtype=torch.int64, device=DEV)
+        C().vocab_argmax_exchange(bufs, vals[0], idx[0], 0, out, 0, status(torch.device(DEV)))
+        torch.cuda.synchronize()
+        full_v = torch.stack(vals)
+        full_i = torch.stack([idx[0], idx[1] + shard])
+        best = full_v.argmax(0)                          # first maximum -> rank 0 on ties
+        ref = full_i.gather(0, best.view(1, -1)).view(-1)
+        assert torch.equal(out, ref)
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            C().comm_free(b)
+
+
+@pytest.mark.parametrize("T", [1, 16, 33, 64, 100, 256, 300])
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 16])
+@pytest.mark.parametrize("packed", [False, True])
+def test_cluster_reduced_gemm_matches_fp32(T, splits, packed):
+    """K split over a thread-block cluster whose CTAs reduce their accumulators through distributed
+    shared memory: bf16 output and the single fp32 plane both equal the fp32 product."""
+    N, K = 384, 1088              # 17 K tiles: uneven slices; 3 weight tiles
+    g = torch.Generator(device=DEV).manual_seed(T * 31 + splits)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=DEV, generator=g) * 0.05).bfloat16()
+    ref = x.float() @ w.float().t()
+    wd = gemm.pack_weight(w).data if packed else w
+    out = torch.full((T, N), float("nan"), device=DEV).bfloat16()
+    empty = torch.empty(0, device=DEV)
+    C().gemm_bf16_reduced(out, x, wd, N, packed, empty, splits, status(torch.device(DEV)), 4 if T <= 64 else 0)
+    assert rel_err(out, ref) < 1e-2
+    plane = torch.full((1, T, N), float("nan"), device=DEV)
+    C().gemm_bf16_reduced(torch.empty(0, device=DEV).bfloat16(), x, wd, N, packed, plane, splits,
+                          status(torch.device(DEV)), 0)
+    assert rel_err(plane[0], ref) < 1e-3
+
+
+@pytest.mark.parametrize("T,splits", [(7, 4), (64, 3), (64, 16), (200, 2)])
+def test_cluster_reduced_silu_gemm(T, splits):
+    I, K = 640, 1024
+    g = torch.Generator(device=DEV).manual_seed(T + splits)
+    x = torch.randn(T, K, device=DEV, generator=g).bfloat16()
+    w = (torch.randn(2 * I, K, device=DEV, generator=g) * 0.05).bfloat16()
+    ref = activation.silu_and_mul_ref((x.float() @ w.float().t()).bfloat16().cpu()).to(DEV)
+    wi = gemm.pack_weight(gemm.interleave_gate_up(w))
+    out = torch.empty(T, I, device=DEV).bfloat16()
+    C().gemm_bf16_silu_reduced(out, x, wi.data, wi.n, True, splits, status(torch.device(DEV)), 4 if T <= 64 else 0)
+    assert rel_err(out, ref) < 1e-2
+
+
+def test_linear_uses_cluster_splits_policy():
+    """The engine's linear on decode shapes (cluster path by default) equals fp32."""
+    for T, N, K in [(64, 6144, 4096), (64, 4096, 512), (16, 24576, 4096), (64, 768, 4096)]:
+        x = torch.randn(T, K, device=DEV).bfloat16()
+        w = gemm.pack_weight((torch.randn(N, K, device=DEV) * 0.02).bfloat16())
+        assert gemm.cluster_splits(T, N, K) >= 1
+        assert rel_err(gemm.linear(x, w), x.float() @ w.unpack().float().t()) < 1e-2
