@@ -81,14 +81,19 @@ class RpcChannel:
                 raise RuntimeError(f"tensor-parallel worker {w + 1} failed: {msg}")
 
     def wait_acks(self, timeout_s: float):
-        deadline = time.monotonic() + timeout_s
+        # acknowledgements normally follow within tens of microseconds (a worker acks as soon as it
+        # has queued its kernels), so spin first and only then back off to sleeps
+        start = time.monotonic()
+        deadline = start + timeout_s
         while True:
             self.check_workers()
             if min((self.worker_status(w)[0] for w in range(self.num_workers)), default=self.seq) >= self.seq:
                 return
-            if time.monotonic() > deadline:
+            now = time.monotonic()
+            if now > deadline:
                 raise RpcTimeout(f"workers did not acknowledge call {self.seq} within {timeout_s}s")
-            time.sleep(0.0005)
+            if now - start > 0.005:
+                time.sleep(0.0002)
 
     # ---- workers -----------------------------------------------------------------------------
     def recv(self, worker: int, idle_timeout_s: float, parent_pid: int):

@@ -214,11 +214,14 @@ def _empty(device, dtype):
 
 # ---- K splits reduced on chip (thread-block cluster + distributed shared memory) -------------
 # With the cluster reduction a K split costs no HBM traffic for partial planes and no reduction
-# kernel, so K is split for parallelism alone: the split count minimises a per-SM cost model
-# (CTAs on the busiest SM x (K tiles per CTA + a fixed per-CTA cost in K tiles)).
-CLUSTER_SPLITK = os.environ.get("LLMSERVE_CLUSTER_SPLITK", "0") == "1"
+# kernel, so K is split for parallelism alone.  The split count (a power of two, at least two K
+# tiles per CTA) minimises waves x (K tiles per CTA + a fixed per-CTA cost), where a wave is every
+# CTA slot of the GPU (two per SM with the shallow ring of decode-sized T).  Fitted to a per-shape
+# sweep of the Qwen3-8B projections at TP 1/2/8 inside CUDA graphs on B200, where it beat the
+# split-K-planes + reduction kernel path on every projection but the 192-tile gate_up (a tie).
+CLUSTER_SPLITK = os.environ.get("LLMSERVE_CLUSTER_SPLITK", "1") != "0"
 CLUSTER_MAX_SPLITS = 16
-CLUSTER_FIXED_KTILES = float(os.environ.get("LLMSERVE_SPLIT_FIXED_KTILES", "4"))
+CLUSTER_FIXED_KTILES = float(os.environ.get("LLMSERVE_SPLIT_FIXED_KTILES", "8"))
 CLUSTER_MAX_T = 511          # from 512 tokens the persistent 2-SM kernel takes over (one plane)
 
 
@@ -226,11 +229,14 @@ CLUSTER_MAX_T = 511          # from 512 tokens the persistent 2-SM kernel takes 
 def cluster_splits(T: int, N: int, K: int, num_sms: int = NUM_SMS) -> int:
     tiles = (-(-N // TILE_M)) * (-(-T // MAX_TILE_T))
     k_tiles = -(-K // TILE_K)
+    slots = num_sms * (2 if T <= SMALL_T else 1)
     best, best_cost = 1, float("inf")
-    for s in range(1, min(CLUSTER_MAX_SPLITS, k_tiles) + 1):
-        cost = (-(-tiles * s // num_sms)) * (-(-k_tiles // s) + CLUSTER_FIXED_KTILES)
+    s = 1
+    while s <= CLUSTER_MAX_SPLITS and (s == 1 or -(-k_tiles // s) >= 2):
+        cost = (-(-tiles * s // slots)) * (-(-k_tiles // s) + CLUSTER_FIXED_KTILES)
         if cost < best_cost - 1e-9:
             best, best_cost = s, cost
+        s *= 2
     return best
 
 
