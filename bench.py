@@ -59,49 +59,102 @@ def parse():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks, power and clock-event reasons of the job's GPUs, sampled every 10 ms by a thread
+    during the timed region through NVML (read-only queries; GPUs found by PCI bus id, so the CUDA
+    and NVML orderings need not agree).  One sample is taken on entry and one on exit, so even a
+    window of a few steps has samples.  Falls back to ``nvidia-smi -lms 50`` without NVML."""
 
-    def __init__(self, indices):
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, indices, interval_s: float = 0.01):
         self.indices = indices
+        self.interval_s = interval_s
+        self.rows = []          # (sm_mhz, max_mhz, power_w, reasons)
         self.proc = None
+        self.nvml = None
         self.path = os.path.join(tempfile.mkdtemp(), "clocks.csv")
 
+    def _nvml_handles(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        handles = []
+        for i in range(len(self.indices)):
+            p = torch.cuda.get_device_properties(i)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            handles.append(pynvml.nvmlDeviceGetHandleByPciBusId(bus))
+        return pynvml, handles
+
+    def _sample(self):
+        nv, handles = self.nvml
+        for h in handles:
+            mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                              float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)),
+                              nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                              {name for name, bit in self.REASONS if mask & getattr(nv, bit)}))
+
+    def _loop(self):
+        while not self._stop.wait(self.interval_s):
+            self._sample()
+
     def __enter__(self):
+        import threading
+        try:
+            self.nvml = self._nvml_handles()
+            self._sample()
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", ",".join(map(str, self.indices))],
+                                          "-lms", "50", "-i", ",".join(map(str, self.indices))],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
+        if self.nvml is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            self._sample()
+            self.nvml[0].nvmlShutdown()
         if self.proc is not None:
             self.proc.terminate()
             self.proc.wait(timeout=10)
             self.f.close()
+            self._read_csv()
 
-    def summary(self):
-        rows = []
+    def _read_csv(self):
+        names = [n for n, _ in self.REASONS]
         try:
             for line in open(self.path):
                 parts = [x.strip() for x in line.split(",")]
                 if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
-                    rows.append(parts)
+                    power = float(parts[3]) if parts[3].replace(".", "").isdigit() else 0.0
+                    self.rows.append((float(parts[1]), float(parts[2]), power,
+                                      {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}))
         except OSError:
             pass
-        if not rows:
+
+    def summary(self):
+        if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(float(r[2]) for r in rows),
-                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
-                "samples": len(rows), "reasons": reasons}
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": max(r[1] for r in self.rows),
+                "power_w_max": round(max(r[2] for r in self.rows), 1), "samples": len(self.rows),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi",
+                "reasons": sorted(set().union(*(r[3] for r in self.rows)))}
 
 
 def visible_indices(n):

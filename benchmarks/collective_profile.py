@@ -26,7 +26,7 @@ import os
 NVLINK_GBS = 770.0           # measured peer copy, per direction per GPU
 
 
-def fused_roofline_us(T: int, hidden: int, inner_shard: int, world: int, splits: int, hbm_gbs: float,
+def fused_roofline_us(T: int, hidden: int, inner_shard: int, world: int, planes: int, hbm_gbs: float,
                       bf16_tflops: float, nvlink_gbs: float = NVLINK_GBS) -> dict:
     """Lower bound of one fused row-parallel step on one rank (µs) and its three terms."""
     rows = -(-T // world)
@@ -34,7 +34,7 @@ def fused_roofline_us(T: int, hidden: int, inner_shard: int, world: int, splits:
     flops = 2.0 * T * hidden * inner_shard
     # the GEMM stores the fp32 partial planes of the other ranks' rows into their inboxes, then the
     # rank pushes its finished rows (normed output + residual, bf16) to the other ranks
-    link_bytes = (T - min(rows, T)) * hidden * 4 * splits + (world - 1) * min(rows, T) * hidden * 2 * 2
+    link_bytes = (T - min(rows, T)) * hidden * 4 * planes + (world - 1) * min(rows, T) * hidden * 2 * 2
     terms = {"hbm_us": weight_bytes / (hbm_gbs * 1e3), "compute_us": flops / (bf16_tflops * 1e6),
              "nvlink_us": link_bytes / (nvlink_gbs * 1e3)}
     return dict(terms, roofline_us=max(terms.values()), nvlink_bytes=link_bytes, weight_bytes=weight_bytes)
@@ -95,17 +95,22 @@ def main(argv=None):
             x = torch.randn(T, k, device=dev, generator=g).bfloat16()
             res = torch.randn(T, args.hidden, device=dev, generator=g).bfloat16()
             splits = min(gemm.splits_for(T, w, streamk=False), 8)
-            row = {"tokens": T, "world": world, "hidden": args.hidden, "inner_shard": k, "splits": splits}
+            # with the cluster-reduced GEMM the K splits meet on chip: one fp32 plane per row crosses
+            planes = 1 if gemm.use_cluster(T, w) else splits
+            row = {"tokens": T, "world": world, "hidden": args.hidden, "inner_shard": k, "planes": planes}
             if comm is not None and comm.can_handle(T, args.hidden):
                 row["fused_us"] = timed(lambda: comm.row_parallel_add_norm(x, w, res, nw, 1e-6))
-            row["gemm_us"] = timed(lambda: gemm.linear_partials(x, w, splits, streamk=False))
+            if planes == 1:
+                row["gemm_us"] = timed(lambda: gemm.linear_reduced(x, w, plane=True))
+            else:
+                row["gemm_us"] = timed(lambda: gemm.linear_partials(x, w, splits, streamk=False))
 
             def nccl():
                 y = gemm.linear(x, w)
                 dist.all_reduce(y)
                 norm_ops.add_rms_norm(y, res, nw, 1e-6)
             row["nccl_us"] = timed(nccl)
-            row.update(fused_roofline_us(T, args.hidden, k, world, splits, hbm, peak))
+            row.update(fused_roofline_us(T, args.hidden, k, world, planes, hbm, peak))
             if "fused_us" in row:
                 row["fraction_of_roofline"] = row["roofline_us"] / row["fused_us"]
             if rank == 0:

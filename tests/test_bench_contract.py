@@ -1,5 +1,5 @@
 """The parts of ``bench.py`` that run without a GPU: the clock sampler's summary of nvidia-smi
-samples (median SM clock, throttle reasons that invalidate a run) and the reference arm's
+samples (NVML thread or nvidia-smi CSV; median SM clock, throttle reasons that invalidate a run) and the reference arm's
 ``unavailable`` line for tensor-parallel runs."""
 import json
 import os
@@ -22,6 +22,7 @@ def test_clock_summary_takes_the_median_and_collects_active_reasons(tmp_path):
         "garbage line",
     ]
     (tmp_path / "clocks.csv").write_text("\n".join(rows) + "\n")
+    s._read_csv()
     out = s.summary()
     assert out["sm_mhz"] == 1890 and out["sm_max_mhz"] == 1965 and out["samples"] == 3
     assert out["reasons"] == ["sw_power_cap"] and out["power_w_max"] == 990.1
@@ -30,7 +31,47 @@ def test_clock_summary_takes_the_median_and_collects_active_reasons(tmp_path):
 def test_clock_summary_without_samples_says_so(tmp_path):
     s = bench.ClockSampler([0])
     s.path = str(tmp_path / "missing.csv")
+    s._read_csv()
     assert s.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+
+class _FakeNvml:
+    """The read-only NVML calls the sampler makes, with fixed answers."""
+    NVML_CLOCK_SM = 1
+    nvmlClocksEventReasonHwSlowdown = 0x8
+    nvmlClocksEventReasonHwThermalSlowdown = 0x40
+    nvmlClocksEventReasonSwThermalSlowdown = 0x20
+    nvmlClocksEventReasonSwPowerCap = 0x4
+
+    def __init__(self):
+        self.calls = 0
+
+    def nvmlDeviceGetCurrentClocksEventReasons(self, h):
+        self.calls += 1
+        return 0x4 if self.calls % 2 else 0x0
+
+    def nvmlDeviceGetClockInfo(self, h, kind):
+        return 1965 if self.calls % 2 else 1800
+
+    def nvmlDeviceGetMaxClockInfo(self, h, kind):
+        return 1965
+
+    def nvmlDeviceGetPowerUsage(self, h):
+        return 995_000
+
+    def nvmlShutdown(self):
+        pass
+
+
+def test_clock_sampler_nvml_thread_samples_inside_a_short_window(monkeypatch):
+    import time
+    fake = _FakeNvml()
+    monkeypatch.setattr(bench.ClockSampler, "_nvml_handles", lambda self: (fake, ["h0"]))
+    with bench.ClockSampler([0], interval_s=0.005) as s:
+        time.sleep(0.05)
+    out = s.summary()
+    assert out["source"] == "nvml" and out["samples"] >= 3
+    assert out["sm_max_mhz"] == 1965 and out["power_w_max"] == 995.0 and out["reasons"] == ["sw_power_cap"]
 
 
 def test_visible_indices_follow_cuda_visible_devices(monkeypatch):

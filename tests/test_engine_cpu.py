@@ -356,3 +356,40 @@ def test_awq_target_with_eagle3_equals_awq_plain_decoding(tmp_path, ckpts):
     base, _ = _run(awq, prompts, max_tokens=12)
     spec, m = _run(awq, prompts, max_tokens=12, speculative_model=draft)
     assert spec == base and m["summary"]["speculative"]["steps"] > 0
+
+
+def test_host_engine_logits_equal_fp32_transformers_forward(tmp_path):
+    """The host (fp32) engine's logits at every step -- prefill over the paged pool, then decode
+    steps crossing block boundaries -- equal transformers' Qwen3 forward of the same weights,
+    teacher-forced on the engine's tokens (an implementation independent of this one)."""
+    import glob
+
+    from safetensors.torch import load_file
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    from tests.support import RecordingSampler, compare_logits
+    cfg = dict(TINY, torch_dtype="bfloat16", num_hidden_layers=2)
+    path = write_qwen3_checkpoint(str(tmp_path / "m"), cfg)
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, cfg["vocab_size"], (int(n),), generator=g).tolist() for n in (33, 7, 40)]
+    n_out = 12
+    llm = LLM(path, device="cpu", enforce_eager=True, max_model_len=256, max_num_batched_tokens=1024, max_num_seqs=4,
+              kvcache_block_size=16, num_kvcache_blocks=64)
+    rec = RecordingSampler()
+    llm.model_runner.sampler = rec
+    out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=n_out, ignore_eos=True),
+                                                use_tqdm=False)]
+    llm.exit()
+    sd = {}
+    for f in glob.glob(f"{path}/*.safetensors"):
+        sd.update(load_file(f))
+    model = Qwen3ForCausalLM(Qwen3Config(**{k: v for k, v in cfg.items() if k not in ("architectures", "torch_dtype")}))
+    model.float().eval().load_state_dict({k: v.float() for k, v in sd.items()}, strict=True)
+    ref = [torch.empty_like(x) for x in rec.logits]
+    with torch.no_grad():
+        for i, (p, toks) in enumerate(zip(prompts, out)):
+            full = model(torch.tensor([p + toks[:-1]])).logits[0]
+            for j in range(n_out):
+                ref[j][i] = full[len(p) - 1 + j]
+    worst, _ = compare_logits(rec.logits, ref, 1e-4)
+    assert worst < 1e-5
