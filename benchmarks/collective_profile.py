@@ -12,10 +12,12 @@ add and the RMSNorm:
   stores), then ``row_parallel_finish`` reduces the rank's rows from its own inbox, adds the
   residual, normalises and pushes the finished rows to every rank (peer stores);
 * ``nccl``    -- the baseline: the same GEMM (bf16 output), ``dist.all_reduce``, add+RMSNorm kernel;
-* ``gemm``    -- the GEMM alone, to separate the collective's share.
+* ``gemm``    -- the GEMM alone, to separate the collective's share;
+* ``finish_only`` -- the finishing kernel alone (signal, wait, reduce, norm, push, signal, wait).
 
-Times are CUDA events on each rank around ``--iters`` back-to-back calls (after warm-up), the max
-over ranks is reported.  The roofline of the fused step is the slowest of its weight bytes at the
+Each variant's ``--iters`` back-to-back calls are captured in one CUDA graph (the form the decode
+step runs them in, without Python launch overhead); times are CUDA events around one replay on
+each rank, divided by ``--iters``, max over ranks.  The roofline of the fused step is the slowest of its weight bytes at the
 measured HBM bandwidth, its FLOPs at the measured bf16 peak, and the bytes that cross NVLink per
 rank at the measured 770 GB/s per direction (``roofline_us``); ``fraction`` = roofline / achieved.
 """
@@ -72,20 +74,40 @@ def main(argv=None):
     hbm, peak = _peaks()
     k = args.inner // world
     g = torch.Generator(device=dev).manual_seed(rank)
-    w = gemm.pack_weight((torch.randn(args.hidden, k, device=dev, generator=g) * 0.02).bfloat16())
+    # enough weight copies, used in turn, that the captured loop streams them from HBM (> L2)
+    copies = max(1, -(-(256 << 20) // (args.hidden * k * 2)))
+    ws = [gemm.pack_weight((torch.randn(args.hidden, k, device=dev, generator=g) * 0.02).bfloat16())
+          for _ in range(copies)]
+    w = ws[0]
+    turn = [0]
+
+    def next_w():
+        turn[0] += 1
+        return ws[turn[0] % copies]
     nw = torch.ones(args.hidden, device=dev).bfloat16()
 
     def timed(fn):
-        for _ in range(5):
+        """Device time per call: ``--iters`` calls captured in one CUDA graph (as the engine runs
+        them), replayed after warm-up; CUDA events around one replay; max over ranks."""
+        for _ in range(3):
             fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=dev)):
+            for _ in range(args.iters):
+                fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        graph.replay()
         torch.cuda.synchronize()
         dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for _ in range(args.iters):
-            fn()
+        graph.replay()
         b.record()
         torch.cuda.synchronize()
+        del graph
         t = torch.tensor([a.elapsed_time(b) * 1e3 / args.iters], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t)
@@ -99,14 +121,15 @@ def main(argv=None):
             planes = 1 if gemm.use_cluster(T, w) else splits
             row = {"tokens": T, "world": world, "hidden": args.hidden, "inner_shard": k, "planes": planes}
             if comm is not None and comm.can_handle(T, args.hidden):
-                row["fused_us"] = timed(lambda: comm.row_parallel_add_norm(x, w, res, nw, 1e-6))
+                row["fused_us"] = timed(lambda: comm.row_parallel_add_norm(x, next_w(), res, nw, 1e-6))
+                row["finish_only_us"] = timed(lambda: comm.finish(res, nw, 1e-6, T, planes))
             if planes == 1:
-                row["gemm_us"] = timed(lambda: gemm.linear_reduced(x, w, plane=True))
+                row["gemm_us"] = timed(lambda: gemm.linear_reduced(x, next_w(), plane=True))
             else:
-                row["gemm_us"] = timed(lambda: gemm.linear_partials(x, w, splits, streamk=False))
+                row["gemm_us"] = timed(lambda: gemm.linear_partials(x, next_w(), splits, streamk=False))
 
             def nccl():
-                y = gemm.linear(x, w)
+                y = gemm.linear(x, next_w())
                 dist.all_reduce(y)
                 norm_ops.add_rms_norm(y, res, nw, 1e-6)
             row["nccl_us"] = timed(nccl)

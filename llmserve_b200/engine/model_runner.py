@@ -705,7 +705,7 @@ class ModelRunner:
             g = torch.cuda.CUDAGraph()
             self._graph_body(bs)                   # warm-up outside capture
             before = LaunchCounter.launches
-            with torch.cuda.graph(g, self.graph_pool):
+            with torch.cuda.graph(g, self.graph_pool, stream=self.capture_stream()):
                 self._graph_body(bs)
             self.graph_launches[bs] = LaunchCounter.launches - before
             if self.graph_pool is None:
@@ -713,6 +713,15 @@ class ModelRunner:
             self.graphs[bs] = g
             torch.cuda.synchronize()
             reset_context()
+
+    def capture_stream(self) -> torch.cuda.Stream:
+        """This runner's side stream for graph capture.  ``torch.cuda.graph`` would otherwise use
+        one class-wide stream created on whichever device captured first; a second runner of the
+        same process on another GPU (prefill/decode disaggregation) would then capture on the first
+        GPU's stream while its kernels run eagerly on its own, leaving an empty graph."""
+        if getattr(self, "_capture_stream", None) is None:
+            self._capture_stream = torch.cuda.Stream(device=self.device)
+        return self._capture_stream
 
     def _graph_body(self, bs: int):
         v = self.graph_vars

@@ -29,7 +29,6 @@ import torch
 
 from llmserve_b200.ops import sampling as sampling_ops
 from llmserve_b200.ops._ext import LaunchCounter
-from llmserve_b200.parallel import state as tp
 from llmserve_b200.speculative.sampling import greedy_accept_packed
 from llmserve_b200.utils.context import reset_context, set_context
 
@@ -108,7 +107,9 @@ class SpeculativeGraphs:
         finally:
             reset_context()
         vals, idx = sampling_ops.local_argmax(logits)
-        target = tp.vocab_parallel_argmax(vals, idx, r.model.lm_head.vocab_start).view(B, n)
+        # global greedy ids: the NVLink (value, index) exchange when the fused collectives are up
+        # (capturable, no NCCL call), else NCCL all-gathers
+        target = r._greedy_from_shards(vals, idx).view(B, n)
         self.packed[:B] = greedy_accept_packed(target, self.drafts[:B], self.ids[:B])
         self.corr_aux[:B] = aux.view(B, n, -1)[self.rows[:B], self.packed[:B, 0]]
 
@@ -121,7 +122,7 @@ class SpeculativeGraphs:
             torch.cuda.synchronize()
             graph = torch.cuda.CUDAGraph()
             before = LaunchCounter.launches
-            with torch.cuda.graph(graph, self.pool):
+            with torch.cuda.graph(graph, self.pool, stream=self.r.capture_stream()):
                 self.body(B)
             self.launches[B] = LaunchCounter.launches - before
             if self.pool is None:

@@ -139,12 +139,28 @@ def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, wor
     return out
 
 
-def prefill_attention(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, scale, max_seqlen_q: int):
+# From this many query rows in the longest sequence of a step, prefill runs on the tcgen05 kernel
+# (128-row query tiles); shorter chunks (verify, small chunked-prefill pieces) on the mma.sync one.
+PREFILL_TC_MIN_Q = int(os.environ.get("LLMSERVE_PREFILL_TC_MIN_Q", str(1 << 30)))
+
+
+def prefill_attention(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, scale, max_seqlen_q: int,
+                      kernel: str = "auto"):
+    """Varlen causal attention of packed query rows against the paged pool.  ``kernel``: "auto"
+    (by ``max_seqlen_q``), "tc" (tcgen05 / TMEM / TMA, ``ops/csrc/prefill_sm100.cu``) or "mma"
+    (mma.sync tiles, ``ops/csrc/attention.cu``)."""
     if not q.is_cuda:
         return prefill_attention_ref(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, scale)
     out = torch.empty_like(q)
-    C().prefill_attention(out, q.contiguous(), k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables,
-                          float(scale), int(max_seqlen_q), status(q.device))
+    q = q.contiguous()
+    bs, hd = k_cache.shape[2], k_cache.shape[3]
+    use_tc = kernel == "tc" or (kernel == "auto" and max_seqlen_q >= PREFILL_TC_MIN_Q)
+    if use_tc and C().prefill_tc_supported(bs, hd):
+        C().prefill_attention_tc(out, q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, float(scale),
+                                 int(max_seqlen_q), status(q.device))
+    else:
+        C().prefill_attention(out, q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables,
+                              float(scale), int(max_seqlen_q), status(q.device))
     return out
 
 

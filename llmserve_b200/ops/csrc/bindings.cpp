@@ -60,6 +60,10 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
                           at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml,
                           at::Tensor counters, int64_t max_splits, int64_t partition, at::Tensor status);
 bool decode_tma_supported(int64_t block_size, int64_t head_dim);
+bool prefill_tc_supported(int64_t block_size, int64_t head_dim);
+void prefill_attention_tc(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,
+                          at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_q,
+                          at::Tensor status);
 void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, at::Tensor partials,
               int64_t splits, at::Tensor status);
 void gemm_bf16_streamk(at::Tensor partials, at::Tensor x, at::Tensor w, int64_t n, int64_t grid, int64_t stages,
@@ -93,6 +97,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_tables"), py::arg("context_lens"), py::arg("scale"), py::arg("part_o"), py::arg("part_ml"),
         py::arg("counters"), py::arg("max_splits"), py::arg("partition"), py::arg("grid_z"), py::arg("status"));
   m.def("prefill_attention", &lsb::prefill_attention);
+  m.def("prefill_attention_tc", &lsb::prefill_attention_tc);
+  m.def("prefill_tc_supported", &lsb::prefill_tc_supported);
   m.def("tree_attention", &lsb::tree_attention);
   m.def("comm_alloc", &lsb::comm_alloc);
   m.def("comm_free", &lsb::comm_free);

@@ -456,6 +456,10 @@ int sm_count() {
 
 }  // namespace
 
+// Tensor map over one layer's K or V pool viewed as [blocks * kv_heads * block_size, head_dim] with a
+// (box_rows x 64 dims) box, 128B swizzle; cached per (pool, box).  Shared with the prefill kernel.
+const CUtensorMap& kv_pool_map(const at::Tensor& pool, int box_rows) { return pool_map(pool, box_rows); }
+
 // Whether decode_attention_tma supports this pool (block size and head dim).
 bool decode_tma_supported(int64_t block_size, int64_t head_dim) {
   return (head_dim == 64 || head_dim == 128) && block_size % 8 == 0 && (block_size % 64 == 0 || 64 % block_size == 0);

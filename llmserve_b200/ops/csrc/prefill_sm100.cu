@@ -1,0 +1,515 @@
+// Varlen causal prefill attention on the 5th-generation tensor cores: S = Q K^T and O += P V are
+// tcgen05.mma with fp32 accumulators in TMEM, Q / K / V tiles arrive by TMA straight from the
+// packed query rows and the paged pool [blocks, kv_heads, block_size, head_dim].
+//
+// One CTA computes 128 query rows of one head (UMMA M = 128) against 64-key tiles:
+//   warp 4, lane 0 : TMA producer.  Q once (two 64-column halves, 128B swizzle), then K and V of
+//                    each 64-key tile into a 3-stage ring; a tile is assembled from per-block boxes
+//                    of min(block_size, 64) keys, so pages need not be contiguous.
+//   warp 5, lane 0 : MMA issuer.  S_j = Q K_j^T into one of two TMEM S buffers (both operands
+//                    K-major), then O += P_{j-1} V_{j-1} (P K-major from shared memory, V read
+//                    MN-major straight from its TMA tile) -- so the tensor pipe computes PV of the
+//                    previous tile and S of the next while the softmax warps work on this one.
+//   warps 0..3     : softmax.  Thread r owns query row r (TMEM lane r): tcgen05.ld of its 64
+//                    scores, causal / length mask, online softmax in the log2 domain, P as bf16
+//                    into a swizzled shared-memory tile.  The running max is only moved when it
+//                    grows by more than 2^8 (P stays <= 256, exact in fp32 sums), so the rescale of
+//                    O in TMEM (tcgen05.ld / st, after the previous PV finished) is rare.  At the
+//                    end the same threads read O from TMEM, divide by the row sum and store bf16.
+// Keys past the context (or from a block id outside the pool, recorded as kBadIndex) get P = 0
+// and their V rows are zeroed in shared memory, so whatever the pool holds there never reaches O.
+// Every wait is bounded; a timeout records an error code, raises a CTA-wide abort flag that every
+// role polls, drains the copies and MMAs in flight and frees TMEM.
+//
+// Short query chunks (EAGLE3 verify, decode-sized chunks) stay on the mma.sync kernel in
+// attention.cu: a 128-row tile would be mostly empty there.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace lsb {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+const CUtensorMap& kv_pool_map(const at::Tensor& pool, int box_rows);
+int* status_ptr(const at::Tensor& status);
+
+namespace {
+
+#define LSB_CHECK(cond, msg) TORCH_CHECK(cond, "llmserve_b200: ", msg)
+
+constexpr int kBQ = 128;        // query rows per CTA (UMMA M)
+constexpr int kBKV = 64;        // keys per tile
+constexpr int kStages = 3;      // K/V ring depth
+constexpr int kThreads = 192;   // 4 softmax warps + producer warp + MMA warp
+constexpr float kRescaleLog2 = 8.f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int HD>
+struct PfLayout {
+  static constexpr int kHalves = HD / 64;                 // 128-byte column halves
+  static constexpr int kQHalf = kBQ * 128;                // 16 KiB
+  static constexpr int kQBytes = kHalves * kQHalf;
+  static constexpr int kKVHalf = kBKV * 128;              // 8 KiB
+  static constexpr int kTileBytes = kHalves * kKVHalf;    // K (or V) of one tile
+  static constexpr int kStageBytes = 2 * kTileBytes;      // K | V
+  static constexpr int kPBytes = kBQ * kBKV * 2;          // 16 KiB, one 128-byte row per query
+  static constexpr int kStageOff = kQBytes;
+  static constexpr int kPOff = kStageOff + kStages * kStageBytes;
+  static constexpr int kBarOff = kPOff + 2 * kPBytes;
+  static constexpr int kBytes = kBarOff + 256 + 1024;     // barriers + alignment slack
+  // TMEM columns: O [0, HD), S buffers [HD, HD + 64) and [HD + 64, HD + 128)
+  static constexpr int kTmemCols = 256;
+};
+
+// ---- tcgen05 / TMA wrappers ---------------------------------------------------------------------
+// Shared-memory matrix descriptor, 128B swizzle, K-major: stride between 8-row groups 1024 B
+// (leading offset unused), descriptor version 1.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// 128B swizzle, MN-major (the V tile: rows = keys = the reduction dimension, head dims contiguous):
+// leading offset = distance between the 64-element column halves, stride offset = distance between
+// 8-key groups (1024 B).
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t saddr, uint32_t half_bytes) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((half_bytes >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, M = 128, N, B major-ness.
+__host__ __device__ constexpr uint32_t idesc(int n, bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(kBQ >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d), "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// 32 lanes x 16 columns of fp32 (no wait; tmem_wait_ld() before use)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait that also gives up once another role raised the abort flag.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                           int code) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  record_error(status, code);
+  *abort_flag = 1;
+  return false;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, bf16* __restrict__ out, const int* __restrict__ cu_q,
+    const int* __restrict__ seqlens_k, const int* __restrict__ block_tables, int bt_stride, float scale_log2, int nh,
+    int nkv, int bs, int box_keys, int tiles_per_seq, int num_seqs, int nblk, int* __restrict__ status) {
+  using L = PfLayout<HD>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* q_full = bars;                       // 1
+  uint64_t* k_full = bars + 1;                   // kStages
+  uint64_t* v_full = k_full + kStages;           // kStages
+  uint64_t* kv_empty = v_full + kStages;         // kStages
+  uint64_t* s_full = kv_empty + kStages;         // 2
+  uint64_t* s_free = s_full + 2;                 // 2
+  uint64_t* p_full = s_free + 2;                 // 2
+  uint64_t* p_free = p_full + 2;                 // 2
+  uint64_t* o_done = p_free + 2;                 // 1
+  uint64_t* drain = o_done + 1;                  // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* bad_keys = reinterpret_cast<uint64_t*>(smem + L::kBarOff + 192);   // kStages masks
+  __shared__ int abort_flag;
+  volatile int* abort_v = &abort_flag;
+
+  pdl_trigger();
+  pdl_wait();
+  // heaviest tiles first: blockIdx.y enumerates (query tile from the last, sequence)
+  const int qt = tiles_per_seq - 1 - (int)blockIdx.y / num_seqs;
+  const int seq = (int)blockIdx.y % num_seqs;
+  const int h = blockIdx.x, kvh = h / (nh / nkv);
+  const int q0 = cu_q[seq], q_len = cu_q[seq + 1] - q0;
+  if (qt * kBQ >= q_len) return;
+  const int k_len = min(seqlens_k[seq], bt_stride * bs);
+  const int shift = seqlens_k[seq] - q_len;                  // absolute position of query row 0
+  const int last_row = min(q_len, (qt + 1) * kBQ) - 1;
+  const int kend = max(0, min(k_len, shift + last_row + 1));
+  const int ntiles = (kend + kBKV - 1) / kBKV;
+  const int* bt = block_tables + (size_t)seq * bt_stride;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 4);
+      mbar_init(&p_full[b], 4);
+      mbar_init(&p_free[b], 1);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(L::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_o = tmem, tmem_s0 = tmem + HD;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && ntiles > 0) {
+      mbar_expect_tx(q_full, L::kQBytes);
+#pragma unroll
+      for (int hf = 0; hf < L::kHalves; ++hf)
+        tma_2d(smem + hf * L::kQHalf, &tm_q, q_full, h * HD + hf * 64, q0 + qt * kBQ);
+      int issued[kStages] = {};
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j % kStages, u = j / kStages;
+        if (u >= 1 && !wait_phase(&kv_empty[s], (u - 1) & 1, abort_v, status, kTimeoutSmemEmpty)) break;
+        uint8_t* stage = smem + L::kStageOff + s * L::kStageBytes;
+        const int k0 = j * kBKV;
+        uint64_t bad = 0;
+        const int segs = kBKV / box_keys;
+        int rows[kBKV / 8];
+        for (int g = 0; g < segs; ++g) {
+          const int kp = k0 + g * box_keys;
+          int blk = 0;
+          if (kp < kend) {
+            blk = bt[kp / bs];
+            if (blk < 0 || blk >= nblk) {
+              record_error(status, kBadIndex);
+              blk = 0;
+              bad |= (box_keys == 64 ? ~0ull : (((1ull << box_keys) - 1) << (g * box_keys)));
+            }
+          }
+          rows[g] = (blk * nkv + kvh) * bs + kp % bs;
+        }
+        bad_keys[s] = bad;       // published to the softmax warps by the v_full arrival below
+        mbar_expect_tx(&k_full[s], L::kTileBytes);
+        for (int g = 0; g < segs; ++g)
+#pragma unroll
+          for (int hf = 0; hf < L::kHalves; ++hf)
+            tma_2d(stage + hf * L::kKVHalf + g * box_keys * 128, &tm_k, &k_full[s], hf * 64, rows[g]);
+        mbar_expect_tx(&v_full[s], L::kTileBytes);
+        for (int g = 0; g < segs; ++g)
+#pragma unroll
+          for (int hf = 0; hf < L::kHalves; ++hf)
+            tma_2d(stage + L::kTileBytes + hf * L::kKVHalf + g * box_keys * 128, &tm_v, &v_full[s], hf * 64,
+                   rows[g]);
+        issued[s] = u + 1;
+      }
+      // drain: every stage's most recent copies have landed before this CTA may exit
+      mbar_wait(q_full, 0);
+      for (int s = 0; s < kStages; ++s) {
+        if (issued[s] > 0) {
+          mbar_wait(&k_full[s], (issued[s] - 1) & 1);
+          mbar_wait(&v_full[s], (issued[s] - 1) & 1);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && ntiles > 0) {
+      constexpr uint32_t id_s = idesc(kBKV, false);
+      constexpr uint32_t id_pv = idesc(HD, true);
+      const uint32_t q_addr = smem_u32(smem);
+      bool ok = wait_phase(q_full, 0, abort_v, status, kTimeoutTmaFull);
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % kStages, u = i / kStages, b = i & 1, ub = i >> 1;
+        if (!wait_phase(&p_full[b], ub & 1, abort_v, status, kTimeoutAccum)) return false;
+        if (!wait_phase(&v_full[s], u & 1, abort_v, status, kTimeoutTmaFull)) return false;
+        fence_after();
+        const uint32_t p_addr = smem_u32(smem + L::kPOff + b * L::kPBytes);
+        const uint32_t v_addr = smem_u32(smem + L::kStageOff + s * L::kStageBytes + L::kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBKV / 16; ++kk)
+          mma(tmem_o, desc_kmajor(p_addr + kk * 32), desc_mnmajor(v_addr + kk * 16 * 128, L::kKVHalf), id_pv,
+              (i | kk) != 0);
+        commit(&kv_empty[s]);
+        commit(&p_free[b]);
+        commit(o_done);
+        return true;
+      };
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int s = j % kStages, u = j / kStages, b = j & 1, ub = j >> 1;
+        if (!wait_phase(&k_full[s], u & 1, abort_v, status, kTimeoutTmaFull)) { ok = false; break; }
+        if (ub >= 1 && !wait_phase(&s_free[b], (ub - 1) & 1, abort_v, status, kTimeoutAccum)) { ok = false; break; }
+        fence_after();
+        const uint32_t k_addr = smem_u32(smem + L::kStageOff + s * L::kStageBytes);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const int hf = kk / 4, c = kk % 4;
+          mma(tmem_s0 + b * kBKV, desc_kmajor(q_addr + hf * L::kQHalf + c * 32),
+              desc_kmajor(k_addr + hf * L::kKVHalf + c * 32), id_s, kk != 0);
+        }
+        commit(&s_full[b]);
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok) issue_pv(ntiles - 1);
+      // every MMA this thread issued has completed before the CTA tears down
+      commit(drain);
+      mbar_wait(drain, 0);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax warps 0..3: query row r = 32 * warp + lane ----------------
+    const int r = warp * 32 + lane;
+    const int qrow = qt * kBQ + r;
+    const bool row_ok = qrow < q_len;
+    const int qpos = shift + qrow;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    // every wait is made warp-uniform (tcgen05.ld / st are warp-collective)
+#define LSB_WAIT_ALL(bar, par, code)                                                     \
+  if (!__all_sync(0xffffffffu, wait_phase(bar, par, abort_v, status, code))) { \
+    ok = false;                                                                          \
+    break;                                                                               \
+  }
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j % kStages, u = j / kStages, b = j & 1, ub = j >> 1;
+      LSB_WAIT_ALL(&s_full[b], ub & 1, kTimeoutAccum);
+      fence_after();
+      uint32_t raw[kBKV];
+#pragma unroll
+      for (int c = 0; c < kBKV; c += 16) tmem_ld16(tmem_s0 + b * kBKV + lane_base + c, raw + c);
+      tmem_wait_ld();
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
+      const int k0 = j * kBKV;
+      const bool tail = k0 + kBKV > kend;
+      // the stage's bad-block mask is published by the producer's arrival on v_full (V has long
+      // landed by now: it was issued right after K, which S needed)
+      LSB_WAIT_ALL(&v_full[s], u & 1, kTimeoutTmaFull);
+      const uint64_t bad = bad_keys[s];
+      float mx = -INFINITY;
+      float sv[kBKV];
+#pragma unroll
+      for (int c = 0; c < kBKV; ++c) {
+        const int kp = k0 + c;
+        const bool valid = row_ok && kp <= qpos && kp < kend && !((bad >> c) & 1ull);
+        sv[c] = valid ? __uint_as_float(raw[c]) * scale_log2 : -INFINITY;
+        mx = fmaxf(mx, sv[c]);
+      }
+      float alpha = 1.f;
+      if (mx > m_used + kRescaleLog2) {
+        alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
+        m_used = mx;
+        l *= alpha;
+      }
+      // P = exp2(s - m_used) as bf16 into the swizzled tile (row r: 128 bytes, chunk c at c ^ (r & 7))
+      if (ub >= 1) {
+        LSB_WAIT_ALL(&p_free[b], (ub - 1) & 1, kTimeoutAccum);
+      }
+      uint8_t* prow = smem + L::kPOff + b * L::kPBytes + r * 128;
+      float sum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < kBKV / 8; ++c8) {
+        float p[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x = sv[c8 * 8 + e];
+          p[e] = x == -INFINITY ? 0.f : exp2f(x - m_used);
+          sum += p[e];
+        }
+        uint4 w;
+        w.x = pack_bf16(p[0], p[1]);
+        w.y = pack_bf16(p[2], p[3]);
+        w.z = pack_bf16(p[4], p[5]);
+        w.w = pack_bf16(p[6], p[7]);
+        *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = w;
+      }
+      l += sum;
+      // zero the V rows of masked keys (past the context or from a bad block) in this stage
+      if (tail || bad != 0ull) {
+        uint8_t* vt = smem + L::kStageOff + s * L::kStageBytes + L::kTileBytes;
+        for (int idx = r; idx < kBKV * L::kHalves * 8; idx += 128) {
+          const int key = idx / (L::kHalves * 8), rem = idx % (L::kHalves * 8);
+          const int hf = rem / 8, ch = rem % 8;
+          if (k0 + key >= kend || ((bad >> key) & 1ull))
+            *reinterpret_cast<uint4*>(vt + hf * L::kKVHalf + key * 128 + ch * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_async_smem();
+      // rescale O in TMEM when some row of this warp moved its max (after the previous PV is done)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        LSB_WAIT_ALL(o_done, (j - 1) & 1, kTimeoutAccum);
+        fence_after();
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+          uint32_t o[16];
+          tmem_ld16(tmem_o + lane_base + c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st16(tmem_o + lane_base + c, o);
+        }
+        tmem_wait_st();
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+#undef LSB_WAIT_ALL
+    // epilogue: O / l -> bf16
+    if (ok && ntiles > 0 &&
+        __all_sync(0xffffffffu, wait_phase(o_done, (ntiles - 1) & 1, abort_v, status, kTimeoutAccum))) {
+      fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      bf16* orow = out + ((size_t)(q0 + (row_ok ? qrow : 0)) * nh + h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 16) {
+        uint32_t o[16];
+        tmem_ld16(tmem_o + lane_base + c, o);
+        tmem_wait_ld();
+        if (row_ok) {
+          uint4 w0, w1;
+          w0.x = pack_bf16(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv);
+          w0.y = pack_bf16(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv);
+          w0.z = pack_bf16(__uint_as_float(o[4]) * inv, __uint_as_float(o[5]) * inv);
+          w0.w = pack_bf16(__uint_as_float(o[6]) * inv, __uint_as_float(o[7]) * inv);
+          w1.x = pack_bf16(__uint_as_float(o[8]) * inv, __uint_as_float(o[9]) * inv);
+          w1.y = pack_bf16(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv);
+          w1.z = pack_bf16(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv);
+          w1.w = pack_bf16(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv);
+          *reinterpret_cast<uint4*>(orow + c) = w0;
+          *reinterpret_cast<uint4*>(orow + c + 8) = w1;
+        }
+      }
+    } else if (row_ok && ntiles == 0) {
+      bf16* orow = out + ((size_t)(q0 + qrow) * nh + h) * HD;
+      for (int c = 0; c < HD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::kTmemCols));
+  }
+}
+
+}  // namespace
+
+// Whether the tensor-core prefill kernel takes this shape (head dim and a TMA-tileable block size).
+bool prefill_tc_supported(int64_t block_size, int64_t head_dim) {
+  return (head_dim == 64 || head_dim == 128) && block_size % 8 == 0 && (block_size % 64 == 0 || 64 % block_size == 0);
+}
+
+// out / q: bf16 [T, nh, hd]; pools [blocks, kv_heads, block_size, hd]; cu_q int32 [B + 1];
+// seqlens_k int32 [B]; block_tables int32 [B, stride].
+void prefill_attention_tc(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,
+                          at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_q,
+                          at::Tensor status) {
+  LSB_CHECK(q.dim() == 3 && q.is_contiguous() && q.scalar_type() == at::kBFloat16, "q must be contiguous bf16 [T, nh, hd]");
+  LSB_CHECK(out.sizes() == q.sizes() && out.is_contiguous() && out.scalar_type() == at::kBFloat16, "bad output");
+  LSB_CHECK(kc.dim() == 4 && vc.sizes() == kc.sizes() && kc.is_contiguous() && vc.is_contiguous() &&
+                kc.scalar_type() == at::kBFloat16 && vc.scalar_type() == at::kBFloat16,
+            "KV pools must be contiguous bf16 [blocks, kv_heads, block_size, head_dim]");
+  LSB_CHECK(cu_q.scalar_type() == at::kInt && seqlens_k.scalar_type() == at::kInt &&
+                block_tables.scalar_type() == at::kInt && block_tables.is_contiguous(),
+            "cu_seqlens_q / seqlens_k / block_tables must be int32");
+  const int T = q.size(0), nh = q.size(1), hd = q.size(2), nkv = kc.size(1), bs = kc.size(2);
+  const int B = seqlens_k.numel();
+  LSB_CHECK(kc.size(3) == hd && nh % nkv == 0, "head layout mismatch");
+  LSB_CHECK(prefill_tc_supported(bs, hd), "block size / head dim unsupported by the tensor-core prefill kernel");
+  LSB_CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0, "q must be 16-byte aligned");
+  LSB_CHECK((int64_t)kc.numel() / hd < (int64_t)INT32_MAX && (int64_t)T * nh * hd < (int64_t)INT32_MAX,
+            "sizes exceed int32 tensor-map coordinates");
+  if (T == 0 || B == 0 || max_q <= 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  CUtensorMap tm_q;
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)nh * hd, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)nh * hd * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)kBQ};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = tensor_map_encoder()(&tm_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q.data_ptr(), dims, strides, box,
+                                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    LSB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed for q (" + std::to_string((int)r) + ")");
+  }
+  const int box_keys = bs >= 64 ? 64 : bs;
+  const CUtensorMap& tm_k = kv_pool_map(kc, box_keys);
+  const CUtensorMap& tm_v = kv_pool_map(vc, box_keys);
+  const int tiles = (int)((max_q + kBQ - 1) / kBQ);
+  LSB_CHECK((int64_t)tiles * B < 65536, "too many query tiles for one launch");
+  const float sl = (float)scale * kLog2e;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int* st = status_ptr(status);
+#define LSB_PF_TC(HD)                                                                                              \
+  do {                                                                                                             \
+    const int smem = PfLayout<HD>::kBytes;                                                                         \
+    ensure_dynamic_smem((const void*)prefill_tc_kernel<HD>, smem);                                               \
+    launch_pdl(prefill_tc_kernel<HD>, dim3(nh, tiles * B), dim3(kThreads), smem, stream, tm_q, tm_k, tm_v,        \
+               (bf16*)out.data_ptr(), cu_q.data_ptr<int>(), seqlens_k.data_ptr<int>(), block_tables.data_ptr<int>(), \
+               (int)block_tables.size(1), sl, nh, nkv, bs, box_keys, tiles, B, (int)kc.size(0), st);               \
+  } while (0)
+  if (hd == 128) LSB_PF_TC(128);
+  else LSB_PF_TC(64);
+#undef LSB_PF_TC
+  auto e = cudaGetLastError();
+  LSB_CHECK(e == cudaSuccess, std::string("prefill_tc launch failed: ") + cudaGetErrorString(e));
+}
+
+}  // namespace lsb

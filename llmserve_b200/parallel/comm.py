@@ -123,8 +123,16 @@ class FusedComm:
             planes = 1 if reduce else splits
             C().gemm_bf16_to_owners(x, data, n, packed, self.inbox_ptrs, self.rank, rows, splits, reduce, st,
                                     gemm.stages_for_tokens(T))
+        return self.finish(residual, norm_weight, eps, T, planes)
+
+    def finish(self, residual, norm_weight, eps, T: int, planes: int):
+        """The collective half alone: reduce this rank's rows from its inbox (``planes`` planes per
+        source rank), add the residual, RMSNorm, push the rows to every rank; outputs alias the
+        buffers."""
+        N = self.hidden
         C().row_parallel_finish(self.out_ptrs, self.res_ptrs, self.flag_ptrs, self.inbox_ptrs[self.rank],
-                                residual.contiguous(), norm_weight, self.rank, planes, T, N, rows, float(eps), st)
+                                residual.contiguous(), norm_weight, self.rank, planes, T, N,
+                                _rows_per_rank(T, self.world), float(eps), status(residual.device))
         return self.out_buf[: T * N].view(T, N), self.res_buf[: T * N].view(T, N)
 
     def argmax(self, values: torch.Tensor, indices: torch.Tensor, shard_offset: int, out: torch.Tensor):

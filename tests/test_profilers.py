@@ -77,3 +77,10 @@ def test_fused_collective_roofline_terms():
     assert r["weight_bytes"] == 4096 * 512 * 2 and r["nvlink_bytes"] == 7 * 8 * 4096 * 8
     assert abs(r["hbm_us"] - 4096 * 512 * 2 / 6553e3) < 1e-9
     assert r["roofline_us"] == max(r["hbm_us"], r["compute_us"], r["nvlink_us"])
+
+
+def test_attention_profile_counts_causal_work_only():
+    from benchmarks.attention_profile import causal_flops
+    # 3 query rows over 3 keys: 1 + 2 + 3 key visits; a 2-row chunk after a 4-key prefix: 5 + 6
+    assert causal_flops([(3, 3)], heads=2, head_dim=8) == 4 * 8 * 2 * 6
+    assert causal_flops([(2, 6)], heads=1, head_dim=128) == 4 * 128 * 11
