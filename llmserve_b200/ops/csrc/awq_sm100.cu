@@ -284,6 +284,7 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
       have = false;
     }
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t ep = pd.call_epoch();   // the collective's epoch of this call (0 off TP)
     if (BN >= 32 || half == 0) {
       const int feat = n0 + q * 32 + lane;
       const uint32_t row_addr = tmem + ((uint32_t)(q * 32) << 16);
@@ -304,14 +305,13 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
             if (tok < T) {
               const float v = __uint_as_float(rr[j]);
               if (pd.base[0] != nullptr)
-                *pd.at(blockIdx.z, tok, N, feat) = v;
+                pd.store(blockIdx.z, tok, N, feat, v, ep);
               else
                 out[(size_t)tok * N + feat] = to_b(v);
             }
           }
         }
       }
-      if (pd.owners > 1) __threadfence_system();   // peer-inbox stores visible before the kernel ends
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -408,9 +408,9 @@ void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztile
 }
 
 // Row-parallel W4A16 projection under tensor parallelism: partial planes of token row t go to the
-// inbox of the rank owning t (see PartDest), as plain stores from the epilogue.
+// inbox of the rank owning t (see PartDest) as epoch-tagged words stored by the epilogue.
 void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, std::vector<int64_t> inboxes,
-                        int64_t rank, int64_t rows_per_rank, int64_t splits, at::Tensor status) {
+                        int64_t rank, int64_t rows_per_rank, int64_t splits, int64_t epoch_ptr, at::Tensor status) {
   const int T = x.size(0), N = (int)n, W = (int)inboxes.size();
   check_awq_operands(x, qtiles, sztiles, N);
   TORCH_CHECK(W >= 1 && W <= kMaxOwners && rank >= 0 && rank < W, "llmserve_b200: one inbox per rank (<= 8)");
@@ -423,6 +423,8 @@ void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int
   pd.slot = (int)rank;
   pd.planes = (int)splits;
   pd.owners = W;
+  TORCH_CHECK(W == 1 || epoch_ptr != 0, "llmserve_b200: tensor-parallel inboxes need an epoch word");
+  pd.epoch = reinterpret_cast<const uint32_t*>(epoch_ptr);
   const at::cuda::CUDAGuard g(x.device());
   awq_dispatch(x, qtiles, sztiles, N, nullptr, pd, (int)splits, status_ptr(status));
 }

@@ -34,21 +34,21 @@ at::Tensor comm_ipc_handle(int64_t p);
 int64_t comm_open_handle(at::Tensor handle);
 void comm_close_handle(int64_t p);
 void comm_set_spin_limit(int64_t polls);
-void row_parallel_finish(std::vector<int64_t> out, std::vector<int64_t> res, std::vector<int64_t> flags,
-                         int64_t inbox, at::Tensor res_in, at::Tensor w, int64_t rank, int64_t S, int64_t T, int64_t N,
-                         int64_t rows_per_rank, double eps, at::Tensor status);
+void row_parallel_finish(std::vector<int64_t> ag, int64_t inbox, int64_t ctrl, int64_t out, int64_t res_out,
+                         at::Tensor res_in, at::Tensor w, int64_t rank, int64_t S, int64_t T, int64_t N,
+                         int64_t rows_per_rank, double eps, int64_t phases, at::Tensor status);
 void vocab_argmax_exchange(std::vector<int64_t> flags, at::Tensor vals, at::Tensor idx, int64_t vocab_start,
                            at::Tensor out, int64_t rank, at::Tensor status);
 int64_t comm_control_bytes();
 void gemm_bf16_to_owners(at::Tensor x, at::Tensor w, int64_t n, bool packed, std::vector<int64_t> inboxes,
-                         int64_t rank, int64_t rows_per_rank, int64_t splits, bool reduce, at::Tensor status,
-                         int64_t max_stages);
+                         int64_t rank, int64_t rows_per_rank, int64_t splits, bool reduce, int64_t epoch_ptr,
+                         at::Tensor status, int64_t max_stages);
 void gemm_bf16_reduced(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, bool packed, at::Tensor plane,
                        int64_t splits, at::Tensor status, int64_t max_stages);
 void gemm_bf16_silu_reduced(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, bool packed, int64_t splits,
                             at::Tensor status, int64_t max_stages);
 void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, std::vector<int64_t> inboxes,
-                        int64_t rank, int64_t rows_per_rank, int64_t splits, at::Tensor status);
+                        int64_t rank, int64_t rows_per_rank, int64_t splits, int64_t epoch_ptr, at::Tensor status);
 void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages);
 void splitk_silu(at::Tensor out, at::Tensor partials);
 void silu_and_mul_interleaved(at::Tensor out, at::Tensor x);

@@ -1,37 +1,36 @@
 // In-kernel tensor-parallel collectives over NVLink peer memory.
 //
 // Symmetric buffer of one rank (allocated per rank, mapped by every peer through CUDA IPC):
-//   [0, kCtrlBytes)   control: flag words (uint32) and the argmax exchange slots
-//   out   bf16 [max_tokens, N]            normalised rows of the last row-parallel layer
-//   res   bf16 [max_tokens, N]            residual rows of the last row-parallel layer
-//   inbox fp32 [W][S][rows][N]            split-K partial planes pushed by every rank's GEMM
-// Flag words: [0, W) phase-1 arrivals, [W, 2W) phase-2 arrivals, [2W] collective epoch,
-// [2W+1] CTA counter, [64, 64 + W) argmax arrivals, [64 + W] argmax epoch.
+//   [0, kCtrlBytes)   control: epoch / CTA-counter words, argmax flag words and exchange slots
+//   out   bf16 [max_tokens, N]   normalised rows of the last row-parallel layer (written locally)
+//   res   bf16 [max_tokens, N]   residual rows of the last row-parallel layer (written locally)
+//   ag    u64  [max_tokens, N]   all-gather inbox: (out, res) bf16 pairs of rows owned by peers
+//   inbox u64  [W][S][rows][N]   reduce inbox: fp32 split-K partials of this rank's rows, from every rank
+// Control words: [0] collective epoch, [1] CTA counter, [64, 64 + W) argmax arrivals, [64 + W]
+// argmax epoch.
 //
-// A row-parallel projection (o_proj / down_proj) finishes in two kernels:
-//   GEMM  (gemm_sm100.cu / awq_sm100.cu, PartDest with one inbox per rank): the epilogue stores
-//         the fp32 partial planes of token row t straight into the inbox of the rank owning t
-//         (rows are dealt to ranks in blocks of `rows_per_rank`), plain st.global over NVLink;
-//   finish (row_parallel_finish_kernel below):
-//     1. signal: the GEMM before this kernel has completed, so this rank's pushes have landed ->
-//        store `epoch` into flags[phase 1][my rank] of every peer (release, system scope);
-//     2. wait (bounded) until every rank's phase-1 flag reached `epoch`;
-//     3. reduce this rank's rows from its OWN inbox (every source rank x split plane: local
-//        reads), round to bf16 (as a bf16 GEMM output would be), add the residual and apply
-//        RMSNorm -- a row is spread over a cluster of CTAs whose sums of squares meet in
-//        distributed shared memory;
-//     4. all-gather by push: each finished row (normalised output and new residual) is stored into
-//        every rank's out / res buffers;
-//     5. the last CTA of the rank signals phase 2 to every peer and waits (bounded) for all of
-//        them, so when the kernel ends every rank holds all rows.
-// Nothing crosses NVLink as a load: the reduce-scatter half travels as the GEMM's stores, the
-// all-gather half as this kernel's stores, and each rank only ever polls its own flag words.
-// `epoch` lives in device memory and is advanced by the kernel itself, so the launch can be
-// captured in a CUDA graph.  Every wait gives up after a bounded number of polls (kSpinLimit unless
-// lowered for a test), records kTimeoutPeerFlag in the status word and lets the kernel finish.
+// Every inbox entry is a low-latency word (common.cuh): 4 bytes of payload and the epoch of the call
+// that wrote it, stored as one 64-bit store.  A row-parallel projection (o_proj / down_proj) of
+// call e finishes in two kernels and crosses NVLink only as stores:
+//   GEMM  (gemm_sm100.cu / awq_sm100.cu, PartDest with one inbox per rank): the epilogue stores the
+//         fp32 partials of token row t, tagged e, into the inbox of the rank owning t (rows are dealt
+//         to ranks in blocks of `rows_per_rank`);
+//   finish (row_parallel_finish_kernel below), one CTA cluster per token row:
+//     * a row this rank owns: poll the W x S inbox words of each column until they carry epoch e,
+//       sum them, round to bf16 (as a bf16 GEMM output would be), add the residual, RMSNorm (the
+//       row's sum of squares meets in distributed shared memory), write out / res locally and store
+//       (out, res) words tagged e into every peer's all-gather inbox;
+//     * a row a peer owns: poll this rank's all-gather inbox for the row's words tagged e and unpack
+//       them into out / res.
+// No fence, no flag and no barrier round: a word with the expected epoch carries its data.  The
+// epoch lives in device memory; the last CTA of the finish kernel advances it, so the launches can
+// be captured in a CUDA graph.  Every poll gives up after a bounded number of attempts (kSpinLimit
+// unless lowered for a test), records kTimeoutPeerFlag in the status word and lets the kernel finish.
 //
-// One inbox suffices: a rank writes a peer's inbox for call k+1 only after it passed phase 2 of
-// call k, i.e. after that peer had reduced (and pushed) everything of call k.
+// Single inboxes suffice: rank A stores call e+1 partials into B's reduce inbox only after A's finish
+// kernel of call e received B's rows, which B pushed after reading its whole inbox of call e; and B
+// pushes call e+1 rows into A's all-gather inbox only after reading A's call e+1 partials, which A's
+// GEMM e+1 wrote after A's finish e had unpacked everything of call e.
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -54,9 +53,10 @@ constexpr int kArgSlotsOff = 1024;        // byte offset of the argmax slots in 
 constexpr int kArgMaxRows = 512;          // rows per argmax exchange
 
 struct PeerPtrs {
-  bf16* out[kMaxRanks];
-  bf16* res[kMaxRanks];
-  uint32_t* flags[kMaxRanks];     // control block of every rank
+  uint32_t* flags[kMaxRanks];     // control block of every rank (argmax exchange)
+};
+struct PeerAg {
+  uint64_t* ag[kMaxRanks];        // all-gather inbox of every rank (this rank's mappings)
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -68,12 +68,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-__device__ __forceinline__ void st_v2(bf16* p, uint2 v) {
-  asm volatile("st.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
-}
-
-// Polls before a peer-flag wait gives up (kSpinLimit unless lowered by comm_set_spin_limit, which
-// the failure-detection test uses to make a wait on a flag nothing sets end in milliseconds).
+// Polls before a wait gives up (kSpinLimit unless lowered by comm_set_spin_limit, which the
+// failure-detection test uses to make a wait on a peer that never writes end in milliseconds).
 __device__ uint32_t g_flag_spin_limit = kSpinLimit;
 
 __device__ bool wait_flags(const uint32_t* flags, int W, uint32_t epoch, int* status) {
@@ -90,132 +86,157 @@ __device__ bool wait_flags(const uint32_t* flags, int W, uint32_t epoch, int* st
   return true;
 }
 
+// The four words p[0..3] once all carry `epoch` (bounded; `live` turns false after a timeout, so
+// one missing peer costs one spin limit per thread, not one per word).
+__device__ __forceinline__ void ll_wait4(const uint64_t* p, uint32_t epoch, uint32_t limit, bool& live, int* status,
+                                         uint64_t* w) {
+  uint32_t i = 0;
+  while (true) {
+    ll_load2(p, w[0], w[1]);
+    ll_load2(p + 2, w[2], w[3]);
+    if ((uint32_t)(w[0] >> 32) == epoch && (uint32_t)(w[1] >> 32) == epoch && (uint32_t)(w[2] >> 32) == epoch &&
+        (uint32_t)(w[3] >> 32) == epoch)
+      return;
+    if (!live || ++i > limit) {
+      if (live) record_error(status, kTimeoutPeerFlag);
+      live = false;
+      return;
+    }
+  }
+}
+
+constexpr int kEpochWord = 0, kCounterWord = 1;
+constexpr int kMaxPer = 4;       // 4-column chunks per thread: N / kCluster <= kMaxPer * 4 * kThreads
+
+// grid (kCluster, T): the kCluster CTAs of cluster y handle token row y, N / kCluster columns each.
+// phases: 1 = rows this rank owns (reduce, norm, push), 2 = rows peers own (receive); the engine
+// runs both in one launch (3); a single-GPU test runs every emulated rank's phase 1 before any
+// phase 2, so no launch waits on a later one.
 __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
-    row_parallel_finish_kernel(PeerPtrs peers, const float* __restrict__ inbox, const bf16* __restrict__ res_in,
+    row_parallel_finish_kernel(const PeerAg peers, const uint64_t* __restrict__ inbox, uint32_t* __restrict__ ctrl,
+                               bf16* __restrict__ out, bf16* __restrict__ res_out, const bf16* __restrict__ res_in,
                                const bf16* __restrict__ w, int rank, int W, int S, int T, int N, float eps,
-                               int rows_per_rank, int* status) {
+                               int rows_per_rank, int phases, int* status) {
   pdl_trigger();
   pdl_wait();
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float red[kThreads / 32];
   __shared__ float cta_ss;
   __shared__ uint32_t s_epoch;
-  __shared__ int s_last;
-  uint32_t* my_flags = peers.flags[rank];
-  if (threadIdx.x == 0) s_epoch = *((volatile uint32_t*)(my_flags + 2 * W)) + 1u;
+  if (threadIdx.x == 0) s_epoch = ld_volatile_u32(ctrl + kEpochWord) + 1u;
   __syncthreads();
   const uint32_t epoch = s_epoch;
+  const uint32_t limit = *((volatile uint32_t*)&g_flag_spin_limit);
+  const int t = blockIdx.y;
+  const int owner = t / rows_per_rank, r = t - owner * rows_per_rank;
   const int crank = (int)cluster.block_rank();
-  const int row_slot = blockIdx.y;
-  const bool first_cta = blockIdx.x == 0 && blockIdx.y == 0;
-
-  // 1. phase-1 signal: our GEMM (the previous kernel) has completed, its inbox stores are done
-  if (first_cta && threadIdx.x < W) {
-    __threadfence_system();
-    st_release_sys(peers.flags[threadIdx.x] + rank, epoch);
-  }
-  // 2. wait for every rank's partials to have landed in our inbox
-  if (threadIdx.x == 0) wait_flags(my_flags, W, epoch, status);
-  __syncthreads();
-
-  // 3. local reduce + residual + RMSNorm for row `row` of this rank
-  const int row = rank * rows_per_rank + row_slot;
-  const bool have_row = row_slot < rows_per_rank && row < T;
   const int cols = N / kCluster;                // columns of this CTA (multiple of 4)
   const int c0 = crank * cols;
-  const size_t plane = (size_t)rows_per_rank * N;
-  float ss = 0.f;
-  constexpr int kMaxPer = 4;                    // float4 chunks per thread (N <= 8192 * 2)
-  float4 val[kMaxPer];
+  bool live = true;
+
+  if (owner == rank && (phases & 1)) {
+    // reduce this rank's row t from its inbox, add the residual, RMSNorm, push (out, res) to peers
+    const size_t plane = (size_t)rows_per_rank * N;
+    float ss = 0.f;
+    float4 val[kMaxPer];
 #pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) {
-    const int col = c0 + (threadIdx.x + k * kThreads) * 4;
-    val[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (!have_row || col >= c0 + cols) continue;
-    const float* src = inbox + (size_t)row_slot * N + col;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int planes = W * S;
-    int p = 0;
-    // four independent loads in flight per step (the planes are local: HBM / L2 latency)
-    for (; p + 4 <= planes; p += 4) {
-      float4 q[4];
+    for (int k = 0; k < kMaxPer; ++k) {
+      const int col = c0 + (threadIdx.x + k * kThreads) * 4;
+      val[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (col >= c0 + cols) continue;
+      const uint64_t* src = inbox + (size_t)r * N + col;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < W * S; ++p) {
+        uint64_t wv[4];
+        ll_wait4(src + (size_t)p * plane, epoch, limit, live, status, wv);
+        acc.x += __uint_as_float((uint32_t)wv[0]);
+        acc.y += __uint_as_float((uint32_t)wv[1]);
+        acc.z += __uint_as_float((uint32_t)wv[2]);
+        acc.w += __uint_as_float((uint32_t)wv[3]);
+      }
+      const size_t off = (size_t)t * N + col;
+      const uint2 rr = *reinterpret_cast<const uint2*>(res_in + off);
+      const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
+      const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
+      val[k].x = to_f(to_b(acc.x)) + __low2float(r01);
+      val[k].y = to_f(to_b(acc.y)) + __high2float(r01);
+      val[k].z = to_f(to_b(acc.z)) + __low2float(r23);
+      val[k].w = to_f(to_b(acc.w)) + __high2float(r23);
+      ss += val[k].x * val[k].x + val[k].y * val[k].y + val[k].z * val[k].z + val[k].w * val[k].w;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float a = 0.f;
+      for (int i = 0; i < kThreads / 32; ++i) a += red[i];
+      cta_ss = a;
+    }
+    cluster.sync();
+    float total = 0.f;
+    for (int c = 0; c < kCluster; ++c) total += *cluster.map_shared_rank(&cta_ss, c);
+    cluster.sync();   // peers' shared memory must stay valid until everyone has read it
+    const float inv = rsqrtf(total / N + eps);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) q[u] = __ldcg(reinterpret_cast<const float4*>(src + (size_t)(p + u) * plane));
+    for (int k = 0; k < kMaxPer; ++k) {
+      const int col = c0 + (threadIdx.x + k * kThreads) * 4;
+      if (col >= c0 + cols) continue;
+      const size_t off = (size_t)t * N + col;
+      const uint2 wr = *reinterpret_cast<const uint2*>(w + col);
+      const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wr.x);
+      const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wr.y);
+      const float v[4] = {val[k].x, val[k].y, val[k].z, val[k].w};
+      const float wv[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
+      bf16 ob[4], sb[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        acc.x += q[u].x; acc.y += q[u].y; acc.z += q[u].z; acc.w += q[u].w;
+      for (int j = 0; j < 4; ++j) {
+        ob[j] = to_b(to_f(to_b(v[j] * inv)) * wv[j]);
+        sb[j] = to_b(v[j]);
+      }
+      *reinterpret_cast<uint2*>(out + off) = *reinterpret_cast<const uint2*>(ob);
+      *reinterpret_cast<uint2*>(res_out + off) = *reinterpret_cast<const uint2*>(sb);
+      uint64_t word[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t pair = (uint32_t)__bfloat16_as_ushort(ob[j]) | ((uint32_t)__bfloat16_as_ushort(sb[j]) << 16);
+        word[j] = ll_word(pair, epoch);
+      }
+      for (int q = 0; q < W; ++q) {
+        if (q == rank) continue;
+        uint64_t* dst = peers.ag[q] + off;
+        ll_store2(dst, word[0], word[1]);
+        ll_store2(dst + 2, word[2], word[3]);
       }
     }
-    for (; p < planes; ++p) {
-      const float4 q = __ldcg(reinterpret_cast<const float4*>(src + (size_t)p * plane));
-      acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
-    }
-    const size_t off = (size_t)row * N + col;
-    const uint2 rr = *reinterpret_cast<const uint2*>(res_in + off);
-    const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
-    const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
-    val[k].x = to_f(to_b(acc.x)) + __low2float(r01);
-    val[k].y = to_f(to_b(acc.y)) + __high2float(r01);
-    val[k].z = to_f(to_b(acc.z)) + __low2float(r23);
-    val[k].w = to_f(to_b(acc.w)) + __high2float(r23);
-    ss += val[k].x * val[k].x + val[k].y * val[k].y + val[k].z * val[k].z + val[k].w * val[k].w;
-  }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int i = 0; i < kThreads / 32; ++i) t += red[i];
-    cta_ss = t;
-  }
-  cluster.sync();
-  float total = 0.f;
-  for (int c = 0; c < kCluster; ++c) total += *cluster.map_shared_rank(&cta_ss, c);
-  cluster.sync();   // peers' shared memory must stay valid until everyone has read it
-  const float inv = rsqrtf(total / N + eps);
-
-  // 4. all-gather by push
+  } else if (owner != rank && (phases & 2)) {
+    // receive row t from its owner
 #pragma unroll
-  for (int k = 0; k < kMaxPer; ++k) {
-    const int col = c0 + (threadIdx.x + k * kThreads) * 4;
-    if (!have_row || col >= c0 + cols) continue;
-    const size_t off = (size_t)row * N + col;
-    const uint2 wr = *reinterpret_cast<const uint2*>(w + col);
-    const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wr.x);
-    const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wr.y);
-    const float v[4] = {val[k].x, val[k].y, val[k].z, val[k].w};
-    const float wv[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
-    float o[4];
+    for (int k = 0; k < kMaxPer; ++k) {
+      const int col = c0 + (threadIdx.x + k * kThreads) * 4;
+      if (col >= c0 + cols) continue;
+      const size_t off = (size_t)t * N + col;
+      uint64_t wv[4];
+      ll_wait4(peers.ag[rank] + off, epoch, limit, live, status, wv);
+      uint16_t ob[4], sb[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = to_f(to_b(to_f(to_b(v[j] * inv)) * wv[j]));
-    __nv_bfloat162 o01 = __floats2bfloat162_rn(o[0], o[1]), o23 = __floats2bfloat162_rn(o[2], o[3]);
-    __nv_bfloat162 s01 = __floats2bfloat162_rn(v[0], v[1]), s23 = __floats2bfloat162_rn(v[2], v[3]);
-    uint2 ov, sv;
-    ov.x = *reinterpret_cast<uint32_t*>(&o01);
-    ov.y = *reinterpret_cast<uint32_t*>(&o23);
-    sv.x = *reinterpret_cast<uint32_t*>(&s01);
-    sv.y = *reinterpret_cast<uint32_t*>(&s23);
-    for (int r = 0; r < W; ++r) {
-      st_v2(peers.out[r] + off, ov);
-      st_v2(peers.res[r] + off, sv);
+      for (int j = 0; j < 4; ++j) {
+        ob[j] = (uint16_t)(wv[j] & 0xffffu);
+        sb[j] = (uint16_t)((wv[j] >> 16) & 0xffffu);
+      }
+      *reinterpret_cast<uint2*>(out + off) = *reinterpret_cast<const uint2*>(ob);
+      *reinterpret_cast<uint2*>(res_out + off) = *reinterpret_cast<const uint2*>(sb);
     }
   }
-  // 5. last CTA of this rank: phase-2 signal, then wait for all ranks' rows
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int total_ctas = gridDim.x * gridDim.y;
-    const uint32_t prev = atomicAdd(my_flags + 2 * W + 1, 1u);
-    s_last = prev == (uint32_t)(total_ctas - 1);
-  }
-  __syncthreads();
-  if (s_last && threadIdx.x == 0) {
-    my_flags[2 * W + 1] = 0u;
-    __threadfence_system();
-    for (int r = 0; r < W; ++r) st_release_sys(peers.flags[r] + W + rank, epoch);
-    wait_flags(my_flags + W, W, epoch, status);
-    *((volatile uint32_t*)(my_flags + 2 * W)) = epoch;
-    __threadfence();
+  // the launch that completes the call advances the epoch once every CTA has read it
+  if (phases & 2) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t total_ctas = gridDim.x * gridDim.y;
+      if (atomicAdd(ctrl + kCounterWord, 1u) == total_ctas - 1) {
+        ctrl[kCounterWord] = 0u;
+        *((volatile uint32_t*)(ctrl + kEpochWord)) = epoch;
+      }
+    }
   }
 }
 
@@ -312,28 +333,27 @@ void comm_set_spin_limit(int64_t polls) {
   LSB_CHECK(e == cudaSuccess, std::string("setting the spin limit failed: ") + cudaGetErrorString(e));
 }
 
-// out/res/flags: W base addresses each (this rank's mapping of every rank's buffers); inbox: this
-// rank's inbox [W][S][rows_per_rank][N] (local).
-void row_parallel_finish(std::vector<int64_t> out, std::vector<int64_t> res, std::vector<int64_t> flags,
-                         int64_t inbox, at::Tensor res_in, at::Tensor w, int64_t rank, int64_t S, int64_t T, int64_t N,
-                         int64_t rows_per_rank, double eps, at::Tensor status) {
-  const int W = out.size();
-  LSB_CHECK(W >= 1 && W <= kMaxRanks && res.size() == (size_t)W && flags.size() == (size_t)W,
-            "peer pointer lists must have one entry per rank (<= 8)");
-  LSB_CHECK(N % (kCluster * 4) == 0 && N / kCluster <= 4 * 4 * kThreads, "hidden size unsupported by the fused path");
+// ag: every rank's all-gather inbox (this rank's mappings); inbox: this rank's reduce inbox
+// [W][S][rows_per_rank][N] (local); ctrl: this rank's control block; out / res_out: this rank's local
+// [T, N] outputs.  phases: 3 in the engine (see the kernel).
+void row_parallel_finish(std::vector<int64_t> ag, int64_t inbox, int64_t ctrl, int64_t out, int64_t res_out,
+                         at::Tensor res_in, at::Tensor w, int64_t rank, int64_t S, int64_t T, int64_t N,
+                         int64_t rows_per_rank, double eps, int64_t phases, at::Tensor status) {
+  const int W = ag.size();
+  LSB_CHECK(W >= 1 && W <= kMaxRanks && rank >= 0 && rank < W, "one all-gather inbox per rank (<= 8)");
+  LSB_CHECK(N % (kCluster * 4) == 0 && N / kCluster <= kMaxPer * 4 * kThreads, "hidden size unsupported by the fused path");
   LSB_CHECK(res_in.scalar_type() == at::kBFloat16 && res_in.is_contiguous() && res_in.numel() >= T * N, "bad residual");
-  LSB_CHECK(rows_per_rank >= 1 && rows_per_rank * W >= T && S >= 1, "bad row layout");
-  PeerPtrs p = {};
-  for (int r = 0; r < W; ++r) {
-    p.out[r] = reinterpret_cast<bf16*>(out[r]);
-    p.res[r] = reinterpret_cast<bf16*>(res[r]);
-    p.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
-  }
-  dim3 grid(kCluster, (unsigned)rows_per_rank);
+  LSB_CHECK(w.scalar_type() == at::kBFloat16 && w.numel() == N, "bad norm weight");
+  LSB_CHECK(rows_per_rank >= 1 && rows_per_rank * W >= T && S >= 1 && phases >= 1 && phases <= 3, "bad row layout");
+  if (T == 0) return;
+  PeerAg p = {};
+  for (int r = 0; r < W; ++r) p.ag[r] = reinterpret_cast<uint64_t*>(ag[r]);
+  dim3 grid(kCluster, (unsigned)T);
   const at::cuda::CUDAGuard g(res_in.device());
   launch_pdl(row_parallel_finish_kernel, grid, dim3(kThreads), 0, at::cuda::getCurrentCUDAStream(), p,
-             reinterpret_cast<const float*>(inbox), (const bf16*)res_in.data_ptr(), (const bf16*)w.data_ptr(),
-             (int)rank, W, (int)S, (int)T, (int)N, (float)eps, (int)rows_per_rank, status_ptr(status));
+             reinterpret_cast<const uint64_t*>(inbox), reinterpret_cast<uint32_t*>(ctrl), reinterpret_cast<bf16*>(out),
+             reinterpret_cast<bf16*>(res_out), (const bf16*)res_in.data_ptr(), (const bf16*)w.data_ptr(), (int)rank,
+             W, (int)S, (int)T, (int)N, (float)eps, (int)rows_per_rank, (int)phases, status_ptr(status));
   auto e = cudaGetLastError();
   LSB_CHECK(e == cudaSuccess, std::string("fused row-parallel finish launch failed: ") + cudaGetErrorString(e));
 }

@@ -25,12 +25,37 @@ enum ErrorCode : int {
 // legitimate wait, and still ends a wait on a flag that is never set.
 constexpr uint32_t kSpinLimit = 1u << 26;
 
+// ---- low-latency words for the tensor-parallel collective ------------------------------------------
+// A 64-bit word whose low half is 4 bytes of payload and whose high half is the epoch (call number)
+// of the collective that wrote it.  An aligned 64-bit store is single-copy atomic, so a reader that
+// sees the expected epoch also sees that call's payload: peers poll the data itself, with no fence
+// and no separate flag.
+__device__ __forceinline__ uint64_t ll_word(uint32_t payload, uint32_t epoch) {
+  return ((uint64_t)epoch << 32) | payload;
+}
+__device__ __forceinline__ void ll_store2(uint64_t* p, uint64_t a, uint64_t b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ void ll_store1(uint64_t* p, uint64_t a) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+}
+__device__ __forceinline__ void ll_load2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Where a GEMM writes its fp32 split-K partial planes.  Off tensor parallelism there is one owner
-// (the local [planes, T, N] buffer).  Under tensor parallelism the token rows are dealt to the
-// ranks in blocks of `rows` (rank o owns rows [o*rows, (o+1)*rows)) and base[o] is rank o's inbox
-// (a peer pointer for o != this rank): [source rank][plane][row][N], this rank writing the
-// source-rank slot `slot`.  The owner then reduces every source's planes from its own memory, so
-// the row-parallel reduction crosses NVLink as stores made by the GEMM epilogue, never as loads.
+// (the local [planes, T, N] fp32 buffer).  Under tensor parallelism the token rows are dealt to
+// the ranks in blocks of `rows` (rank o owns rows [o*rows, (o+1)*rows)) and base[o] is rank o's
+// inbox (a peer pointer for o != this rank) of 64-bit low-latency words
+// [source rank][plane][row][N], this rank writing the source-rank slot `slot`, each word carrying
+// the value and the call's epoch (the word at `epoch` plus one).  The owner polls its own memory
+// for the words of the current epoch and reduces them, so the row-parallel reduction crosses NVLink
+// as stores made by the GEMM epilogue, never as loads, and needs no fence or flag.
 constexpr int kMaxOwners = 8;
 struct PartDest {
   float* base[kMaxOwners];
@@ -38,14 +63,35 @@ struct PartDest {
   int slot;      // this rank's source slot in every owner's inbox (0 with one owner)
   int planes;    // split-K planes per source (the GEMM's gridDim.z)
   int owners;    // 1, or the tensor-parallel size
-  __device__ __forceinline__ float* at(int z, int t, int N, int feat) const {
-    if (owners == 1) return base[0] + ((size_t)z * rows + t) * N + feat;   // local planes: no division
+  const uint32_t* epoch;   // owners > 1: this rank's epoch word of the collective
+  __device__ __forceinline__ uint32_t call_epoch() const { return owners > 1 ? ld_volatile_u32(epoch) + 1u : 0u; }
+  __device__ __forceinline__ float* at(int z, int t, int N, int feat) const {   // owners == 1 only
+    return base[0] + ((size_t)z * rows + t) * N + feat;
+  }
+  __device__ __forceinline__ uint64_t* ll_at(int z, int t, int N, int feat) const {
     const int o = t / rows, r = t - o * rows;
     float* b = base[0];
 #pragma unroll
     for (int i = 1; i < kMaxOwners; ++i)   // select without indexing the parameter array dynamically
       if (i == o) b = base[i];
-    return b + ((size_t)(slot * planes + z) * rows + r) * N + feat;
+    return reinterpret_cast<uint64_t*>(b) + ((size_t)(slot * planes + z) * rows + r) * N + feat;
+  }
+  // one value of plane z, token row t, feature feat
+  __device__ __forceinline__ void store(int z, int t, int N, int feat, float v, uint32_t e) const {
+    if (owners == 1) *at(z, t, N, feat) = v;
+    else ll_store1(ll_at(z, t, N, feat), ll_word(__float_as_uint(v), e));
+  }
+  // four consecutive features feat..feat+3 (feat % 4 == 0, N % 4 == 0)
+  __device__ __forceinline__ void store4(int z, int t, int N, int feat, const float* v, uint32_t e) const {
+    if (owners == 1) {
+      float* p = at(z, t, N, feat);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) p[q] = v[q];
+    } else {
+      uint64_t* p = ll_at(z, t, N, feat);
+      ll_store2(p, ll_word(__float_as_uint(v[0]), e), ll_word(__float_as_uint(v[1]), e));
+      ll_store2(p + 2, ll_word(__float_as_uint(v[2]), e), ll_word(__float_as_uint(v[3]), e));
+    }
   }
 };
 
@@ -56,6 +102,7 @@ inline PartDest local_part_dest(float* partials, int T, int planes) {
   d.slot = 0;
   d.planes = planes;
   d.owners = 1;
+  d.epoch = nullptr;
   return d;
 }
 

@@ -254,6 +254,9 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
     }
   }
   tc_fence_after();
+  // the collective's epoch of this call (0 off tensor parallelism); every thread waited for the
+  // predecessor above, so the word is the previous call's final value
+  const uint32_t ep = pd.call_epoch();
   const int feat = n0 + warp * 32 + lane;
   const uint32_t row_addr = tmem + ((uint32_t)(warp * 32) << 16);
   if (cluster_red > 0) {
@@ -297,11 +300,15 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
       const float va[4] = {a.x, a.y, a.z, a.w};
       if constexpr (EPI == 0) {
         const int f0 = n0 + g * 4;
+        if (pd.base[0] != nullptr && (pd.owners > 1 || f0 + 3 < N)) {
+          pd.store4(0, t, N, f0, va, ep);          // N % 4 == 0 under tensor parallelism
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if (f0 + q >= N) break;
-          if (pd.base[0] != nullptr) *pd.at(0, t, N, f0 + q) = va[q];
-          else out[(size_t)t * N + f0 + q] = to_b(va[q]);
+          for (int q = 0; q < 4; ++q) {
+            if (f0 + q >= N) break;
+            if (pd.base[0] != nullptr) *pd.at(0, t, N, f0 + q) = va[q];
+            else out[(size_t)t * N + f0 + q] = to_b(va[q]);
+          }
         }
       } else {
         const float vb[4] = {b.x, b.y, b.z, b.w};
@@ -314,7 +321,6 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
         }
       }
     }
-    if (pd.owners > 1) __threadfence_system();   // peer-inbox stores visible before the kernel ends
     cluster.sync();   // keep this CTA's tile alive until every peer CTA has read it
   } else if constexpr (EPI == 0) {
 #pragma unroll 1
@@ -333,16 +339,13 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
           if (t < T) {
             const float v = __uint_as_float(r[j]);
             if (pd.base[0] != nullptr)
-              *pd.at(blockIdx.z, t, N, feat) = v;
+              pd.store(blockIdx.z, t, N, feat, v, ep);
             else
               out[(size_t)t * N + feat] = to_b(v);
           }
         }
       }
     }
-    // stores into peers' inboxes: make them visible system-wide before the kernel ends (the
-    // finishing kernel then publishes them with a release flag)
-    if (pd.owners > 1) __threadfence_system();
   } else {
     // warps 2-3 hold the up rows: hand them to warps 0-1 (same row offset) through shared memory
     float* xch = reinterpret_cast<float*>(smem);            // stage buffers are free now
@@ -688,8 +691,8 @@ static void gemm_dispatch(at::Tensor out, at::Tensor x, at::Tensor w, int64_t N,
 // plain stores from the epilogue (no TMA touches peer memory).  w: row-major [n, K], or (packed)
 // the tile image of a weight with n logical rows.
 void gemm_bf16_to_owners(at::Tensor x, at::Tensor w, int64_t n, bool packed, std::vector<int64_t> inboxes,
-                         int64_t rank, int64_t rows_per_rank, int64_t splits, bool reduce, at::Tensor status,
-                         int64_t max_stages) {
+                         int64_t rank, int64_t rows_per_rank, int64_t splits, bool reduce, int64_t epoch_ptr,
+                         at::Tensor status, int64_t max_stages) {
   LSB_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
             "gemm operands must be bf16 CUDA tensors");
   LSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && (x.stride(0) * 2) % 16 == 0 &&
@@ -713,6 +716,8 @@ void gemm_bf16_to_owners(at::Tensor x, at::Tensor w, int64_t n, bool packed, std
   pd.slot = (int)rank;
   pd.planes = reduce ? 1 : (int)splits;   // a cluster-reduced projection sends one plane per rank
   pd.owners = W;
+  LSB_CHECK(W == 1 || (n % 4 == 0 && epoch_ptr != 0), "tensor-parallel inboxes need N % 4 == 0 and an epoch word");
+  pd.epoch = reinterpret_cast<const uint32_t*>(epoch_ptr);
   const at::cuda::CUDAGuard g(x.device());
   tile_dispatch(x, w, (int)n, packed, nullptr, pd, (int)splits, status_ptr(status), max_stages, reduce);
 }

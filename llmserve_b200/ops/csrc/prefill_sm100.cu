@@ -2,24 +2,30 @@
 // tcgen05.mma with fp32 accumulators in TMEM, Q / K / V tiles arrive by TMA straight from the
 // packed query rows and the paged pool [blocks, kv_heads, block_size, head_dim].
 //
-// One CTA computes 128 query rows of one head (UMMA M = 128) against 64-key tiles:
-//   warp 4, lane 0 : TMA producer.  Q once (two 64-column halves, 128B swizzle), then K and V of
-//                    each 64-key tile into a 3-stage ring; a tile is assembled from per-block boxes
-//                    of min(block_size, 64) keys, so pages need not be contiguous.
-//   warp 5, lane 0 : MMA issuer.  S_j = Q K_j^T into one of two TMEM S buffers (both operands
-//                    K-major), then O += P_{j-1} V_{j-1} (P K-major from shared memory, V read
-//                    MN-major straight from its TMA tile) -- so the tensor pipe computes PV of the
-//                    previous tile and S of the next while the softmax warps work on this one.
-//   warps 0..3     : softmax.  Thread r owns query row r (TMEM lane r): tcgen05.ld of its 64
-//                    scores, causal / length mask, online softmax in the log2 domain, P as bf16
-//                    into a swizzled shared-memory tile.  The running max is only moved when it
-//                    grows by more than 2^8 (P stays <= 256, exact in fp32 sums), so the rescale of
-//                    O in TMEM (tcgen05.ld / st, after the previous PV finished) is rare.  At the
-//                    end the same threads read O from TMEM, divide by the row sum and store bf16.
-// Keys past the context (or from a block id outside the pool, recorded as kBadIndex) get P = 0
-// and their V rows are zeroed in shared memory, so whatever the pool holds there never reaches O.
-// Every wait is bounded; a timeout records an error code, raises a CTA-wide abort flag that every
-// role polls, drains the copies and MMAs in flight and frees TMEM.
+// One CTA computes two 128-row query tiles ("A" and "B", UMMA M = 128 each) of one head against
+// shared 64-key K/V tiles, so the tensor pipe always has one tile's MMAs to run while the other
+// tile's softmax warps work:
+//   warp 8, lane 0 : TMA producer.  Q of both tiles once (64-column halves, 128B swizzle), then K
+//                    and V of each 64-key tile into a 3-stage ring; a K/V tile is assembled from
+//                    per-block boxes of min(block_size, 64) keys, so pages need not be contiguous.
+//   warp 9, lane 0 : MMA issuer.  S_t(j) = Q_t K_j^T into one of two TMEM S buffers per tile (both
+//                    operands K-major); O_t += P_t(j) V_j (P K-major from shared memory, V read
+//                    MN-major straight from its TMA tile).  Order: PV_A(j), PV_B(j), then S_A(j+2),
+//                    S_B(j+2) -- the S of the next tile is always computed ahead, so each softmax
+//                    warpgroup runs its tiles back to back.
+//   warps 0..3 / 4..7 : softmax of tile A / B.  Thread r of a warpgroup owns query row r (TMEM lane
+//                    r): tcgen05.ld of its 64 raw scores, causal / length mask (edge tiles only),
+//                    online softmax in the log2 domain with one FFMA + ex2 per score, P as bf16 into
+//                    the tile's swizzled shared-memory P buffer (reused once the tile's previous PV
+//                    completed).  The running max only moves when it grows by more than 2^8 (P stays
+//                    <= 256, exact in fp32 sums), so rescaling O in TMEM (tcgen05.ld / st after the
+//                    previous PV completed) is rare.  At the end the same threads read O from TMEM,
+//                    divide by the row sum and store bf16.
+// Keys past the context (or from a block id outside the pool, recorded as kBadIndex) get P = 0,
+// and their V rows are zeroed in shared memory by every warpgroup that uses the tile before its PV,
+// so whatever the pool holds there never reaches O.  Every wait is bounded; a timeout records an
+// error code, raises a CTA-wide abort flag that every role polls, drains the copies and MMAs in
+// flight and frees TMEM.
 //
 // Short query chunks (EAGLE3 verify, decode-sized chunks) stay on the mma.sync kernel in
 // attention.cu: a 128-row tile would be mostly empty there.
@@ -40,10 +46,11 @@ namespace {
 
 #define LSB_CHECK(cond, msg) TORCH_CHECK(cond, "llmserve_b200: ", msg)
 
-constexpr int kBQ = 128;        // query rows per CTA (UMMA M)
-constexpr int kBKV = 64;        // keys per tile
+constexpr int kBQ = 128;        // query rows per tile (UMMA M)
+constexpr int kQTiles = 2;      // query tiles per CTA, one softmax warpgroup each
+constexpr int kBKV = 64;        // keys per K/V tile
 constexpr int kStages = 3;      // K/V ring depth
-constexpr int kThreads = 192;   // 4 softmax warps + producer warp + MMA warp
+constexpr int kThreads = 320;   // 8 softmax warps + producer warp + MMA warp
 constexpr float kRescaleLog2 = 8.f;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -51,17 +58,17 @@ template <int HD>
 struct PfLayout {
   static constexpr int kHalves = HD / 64;                 // 128-byte column halves
   static constexpr int kQHalf = kBQ * 128;                // 16 KiB
-  static constexpr int kQBytes = kHalves * kQHalf;
+  static constexpr int kQTile = kHalves * kQHalf;
   static constexpr int kKVHalf = kBKV * 128;              // 8 KiB
   static constexpr int kTileBytes = kHalves * kKVHalf;    // K (or V) of one tile
   static constexpr int kStageBytes = 2 * kTileBytes;      // K | V
   static constexpr int kPBytes = kBQ * kBKV * 2;          // 16 KiB, one 128-byte row per query
-  static constexpr int kStageOff = kQBytes;
+  static constexpr int kStageOff = kQTiles * kQTile;
   static constexpr int kPOff = kStageOff + kStages * kStageBytes;
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
+  static constexpr int kBarOff = kPOff + kQTiles * kPBytes;
   static constexpr int kBytes = kBarOff + 256 + 1024;     // barriers + alignment slack
-  // TMEM columns: O [0, HD), S buffers [HD, HD + 64) and [HD + 64, HD + 128)
-  static constexpr int kTmemCols = 256;
+  // TMEM columns: O_t at 128 t; S_t buffers at 256 + 128 t + 64 b
+  static constexpr int kTmemCols = 512;
 };
 
 // ---- tcgen05 / TMA wrappers ---------------------------------------------------------------------
@@ -126,6 +133,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// 2^x on the special-function unit (the PTX instruction; flushes subnormal results to zero)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Bounded wait that also gives up once another role raised the abort flag.
 __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
                                            int code) {
@@ -148,39 +162,46 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, bf16* __restrict__ out, const int* __restrict__ cu_q,
     const int* __restrict__ seqlens_k, const int* __restrict__ block_tables, int bt_stride, float scale_log2, int nh,
-    int nkv, int bs, int box_keys, int tiles_per_seq, int num_seqs, int nblk, int* __restrict__ status) {
+    int nkv, int bs, int box_keys, int pairs_per_seq, int num_seqs, int nblk, int* __restrict__ status) {
   using L = PfLayout<HD>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* q_full = bars;                       // 1
-  uint64_t* k_full = bars + 1;                   // kStages
-  uint64_t* v_full = k_full + kStages;           // kStages
-  uint64_t* kv_empty = v_full + kStages;         // kStages
-  uint64_t* s_full = kv_empty + kStages;         // 2
-  uint64_t* s_free = s_full + 2;                 // 2
-  uint64_t* p_full = s_free + 2;                 // 2
-  uint64_t* p_free = p_full + 2;                 // 2
-  uint64_t* o_done = p_free + 2;                 // 1
-  uint64_t* drain = o_done + 1;                  // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  uint64_t* bad_keys = reinterpret_cast<uint64_t*>(smem + L::kBarOff + 192);   // kStages masks
+  uint64_t* q_full = bars;                         // 1
+  uint64_t* k_full = bars + 1;                     // kStages
+  uint64_t* v_full = k_full + kStages;             // kStages
+  uint64_t* kv_empty = v_full + kStages;           // kStages
+  uint64_t* s_full = kv_empty + kStages;           // [tile][buffer]: 4
+  uint64_t* s_free = s_full + 4;                   // 4
+  uint64_t* p_full = s_free + 4;                   // [tile]: 2
+  uint64_t* o_done = p_full + 2;                   // [tile]: 2 (one phase per PV of the tile)
+  uint64_t* drain = o_done + 2;                    // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);   // byte 184 of the barrier block
+  uint64_t* bad_keys = reinterpret_cast<uint64_t*>(smem + L::kBarOff + 208);   // kStages masks
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
 
   pdl_trigger();
   pdl_wait();
-  // heaviest tiles first: blockIdx.y enumerates (query tile from the last, sequence)
-  const int qt = tiles_per_seq - 1 - (int)blockIdx.y / num_seqs;
+  // heaviest tile pairs first: blockIdx.y enumerates (pair from the last, sequence)
+  const int qp = pairs_per_seq - 1 - (int)blockIdx.y / num_seqs;
   const int seq = (int)blockIdx.y % num_seqs;
   const int h = blockIdx.x, kvh = h / (nh / nkv);
   const int q0 = cu_q[seq], q_len = cu_q[seq + 1] - q0;
-  if (qt * kBQ >= q_len) return;
+  if (qp * kQTiles * kBQ >= q_len) return;
   const int k_len = min(seqlens_k[seq], bt_stride * bs);
   const int shift = seqlens_k[seq] - q_len;                  // absolute position of query row 0
-  const int last_row = min(q_len, (qt + 1) * kBQ) - 1;
-  const int kend = max(0, min(k_len, shift + last_row + 1));
-  const int ntiles = (kend + kBKV - 1) / kBKV;
+  // per query tile: key range (causal) and number of K/V tiles; tile B may be empty
+  int kend_t[kQTiles], nt[kQTiles];
+#pragma unroll
+  for (int t = 0; t < kQTiles; ++t) {
+    const int first = (qp * kQTiles + t) * kBQ;
+    const int last = min(q_len, first + kBQ) - 1;
+    kend_t[t] = first < q_len ? max(0, min(k_len, shift + last + 1)) : 0;
+    nt[t] = (kend_t[t] + kBKV - 1) / kBKV;
+  }
+  const int kend = max(kend_t[0], kend_t[1]);
+  const int ntiles = max(nt[0], nt[1]);
   const int* bt = block_tables + (size_t)seq * bt_stride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -192,17 +213,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 4);
-      mbar_init(&p_full[b], 4);
-      mbar_init(&p_free[b], 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
     }
-    mbar_init(o_done, 1);
+    for (int t = 0; t < kQTiles; ++t) {
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_done[t], 1);
+    }
     mbar_init(drain, 1);
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(L::kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -211,15 +233,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_o = tmem, tmem_s0 = tmem + HD;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------- TMA producer ----------------
     if (lane == 0 && ntiles > 0) {
-      mbar_expect_tx(q_full, L::kQBytes);
+      mbar_expect_tx(q_full, kQTiles * L::kQTile);
 #pragma unroll
-      for (int hf = 0; hf < L::kHalves; ++hf)
-        tma_2d(smem + hf * L::kQHalf, &tm_q, q_full, h * HD + hf * 64, q0 + qt * kBQ);
+      for (int t = 0; t < kQTiles; ++t)
+#pragma unroll
+        for (int hf = 0; hf < L::kHalves; ++hf)
+          tma_2d(smem + t * L::kQTile + hf * L::kQHalf, &tm_q, q_full, h * HD + hf * 64,
+                 q0 + (qp * kQTiles + t) * kBQ);
       int issued[kStages] = {};
       for (int j = 0; j < ntiles; ++j) {
         const int s = j % kStages, u = j / kStages;
@@ -266,57 +290,75 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && ntiles > 0) {
       constexpr uint32_t id_s = idesc(kBKV, false);
       constexpr uint32_t id_pv = idesc(HD, true);
       const uint32_t q_addr = smem_u32(smem);
       bool ok = wait_phase(q_full, 0, abort_v, status, kTimeoutTmaFull);
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i % kStages, u = i / kStages, b = i & 1, ub = i >> 1;
-        if (!wait_phase(&p_full[b], ub & 1, abort_v, status, kTimeoutAccum)) return false;
-        if (!wait_phase(&v_full[s], u & 1, abort_v, status, kTimeoutTmaFull)) return false;
-        fence_after();
-        const uint32_t p_addr = smem_u32(smem + L::kPOff + b * L::kPBytes);
-        const uint32_t v_addr = smem_u32(smem + L::kStageOff + s * L::kStageBytes + L::kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < kBKV / 16; ++kk)
-          mma(tmem_o, desc_kmajor(p_addr + kk * 32), desc_mnmajor(v_addr + kk * 16 * 128, L::kKVHalf), id_pv,
-              (i | kk) != 0);
-        commit(&kv_empty[s]);
-        commit(&p_free[b]);
-        commit(o_done);
-        return true;
-      };
-      for (int j = 0; ok && j < ntiles; ++j) {
+      // S_t(j) into buffer j & 1 of tile t
+      auto issue_s = [&](int t, int j) -> bool {
         const int s = j % kStages, u = j / kStages, b = j & 1, ub = j >> 1;
-        if (!wait_phase(&k_full[s], u & 1, abort_v, status, kTimeoutTmaFull)) { ok = false; break; }
-        if (ub >= 1 && !wait_phase(&s_free[b], (ub - 1) & 1, abort_v, status, kTimeoutAccum)) { ok = false; break; }
+        if (!wait_phase(&k_full[s], u & 1, abort_v, status, kTimeoutTmaFull)) return false;
+        if (ub >= 1 && !wait_phase(&s_free[t * 2 + b], (ub - 1) & 1, abort_v, status, kTimeoutAccum)) return false;
         fence_after();
         const uint32_t k_addr = smem_u32(smem + L::kStageOff + s * L::kStageBytes);
+        const uint32_t qa = q_addr + t * L::kQTile;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const int hf = kk / 4, c = kk % 4;
-          mma(tmem_s0 + b * kBKV, desc_kmajor(q_addr + hf * L::kQHalf + c * 32),
+          mma(tmem + 256 + t * 128 + b * kBKV, desc_kmajor(qa + hf * L::kQHalf + c * 32),
               desc_kmajor(k_addr + hf * L::kKVHalf + c * 32), id_s, kk != 0);
         }
-        commit(&s_full[b]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        commit(&s_full[t * 2 + b]);
+        return true;
+      };
+      // O_t += P_t(j) V_j
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int s = j % kStages, u = j / kStages;
+        if (!wait_phase(&p_full[t], j & 1, abort_v, status, kTimeoutAccum)) return false;
+        if (!wait_phase(&v_full[s], u & 1, abort_v, status, kTimeoutTmaFull)) return false;
+        fence_after();
+        const uint32_t p_addr = smem_u32(smem + L::kPOff + t * L::kPBytes);
+        const uint32_t v_addr = smem_u32(smem + L::kStageOff + s * L::kStageBytes + L::kTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < kBKV / 16; ++kk)
+          mma(tmem + t * 128, desc_kmajor(p_addr + kk * 32), desc_mnmajor(v_addr + kk * 16 * 128, L::kKVHalf),
+              id_pv, (j | kk) != 0);
+        commit(&o_done[t]);
+        return true;
+      };
+      for (int j = 0; ok && j < 2; ++j)
+        for (int t = 0; ok && t < kQTiles; ++t)
+          if (j < nt[t]) ok = issue_s(t, j);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        for (int t = 0; ok && t < kQTiles; ++t)
+          if (j < nt[t]) ok = issue_pv(t, j);
+        if (!ok) break;
+        commit(&kv_empty[j % kStages]);          // every MMA reading tile j's stage was issued
+        for (int t = 0; ok && t < kQTiles; ++t)
+          if (j + 2 < nt[t]) ok = issue_s(t, j + 2);
       }
-      if (ok) issue_pv(ntiles - 1);
       // every MMA this thread issued has completed before the CTA tears down
       commit(drain);
       mbar_wait(drain, 0);
     }
     __syncwarp();
   } else {
-    // ---------------- softmax warps 0..3: query row r = 32 * warp + lane ----------------
-    const int r = warp * 32 + lane;
-    const int qrow = qt * kBQ + r;
+    // ---------------- softmax: warpgroup t = tile t, query row r = 32 * (warp % 4) + lane ----------------
+    const int t = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const int qrow = (qp * kQTiles + t) * kBQ + r;
     const bool row_ok = qrow < q_len;
     const int qpos = shift + qrow;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int kend_me = kend_t[t], n_me = nt[t];
+    // the warp's smallest query position (its lane 0) bounds which key tiles need the causal mask
+    const int qpos_warp0 = shift + (qp * kQTiles + t) * kBQ + (warp & 3) * 32;
+    const bool warp_rows_ok = (qrow - lane + 31) < q_len;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tmem_o = tmem + t * 128 + lane_base;
+    const uint32_t tmem_s = tmem + 256 + t * 128 + lane_base;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     // every wait is made warp-uniform (tcgen05.ld / st are warp-collective)
@@ -325,52 +367,64 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     ok = false;                                                                          \
     break;                                                                               \
   }
-    for (int j = 0; j < ntiles; ++j) {
+    for (int j = 0; j < n_me; ++j) {
       const int s = j % kStages, u = j / kStages, b = j & 1, ub = j >> 1;
-      LSB_WAIT_ALL(&s_full[b], ub & 1, kTimeoutAccum);
+      LSB_WAIT_ALL(&s_full[t * 2 + b], ub & 1, kTimeoutAccum);
       fence_after();
       uint32_t raw[kBKV];
 #pragma unroll
-      for (int c = 0; c < kBKV; c += 16) tmem_ld16(tmem_s0 + b * kBKV + lane_base + c, raw + c);
+      for (int c = 0; c < kBKV; c += 16) tmem_ld16(tmem_s + b * kBKV + c, raw + c);
       tmem_wait_ld();
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[b]);
+      if (lane == 0) mbar_arrive(&s_free[t * 2 + b]);
       const int k0 = j * kBKV;
-      const bool tail = k0 + kBKV > kend;
       // the stage's bad-block mask is published by the producer's arrival on v_full (V has long
       // landed by now: it was issued right after K, which S needed)
       LSB_WAIT_ALL(&v_full[s], u & 1, kTimeoutTmaFull);
       const uint64_t bad = bad_keys[s];
-      float mx = -INFINITY;
-      float sv[kBKV];
+      // interior tile for the whole warp: every key valid for every row -> no mask
+      const bool interior = bad == 0ull && k0 + kBKV <= kend_me && k0 + kBKV - 1 <= qpos_warp0 && warp_rows_ok;
+      float mx8[8];
 #pragma unroll
-      for (int c = 0; c < kBKV; ++c) {
-        const int kp = k0 + c;
-        const bool valid = row_ok && kp <= qpos && kp < kend && !((bad >> c) & 1ull);
-        sv[c] = valid ? __uint_as_float(raw[c]) * scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[c]);
+      for (int e = 0; e < 8; ++e) mx8[e] = -INFINITY;
+      if (interior) {
+#pragma unroll
+        for (int c = 0; c < kBKV; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(raw[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < kBKV; ++c) {
+          const int kp = k0 + c;
+          const bool valid = row_ok && kp <= qpos && kp < kend_me && !((bad >> c) & 1ull);
+          if (!valid) raw[c] = __float_as_uint(-INFINITY);
+          mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(raw[c]));
+        }
       }
+      const float mx_raw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                 fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float mx = mx_raw * scale_log2;      // scale > 0: max commutes with the scaling
       float alpha = 1.f;
       if (mx > m_used + kRescaleLog2) {
-        alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
+        alpha = m_used == -INFINITY ? 0.f : ex2(m_used - mx);
         m_used = mx;
         l *= alpha;
       }
-      // P = exp2(s - m_used) as bf16 into the swizzled tile (row r: 128 bytes, chunk c at c ^ (r & 7))
-      if (ub >= 1) {
-        LSB_WAIT_ALL(&p_free[b], (ub - 1) & 1, kTimeoutAccum);
+      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;   // a fully masked row: all P = 0
+      // the P buffer is free once this tile's previous PV completed
+      if (j >= 1) {
+        LSB_WAIT_ALL(&o_done[t], (j - 1) & 1, kTimeoutAccum);
       }
-      uint8_t* prow = smem + L::kPOff + b * L::kPBytes + r * 128;
-      float sum = 0.f;
+      uint8_t* prow = smem + L::kPOff + t * L::kPBytes + r * 128;
+      float sum8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum8[e] = 0.f;
 #pragma unroll
       for (int c8 = 0; c8 < kBKV / 8; ++c8) {
         float p[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float x = sv[c8 * 8 + e];
-          p[e] = x == -INFINITY ? 0.f : exp2f(x - m_used);
-          sum += p[e];
+          p[e] = ex2(fmaf(__uint_as_float(raw[c8 * 8 + e]), scale_log2, neg_m));   // ex2(-inf) = 0
+          sum8[e] += p[e];
         }
         uint4 w;
         w.x = pack_bf16(p[0], p[1]);
@@ -379,11 +433,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
         w.w = pack_bf16(p[6], p[7]);
         *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = w;
       }
-      l += sum;
-      // zero the V rows of masked keys (past the context or from a bad block) in this stage
-      if (tail || bad != 0ull) {
+      l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      // zero the V rows of keys no query may see (past the context, or from a bad block)
+      if (k0 + kBKV > kend || bad != 0ull) {
         uint8_t* vt = smem + L::kStageOff + s * L::kStageBytes + L::kTileBytes;
-        for (int idx = r; idx < kBKV * L::kHalves * 8; idx += 128) {
+        for (int idx = r; idx < kBKV * L::kHalves * 8; idx += kBQ) {
           const int key = idx / (L::kHalves * 8), rem = idx % (L::kHalves * 8);
           const int hf = rem / 8, ch = rem % 8;
           if (k0 + key >= kend || ((bad >> key) & 1ull))
@@ -391,36 +445,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
         }
       }
       fence_async_smem();
-      // rescale O in TMEM when some row of this warp moved its max (after the previous PV is done)
+      // rescale O in TMEM when some row of this warp moved its max (the previous PV is done)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-        LSB_WAIT_ALL(o_done, (j - 1) & 1, kTimeoutAccum);
         fence_after();
 #pragma unroll 1
         for (int c = 0; c < HD; c += 16) {
           uint32_t o[16];
-          tmem_ld16(tmem_o + lane_base + c, o);
+          tmem_ld16(tmem_o + c, o);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st16(tmem_o + lane_base + c, o);
+          tmem_st16(tmem_o + c, o);
         }
         tmem_wait_st();
       }
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
 #undef LSB_WAIT_ALL
     // epilogue: O / l -> bf16
-    if (ok && ntiles > 0 &&
-        __all_sync(0xffffffffu, wait_phase(o_done, (ntiles - 1) & 1, abort_v, status, kTimeoutAccum))) {
+    if (ok && n_me > 0 &&
+        __all_sync(0xffffffffu, wait_phase(&o_done[t], (n_me - 1) & 1, abort_v, status, kTimeoutAccum))) {
       fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       bf16* orow = out + ((size_t)(q0 + (row_ok ? qrow : 0)) * nh + h) * HD;
 #pragma unroll 1
       for (int c = 0; c < HD; c += 16) {
         uint32_t o[16];
-        tmem_ld16(tmem_o + lane_base + c, o);
+        tmem_ld16(tmem_o + c, o);
         tmem_wait_ld();
         if (row_ok) {
           uint4 w0, w1;
@@ -436,14 +489,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
           *reinterpret_cast<uint4*>(orow + c + 8) = w1;
         }
       }
-    } else if (row_ok && ntiles == 0) {
+    } else if (row_ok && n_me == 0) {
       bf16* orow = out + ((size_t)(q0 + qrow) * nh + h) * HD;
       for (int c = 0; c < HD; c += 8) *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
     }
   }
   fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::kTmemCols));
   }
@@ -492,8 +545,8 @@ void prefill_attention_tc(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
   const int box_keys = bs >= 64 ? 64 : bs;
   const CUtensorMap& tm_k = kv_pool_map(kc, box_keys);
   const CUtensorMap& tm_v = kv_pool_map(vc, box_keys);
-  const int tiles = (int)((max_q + kBQ - 1) / kBQ);
-  LSB_CHECK((int64_t)tiles * B < 65536, "too many query tiles for one launch");
+  const int pairs = (int)((max_q + kQTiles * kBQ - 1) / (kQTiles * kBQ));
+  LSB_CHECK((int64_t)pairs * B < 65536, "too many query tiles for one launch");
   const float sl = (float)scale * kLog2e;
   auto stream = at::cuda::getCurrentCUDAStream();
   int* st = status_ptr(status);
@@ -501,9 +554,9 @@ void prefill_attention_tc(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
   do {                                                                                                             \
     const int smem = PfLayout<HD>::kBytes;                                                                         \
     ensure_dynamic_smem((const void*)prefill_tc_kernel<HD>, smem);                                               \
-    launch_pdl(prefill_tc_kernel<HD>, dim3(nh, tiles * B), dim3(kThreads), smem, stream, tm_q, tm_k, tm_v,        \
+    launch_pdl(prefill_tc_kernel<HD>, dim3(nh, pairs * B), dim3(kThreads), smem, stream, tm_q, tm_k, tm_v,        \
                (bf16*)out.data_ptr(), cu_q.data_ptr<int>(), seqlens_k.data_ptr<int>(), block_tables.data_ptr<int>(), \
-               (int)block_tables.size(1), sl, nh, nkv, bs, box_keys, tiles, B, (int)kc.size(0), st);               \
+               (int)block_tables.size(1), sl, nh, nkv, bs, box_keys, pairs, B, (int)kc.size(0), st);               \
   } while (0)
   if (hd == 128) LSB_PF_TC(128);
   else LSB_PF_TC(64);

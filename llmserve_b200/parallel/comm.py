@@ -1,13 +1,16 @@
 """Peer-mapped buffers and the fused row-parallel collective (``ops/csrc/comm.cu``).
 
-Every rank ``cudaMalloc``s one buffer ``[control | normed out | residual | inbox]``, exports its
-CUDA IPC handle, and maps every peer's buffer (handles exchanged through ``torch.distributed`` at
-start-up only).  A row-parallel projection then runs as two kernels:
+Every rank ``cudaMalloc``s one buffer ``[control | out | residual | all-gather inbox | reduce
+inbox]``, exports its CUDA IPC handle, and maps every peer's buffer (handles exchanged through
+``torch.distributed`` at start-up only).  A row-parallel projection then runs as two kernels:
 
 * the sm_100a GEMM (dense or W4A16) whose epilogue stores the fp32 split-K partials of each token
-  row straight into the inbox of the rank that owns the row (peer stores over NVLink);
-* ``row_parallel_finish``: signal, wait, reduce the rank's own rows from its local inbox, add the
-  residual, RMSNorm, push the finished rows into every rank's out/residual buffers, signal, wait.
+  row straight into the reduce inbox of the rank that owns the row (peer stores over NVLink), each
+  value in a 64-bit word tagged with the call's epoch;
+* ``row_parallel_finish``: for the rows this rank owns, poll the inbox until every word carries the
+  epoch, reduce, add the residual, RMSNorm, and store the finished (out, residual) pairs into every
+  peer's all-gather inbox (again epoch-tagged words); for the other rows, poll the all-gather inbox
+  and unpack.  No fence, flag or barrier round: a word with the expected epoch carries its data.
 
 The outputs alias the buffers (valid until the next fused call), which also makes the path
 CUDA-graph friendly.  The control block also carries the greedy vocab-parallel argmax exchange
@@ -43,20 +46,32 @@ class FusedComm:
         self.rank, self.world = tp.get_tp_rank(), tp.get_tp_size()
         self.base = base
         self.opened = opened
+        self.ctrl_ptrs = list(peers)
+        off = self.offsets(hidden, max_tokens, self.world)
+        self.ag_ptrs = [p + off["ag"] for p in peers]
+        self.inbox_ptrs = [p + off["inbox"] for p in peers]
+        self.epoch_ptr = base                      # this rank's epoch word (control word 0)
+        self._local = _wrap(base, off["total"], device)
         out_bytes = max_tokens * hidden * 2
-        self.flag_ptrs = list(peers)
-        self.out_ptrs = [p + CTRL_BYTES for p in peers]
-        self.res_ptrs = [p + CTRL_BYTES + out_bytes for p in peers]
-        self.inbox_ptrs = [p + CTRL_BYTES + 2 * out_bytes for p in peers]
-        nbytes = self.buffer_bytes(hidden, max_tokens, self.world)
-        self._local = _wrap(base, nbytes, device)
-        self.out_buf = self._local[CTRL_BYTES:CTRL_BYTES + out_bytes].view(torch.bfloat16)
-        self.res_buf = self._local[CTRL_BYTES + out_bytes:CTRL_BYTES + 2 * out_bytes].view(torch.bfloat16)
+        self.out_ptr, self.res_ptr = base + off["out"], base + off["res"]
+        self.out_buf = self._local[off["out"]:off["out"] + out_bytes].view(torch.bfloat16)
+        self.res_buf = self._local[off["res"]:off["res"] + out_bytes].view(torch.bfloat16)
+
+    @staticmethod
+    def offsets(hidden: int, max_tokens: int, world: int) -> dict:
+        """Byte offsets of the regions of one rank's buffer (see ``ops/csrc/comm.cu``)."""
+        out_bytes = max_tokens * hidden * 2
+        ag_bytes = max_tokens * hidden * 8
+        inbox_bytes = world * MAX_SPLITS * _rows_per_rank(max_tokens, world) * hidden * 8
+        out = CTRL_BYTES
+        res = out + out_bytes
+        ag = res + out_bytes
+        inbox = ag + ag_bytes
+        return {"out": out, "res": res, "ag": ag, "inbox": inbox, "total": inbox + inbox_bytes}
 
     @staticmethod
     def buffer_bytes(hidden: int, max_tokens: int, world: int) -> int:
-        inbox = world * MAX_SPLITS * _rows_per_rank(max_tokens, world) * hidden * 4
-        return CTRL_BYTES + 2 * max_tokens * hidden * 2 + inbox
+        return FusedComm.offsets(hidden, max_tokens, world)["total"]
 
     @classmethod
     def create(cls, device, hidden: int, max_tokens: int, timeout_s: float = 120.0):
@@ -105,7 +120,6 @@ class FusedComm:
         from llmserve_b200.ops import awq as awq_ops
         from llmserve_b200.parallel.fused import ROW_PARALLEL_MAX_SPLITS
         T, K = x.shape
-        N = weight.shape[0]
         rows = _rows_per_rank(T, self.world)
         st = status(x.device)
         if isinstance(weight, awq_ops.AWQPacked):
@@ -113,7 +127,7 @@ class FusedComm:
             splits = min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS)
             planes = splits
             C().awq_gemm_to_owners(x, weight.qtiles, weight.sztiles, weight.n, self.inbox_ptrs, self.rank, rows,
-                                   splits, st)
+                                   splits, self.epoch_ptr, st)
         else:
             # dense: the K splits reduce on chip, one fp32 plane per rank crosses NVLink
             data, n, packed = gemm._operand(weight)
@@ -121,24 +135,24 @@ class FusedComm:
             splits = (gemm.cluster_splits(T, n, K) if reduce
                       else min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS))
             planes = 1 if reduce else splits
-            C().gemm_bf16_to_owners(x, data, n, packed, self.inbox_ptrs, self.rank, rows, splits, reduce, st,
-                                    gemm.stages_for_tokens(T))
+            C().gemm_bf16_to_owners(x, data, n, packed, self.inbox_ptrs, self.rank, rows, splits, reduce,
+                                    self.epoch_ptr, st, gemm.stages_for_tokens(T))
         return self.finish(residual, norm_weight, eps, T, planes)
 
-    def finish(self, residual, norm_weight, eps, T: int, planes: int):
+    def finish(self, residual, norm_weight, eps, T: int, planes: int, phases: int = 3):
         """The collective half alone: reduce this rank's rows from its inbox (``planes`` planes per
-        source rank), add the residual, RMSNorm, push the rows to every rank; outputs alias the
-        buffers."""
+        source rank), add the residual, RMSNorm, push the rows to every rank, receive the others;
+        outputs alias the buffers."""
         N = self.hidden
-        C().row_parallel_finish(self.out_ptrs, self.res_ptrs, self.flag_ptrs, self.inbox_ptrs[self.rank],
-                                residual.contiguous(), norm_weight, self.rank, planes, T, N,
-                                _rows_per_rank(T, self.world), float(eps), status(residual.device))
+        C().row_parallel_finish(self.ag_ptrs, self.inbox_ptrs[self.rank], self.ctrl_ptrs[self.rank], self.out_ptr,
+                                self.res_ptr, residual.contiguous(), norm_weight, self.rank, planes, T, N,
+                                _rows_per_rank(T, self.world), float(eps), phases, status(residual.device))
         return self.out_buf[: T * N].view(T, N), self.res_buf[: T * N].view(T, N)
 
     def argmax(self, values: torch.Tensor, indices: torch.Tensor, shard_offset: int, out: torch.Tensor):
         """Greedy token ids ``out[int64 rows]`` from every rank's per-shard (max value, local index),
         exchanged through the control blocks (one kernel, capturable; ties -> lowest global id)."""
-        C().vocab_argmax_exchange(self.flag_ptrs, values, indices, int(shard_offset), out, self.rank,
+        C().vocab_argmax_exchange(self.ctrl_ptrs, values, indices, int(shard_offset), out, self.rank,
                                   status(values.device))
         return out
 

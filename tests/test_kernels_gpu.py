@@ -444,24 +444,21 @@ def test_greedy_accept_kernel_matches_batched_reference():
 
 def test_fused_collective_wait_on_unset_flag_returns_error_status():
     """Failure detection on the device without a fault: a two-rank fused collective whose second
-    rank never runs (its buffer is local memory that nothing signals).  Rank 0's waits for the
-    peer's flags give up after the (lowered) spin limit, record the error in the status word and
-    let the kernel finish; the host raises, and the context stays usable.  The same holds for the
-    vocab-parallel argmax exchange."""
-    from llmserve_b200.parallel.comm import CTRL_BYTES, FusedComm
+    rank never runs (its buffer is local memory nothing writes).  Rank 0's polls for the peer's
+    epoch-tagged words give up after the (lowered) spin limit, record the error in the status word
+    and let the kernel finish; the host raises, and the context stays usable.  The same holds for
+    the vocab-parallel argmax exchange."""
+    from llmserve_b200.parallel.comm import FusedComm
     hidden, T, cap, world = 4096, 4, 64, 2
-    nbytes = FusedComm.buffer_bytes(hidden, cap, world)
-    bufs = [C().comm_alloc(nbytes) for _ in range(world)]
+    off = FusedComm.offsets(hidden, cap, world)
+    bufs = [C().comm_alloc(off["total"]) for _ in range(world)]
     dev = torch.device("cuda", torch.cuda.current_device())
     try:
-        out_b = cap * hidden * 2
-        outs = [b + CTRL_BYTES for b in bufs]
-        res = [b + CTRL_BYTES + out_b for b in bufs]
-        inbox = bufs[0] + CTRL_BYTES + 2 * out_b
         res_in = torch.randn(T, hidden, device=dev).bfloat16()
         w = torch.ones(hidden, device=dev).bfloat16()
         C().comm_set_spin_limit(1 << 16)
-        C().row_parallel_finish(outs, res, bufs, inbox, res_in, w, 0, 1, T, hidden, 2, 1e-6, status(dev))
+        C().row_parallel_finish([b + off["ag"] for b in bufs], bufs[0] + off["inbox"], bufs[0], bufs[0] + off["out"],
+                                bufs[0] + off["res"], res_in, w, 0, 1, T, hidden, 2, 1e-6, 3, status(dev))
         torch.cuda.synchronize()
         with pytest.raises(RuntimeError, match="peer flag wait timed out"):
             check_status(dev)
@@ -488,48 +485,46 @@ def _wrap_dev(ptr, nbytes, dtype):
 
 @pytest.mark.parametrize("reduce", [False, True])
 @pytest.mark.parametrize("world,T,packed", [(1, 5, False), (2, 64, True), (4, 7, True), (4, 64, False)])
-def test_row_parallel_push_layout_single_gpu(world, T, packed, reduce):
+@pytest.mark.parametrize("calls", [1, 2])
+def test_row_parallel_push_layout_single_gpu(world, T, packed, reduce, calls):
     """The fused row-parallel path's data layout on one GPU: each emulated rank's GEMM stores its
-    partial planes into the owners' inboxes, then each rank's finish kernel runs alone (the peers'
-    arrival flags it would wait for are pre-set, so no kernel waits on another launch) and
-    reduces its rows, normalises them and pushes them to every buffer.  Every buffer must then
-    hold add+RMSNorm of the full fp32 product."""
-    from llmserve_b200.parallel.comm import CTRL_BYTES, FusedComm
+    epoch-tagged partial planes into the owners' inboxes, then every rank's finish kernel reduces
+    the rows it owns, normalises them and pushes them (phase 1, all ranks), then every rank unpacks
+    the rows the others own (phase 2), so no launch waits on a later one.  Every rank must then hold
+    add+RMSNorm of the full fp32 product; a second call (next epoch, new inputs) must not see the
+    first call's words."""
+    from llmserve_b200.parallel.comm import FusedComm
     hidden, K, cap, S = 512, 256, 64, 3
-    nbytes = FusedComm.buffer_bytes(hidden, cap, world)
-    bufs = [C().comm_alloc(nbytes) for _ in range(world)]
+    off = FusedComm.offsets(hidden, cap, world)
+    bufs = [C().comm_alloc(off["total"]) for _ in range(world)]
     st = status(torch.device(DEV))
     try:
-        out_b = cap * hidden * 2
-        outs = [b + CTRL_BYTES for b in bufs]
-        res = [b + CTRL_BYTES + out_b for b in bufs]
-        inboxes = [b + CTRL_BYTES + 2 * out_b for b in bufs]
-        g = torch.Generator(device=DEV).manual_seed(world * 100 + T)
-        xs = [torch.randn(T, K, device=DEV, generator=g).bfloat16() for _ in range(world)]
-        ws = [(torch.randn(hidden, K, device=DEV, generator=g) * 0.05).bfloat16() for _ in range(world)]
-        res_in = torch.randn(T, hidden, device=DEV, generator=g).bfloat16()
-        nw = (1 + 0.1 * torch.randn(hidden, device=DEV, generator=g)).bfloat16()
+        ags = [b + off["ag"] for b in bufs]
+        inboxes = [b + off["inbox"] for b in bufs]
         rows = -(-T // world)
-        for r in range(world):
-            w = gemm.pack_weight(ws[r]).data if packed else ws[r]
-            C().gemm_bf16_to_owners(xs[r], w, hidden, packed, inboxes, r, rows, S, reduce, st, 0)
-        # pre-set, in every rank's control block, the arrival flags of the ranks that run later
-        for r in range(world):
-            flags = _wrap_dev(bufs[r], 256, torch.int32)
-            for later in range(r + 1, world):
-                flags[later] = 1
-                flags[world + later] = 1
-        for r in range(world):
-            C().row_parallel_finish(outs, res, bufs, inboxes[r], res_in, nw, r, 1 if reduce else S, T, hidden, rows,
-                                    1e-6, st)
-        torch.cuda.synchronize()
-        y = sum(x.float() @ w.float().t() for x, w in zip(xs, ws)).bfloat16()
-        href, rref = norm.add_rms_norm_ref(y.cpu(), res_in.cpu(), nw.cpu(), 1e-6)
-        for r in range(world):
-            h = _wrap_dev(outs[r], T * hidden * 2, torch.bfloat16).view(T, hidden)
-            rr = _wrap_dev(res[r], T * hidden * 2, torch.bfloat16).view(T, hidden)
-            assert rel_err(h, href.to(DEV)) < 1e-2
-            assert rel_err(rr, rref.to(DEV)) < 1e-2
+        for call in range(calls):
+            g = torch.Generator(device=DEV).manual_seed(world * 100 + T + 7 * call)
+            xs = [torch.randn(T, K, device=DEV, generator=g).bfloat16() for _ in range(world)]
+            ws = [(torch.randn(hidden, K, device=DEV, generator=g) * 0.05).bfloat16() for _ in range(world)]
+            res_in = torch.randn(T, hidden, device=DEV, generator=g).bfloat16()
+            nw = (1 + 0.1 * torch.randn(hidden, device=DEV, generator=g)).bfloat16()
+            for r in range(world):
+                w = gemm.pack_weight(ws[r]).data if packed else ws[r]
+                C().gemm_bf16_to_owners(xs[r], w, hidden, packed, inboxes, r, rows, S, reduce, bufs[r], st, 0)
+            planes = 1 if reduce else S
+            for phase in (1, 2):
+                for r in range(world):
+                    C().row_parallel_finish(ags, inboxes[r], bufs[r], bufs[r] + off["out"], bufs[r] + off["res"],
+                                            res_in, nw, r, planes, T, hidden, rows, 1e-6, phase, st)
+            torch.cuda.synchronize()
+            y = sum(x.float() @ w.float().t() for x, w in zip(xs, ws)).bfloat16()
+            href, rref = norm.add_rms_norm_ref(y.cpu(), res_in.cpu(), nw.cpu(), 1e-6)
+            for r in range(world):
+                h = _wrap_dev(bufs[r] + off["out"], T * hidden * 2, torch.bfloat16).view(T, hidden)
+                rr = _wrap_dev(bufs[r] + off["res"], T * hidden * 2, torch.bfloat16).view(T, hidden)
+                assert rel_err(h, href.to(DEV)) < 1e-2, (call, r)
+                assert rel_err(rr, rref.to(DEV)) < 1e-2, (call, r)
+                assert int(_wrap_dev(bufs[r], 8, torch.int32)[0]) == call + 1     # epoch advanced once per call
     finally:
         torch.cuda.synchronize()
         for b in bufs:
