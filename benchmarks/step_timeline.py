@@ -1,6 +1,7 @@
 """Device timeline of serving steps: per-kernel exclusive time and GPU idle gaps.
 
-``python -m benchmarks.step_timeline [--layers 36] [--concurrency 64] [--warmup 30] [--steps 5] [--tp N]``
+``python -m benchmarks.step_timeline [--layers 36] [--concurrency 64] [--warmup 30] [--steps 5] [--tp N]
+[--nccl-only] [--eagle3]``
 
 Runs the headline closed-loop workload (Qwen3-8B shapes, random weights, 256-token prompts) to a
 steady decode state, records ``--steps`` engine steps with ``torch.profiler`` (CUPTI kernel
@@ -46,6 +47,8 @@ def main(argv=None):
     p.add_argument("--json", default=None, help="write the raw (name, start, end) rows here")
     p.add_argument("--tp", type=int, default=1, help="tensor-parallel size (the timeline is rank 0's GPU)")
     p.add_argument("--nccl-only", action="store_true", help="NCCL collectives instead of the fused NVLink path")
+    p.add_argument("--eagle3", action="store_true",
+                   help="EAGLE3 speculative steps (gamma 3, random-init Qwen3-8B speculator, step CUDA graphs)")
     args = p.parse_args(argv)
 
     import torch
@@ -54,10 +57,18 @@ def main(argv=None):
     import bench
     from llmserve_b200 import LLM, SamplingParams
     from llmserve_b200.engine.model_runner import GreedySampler
+    extra = {}
+    if args.eagle3:
+        import os
+        import tempfile
+
+        from llmserve_b200.models.synthetic import EAGLE3_8B, write_config_only
+        extra = dict(speculative_model=write_config_only(os.path.join(tempfile.gettempdir(), "llmserve_b200_eagle3_8b"),
+                                                         EAGLE3_8B), speculative_gamma=3, speculative_cuda_graphs=True)
     llm = LLM(bench.model_dir(args.layers), load_format="dummy", max_model_len=args.input_len + args.output_len + 16,
               max_num_batched_tokens=max(16384, args.concurrency * args.input_len), max_num_seqs=args.concurrency,
               kvcache_block_size=256, gpu_memory_utilization=args.mem_util, tensor_parallel_size=args.tp,
-              fused_collectives=not args.nccl_only)
+              fused_collectives=not args.nccl_only, **extra)
     llm.model_runner.sampler = GreedySampler()
     stream = bench.request_stream(llm.config.hf_config.vocab_size, args.input_len)
     sp = SamplingParams(temperature=1.0, max_tokens=args.output_len, ignore_eos=True)

@@ -141,7 +141,7 @@ def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, wor
 
 # From this many query rows in the longest sequence of a step, prefill runs on the tcgen05 kernel
 # (128-row query tiles); shorter chunks (verify, small chunked-prefill pieces) on the mma.sync one.
-PREFILL_TC_MIN_Q = int(os.environ.get("LLMSERVE_PREFILL_TC_MIN_Q", str(1 << 30)))
+PREFILL_TC_MIN_Q = int(os.environ.get("LLMSERVE_PREFILL_TC_MIN_Q", "65"))
 
 
 def prefill_attention(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables, scale, max_seqlen_q: int,

@@ -423,7 +423,8 @@ void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int
   pd.slot = (int)rank;
   pd.planes = (int)splits;
   pd.owners = W;
-  TORCH_CHECK(W == 1 || epoch_ptr != 0, "llmserve_b200: tensor-parallel inboxes need an epoch word");
+  TORCH_CHECK(epoch_ptr != 0, "llmserve_b200: the collective's inboxes need an epoch word");
+  pd.ll = 1;
   pd.epoch = reinterpret_cast<const uint32_t*>(epoch_ptr);
   const at::cuda::CUDAGuard g(x.device());
   awq_dispatch(x, qtiles, sztiles, N, nullptr, pd, (int)splits, status_ptr(status));

@@ -63,9 +63,10 @@ struct PartDest {
   int slot;      // this rank's source slot in every owner's inbox (0 with one owner)
   int planes;    // split-K planes per source (the GEMM's gridDim.z)
   int owners;    // 1, or the tensor-parallel size
-  const uint32_t* epoch;   // owners > 1: this rank's epoch word of the collective
-  __device__ __forceinline__ uint32_t call_epoch() const { return owners > 1 ? ld_volatile_u32(epoch) + 1u : 0u; }
-  __device__ __forceinline__ float* at(int z, int t, int N, int feat) const {   // owners == 1 only
+  int ll;        // 1: the collective's inboxes (epoch-tagged words), whatever the number of owners
+  const uint32_t* epoch;   // ll: this rank's epoch word of the collective
+  __device__ __forceinline__ uint32_t call_epoch() const { return ll ? ld_volatile_u32(epoch) + 1u : 0u; }
+  __device__ __forceinline__ float* at(int z, int t, int N, int feat) const {   // local planes (ll == 0)
     return base[0] + ((size_t)z * rows + t) * N + feat;
   }
   __device__ __forceinline__ uint64_t* ll_at(int z, int t, int N, int feat) const {
@@ -78,12 +79,12 @@ struct PartDest {
   }
   // one value of plane z, token row t, feature feat
   __device__ __forceinline__ void store(int z, int t, int N, int feat, float v, uint32_t e) const {
-    if (owners == 1) *at(z, t, N, feat) = v;
+    if (!ll) *at(z, t, N, feat) = v;
     else ll_store1(ll_at(z, t, N, feat), ll_word(__float_as_uint(v), e));
   }
   // four consecutive features feat..feat+3 (feat % 4 == 0, N % 4 == 0)
   __device__ __forceinline__ void store4(int z, int t, int N, int feat, const float* v, uint32_t e) const {
-    if (owners == 1) {
+    if (!ll) {
       float* p = at(z, t, N, feat);
 #pragma unroll
       for (int q = 0; q < 4; ++q) p[q] = v[q];
@@ -102,6 +103,7 @@ inline PartDest local_part_dest(float* partials, int T, int planes) {
   d.slot = 0;
   d.planes = planes;
   d.owners = 1;
+  d.ll = 0;
   d.epoch = nullptr;
   return d;
 }

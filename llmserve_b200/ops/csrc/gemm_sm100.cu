@@ -300,8 +300,8 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
       const float va[4] = {a.x, a.y, a.z, a.w};
       if constexpr (EPI == 0) {
         const int f0 = n0 + g * 4;
-        if (pd.base[0] != nullptr && (pd.owners > 1 || f0 + 3 < N)) {
-          pd.store4(0, t, N, f0, va, ep);          // N % 4 == 0 under tensor parallelism
+        if (pd.base[0] != nullptr && (pd.ll || f0 + 3 < N)) {
+          pd.store4(0, t, N, f0, va, ep);          // N % 4 == 0 for the collective's inboxes
         } else {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -716,7 +716,8 @@ void gemm_bf16_to_owners(at::Tensor x, at::Tensor w, int64_t n, bool packed, std
   pd.slot = (int)rank;
   pd.planes = reduce ? 1 : (int)splits;   // a cluster-reduced projection sends one plane per rank
   pd.owners = W;
-  LSB_CHECK(W == 1 || (n % 4 == 0 && epoch_ptr != 0), "tensor-parallel inboxes need N % 4 == 0 and an epoch word");
+  LSB_CHECK(n % 4 == 0 && epoch_ptr != 0, "the collective's inboxes need N % 4 == 0 and an epoch word");
+  pd.ll = 1;
   pd.epoch = reinterpret_cast<const uint32_t*>(epoch_ptr);
   const at::cuda::CUDAGuard g(x.device());
   tile_dispatch(x, w, (int)n, packed, nullptr, pd, (int)splits, status_ptr(status), max_stages, reduce);

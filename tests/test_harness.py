@@ -383,3 +383,29 @@ def test_run_suite_command_line_end_to_end_on_the_host_tier(tmp_path):
     rows = list(csv.DictReader(open(tmp_path / "out" / "summary.csv")))
     assert len(rows) == 2 and all(float(r["output_throughput_tps"]) > 0 for r in rows)
     assert str(tmp_path) not in (tmp_path / "out" / "runs" / f"{rows[0]['point_id']}.json").read_text()
+
+
+def test_b200_tp1_suite_expands_and_runs_with_a_fake_engine():
+    """The one-GPU B200 suite (decode-heavy closed loop, EAGLE3 graphs, chunked prefill on the mixed
+    profile, closed loop and Poisson) expands to its 16 points, each of which runs through
+    ``run_point`` against a fake engine with the runtime knobs it names."""
+    suite = json.load(open("benchmarks/suites/b200-serving-tp1.json"))
+    points = expand_suite(suite)
+    assert len(points) == 16 and len({p["point_id"] for p in points}) == 16
+    assert {p["experiment"] for p in points} == {"bf16-closed-loop-tp1", "eagle-closed-loop-tp1",
+                                                 "chunked-closed-loop-tp1", "chunked-poisson-tp1"}
+    seen = []
+    clock = FakeClock()
+
+    def factory(model, **kw):
+        seen.append(kw)
+        return FakeEngine(clock)
+
+    for p in points:
+        p = dict(p, warmup_seconds=0.05, measurement_seconds=0.1)
+        result = run_point(p, "/models/tiny", speculative_model="/models/eagle3", engine_factory=factory,
+                           make_sampling_params=_sp, clock=clock, sleep=clock.sleep, metadata={"git_commit": "abc"})
+        assert result["complete"], p["point_id"]
+    assert all(kw["tensor_parallel_size"] == 1 for kw in seen)
+    assert sum(bool(kw.get("enable_chunked_prefill")) for kw in seen) == 4
+    assert sum(bool(kw.get("speculative_cuda_graphs")) for kw in seen) == 2

@@ -161,3 +161,21 @@ def test_engine_tp_logits_match_tp1_every_step(tmp_path, world):
     assert len(one.logits) == 20
     worst, checked = compare_logits(many.logits, one.logits, 3e-2)
     assert checked >= 40, (worst, checked)
+
+
+@needs2
+@pytest.mark.timeout(900)
+@pytest.mark.parametrize("world", [w for w in (2, 8) if w <= NGPU])
+def test_awq_engine_tp_logits_match_tp1_every_step(tmp_path, world):
+    """AutoAWQ W4A16 at TP > 1: the packed qweight / qzeros / scales sliced per rank, the row-parallel
+    W4A16 GEMM storing its epoch-tagged split-K partials into the owners' inboxes of the fused
+    collective.  Every step's logits match the TP = 1 AWQ engine's (teacher-forced)."""
+    from llmserve_b200.models.synthetic import TINY, write_awq_checkpoint
+    from tests.support import compare_logits
+    cfg = dict(TINY, hidden_size=1024, num_attention_heads=16, num_key_value_heads=8, intermediate_size=2048,
+               head_dim=64, num_hidden_layers=4)
+    path = write_awq_checkpoint(str(tmp_path / "awq"), cfg)
+    one = _tp_logits(path, 1, None, graphs=True)
+    many = _tp_logits(path, world, one.tokens, graphs=True)
+    worst, checked = compare_logits(many.logits, one.logits, 3e-2)
+    assert checked >= 40, (worst, checked)
