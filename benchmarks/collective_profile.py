@@ -9,11 +9,12 @@ add and the RMSNorm:
 
 * ``fused``   -- the engine's path (``FusedComm.row_parallel_add_norm``): the tcgen05 GEMM's epilogue
   stores each token row's split-K partials into the inbox of the rank owning the row (peer
-  stores), then ``row_parallel_finish`` reduces the rank's rows from its own inbox, adds the
-  residual, normalises and pushes the finished rows to every rank (peer stores);
+  stores of epoch-tagged words), then ``row_parallel_finish`` reduces the rank's rows from its own
+  inbox, adds the residual, normalises, pushes the finished rows to every rank and unpacks the
+  rows the peers pushed;
 * ``nccl``    -- the baseline: the same GEMM (bf16 output), ``dist.all_reduce``, add+RMSNorm kernel;
-* ``gemm``    -- the GEMM alone, to separate the collective's share;
-* ``finish_only`` -- the finishing kernel alone (signal, wait, reduce, norm, push, signal, wait).
+* ``gemm``    -- the same GEMM alone writing local planes, to separate the collective's share
+  (the finishing kernel cannot run alone: it waits for the GEMM's words of its own call).
 
 Each variant's ``--iters`` back-to-back calls are captured in one CUDA graph (the form the decode
 step runs them in, without Python launch overhead); times are CUDA events around one replay on
@@ -35,8 +36,9 @@ def fused_roofline_us(T: int, hidden: int, inner_shard: int, world: int, planes:
     weight_bytes = hidden * inner_shard * 2
     flops = 2.0 * T * hidden * inner_shard
     # the GEMM stores the fp32 partial planes of the other ranks' rows into their inboxes, then the
-    # rank pushes its finished rows (normed output + residual, bf16) to the other ranks
-    link_bytes = (T - min(rows, T)) * hidden * 4 * planes + (world - 1) * min(rows, T) * hidden * 2 * 2
+    # rank pushes its finished rows (normed output + residual, bf16) to the other ranks; every value
+    # travels in an 8-byte epoch-tagged word (4 bytes of payload)
+    link_bytes = (T - min(rows, T)) * hidden * 8 * planes + (world - 1) * min(rows, T) * hidden * 8
     terms = {"hbm_us": weight_bytes / (hbm_gbs * 1e3), "compute_us": flops / (bf16_tflops * 1e6),
              "nvlink_us": link_bytes / (nvlink_gbs * 1e3)}
     return dict(terms, roofline_us=max(terms.values()), nvlink_bytes=link_bytes, weight_bytes=weight_bytes)
@@ -122,7 +124,6 @@ def main(argv=None):
             row = {"tokens": T, "world": world, "hidden": args.hidden, "inner_shard": k, "planes": planes}
             if comm is not None and comm.can_handle(T, args.hidden):
                 row["fused_us"] = timed(lambda: comm.row_parallel_add_norm(x, next_w(), res, nw, 1e-6))
-                row["finish_only_us"] = timed(lambda: comm.finish(res, nw, 1e-6, T, planes))
             if planes == 1:
                 row["gemm_us"] = timed(lambda: gemm.linear_reduced(x, next_w(), plane=True))
             else:

@@ -883,14 +883,23 @@ class ModelRunner:
         self.inflight_bs = bs
 
     # ---- device timing (benchmarks): every rank records, rank 0 gathers -------------------------
-    def mark_event(self, tag: str):
+    def mark_event(self, tag: str, fence: str = ""):
+        """Record a CUDA event ``tag`` on this rank's stream.  ``fence="before"`` first drains this
+        GPU and meets every rank at a barrier (a window opened this way starts with nothing in
+        flight on any rank); ``fence="after"`` drains and meets after recording."""
         if not hasattr(self, "_events"):
             self._events = {}
+        if fence == "before" and self.is_cuda:
+            torch.cuda.synchronize()
+            tp.barrier()
         if self.is_cuda:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
             self._events[tag] = e
         self._events[tag + ":launches"] = LaunchCounter.launches
+        if fence == "after" and self.is_cuda:
+            torch.cuda.synchronize()
+            tp.barrier()
 
     def gather_elapsed(self, start: str, end: str):
         """Per-rank (device ms between two marks, kernel launches between them)."""

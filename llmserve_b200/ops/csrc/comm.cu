@@ -36,6 +36,9 @@
 #include <c10/cuda/CUDAStream.h>
 #include <cooperative_groups.h>
 
+#include <mutex>
+#include <unordered_map>
+
 #include "common.cuh"
 
 namespace cg = cooperative_groups;
@@ -108,7 +111,8 @@ __device__ __forceinline__ void ll_wait4(const uint64_t* p, uint32_t epoch, uint
 constexpr int kEpochWord = 0, kCounterWord = 1;
 constexpr int kMaxPer = 4;       // 4-column chunks per thread: N / kCluster <= kMaxPer * 4 * kThreads
 
-// grid (kCluster, T): the kCluster CTAs of cluster y handle token row y, N / kCluster columns each.
+// grid (kCluster, G <= T): the kCluster CTAs of a cluster handle rows y, y + G, ... of this rank's
+// rows, then of the peers' rows, N / kCluster columns each.
 // phases: 1 = rows this rank owns (reduce, norm, push), 2 = rows peers own (receive); the engine
 // runs both in one launch (3); a single-GPU test runs every emulated rank's phase 1 before any
 // phase 2, so no launch waits on a later one.
@@ -127,104 +131,115 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   __syncthreads();
   const uint32_t epoch = s_epoch;
   const uint32_t limit = *((volatile uint32_t*)&g_flag_spin_limit);
-  const int t = blockIdx.y;
-  const int owner = t / rows_per_rank, r = t - owner * rows_per_rank;
   const int crank = (int)cluster.block_rank();
   const int cols = N / kCluster;                // columns of this CTA (multiple of 4)
   const int c0 = crank * cols;
   bool live = true;
 
-  if (owner == rank && (phases & 1)) {
-    // reduce this rank's row t from its inbox, add the residual, RMSNorm, push (out, res) to peers
-    const size_t plane = (size_t)rows_per_rank * N;
-    float ss = 0.f;
-    float4 val[kMaxPer];
+  // Rows are dealt to the gridDim.y clusters (all co-resident: the host caps the grid at the
+  // device's active-cluster capacity).  Every cluster first finishes the rows this rank owns, which
+  // wait only for the GEMMs' words, then receives the peers' rows -- so no cluster waits on work of
+  // a cluster that cannot run.
+  const int own_lo = min(T, rank * rows_per_rank), own_hi = min(T, (rank + 1) * rows_per_rank);
+  if (phases & 1) {
+    for (int t = own_lo + (int)blockIdx.y; t < own_hi; t += gridDim.y) {
+      const int r = t - own_lo;
+      // reduce this rank's row t from its inbox, add the residual, RMSNorm, push (out, res) to peers
+      const size_t plane = (size_t)rows_per_rank * N;
+      float ss = 0.f;
+      float4 val[kMaxPer];
 #pragma unroll
-    for (int k = 0; k < kMaxPer; ++k) {
-      const int col = c0 + (threadIdx.x + k * kThreads) * 4;
-      val[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (col >= c0 + cols) continue;
-      const uint64_t* src = inbox + (size_t)r * N + col;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p = 0; p < W * S; ++p) {
+      for (int k = 0; k < kMaxPer; ++k) {
+        const int col = c0 + (threadIdx.x + k * kThreads) * 4;
+        val[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (col >= c0 + cols) continue;
+        const uint64_t* src = inbox + (size_t)r * N + col;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p = 0; p < W * S; ++p) {
+          uint64_t wv[4];
+          ll_wait4(src + (size_t)p * plane, epoch, limit, live, status, wv);
+          acc.x += __uint_as_float((uint32_t)wv[0]);
+          acc.y += __uint_as_float((uint32_t)wv[1]);
+          acc.z += __uint_as_float((uint32_t)wv[2]);
+          acc.w += __uint_as_float((uint32_t)wv[3]);
+        }
+        const size_t off = (size_t)t * N + col;
+        const uint2 rr = *reinterpret_cast<const uint2*>(res_in + off);
+        const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
+        const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
+        val[k].x = to_f(to_b(acc.x)) + __low2float(r01);
+        val[k].y = to_f(to_b(acc.y)) + __high2float(r01);
+        val[k].z = to_f(to_b(acc.z)) + __low2float(r23);
+        val[k].w = to_f(to_b(acc.w)) + __high2float(r23);
+        ss += val[k].x * val[k].x + val[k].y * val[k].y + val[k].z * val[k].z + val[k].w * val[k].w;
+      }
+      ss = warp_sum(ss);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float a = 0.f;
+        for (int i = 0; i < kThreads / 32; ++i) a += red[i];
+        cta_ss = a;
+      }
+      cluster.sync();
+      float total = 0.f;
+      for (int c = 0; c < kCluster; ++c) total += *cluster.map_shared_rank(&cta_ss, c);
+      cluster.sync();   // peers' shared memory must stay valid until everyone has read it
+      const float inv = rsqrtf(total / N + eps);
+#pragma unroll
+      for (int k = 0; k < kMaxPer; ++k) {
+        const int col = c0 + (threadIdx.x + k * kThreads) * 4;
+        if (col >= c0 + cols) continue;
+        const size_t off = (size_t)t * N + col;
+        const uint2 wr = *reinterpret_cast<const uint2*>(w + col);
+        const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wr.x);
+        const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wr.y);
+        const float v[4] = {val[k].x, val[k].y, val[k].z, val[k].w};
+        const float wv[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
+        bf16 ob[4], sb[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          ob[j] = to_b(to_f(to_b(v[j] * inv)) * wv[j]);
+          sb[j] = to_b(v[j]);
+        }
+        *reinterpret_cast<uint2*>(out + off) = *reinterpret_cast<const uint2*>(ob);
+        *reinterpret_cast<uint2*>(res_out + off) = *reinterpret_cast<const uint2*>(sb);
+        uint64_t word[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t pair = (uint32_t)__bfloat16_as_ushort(ob[j]) | ((uint32_t)__bfloat16_as_ushort(sb[j]) << 16);
+          word[j] = ll_word(pair, epoch);
+        }
+        for (int q = 0; q < W; ++q) {
+          if (q == rank) continue;
+          uint64_t* dst = peers.ag[q] + off;
+          ll_store2(dst, word[0], word[1]);
+          ll_store2(dst + 2, word[2], word[3]);
+        }
+      }
+    }
+  }
+  if (phases & 2) {
+    const int others = T - (own_hi - own_lo);
+    for (int i = (int)blockIdx.y; i < others; i += gridDim.y) {
+      const int t = i < own_lo ? i : i + (own_hi - own_lo);
+      // receive row t from its owner
+#pragma unroll
+      for (int k = 0; k < kMaxPer; ++k) {
+        const int col = c0 + (threadIdx.x + k * kThreads) * 4;
+        if (col >= c0 + cols) continue;
+        const size_t off = (size_t)t * N + col;
         uint64_t wv[4];
-        ll_wait4(src + (size_t)p * plane, epoch, limit, live, status, wv);
-        acc.x += __uint_as_float((uint32_t)wv[0]);
-        acc.y += __uint_as_float((uint32_t)wv[1]);
-        acc.z += __uint_as_float((uint32_t)wv[2]);
-        acc.w += __uint_as_float((uint32_t)wv[3]);
-      }
-      const size_t off = (size_t)t * N + col;
-      const uint2 rr = *reinterpret_cast<const uint2*>(res_in + off);
-      const __nv_bfloat162 r01 = *reinterpret_cast<const __nv_bfloat162*>(&rr.x);
-      const __nv_bfloat162 r23 = *reinterpret_cast<const __nv_bfloat162*>(&rr.y);
-      val[k].x = to_f(to_b(acc.x)) + __low2float(r01);
-      val[k].y = to_f(to_b(acc.y)) + __high2float(r01);
-      val[k].z = to_f(to_b(acc.z)) + __low2float(r23);
-      val[k].w = to_f(to_b(acc.w)) + __high2float(r23);
-      ss += val[k].x * val[k].x + val[k].y * val[k].y + val[k].z * val[k].z + val[k].w * val[k].w;
-    }
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float a = 0.f;
-      for (int i = 0; i < kThreads / 32; ++i) a += red[i];
-      cta_ss = a;
-    }
-    cluster.sync();
-    float total = 0.f;
-    for (int c = 0; c < kCluster; ++c) total += *cluster.map_shared_rank(&cta_ss, c);
-    cluster.sync();   // peers' shared memory must stay valid until everyone has read it
-    const float inv = rsqrtf(total / N + eps);
+        ll_wait4(peers.ag[rank] + off, epoch, limit, live, status, wv);
+        uint16_t ob[4], sb[4];
 #pragma unroll
-    for (int k = 0; k < kMaxPer; ++k) {
-      const int col = c0 + (threadIdx.x + k * kThreads) * 4;
-      if (col >= c0 + cols) continue;
-      const size_t off = (size_t)t * N + col;
-      const uint2 wr = *reinterpret_cast<const uint2*>(w + col);
-      const __nv_bfloat162 w01 = *reinterpret_cast<const __nv_bfloat162*>(&wr.x);
-      const __nv_bfloat162 w23 = *reinterpret_cast<const __nv_bfloat162*>(&wr.y);
-      const float v[4] = {val[k].x, val[k].y, val[k].z, val[k].w};
-      const float wv[4] = {__low2float(w01), __high2float(w01), __low2float(w23), __high2float(w23)};
-      bf16 ob[4], sb[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        ob[j] = to_b(to_f(to_b(v[j] * inv)) * wv[j]);
-        sb[j] = to_b(v[j]);
+        for (int j = 0; j < 4; ++j) {
+          ob[j] = (uint16_t)(wv[j] & 0xffffu);
+          sb[j] = (uint16_t)((wv[j] >> 16) & 0xffffu);
+        }
+        *reinterpret_cast<uint2*>(out + off) = *reinterpret_cast<const uint2*>(ob);
+        *reinterpret_cast<uint2*>(res_out + off) = *reinterpret_cast<const uint2*>(sb);
       }
-      *reinterpret_cast<uint2*>(out + off) = *reinterpret_cast<const uint2*>(ob);
-      *reinterpret_cast<uint2*>(res_out + off) = *reinterpret_cast<const uint2*>(sb);
-      uint64_t word[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t pair = (uint32_t)__bfloat16_as_ushort(ob[j]) | ((uint32_t)__bfloat16_as_ushort(sb[j]) << 16);
-        word[j] = ll_word(pair, epoch);
-      }
-      for (int q = 0; q < W; ++q) {
-        if (q == rank) continue;
-        uint64_t* dst = peers.ag[q] + off;
-        ll_store2(dst, word[0], word[1]);
-        ll_store2(dst + 2, word[2], word[3]);
-      }
-    }
-  } else if (owner != rank && (phases & 2)) {
-    // receive row t from its owner
-#pragma unroll
-    for (int k = 0; k < kMaxPer; ++k) {
-      const int col = c0 + (threadIdx.x + k * kThreads) * 4;
-      if (col >= c0 + cols) continue;
-      const size_t off = (size_t)t * N + col;
-      uint64_t wv[4];
-      ll_wait4(peers.ag[rank] + off, epoch, limit, live, status, wv);
-      uint16_t ob[4], sb[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        ob[j] = (uint16_t)(wv[j] & 0xffffu);
-        sb[j] = (uint16_t)((wv[j] >> 16) & 0xffffu);
-      }
-      *reinterpret_cast<uint2*>(out + off) = *reinterpret_cast<const uint2*>(ob);
-      *reinterpret_cast<uint2*>(res_out + off) = *reinterpret_cast<const uint2*>(sb);
     }
   }
   // the launch that completes the call advances the epoch once every CTA has read it
@@ -294,6 +309,29 @@ __global__ void __launch_bounds__(512) vocab_argmax_exchange_kernel(const PeerPt
 
 int* status_ptr(const at::Tensor& status);
 
+namespace {
+// Clusters of the finishing kernel that can be resident at once on the current device (every one
+// of them must be, since clusters wait on each other's rows across GPUs); cached per device.
+int64_t finish_cluster_capacity() {
+  static std::mutex mu;
+  static std::unordered_map<int, int64_t> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kCluster, 1024);
+  cfg.blockDim = dim3(kThreads);
+  int n = 0;
+  auto e = cudaOccupancyMaxActiveClusters(&n, row_parallel_finish_kernel, &cfg);
+  LSB_CHECK(e == cudaSuccess && n > 0, std::string("cluster occupancy query failed: ") + cudaGetErrorString(e));
+  const int64_t cap = std::max<int64_t>(1, n / 2);   // half: room for the kernels PDL overlaps with it
+  cache.emplace(dev, cap);
+  return cap;
+}
+}  // namespace
+
 // ---- host: symmetric buffers via CUDA IPC -------------------------------------------------------
 int64_t comm_alloc(int64_t nbytes) {
   void* p = nullptr;
@@ -348,8 +386,8 @@ void row_parallel_finish(std::vector<int64_t> ag, int64_t inbox, int64_t ctrl, i
   if (T == 0) return;
   PeerAg p = {};
   for (int r = 0; r < W; ++r) p.ag[r] = reinterpret_cast<uint64_t*>(ag[r]);
-  dim3 grid(kCluster, (unsigned)T);
   const at::cuda::CUDAGuard g(res_in.device());
+  dim3 grid(kCluster, (unsigned)std::min<int64_t>(T, finish_cluster_capacity()));
   launch_pdl(row_parallel_finish_kernel, grid, dim3(kThreads), 0, at::cuda::getCurrentCUDAStream(), p,
              reinterpret_cast<const uint64_t*>(inbox), reinterpret_cast<uint32_t*>(ctrl), reinterpret_cast<bf16*>(out),
              reinterpret_cast<bf16*>(res_out), (const bf16*)res_in.data_ptr(), (const bf16*)w.data_ptr(), (int)rank,

@@ -5,9 +5,11 @@
 // One CTA computes two 128-row query tiles ("A" and "B", UMMA M = 128 each) of one head against
 // shared 64-key K/V tiles, so the tensor pipe always has one tile's MMAs to run while the other
 // tile's softmax warps work:
-//   warp 8, lane 0 : TMA producer.  Q of both tiles once (64-column halves, 128B swizzle), then K
-//                    and V of each 64-key tile into a 3-stage ring; a K/V tile is assembled from
-//                    per-block boxes of min(block_size, 64) keys, so pages need not be contiguous.
+//   warps 8 / 10, lane 0 : TMA producers.  Warp 8: Q of both tiles once (64-column halves, 128B
+//                    swizzle), then K of each 64-key tile into a 4-stage ring freed as soon as the
+//                    tile's S MMAs are done; warp 10: V into a 3-stage ring freed after the PV MMAs.
+//                    A K/V tile is assembled from per-block boxes of min(block_size, 64) keys, so
+//                    pages need not be contiguous; loads run three to four tiles ahead.
 //   warp 9, lane 0 : MMA issuer.  S_t(j) = Q_t K_j^T into one of two TMEM S buffers per tile (both
 //                    operands K-major); O_t += P_t(j) V_j (P K-major from shared memory, V read
 //                    MN-major straight from its TMA tile).  Order: PV_A(j), PV_B(j), then S_A(j+2),
@@ -49,8 +51,9 @@ namespace {
 constexpr int kBQ = 128;        // query rows per tile (UMMA M)
 constexpr int kQTiles = 2;      // query tiles per CTA, one softmax warpgroup each
 constexpr int kBKV = 64;        // keys per K/V tile
-constexpr int kStages = 3;      // K/V ring depth
-constexpr int kThreads = 320;   // 8 softmax warps + producer warp + MMA warp
+constexpr int kStagesK = 4;     // K ring depth (a K tile is free once both S MMAs of its tile are done)
+constexpr int kStagesV = 3;     // V ring depth (a V tile is free once both PV MMAs of its tile are done)
+constexpr int kThreads = 352;   // 8 softmax warps + K producer warp + MMA warp + V producer warp
 constexpr float kRescaleLog2 = 8.f;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -61,10 +64,10 @@ struct PfLayout {
   static constexpr int kQTile = kHalves * kQHalf;
   static constexpr int kKVHalf = kBKV * 128;              // 8 KiB
   static constexpr int kTileBytes = kHalves * kKVHalf;    // K (or V) of one tile
-  static constexpr int kStageBytes = 2 * kTileBytes;      // K | V
   static constexpr int kPBytes = kBQ * kBKV * 2;          // 16 KiB, one 128-byte row per query
-  static constexpr int kStageOff = kQTiles * kQTile;
-  static constexpr int kPOff = kStageOff + kStages * kStageBytes;
+  static constexpr int kKOff = kQTiles * kQTile;
+  static constexpr int kVOff = kKOff + kStagesK * kTileBytes;
+  static constexpr int kPOff = kVOff + kStagesV * kTileBytes;
   static constexpr int kBarOff = kPOff + kQTiles * kPBytes;
   static constexpr int kBytes = kBarOff + 256 + 1024;     // barriers + alignment slack
   // TMEM columns: O_t at 128 t; S_t buffers at 256 + 128 t + 64 b
@@ -168,16 +171,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars;                         // 1
-  uint64_t* k_full = bars + 1;                     // kStages
-  uint64_t* v_full = k_full + kStages;             // kStages
-  uint64_t* kv_empty = v_full + kStages;           // kStages
-  uint64_t* s_full = kv_empty + kStages;           // [tile][buffer]: 4
+  uint64_t* k_full = bars + 1;                     // kStagesK
+  uint64_t* k_empty = k_full + kStagesK;           // kStagesK
+  uint64_t* v_full = k_empty + kStagesK;           // kStagesV
+  uint64_t* v_empty = v_full + kStagesV;           // kStagesV
+  uint64_t* s_full = v_empty + kStagesV;           // [tile][buffer]: 4
   uint64_t* s_free = s_full + 4;                   // 4
   uint64_t* p_full = s_free + 4;                   // [tile]: 2
   uint64_t* o_done = p_full + 2;                   // [tile]: 2 (one phase per PV of the tile)
   uint64_t* drain = o_done + 2;                    // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);   // byte 184 of the barrier block
-  uint64_t* bad_keys = reinterpret_cast<uint64_t*>(smem + L::kBarOff + 208);   // kStages masks
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);   // byte 224 of the barrier block (28 barriers)
+  uint64_t* bad_keys = reinterpret_cast<uint64_t*>(smem + L::kBarOff + 232);   // kStagesV masks, to byte 256
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
 
@@ -208,10 +212,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(q_full, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kStagesK; ++s) {
       mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kStagesV; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
@@ -234,21 +241,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
-    // ---------------- TMA producer ----------------
+  if (warp == 8 || warp == 10) {
+    // ---------------- TMA producers: warp 8 Q and K, warp 10 V ----------------
+    const bool is_k = warp == 8;
     if (lane == 0 && ntiles > 0) {
-      mbar_expect_tx(q_full, kQTiles * L::kQTile);
+      if (is_k) {
+        mbar_expect_tx(q_full, kQTiles * L::kQTile);
 #pragma unroll
-      for (int t = 0; t < kQTiles; ++t)
+        for (int t = 0; t < kQTiles; ++t)
 #pragma unroll
-        for (int hf = 0; hf < L::kHalves; ++hf)
-          tma_2d(smem + t * L::kQTile + hf * L::kQHalf, &tm_q, q_full, h * HD + hf * 64,
-                 q0 + (qp * kQTiles + t) * kBQ);
-      int issued[kStages] = {};
+          for (int hf = 0; hf < L::kHalves; ++hf)
+            tma_2d(smem + t * L::kQTile + hf * L::kQHalf, &tm_q, q_full, h * HD + hf * 64,
+                   q0 + (qp * kQTiles + t) * kBQ);
+      }
+      const int nst = is_k ? kStagesK : kStagesV;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      const CUtensorMap* map = is_k ? &tm_k : &tm_v;
+      int issued[kStagesK] = {};
       for (int j = 0; j < ntiles; ++j) {
-        const int s = j % kStages, u = j / kStages;
-        if (u >= 1 && !wait_phase(&kv_empty[s], (u - 1) & 1, abort_v, status, kTimeoutSmemEmpty)) break;
-        uint8_t* stage = smem + L::kStageOff + s * L::kStageBytes;
+        const int s = j % nst, u = j / nst;
+        if (u >= 1 && !wait_phase(&empty[s], (u - 1) & 1, abort_v, status, kTimeoutSmemEmpty)) break;
+        uint8_t* stage = smem + (is_k ? L::kKOff : L::kVOff) + s * L::kTileBytes;
         const int k0 = j * kBKV;
         uint64_t bad = 0;
         const int segs = kBKV / box_keys;
@@ -259,35 +273,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
           if (kp < kend) {
             blk = bt[kp / bs];
             if (blk < 0 || blk >= nblk) {
-              record_error(status, kBadIndex);
+              if (!is_k) record_error(status, kBadIndex);
               blk = 0;
               bad |= (box_keys == 64 ? ~0ull : (((1ull << box_keys) - 1) << (g * box_keys)));
             }
           }
           rows[g] = (blk * nkv + kvh) * bs + kp % bs;
         }
-        bad_keys[s] = bad;       // published to the softmax warps by the v_full arrival below
-        mbar_expect_tx(&k_full[s], L::kTileBytes);
+        if (!is_k) bad_keys[s] = bad;   // published to the softmax warps by the v_full arrival below
+        mbar_expect_tx(&full[s], L::kTileBytes);
         for (int g = 0; g < segs; ++g)
 #pragma unroll
           for (int hf = 0; hf < L::kHalves; ++hf)
-            tma_2d(stage + hf * L::kKVHalf + g * box_keys * 128, &tm_k, &k_full[s], hf * 64, rows[g]);
-        mbar_expect_tx(&v_full[s], L::kTileBytes);
-        for (int g = 0; g < segs; ++g)
-#pragma unroll
-          for (int hf = 0; hf < L::kHalves; ++hf)
-            tma_2d(stage + L::kTileBytes + hf * L::kKVHalf + g * box_keys * 128, &tm_v, &v_full[s], hf * 64,
-                   rows[g]);
+            tma_2d(stage + hf * L::kKVHalf + g * box_keys * 128, map, &full[s], hf * 64, rows[g]);
         issued[s] = u + 1;
       }
       // drain: every stage's most recent copies have landed before this CTA may exit
-      mbar_wait(q_full, 0);
-      for (int s = 0; s < kStages; ++s) {
-        if (issued[s] > 0) {
-          mbar_wait(&k_full[s], (issued[s] - 1) & 1);
-          mbar_wait(&v_full[s], (issued[s] - 1) & 1);
-        }
-      }
+      if (is_k) mbar_wait(q_full, 0);
+      for (int s = 0; s < nst; ++s)
+        if (issued[s] > 0) mbar_wait(&full[s], (issued[s] - 1) & 1);
     }
     __syncwarp();
   } else if (warp == 9) {
@@ -299,11 +303,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       bool ok = wait_phase(q_full, 0, abort_v, status, kTimeoutTmaFull);
       // S_t(j) into buffer j & 1 of tile t
       auto issue_s = [&](int t, int j) -> bool {
-        const int s = j % kStages, u = j / kStages, b = j & 1, ub = j >> 1;
+        const int s = j % kStagesK, u = j / kStagesK, b = j & 1, ub = j >> 1;
         if (!wait_phase(&k_full[s], u & 1, abort_v, status, kTimeoutTmaFull)) return false;
         if (ub >= 1 && !wait_phase(&s_free[t * 2 + b], (ub - 1) & 1, abort_v, status, kTimeoutAccum)) return false;
         fence_after();
-        const uint32_t k_addr = smem_u32(smem + L::kStageOff + s * L::kStageBytes);
+        const uint32_t k_addr = smem_u32(smem + L::kKOff + s * L::kTileBytes);
         const uint32_t qa = q_addr + t * L::kQTile;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -312,16 +316,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
               desc_kmajor(k_addr + hf * L::kKVHalf + c * 32), id_s, kk != 0);
         }
         commit(&s_full[t * 2 + b]);
+        // the K tile is free once the S MMAs of every query tile that uses it are done
+        if (t == kQTiles - 1 || j >= nt[kQTiles - 1]) commit(&k_empty[s]);
         return true;
       };
       // O_t += P_t(j) V_j
       auto issue_pv = [&](int t, int j) -> bool {
-        const int s = j % kStages, u = j / kStages;
+        const int s = j % kStagesV, u = j / kStagesV;
         if (!wait_phase(&p_full[t], j & 1, abort_v, status, kTimeoutAccum)) return false;
         if (!wait_phase(&v_full[s], u & 1, abort_v, status, kTimeoutTmaFull)) return false;
         fence_after();
         const uint32_t p_addr = smem_u32(smem + L::kPOff + t * L::kPBytes);
-        const uint32_t v_addr = smem_u32(smem + L::kStageOff + s * L::kStageBytes + L::kTileBytes);
+        const uint32_t v_addr = smem_u32(smem + L::kVOff + s * L::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < kBKV / 16; ++kk)
           mma(tmem + t * 128, desc_kmajor(p_addr + kk * 32), desc_mnmajor(v_addr + kk * 16 * 128, L::kKVHalf),
@@ -336,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
         for (int t = 0; ok && t < kQTiles; ++t)
           if (j < nt[t]) ok = issue_pv(t, j);
         if (!ok) break;
-        commit(&kv_empty[j % kStages]);          // every MMA reading tile j's stage was issued
+        commit(&v_empty[j % kStagesV]);          // every MMA reading V tile j was issued
         for (int t = 0; ok && t < kQTiles; ++t)
           if (j + 2 < nt[t]) ok = issue_s(t, j + 2);
       }
@@ -368,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
     break;                                                                               \
   }
     for (int j = 0; j < n_me; ++j) {
-      const int s = j % kStages, u = j / kStages, b = j & 1, ub = j >> 1;
+      const int s = j % kStagesV, u = j / kStagesV, b = j & 1, ub = j >> 1;
       LSB_WAIT_ALL(&s_full[t * 2 + b], ub & 1, kTimeoutAccum);
       fence_after();
       uint32_t raw[kBKV];
@@ -436,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       // zero the V rows of keys no query may see (past the context, or from a bad block)
       if (k0 + kBKV > kend || bad != 0ull) {
-        uint8_t* vt = smem + L::kStageOff + s * L::kStageBytes + L::kTileBytes;
+        uint8_t* vt = smem + L::kVOff + s * L::kTileBytes;
         for (int idx = r; idx < kBKV * L::kHalves * 8; idx += kBQ) {
           const int key = idx / (L::kHalves * 8), rem = idx % (L::kHalves * 8);
           const int hf = rem / 8, ch = rem % 8;

@@ -73,8 +73,9 @@ def test_step_timeline_exclusive_time_and_gaps():
 def test_fused_collective_roofline_terms():
     from benchmarks.collective_profile import fused_roofline_us
     r = fused_roofline_us(T=64, hidden=4096, inner_shard=512, world=8, planes=1, hbm_gbs=6553.0, bf16_tflops=1655.0)
-    # weights 4096 x 512 bf16 = 4 MiB at 6553 GB/s; NVLink: 7 peers x 8 rows x 4096 x (4 + 4) B
-    assert r["weight_bytes"] == 4096 * 512 * 2 and r["nvlink_bytes"] == 7 * 8 * 4096 * 8
+    # weights 4096 x 512 bf16 = 4 MiB at 6553 GB/s; NVLink, 8-byte words: 56 other rows' partials
+    # to their owners + this rank's 8 rows to 7 peers
+    assert r["weight_bytes"] == 4096 * 512 * 2 and r["nvlink_bytes"] == 56 * 4096 * 8 + 7 * 8 * 4096 * 8
     assert abs(r["hbm_us"] - 4096 * 512 * 2 / 6553e3) < 1e-9
     assert r["roofline_us"] == max(r["hbm_us"], r["compute_us"], r["nvlink_us"])
 
