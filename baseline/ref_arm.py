@@ -107,7 +107,7 @@ def make_eagle3_checkpoint() -> str:
     return path
 
 
-def run(args, metric: str, window_latency):
+def run(args, metric: str, window_latency, clocks=None):
     rank = int(os.environ.get("RANK", 0))
     if rank > 0:
         return          # the reference spawns its own tensor-parallel workers from rank 0
@@ -162,6 +162,10 @@ def run(args, metric: str, window_latency):
         outs, _ = llm.step()
         active -= len(outs)
         refill()
+    # the clock sampler (this repo's bench.ClockSampler: read-only NVML queries on a thread) starts
+    # before the window opens, as in the llmserve_b200 arm
+    if clocks is not None:
+        clocks.__enter__()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     tok0 = tokens()
@@ -174,6 +178,8 @@ def run(args, metric: str, window_latency):
     end.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - t0
+    if clocks is not None:
+        clocks.__exit__(None, None, None)
     ms = start.elapsed_time(end)
     n = tokens() - tok0
     # the same latency window as the llmserve_b200 arm: one full wave of requests admitted after
@@ -210,4 +216,6 @@ def run(args, metric: str, window_latency):
         | {"step_latency_p50_ms": None if (m.get("speculative_step_latency") or {}).get("p50") is None
            else round(m["speculative_step_latency"]["p50"] * 1e3, 3)},
         "timing": "CUDA events on the reference's rank-0 device", "checkpoint_write_s": round(t_ckpt, 1),
+        "clocks": clocks.summary() if clocks is not None else {"sm_mhz": None, "sm_max_mhz": None,
+                                                              "reasons": ["unsampled"]},
     }), flush=True)

@@ -248,12 +248,13 @@ def run_ours(args):
     # the timed window: a barrier + synchronize on every rank on both sides; the step in flight from
     # the warm-up (overlapped loop) completes before the start mark, so the window holds the GPU work
     # of exactly the timed steps' launches
-    runner.call("mark_event", "bench_start", "before")
-    tok0 = tokens_so_far()
-    h2d0, d2h0 = runner.h2d_bytes, runner.d2h_bytes
-    if args.profile_range:
-        torch.cuda.profiler.start()
+    # the clock sampler starts (NVML set-up) before the window opens, so its set-up is in neither clock
     with ClockSampler(visible_indices(world)) as clocks:
+        runner.call("mark_event", "bench_start", "before")
+        tok0 = tokens_so_far()
+        h2d0, d2h0 = runner.h2d_bytes, runner.d2h_bytes
+        if args.profile_range:
+            torch.cuda.profiler.start()
         t0 = time.perf_counter()
         for _ in range(args.steps):
             outs, _ = llm.step()
@@ -338,7 +339,7 @@ def run_reference(args):
         return
     sys.path.insert(0, os.path.join(ROOT, "baseline"))
     from ref_arm import run as ref_run  # noqa: E402
-    ref_run(args, METRIC, window_latency)
+    ref_run(args, METRIC, window_latency, ClockSampler(visible_indices(1)))
 
 
 def main():

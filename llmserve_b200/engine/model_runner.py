@@ -346,8 +346,9 @@ class ModelRunner:
             max_ctx = -(-(cfg.max_model_len + cfg.speculative_gamma + 16) // self.block_size) * self.block_size
             heads = max(hf.num_attention_heads // self.world_size,
                         self.draft_model.num_heads if self.draft_model is not None else 0)
-            self.decode_workspace = attn_ops.DecodeWorkspace(
-                max(cfg.max_num_seqs, 16), heads, hf.head_dim, max_ctx, self.device)
+            # rows: one per sequence for decode, gamma + 1 per sequence for a packed EAGLE3 verify
+            rows = cfg.max_num_seqs * (cfg.speculative_gamma + 1 if self.draft_model is not None else 1)
+            self.decode_workspace = attn_ops.DecodeWorkspace(max(rows, 16), heads, hf.head_dim, max_ctx, self.device)
 
     # ---- prefill/decode disaggregation: KV pools shared across processes ---------------------
     def _exportable_pools(self, shape, key: str):

@@ -273,7 +273,8 @@ class SpeculativeExecutor:
         set_context(True, cu_seqlens_q=torch.arange(0, (B + 1) * n, n, dtype=torch.int32, device=dev),
                     max_seqlen_q=n, max_seqlen_k=max(base) + n, slot_mapping=vslots,
                     block_tables=r.prepare_block_tables(seqs),
-                    seqlens_k=torch.tensor([b + n for b in base], dtype=torch.int32, device=dev))
+                    seqlens_k=torch.tensor([b + n for b in base], dtype=torch.int32, device=dev),
+                    uniform_q=n, decode_workspace=r.decode_workspace)
         try:
             with nvtx_range("verify"):
                 hidden, aux = r.model.forward_with_eagle3_aux(vin, vpos)

@@ -100,7 +100,7 @@ class SpeculativeGraphs:
             cur_ids, cur_in = nxt, hidden
         vin = torch.cat([self.ids[:B].unsqueeze(1), self.drafts[:B]], 1).reshape(-1)
         set_context(True, cu_seqlens_q=self.cu_q[:B + 1], max_seqlen_q=n, slot_mapping=vslot,
-                    block_tables=tables, seqlens_k=seqk)
+                    block_tables=tables, seqlens_k=seqk, uniform_q=n, decode_workspace=r.decode_workspace)
         try:
             hidden, aux = r.model.forward_with_eagle3_aux(vin, vpos.long())
             logits = r.model.compute_logits(hidden, all_tokens=True)

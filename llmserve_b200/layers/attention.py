@@ -37,7 +37,11 @@ class Attention(nn.Module):
         q, _, _ = rope_ops.qkv_norm_rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, eps,
                                                self.k_cache, self.v_cache, ctx.slot_mapping,
                                                self.num_heads, self.num_kv_heads, self.head_dim)
-        if ctx.is_prefill:
+        if ctx.is_prefill and ctx.uniform_q and q.is_cuda and attn_ops.verify_fits_decode_kernel(
+                ctx.uniform_q, self.num_heads, self.num_kv_heads, self.k_cache.shape[2], self.head_dim):
+            o = attn_ops.verify_attention(q, self.k_cache, self.v_cache, ctx.block_tables, ctx.seqlens_k, self.scale,
+                                          ctx.uniform_q, ctx.decode_workspace)
+        elif ctx.is_prefill:
             o = attn_ops.prefill_attention(q, self.k_cache, self.v_cache, ctx.cu_seqlens_q, ctx.seqlens_k,
                                            ctx.block_tables, self.scale, ctx.max_seqlen_q)
         else:

@@ -130,12 +130,39 @@ def decode_attention(q, k_cache, v_cache, block_tables, context_lens, scale, wor
     if _DECODE_TMA and C().decode_tma_supported(k_cache.shape[2], hd):
         C().decode_attention_tma(out, q.contiguous(), k_cache, v_cache, block_tables, context_lens, float(scale),
                                  workspace.partial_out, workspace.partial_ml, workspace.counters,
-                                 workspace.max_splits, tma_partition(B, k_cache.shape[1]), status(q.device))
+                                 workspace.max_splits, tma_partition(B, k_cache.shape[1]), 1, status(q.device))
         return out
     part = decode_partition(B, k_cache.shape[1])
     C().decode_attention(out, q.contiguous(), k_cache, v_cache, block_tables, context_lens, float(scale),
                          workspace.partial_out, workspace.partial_ml, workspace.counters,
                          -(-workspace.max_splits * 128 // part), part, 0, status(q.device))
+    return out
+
+
+def verify_fits_decode_kernel(nq: int, num_heads: int, num_kv_heads: int, block_size: int, head_dim: int) -> bool:
+    """Whether a packed verify chunk of ``nq`` queries per sequence runs on the TMA decode kernel:
+    every (query, head) row of a KV head in one 16-row MMA tile."""
+    return (_DECODE_TMA and nq >= 1 and nq * (num_heads // num_kv_heads) <= 16
+            and C().decode_tma_supported(block_size, head_dim))
+
+
+def verify_attention(q, k_cache, v_cache, block_tables, seqlens_k, scale, nq: int, workspace=None):
+    """Causal attention of ``nq`` consecutive new tokens per sequence (an EAGLE3 verify chunk,
+    ``q [B * nq, nh, hd]``, sequence b's tokens at positions ``seqlens_k[b] - nq ..``) against the
+    paged pool, on the TMA decode kernel: the (query, head) rows of one KV head share an MMA tile,
+    so every K/V byte is read once per KV head instead of once per query head."""
+    T, nh, hd = q.shape
+    B = T // nq
+    if not q.is_cuda:
+        cu = torch.arange(0, (B + 1) * nq, nq, dtype=torch.int32)
+        return prefill_attention_ref(q, k_cache, v_cache, cu, seqlens_k, block_tables, scale)
+    cap = block_tables.shape[1] * k_cache.shape[2]
+    if workspace is None or workspace.max_batch < T or workspace.max_splits * 128 < cap:
+        workspace = DecodeWorkspace(T, nh, hd, cap, q.device)
+    out = torch.empty_like(q)
+    C().decode_attention_tma(out, q.contiguous(), k_cache, v_cache, block_tables, seqlens_k, float(scale),
+                             workspace.partial_out, workspace.partial_ml, workspace.counters,
+                             workspace.max_splits, tma_partition(B, k_cache.shape[1]), int(nq), status(q.device))
     return out
 
 

@@ -58,7 +58,8 @@ void gemm_bf16_packed(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, at:
                       at::Tensor status, int64_t max_stages);
 void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
                           at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml,
-                          at::Tensor counters, int64_t max_splits, int64_t partition, at::Tensor status);
+                          at::Tensor counters, int64_t max_splits, int64_t partition, int64_t nq,
+                          at::Tensor status);
 bool decode_tma_supported(int64_t block_size, int64_t head_dim);
 bool prefill_tc_supported(int64_t block_size, int64_t head_dim);
 void prefill_attention_tc(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,

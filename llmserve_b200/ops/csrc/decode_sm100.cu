@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
     const bf16* __restrict__ q, const int* __restrict__ block_tables, int bt_stride,
     const int* __restrict__ context_lens, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml,
     int* __restrict__ counters, int max_splits, int partition, int max_chunks, int B, int nh, int nkv, int bs,
-    int box_rows, int nblk, int* __restrict__ status) {
+    int box_rows, int nblk, int nq, int* __restrict__ status) {
   using LY = DecLayout<HD>;
   constexpr int S = LY::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -207,8 +207,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
             *aborted = 1;
             break;
           }
-          // the previous kernel writes the newest position's K/V: wait for it before that stage
-          if (!waited && st + kDecKeys > ctx - 1) {
+          // the previous kernel writes the newest nq positions' K/V: wait for it before those stages
+          if (!waited && st + kDecKeys > ctx - nq) {
             pdl_wait();
             waited = true;
           }
@@ -249,10 +249,11 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
 
   // ---------------- consumers ----------------
   pdl_wait();
-  float* so = reinterpret_cast<float*>(smem + LY::kMergeOff);   // [4 warps][G rows][HD]
-  float* sm = so + 4 * G * HD;
+  float* so = reinterpret_cast<float*>(smem + LY::kMergeOff);   // [4 warps][nq * G rows][HD]
+  float* sm = so + 4 * nq * G * HD;
   float* sl = sm + 64;
   const int g = lane >> 2, c2 = (lane & 3) * 2;
+  const int R = nq * G;            // tile rows: (query i, head gg) at row i * G + gg
   uint32_t gphase = 0;
   int it = 0;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -262,22 +263,27 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
     const int ks = chunk * partition;
     if (ks >= ctx) {
       if (chunk == 0 && warp == 0)   // empty context: defined output
-        for (int i = lane; i < G * HD; i += 32) out[((size_t)b * nh + kvh * G) * HD + i] = to_b(0.f);
+        for (int i = lane; i < R * HD; i += 32) {
+          const int r = i / HD;
+          out[((size_t)(b * nq + r / G) * nh + kvh * G + r % G) * HD + i % HD] = to_b(0.f);
+        }
       continue;
     }
     const int ke = min(ks + partition, ctx);
     const int nchunks = (ctx + partition - 1) / partition;
 
+    // query i of sequence b at absolute position ctx - nq + i sees keys [0, ctx - nq + i]
+    const int limA = min(ke, ctx - nq + g / G + 1), limB = min(ke, ctx - nq + (g + 8) / G + 1);
     uint32_t qa[HD / 16][4];
     {
       const int r0 = lane >> 2, c = (lane & 3) * 2;
-      const bf16* qb = q + ((size_t)b * nh + kvh * G) * HD;
 #pragma unroll
       for (int kk = 0; kk < HD / 16; ++kk) {
         const int col = kk * 16 + c;
         auto ld = [&](int r, int cc) -> uint32_t {
-          if (r >= G) return 0u;
-          return *reinterpret_cast<const uint32_t*>(qb + (size_t)r * HD + cc);
+          if (r >= R) return 0u;
+          const bf16* qr = q + ((size_t)(b * nq + r / G) * nh + kvh * G + r % G) * HD;
+          return *reinterpret_cast<const uint32_t*>(qr + cc);
         };
         qa[kk][0] = ld(r0, col);
         qa[kk][1] = ld(r0 + 8, col);
@@ -317,8 +323,9 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int kp = kb + (i & 1);
-        s0[i] = kp < ke ? s0[i] * scale_log2 : -INFINITY;
-        s1[i] = kp + 8 < ke ? s1[i] * scale_log2 : -INFINITY;
+        const int lim = i < 2 ? limA : limB;
+        s0[i] = kp < lim ? s0[i] * scale_log2 : -INFINITY;
+        s1[i] = kp + 8 < lim ? s1[i] * scale_log2 : -INFINITY;
       }
       softmax_pv_t<HD>(s0, s1, m, l, o, vt, key0);
       __syncwarp();
@@ -334,18 +341,18 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
       l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
     }
     if (!group_sync(group, gphase, status)) return;   // previous item's merge reads are done
-    if (g < G) {
+    if (g < R) {
 #pragma unroll
       for (int n = 0; n < HD / 8; ++n) {
-        so[(warp * G + g) * HD + n * 8 + c2] = o[n][0];
-        so[(warp * G + g) * HD + n * 8 + c2 + 1] = o[n][1];
+        so[(warp * R + g) * HD + n * 8 + c2] = o[n][0];
+        so[(warp * R + g) * HD + n * 8 + c2 + 1] = o[n][1];
       }
     }
-    if (g + 8 < G) {
+    if (g + 8 < R) {
 #pragma unroll
       for (int n = 0; n < HD / 8; ++n) {
-        so[(warp * G + g + 8) * HD + n * 8 + c2] = o[n][2];
-        so[(warp * G + g + 8) * HD + n * 8 + c2 + 1] = o[n][3];
+        so[(warp * R + g + 8) * HD + n * 8 + c2] = o[n][2];
+        so[(warp * R + g + 8) * HD + n * 8 + c2 + 1] = o[n][3];
       }
     }
     if ((lane & 3) == 0) {
@@ -355,8 +362,9 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
       sl[warp * 16 + g + 8] = l[1];
     }
     if (!group_sync(group, gphase, status)) return;
-    for (int idx = threadIdx.x; idx < G * HD; idx += 128) {
+    for (int idx = threadIdx.x; idx < R * HD; idx += 128) {
       const int r = idx / HD, d = idx % HD;
+      const size_t qrow = (size_t)b * nq + r / G;   // output row of query r / G
       float M = -INFINITY;
 #pragma unroll
       for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
@@ -366,13 +374,13 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
       for (int w = 0; w < 4; ++w) {
         const float f = exp2f(sm[w * 16 + r] - Mu);
         L += sl[w * 16 + r] * f;
-        O += so[(w * G + r) * HD + d] * f;
+        O += so[(w * R + r) * HD + d] * f;
       }
-      const int h = kvh * G + r;
+      const int h = kvh * G + r % G;
       if (nchunks == 1) {
-        out[((size_t)b * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
+        out[(qrow * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
       } else {
-        const size_t base = ((size_t)b * nh + h) * max_splits + chunk;
+        const size_t base = (qrow * nh + h) * max_splits + chunk;
         part_o[base * HD + d] = O;
         if (d == 0) {
           part_ml[base * 2] = M;
@@ -393,10 +401,11 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
     if (!group_sync(group, gphase, status)) return;
     if (!is_last) continue;
     __threadfence();
-    for (int idx = threadIdx.x; idx < G * HD; idx += 128) {
+    for (int idx = threadIdx.x; idx < R * HD; idx += 128) {
       const int r = idx / HD, d = idx % HD;
-      const int h = kvh * G + r;
-      const size_t base = ((size_t)b * nh + h) * max_splits;
+      const size_t qrow = (size_t)b * nq + r / G;
+      const int h = kvh * G + r % G;
+      const size_t base = (qrow * nh + h) * max_splits;
       float M = -INFINITY;
       for (int sp = 0; sp < nchunks; ++sp) M = fmaxf(M, __ldcg(&part_ml[(base + sp) * 2]));
       const float Mu = M == -INFINITY ? 0.f : M;
@@ -406,7 +415,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
         L += __ldcg(&part_ml[(base + sp) * 2 + 1]) * f;
         O += __ldcg(&part_o[(base + sp) * HD + d]) * f;
       }
-      out[((size_t)b * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
+      out[(qrow * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
     }
   }
 }
@@ -465,23 +474,30 @@ bool decode_tma_supported(int64_t block_size, int64_t head_dim) {
   return (head_dim == 64 || head_dim == 128) && block_size % 8 == 0 && (block_size % 64 == 0 || 64 % block_size == 0);
 }
 
+// q / out: bf16 [B * nq, nh, hd] -- nq consecutive query rows per sequence (nq = 1: decode; nq > 1:
+// a packed verify chunk at the last nq positions of each context, causal among themselves), with
+// nq * (nh / nkv) <= 16 so all of a (sequence, kv head)'s rows share one MMA tile.
 void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_tables,
                           at::Tensor context_lens, double scale, at::Tensor part_o, at::Tensor part_ml,
-                          at::Tensor counters, int64_t max_splits, int64_t partition, at::Tensor status) {
+                          at::Tensor counters, int64_t max_splits, int64_t partition, int64_t nq,
+                          at::Tensor status) {
   TORCH_CHECK(kc.dim() == 4 && vc.sizes() == kc.sizes() && kc.is_contiguous() && vc.is_contiguous() &&
                   kc.scalar_type() == at::kBFloat16 && vc.scalar_type() == at::kBFloat16,
               "llmserve_b200: KV pools must be contiguous bf16 [blocks, kv_heads, block_size, head_dim]");
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "llmserve_b200: q must be bf16 [B, nh, hd]");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.is_contiguous(), "llmserve_b200: block_tables int32");
   TORCH_CHECK(context_lens.scalar_type() == at::kInt && counters.scalar_type() == at::kInt, "llmserve_b200: int32 lens/counters");
-  const int B = q.size(0), nh = q.size(1), hd = q.size(2), nkv = kc.size(1), bs = kc.size(2);
-  TORCH_CHECK(kc.size(3) == hd && nh % nkv == 0 && nh / nkv <= 16, "llmserve_b200: head layout unsupported (group size <= 16)");
+  TORCH_CHECK(nq >= 1 && q.size(0) % nq == 0, "llmserve_b200: q rows must be a multiple of nq");
+  const int B = q.size(0) / nq, nh = q.size(1), hd = q.size(2), nkv = kc.size(1), bs = kc.size(2);
+  TORCH_CHECK(kc.size(3) == hd && nh % nkv == 0 && nq * (nh / nkv) <= 16,
+              "llmserve_b200: head layout unsupported (queries x group size <= 16)");
   TORCH_CHECK(decode_tma_supported(bs, hd), "llmserve_b200: block size / head dim unsupported by the TMA decode kernel");
   TORCH_CHECK(partition % kDecKeys == 0 && partition > 0, "llmserve_b200: partition must be a multiple of 64");
   const int64_t cap = block_tables.size(1) * (int64_t)bs;
   const int max_chunks = (int)((cap + partition - 1) / partition);
   TORCH_CHECK(max_chunks <= max_splits, "llmserve_b200: workspace has too few splits");
-  TORCH_CHECK(part_o.numel() >= (int64_t)B * nh * max_splits * hd && part_ml.numel() >= (int64_t)B * nh * max_splits * 2,
+  TORCH_CHECK(part_o.numel() >= (int64_t)B * nq * nh * max_splits * hd &&
+                  part_ml.numel() >= (int64_t)B * nq * nh * max_splits * 2,
               "llmserve_b200: decode workspace too small");
   TORCH_CHECK(counters.numel() >= (int64_t)B * nkv, "llmserve_b200: decode counters too small");
   TORCH_CHECK((int64_t)kc.numel() / hd < (int64_t)INT32_MAX, "llmserve_b200: KV pool rows exceed int32");
@@ -497,7 +513,7 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
   int* st = status_ptr(status);
 #define LSB_DEC_TMA(HD)                                                                                             \
   do {                                                                                                              \
-    const int smem = DecLayout<HD>::smem_bytes(G);                                                                  \
+    const int smem = DecLayout<HD>::smem_bytes(G * (int)nq);                                                      \
     ensure_dynamic_smem((const void*)decode_tma_kernel<HD>, smem);                                                \
     int per_sm = 1;                                                                                                 \
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_tma_kernel<HD>, kDecThreads, smem);               \
@@ -506,7 +522,7 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
                (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), block_tables.data_ptr<int>(),                      \
                (int)block_tables.size(1), context_lens.data_ptr<int>(), sl, part_o.data_ptr<float>(),               \
                part_ml.data_ptr<float>(), counters.data_ptr<int>(), (int)max_splits, (int)partition, max_chunks, B, \
-               nh, nkv, bs, box_rows, (int)kc.size(0), st);                                                          \
+               nh, nkv, bs, box_rows, (int)kc.size(0), (int)nq, st);                                                \
   } while (0)
   if (hd == 128) LSB_DEC_TMA(128);
   else LSB_DEC_TMA(64);

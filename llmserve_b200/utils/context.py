@@ -2,7 +2,8 @@
 
 Field set of ``llmserve/utils/context.py:5-18`` of the reference plus what the paged kernels
 need: ``seqlens_k`` (keys per sequence, int32), ``decode_workspace`` (split-KV scratch),
-``last_token_indices`` (LM-head row selection) and the tree-verify / tree-draft inputs.
+``last_token_indices`` (LM-head row selection), the tree-verify / tree-draft inputs and
+``uniform_q`` (a verify chunk of equal length per sequence, run on the decode kernel).
 """
 from dataclasses import dataclass
 
@@ -30,6 +31,8 @@ class Context:
     tree_rows: list | None = None
     tree_side_k: torch.Tensor | None = None
     tree_side_v: torch.Tensor | None = None
+    # > 0: a packed verify chunk with exactly this many query rows per sequence (prefill mode)
+    uniform_q: int = 0
 
 
 _CONTEXT = Context()

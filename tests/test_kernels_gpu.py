@@ -191,7 +191,7 @@ def test_decode_attention_tma_poisoned_pool(B, partition):
     for _ in range(3):
         out = torch.empty_like(q)
         C().decode_attention_tma(out, q, kc, vc, perm, ctx, scale, ws.partial_out, ws.partial_ml, ws.counters,
-                                 ws.max_splits, partition, status(torch.device(DEV)))
+                                 ws.max_splits, partition, 1, status(torch.device(DEV)))
         torch.cuda.synchronize()
         assert torch.isfinite(out.float()).all()
         assert rel_err(out, ref) < 1e-2
@@ -223,7 +223,7 @@ def test_decode_attention_out_of_range_blocks_and_long_context(tma):
         out = torch.empty_like(q)
         if tma:
             C().decode_attention_tma(out, q, kc, vc, t, c, scale, ws.partial_out, ws.partial_ml, ws.counters,
-                                     ws.max_splits, 128, st)
+                                     ws.max_splits, 128, 1, st)
         else:
             C().decode_attention(out, q, kc, vc, t, c, scale, ws.partial_out, ws.partial_ml, ws.counters,
                                  ws.max_splits, 128, 0, st)
@@ -249,6 +249,44 @@ def test_decode_attention_out_of_range_blocks_and_long_context(tma):
     assert rel_err(out, ref) < 1e-2          # 192 == the clamp for row 2
     assert int(ws.counters.abs().sum()) == 0
     assert rel_err(run(tables, ctx), ref) < 1e-2
+
+
+@pytest.mark.parametrize("nq", [1, 2, 4])
+@pytest.mark.parametrize("bs", [16, 256])
+@pytest.mark.parametrize("hd,nh,nkv", [(128, 32, 8), (64, 8, 4)])
+def test_verify_attention_on_decode_kernel_matches_fp32(nq, bs, hd, nh, nkv):
+    """A packed verify chunk (nq new tokens per sequence, causal among themselves) on the TMA decode
+    kernel, the (query, head) rows of each KV head in one MMA tile, against fp32 varlen attention;
+    contexts from a few keys to several split-KV chunks, NaN in every pool slot no context reaches."""
+    g = torch.Generator(device=DEV).manual_seed(nq * 10 + bs)
+    lens = [nq + 3, 90, 300, 1000, 129, 64 + nq]
+    maxblk = max(-(-k // bs) for k in lens)
+    nblk = len(lens) * maxblk + 2
+    kc = torch.randn(nblk, nkv, bs, hd, device=DEV, generator=g).bfloat16()
+    vc = torch.randn(nblk, nkv, bs, hd, device=DEV, generator=g).bfloat16()
+    tables = torch.randperm(nblk, device=DEV, generator=g)[:len(lens) * maxblk].to(torch.int32).view(len(lens), maxblk)
+    used = torch.zeros(nblk, bs, dtype=torch.bool, device=DEV)
+    for i, k in enumerate(lens):
+        pos = torch.arange(k, device=DEV)
+        used[tables[i, pos // bs].long(), pos % bs] = True
+    keep = used.unsqueeze(1).unsqueeze(-1).expand_as(kc)
+    ref_k, ref_v = kc.float().cpu(), vc.float().cpu()
+    kc[~keep] = float("nan")
+    vc[~keep] = float("nan")
+    B = len(lens)
+    q = torch.randn(B * nq, nh, hd, device=DEV, generator=g).bfloat16()
+    seqk = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    scale = 1 / math.sqrt(hd)
+    ws = attention.DecodeWorkspace(B * nq, nh, hd, maxblk * bs, DEV)
+    assert attention.verify_fits_decode_kernel(nq, nh, nkv, bs, hd)
+    cu = torch.arange(0, (B + 1) * nq, nq, dtype=torch.int32)
+    ref = attention.prefill_attention_ref(q.cpu().float(), ref_k, ref_v, cu, seqk.cpu(), tables.cpu(), scale)
+    for _ in range(2):    # twice: the split counters must reset themselves
+        out = attention.verify_attention(q, kc, vc, tables, seqk, scale, nq, ws)
+        torch.cuda.synchronize()
+        assert torch.isfinite(out.float()).all()
+        assert rel_err(out, ref.to(DEV)) < 1e-2
+    assert int(ws.counters.abs().sum()) == 0
 
 
 def test_prefill_and_tree_attention_skip_out_of_range_blocks():
