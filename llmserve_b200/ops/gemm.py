@@ -222,7 +222,7 @@ def _empty(device, dtype):
 CLUSTER_SPLITK = os.environ.get("LLMSERVE_CLUSTER_SPLITK", "1") != "0"
 CLUSTER_MAX_SPLITS = 16
 CLUSTER_FIXED_KTILES = float(os.environ.get("LLMSERVE_SPLIT_FIXED_KTILES", "8"))
-CLUSTER_MAX_T = 511          # from 512 tokens the persistent 2-SM kernel takes over (one plane)
+CLUSTER_MAX_T = int(os.environ.get("LLMSERVE_CLUSTER_MAX_T", "511"))   # from 512 tokens the persistent 2-SM kernel takes over
 
 
 @functools.lru_cache(maxsize=None)
