@@ -151,22 +151,26 @@ class SpeculativeGraphs:
 
     def fill(self, seqs, kv0: list[int], base: list[int]):
         """Host metadata of one step: draft depth ``d`` of sequence ``i`` writes draft position
-        ``kv0[i] + d``; the verify covers target positions ``base[i] .. base[i] + gamma``."""
+        ``kv0[i] + d``; the verify covers target positions ``base[i] .. base[i] + gamma``.  Built
+        with whole-batch array operations (one pass over the sequences copies the block tables)."""
         a, mb, g, n, W, bsz = self.host_np, self.mb, self.g, self.n, self.W, self.r.block_size
         B = len(seqs)
+        tables = a[self.off_tables:self.off_tables + mb * W].reshape(mb, W)
         for i, s in enumerate(seqs):
-            table = np.asarray(s.block_table, dtype=np.int64)
-            dp = kv0[i] + np.arange(g)
-            a[self.off_dslot + i:self.off_dslot + g * mb:mb] = table[dp // bsz] * bsz + dp % bsz
-            a[self.off_dlen + i:self.off_dlen + g * mb:mb] = dp + 1
-            a[self.off_dpos + i:self.off_dpos + g * mb:mb] = dp
-            vp = base[i] + np.arange(n)
-            a[self.off_vpos + i * n:self.off_vpos + (i + 1) * n] = vp
-            a[self.off_vslot + i * n:self.off_vslot + (i + 1) * n] = table[vp // bsz] * bsz + vp % bsz
-            a[self.off_seqk + i] = base[i] + n
-            row = a[self.off_tables + i * W:self.off_tables + (i + 1) * W]
-            row[:len(table)] = table
-            row[len(table):] = 0
+            t = s.block_table
+            tables[i, :len(t)] = t
+            tables[i, len(t):] = 0
+        tb = tables[:B].astype(np.int64)
+        dp = np.asarray(kv0, dtype=np.int64)[:, None] + np.arange(g)            # [B, g]
+        dslot = np.take_along_axis(tb, dp // bsz, 1) * bsz + dp % bsz
+        a[self.off_dslot:self.off_dslot + g * mb].reshape(g, mb)[:, :B] = dslot.T
+        a[self.off_dlen:self.off_dlen + g * mb].reshape(g, mb)[:, :B] = (dp + 1).T
+        a[self.off_dpos:self.off_dpos + g * mb].reshape(g, mb)[:, :B] = dp.T
+        bs_ = np.asarray(base, dtype=np.int64)
+        vp = bs_[:, None] + np.arange(n)                                         # [B, n]
+        a[self.off_vpos:self.off_vpos + B * n] = vp.reshape(-1)
+        a[self.off_vslot:self.off_vslot + B * n] = (np.take_along_axis(tb, vp // bsz, 1) * bsz + vp % bsz).reshape(-1)
+        a[self.off_seqk:self.off_seqk + B] = bs_ + n
         self._fill_padding(B)
         if self.r.config.debug_bounds_checks:
             self._check(B)

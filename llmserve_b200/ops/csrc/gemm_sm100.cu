@@ -288,7 +288,26 @@ __global__ void __launch_bounds__(128, 1) gemm_bf16_kernel(const __grid_constant
       const int j = e / kGroups, g = e - j * kGroups;
       const int t = t0 + j;
       float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int src = 0; src < S; ++src) {
+      // four distributed-shared-memory loads in flight per round (their latency, not the adds,
+      // bounds this loop), then the sums in source order
+      int src = 0;
+      for (; src + 4 <= S; src += 4) {
+        float4 x[4], y[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float* rs = cluster.map_shared_rank(red, src + u) + j * BM;
+          x[u] = *reinterpret_cast<const float4*>(rs + g * 4);
+          if constexpr (EPI == 1) y[u] = *reinterpret_cast<const float4*>(rs + BM / 2 + g * 4);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          a.x += x[u].x; a.y += x[u].y; a.z += x[u].z; a.w += x[u].w;
+          if constexpr (EPI == 1) {
+            b.x += y[u].x; b.y += y[u].y; b.z += y[u].z; b.w += y[u].w;
+          }
+        }
+      }
+      for (; src < S; ++src) {
         const float* rs = cluster.map_shared_rank(red, src) + j * BM;
         const float4 x = *reinterpret_cast<const float4*>(rs + g * 4);
         a.x += x.x; a.y += x.y; a.z += x.z; a.w += x.w;
