@@ -416,11 +416,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
         l *= alpha;
       }
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;   // a fully masked row: all P = 0
-      // the P buffer is free once this tile's previous PV completed
-      if (j >= 1) {
-        LSB_WAIT_ALL(&o_done[t], (j - 1) & 1, kTimeoutAccum);
-      }
-      uint8_t* prow = smem + L::kPOff + t * L::kPBytes + r * 128;
+      // P = exp2(s - m) packed to bf16 in registers first: the exponentials overlap this tile's
+      // previous PV, which must finish before the P buffer is overwritten
+      uint32_t pw[kBKV / 2];
       float sum8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) sum8[e] = 0.f;
@@ -432,14 +430,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
           p[e] = ex2(fmaf(__uint_as_float(raw[c8 * 8 + e]), scale_log2, neg_m));   // ex2(-inf) = 0
           sum8[e] += p[e];
         }
-        uint4 w;
-        w.x = pack_bf16(p[0], p[1]);
-        w.y = pack_bf16(p[2], p[3]);
-        w.z = pack_bf16(p[4], p[5]);
-        w.w = pack_bf16(p[6], p[7]);
-        *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) = w;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pw[c8 * 4 + e] = pack_bf16(p[2 * e], p[2 * e + 1]);
       }
       l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      if (j >= 1) {
+        LSB_WAIT_ALL(&o_done[t], (j - 1) & 1, kTimeoutAccum);
+      }
+      uint8_t* prow = smem + L::kPOff + t * L::kPBytes + r * 128;
+#pragma unroll
+      for (int c8 = 0; c8 < kBKV / 8; ++c8)
+        *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) =
+            make_uint4(pw[c8 * 4], pw[c8 * 4 + 1], pw[c8 * 4 + 2], pw[c8 * 4 + 3]);
       // zero the V rows of keys no query may see (past the context, or from a bad block)
       if (k0 + kBKV > kend || bad != 0ull) {
         uint8_t* vt = smem + L::kVOff + s * L::kTileBytes;
