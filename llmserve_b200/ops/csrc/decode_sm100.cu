@@ -420,15 +420,19 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
   }
 }
 
+// A cached map is valid only for the exact geometry it was encoded with: a later pool allocated at
+// the same address (the caching allocator reuses freed blocks) may have the same row count but a
+// different head dim, so the key holds every parameter of the encoding.
 struct PoolKey {
   const void* p;
-  int64_t rows;
+  int64_t rows, hd;
   int box;
-  bool operator==(const PoolKey& o) const { return p == o.p && rows == o.rows && box == o.box; }
+  bool operator==(const PoolKey& o) const { return p == o.p && rows == o.rows && hd == o.hd && box == o.box; }
 };
 struct PoolKeyHash {
   size_t operator()(const PoolKey& k) const {
-    return std::hash<const void*>()(k.p) ^ (std::hash<int64_t>()(k.rows) * 31) ^ (size_t)k.box;
+    return std::hash<const void*>()(k.p) ^ (std::hash<int64_t>()(k.rows) * 31) ^ (std::hash<int64_t>()(k.hd) * 131) ^
+           (size_t)k.box;
   }
 };
 
@@ -437,7 +441,7 @@ const CUtensorMap& pool_map(const at::Tensor& pool, int box_rows) {
   static std::unordered_map<PoolKey, CUtensorMap, PoolKeyHash> cache;
   static std::mutex mu;
   const int64_t hd = pool.size(3), rows = pool.numel() / hd;
-  PoolKey key{pool.data_ptr(), rows, box_rows};
+  PoolKey key{pool.data_ptr(), rows, hd, box_rows};
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
