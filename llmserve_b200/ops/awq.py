@@ -17,6 +17,7 @@ bf16, times ``s`` rounds once) and accumulates in TMEM; split-K partials are sum
 reduction kernel.  Replaces the reference's ``awq_w4a16_kernel`` (``mma.sync``) and its Triton
 GEMV/GEMM (``awq_triton.py``).
 """
+import os
 from dataclasses import dataclass
 
 import torch
@@ -74,12 +75,17 @@ def prepare_awq_weights(qweight: torch.Tensor, qzeros: torch.Tensor, scales: tor
     return AWQPacked(qtiles, sztiles, N, K)
 
 
+# CTAs per SM of the W4A16 kernel: 2 (two operand buffers, default) or 3 (LLMSERVE_AWQ_WBUF=1:
+# one operand buffer and a shorter ring, for more CTAs in flight)
+AWQ_CTAS_PER_SM = 3 if os.environ.get("LLMSERVE_AWQ_WBUF", "2") == "1" else 2
+
+
 def choose_awq_splits(T: int, n: int, k: int) -> int:
-    """Split K so the grid fills the two CTA slots of every SM about once; >= 8 K steps per split."""
+    """Split K so the grid fills the CTA slots of every SM about once; >= 8 K steps per split."""
     bn = 16 if T <= 16 else 32 if T <= 32 else 64 if T <= 64 else 128 if T <= 128 else 256
     tiles = (-(-n // TILE_N)) * (-(-T // bn))
     k_tiles = k // TILE_K
-    slots = 2 * NUM_SMS
+    slots = AWQ_CTAS_PER_SM * NUM_SMS
     if tiles >= slots:
         return 1
     return max(1, min(slots // tiles, k_tiles // 8, 16))

@@ -49,10 +49,11 @@ struct QSmem {
   static constexpr int kBytes = kBarOff + (2 * STAGES + 2 * WB + 1) * 8 + 16 + 1024;
 };
 
-// WB operand buffers; shared memory budget per CTA (two CTAs per SM when WB == 2).
+// WB operand buffers; shared memory budget per CTA: two CTAs per SM when WB == 2, three with the
+// lean ring (WB == 1: one operand buffer, ~72 KB), one otherwise.
 template <int BN, int WB>
 constexpr int qstages() {
-  constexpr int budget = (WB == 2 ? 110 : 200) * 1024 - WB * kWTile;
+  constexpr int budget = (WB == 1 ? 72 : WB == 2 ? 110 : 200) * 1024 - WB * kWTile;
   constexpr int st = budget / QSmem<BN, 1, WB>::kStage;
   return st > 8 ? 8 : st < 2 ? 2 : st;
 }
@@ -353,6 +354,7 @@ void awq_launch_any(const at::Tensor& x, const at::Tensor& qt, const at::Tensor&
   const int wb = awq_wbuf();
   if (wb >= 8) awq_launch<BN, 8>(x, qt, sz, N, out, pd, splits, status);
   else if (wb >= 4) awq_launch<BN, 4>(x, qt, sz, N, out, pd, splits, status);
+  else if (wb == 1) awq_launch<BN, 1>(x, qt, sz, N, out, pd, splits, status);
   else awq_launch<BN, 2>(x, qt, sz, N, out, pd, splits, status);
 }
 

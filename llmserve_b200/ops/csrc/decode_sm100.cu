@@ -264,31 +264,31 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
     if (ks >= ctx) {
       if (chunk == 0 && warp == 0)   // empty context: defined output
         for (int i = lane; i < R * HD; i += 32) {
-          const int r = i / HD;
-          out[((size_t)(b * nq + r / G) * nh + kvh * G + r % G) * HD + i % HD] = to_b(0.f);
+          const int r = i / HD, qi = nq == 1 ? 0 : r / G;
+          out[((size_t)(b * nq + qi) * nh + kvh * G + r - qi * G) * HD + i % HD] = to_b(0.f);
         }
       continue;
     }
     const int ke = min(ks + partition, ctx);
     const int nchunks = (ctx + partition - 1) / partition;
 
+    // this lane's two tile rows g and g + 8: (query, head) pairs and their query-row pointers,
+    // worked out once per item (no division in the loops; nq = 1 is plain decode)
+    const int qA = nq == 1 ? 0 : g / G, qB = nq == 1 ? 0 : (g + 8) / G;
+    const bf16* qrA = g < R ? q + ((size_t)(b * nq + qA) * nh + kvh * G + (g - qA * G)) * HD : nullptr;
+    const bf16* qrB = g + 8 < R ? q + ((size_t)(b * nq + qB) * nh + kvh * G + (g + 8 - qB * G)) * HD : nullptr;
     // query i of sequence b at absolute position ctx - nq + i sees keys [0, ctx - nq + i]
-    const int limA = min(ke, ctx - nq + g / G + 1), limB = min(ke, ctx - nq + (g + 8) / G + 1);
+    const int limA = min(ke, ctx - nq + qA + 1), limB = min(ke, ctx - nq + qB + 1);
     uint32_t qa[HD / 16][4];
     {
-      const int r0 = lane >> 2, c = (lane & 3) * 2;
+      const int c = (lane & 3) * 2;
 #pragma unroll
       for (int kk = 0; kk < HD / 16; ++kk) {
         const int col = kk * 16 + c;
-        auto ld = [&](int r, int cc) -> uint32_t {
-          if (r >= R) return 0u;
-          const bf16* qr = q + ((size_t)(b * nq + r / G) * nh + kvh * G + r % G) * HD;
-          return *reinterpret_cast<const uint32_t*>(qr + cc);
-        };
-        qa[kk][0] = ld(r0, col);
-        qa[kk][1] = ld(r0 + 8, col);
-        qa[kk][2] = ld(r0, col + 8);
-        qa[kk][3] = ld(r0 + 8, col + 8);
+        qa[kk][0] = qrA ? *reinterpret_cast<const uint32_t*>(qrA + col) : 0u;
+        qa[kk][1] = qrB ? *reinterpret_cast<const uint32_t*>(qrB + col) : 0u;
+        qa[kk][2] = qrA ? *reinterpret_cast<const uint32_t*>(qrA + col + 8) : 0u;
+        qa[kk][3] = qrB ? *reinterpret_cast<const uint32_t*>(qrB + col + 8) : 0u;
       }
     }
     float o[HD / 8][4];
@@ -364,7 +364,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
     if (!group_sync(group, gphase, status)) return;
     for (int idx = threadIdx.x; idx < R * HD; idx += 128) {
       const int r = idx / HD, d = idx % HD;
-      const size_t qrow = (size_t)b * nq + r / G;   // output row of query r / G
+      const int qi = nq == 1 ? 0 : r / G;
+      const size_t qrow = (size_t)b * nq + qi;      // output row of query qi
       float M = -INFINITY;
 #pragma unroll
       for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
@@ -376,7 +377,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
         L += sl[w * 16 + r] * f;
         O += so[(w * R + r) * HD + d] * f;
       }
-      const int h = kvh * G + r % G;
+      const int h = kvh * G + r - qi * G;
       if (nchunks == 1) {
         out[(qrow * nh + h) * HD + d] = to_b(L > 0.f ? O / L : 0.f);
       } else {
@@ -403,8 +404,9 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
     __threadfence();
     for (int idx = threadIdx.x; idx < R * HD; idx += 128) {
       const int r = idx / HD, d = idx % HD;
-      const size_t qrow = (size_t)b * nq + r / G;
-      const int h = kvh * G + r % G;
+      const int qi = nq == 1 ? 0 : r / G;
+      const size_t qrow = (size_t)b * nq + qi;
+      const int h = kvh * G + r - qi * G;
       const size_t base = (qrow * nh + h) * max_splits;
       float M = -INFINITY;
       for (int sp = 0; sp < nchunks; ++sp) M = fmaxf(M, __ldcg(&part_ml[(base + sp) * 2]));
