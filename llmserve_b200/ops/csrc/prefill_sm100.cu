@@ -36,8 +36,6 @@
 #include <c10/cuda/CUDAStream.h>
 #include <cudaTypedefs.h>
 
-#include <type_traits>
-
 #include "common.cuh"
 
 namespace lsb {
@@ -155,21 +153,6 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volat
   record_error(status, code);
   *abort_flag = 1;
   return false;
-}
-
-// 2^x on the FMA and integer pipes, for x in [-120, 8]: x = j + f with j = round(x) taken by the
-// 1.5 * 2^23 shifter (|f| <= 1/2), a cubic for 2^f (coefficients fitted for this kernel by least
-// squares in relative error at Chebyshev nodes of [-1/2, 1/2]: max relative error 7.7e-5, far below
-// the bf16 rounding that P gets next), and j added to the exponent field.  Used for a quarter of
-// the scores of interior tiles so the special-function unit is not the only exponential pipe.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -120.f);
-  const float t = x + 12582912.f;
-  const float j = t - 12582912.f;
-  const float f = x - j;
-  const float p = fmaf(fmaf(fmaf(0.05508868396282196f, f, 0.24260404706001282f), f, 0.6932762265205383f), f,
-                       0.9999289512634277f);
-  return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -435,29 +418,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;   // a fully masked row: all P = 0
       // P = exp2(s - m) packed to bf16 in registers first: the exponentials overlap this tile's
       // previous PV, which must finish before the P buffer is overwritten
-      // P is rounded toward zero to bf16 (the high half of each float, two packed by one byte
-      // permute) and the row sum adds the same rounded values, so O / l stays unbiased
       uint32_t pw[kBKV / 2];
       float sum8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) sum8[e] = 0.f;
-      auto exps = [&](auto use_fma) {
 #pragma unroll
-        for (int c8 = 0; c8 < kBKV / 8; ++c8) {
-          uint32_t u[8];
+      for (int c8 = 0; c8 < kBKV / 8; ++c8) {
+        float p[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float x = fmaf(__uint_as_float(raw[c8 * 8 + e]), scale_log2, neg_m);
-            const float p = (decltype(use_fma)::value && (c8 & 3) == 2) ? exp2_fma(x) : ex2(x);   // ex2(-inf) = 0
-            u[e] = __float_as_uint(p) & 0xFFFF0000u;
-            sum8[e] += __uint_as_float(u[e]);
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) pw[c8 * 4 + e] = __byte_perm(u[2 * e], u[2 * e + 1], 0x7632);
+        for (int e = 0; e < 8; ++e) {
+          p[e] = ex2(fmaf(__uint_as_float(raw[c8 * 8 + e]), scale_log2, neg_m));   // ex2(-inf) = 0
+          sum8[e] += p[e];
         }
-      };
-      if (interior) exps(std::true_type{});    // every score finite: a quarter on the FMA pipe
-      else exps(std::false_type{});            // masked scores are -inf: special-function unit only
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pw[c8 * 4 + e] = pack_bf16(p[2 * e], p[2 * e + 1]);
+      }
       l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       if (j >= 1) {
         LSB_WAIT_ALL(&o_done[t], (j - 1) & 1, kTimeoutAccum);
