@@ -78,6 +78,9 @@ def prepare_awq_weights(qweight: torch.Tensor, qzeros: torch.Tensor, scales: tor
 # CTAs per SM of the W4A16 kernel: 2 (two operand buffers, default) or 3 (LLMSERVE_AWQ_WBUF=1:
 # one operand buffer and a shorter ring, for more CTAs in flight)
 AWQ_CTAS_PER_SM = 3 if os.environ.get("LLMSERVE_AWQ_WBUF", "2") == "1" else 2
+# decode-sized W4A16 products reduce their K splits in a thread-block cluster (LLMSERVE_AWQ_CLUSTER=0:
+# fp32 partial planes + the reduction kernel)
+AWQ_CLUSTER = os.environ.get("LLMSERVE_AWQ_CLUSTER", "1") != "0"
 
 
 def choose_awq_splits(T: int, n: int, k: int) -> int:
@@ -99,6 +102,10 @@ def awq_linear(x: torch.Tensor, packed: AWQPacked) -> torch.Tensor:
         return out.view(*x.shape[:-1], packed.n)
     splits = choose_awq_splits(T, packed.n, packed.k)
     empty32 = torch.empty(0, dtype=torch.float32, device=x.device)
+    if AWQ_CLUSTER and splits > 1 and T <= 128:
+        # the K splits of a tile reduce in a thread-block cluster: bf16 out, no partial planes
+        C().awq_gemm_reduced(out, x2, packed.qtiles, packed.sztiles, packed.n, min(splits, 8), status(x.device))
+        return out.view(*x.shape[:-1], packed.n)
     if splits == 1:
         C().awq_gemm(out, x2, packed.qtiles, packed.sztiles, packed.n, empty32, 1, status(x.device))
     else:

@@ -21,11 +21,14 @@
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
+#include <cooperative_groups.h>
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
 
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace lsb {
 
@@ -123,7 +126,8 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
                                                           const uint32_t* __restrict__ qtiles,
                                                           const uint2* __restrict__ sztiles, bf16* __restrict__ out,
                                                           const PartDest pd, int T, int N, int k_tiles,
-                                                          int k_tiles_per_split, int* __restrict__ status) {
+                                                          int k_tiles_per_split, int cluster_red,
+                                                          int* __restrict__ status) {
   using L = QSmem<BN, STAGES, WB>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -299,7 +303,12 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
 #pragma unroll
           for (int j = 0; j < 16; ++j) rr[j] = 0u;
         }
-        if (feat < N) {
+        if (cluster_red > 0) {
+          // park this K slice's tile [token][128 features] in the (now idle) ring memory
+          float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) red[(c0 + j) * QBM + q * 32 + lane] = __uint_as_float(rr[j]);
+        } else if (feat < N) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int tok = t0 + c0 + j;
@@ -315,6 +324,54 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
       }
     }
   }
+  if (cluster_red > 0) {
+    // the cluster_red K-slice CTAs of this tile sum their parked tiles through distributed shared
+    // memory: CTA z writes slice z of the elements once (bf16, or one fp32 plane through pd)
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const uint32_t ep = pd.call_epoch();
+    float* red = reinterpret_cast<float*>(smem);
+    const int S = cluster_red, z = (int)cluster.block_rank();
+    const int nvalid = max(0, min(BN, T - t0));
+    const int E = nvalid * (QBM / 4);   // float4 groups: token j, features 4g..4g+3
+    const int per = (E + S - 1) / S;
+    const int e_end = min(E, (z + 1) * per);
+    if (threadIdx.x >= 64) {
+      for (int e = z * per + (int)threadIdx.x - 64; e < e_end; e += kQThreads - 64) {
+        const int j = e / (QBM / 4), g = e - j * (QBM / 4);
+        const int tok = t0 + j;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        int src = 0;
+        for (; src + 4 <= S; src += 4) {
+          float4 xv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            xv[u] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(red, src + u) + j * QBM + g * 4);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            a.x += xv[u].x; a.y += xv[u].y; a.z += xv[u].z; a.w += xv[u].w;
+          }
+        }
+        for (; src < S; ++src) {
+          const float4 xv = *reinterpret_cast<const float4*>(cluster.map_shared_rank(red, src) + j * QBM + g * 4);
+          a.x += xv.x; a.y += xv.y; a.z += xv.z; a.w += xv.w;
+        }
+        const float va[4] = {a.x, a.y, a.z, a.w};
+        const int f0 = n0 + g * 4;
+        if (pd.base[0] != nullptr && (pd.ll || f0 + 3 < N)) {
+          pd.store4(0, tok, N, f0, va, ep);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (f0 + u >= N) break;
+            if (pd.base[0] != nullptr) *pd.at(0, tok, N, f0 + u) = va[u];
+            else out[(size_t)tok * N + f0 + u] = to_b(va[u]);
+          }
+        }
+      }
+    }
+    cluster.sync();   // keep this CTA's tile alive until every peer CTA has read it
+  }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1) {
@@ -323,9 +380,11 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
   }
 }
 
+// reduce: the `splits` K slices of a tile reduce in a thread-block cluster (splits <= 8, the tile
+// [BN][128] fp32 fitting in the ring + operand memory) and write bf16 `out` or one plane via `pd`.
 template <int BN, int WB>
 void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out,
-                const PartDest& pd, int splits, int* status) {
+                const PartDest& pd, int splits, int* status, bool reduce = false) {
   constexpr int ST = qstages<BN, WB>();
   using L = QSmem<BN, ST, WB>;
   static_assert(L::kStage % 1024 == 0, "stage size must keep 1024-byte alignment");
@@ -336,8 +395,29 @@ void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz,
   auto kern = awq_gemm_kernel<BN, ST, WB>;
   ensure_dynamic_smem((const void*)kern, L::kBytes);
   dim3 grid(((N + QBM - 1) / QBM) * ((T + BN - 1) / BN), 1, splits);
-  launch_pdl(kern, grid, dim3(kQThreads), L::kBytes, at::cuda::getCurrentCUDAStream(), mx,
-             (const uint32_t*)qt.data_ptr(), (const uint2*)sz.data_ptr(), out, pd, T, N, k_tiles, kps, status);
+  const int cred = reduce && splits > 1 ? splits : 0;
+  TORCH_CHECK(cred == 0 || (cred <= 8 && BN * QBM * 4 <= L::kBarOff),
+              "llmserve_b200: AWQ cluster reduction needs <= 8 splits and a tile that fits the ring");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kQThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  int nattr = 1;
+  if (cred > 0) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = cred;
+    nattr = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  cudaLaunchKernelEx(&cfg, kern, mx, (const uint32_t*)qt.data_ptr(), (const uint2*)sz.data_ptr(), out, pd, T, N,
+                     k_tiles, kps, cred, status);
 }
 
 int awq_wbuf() {
@@ -350,22 +430,25 @@ int awq_wbuf() {
 
 template <int BN>
 void awq_launch_any(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out,
-                    const PartDest& pd, int splits, int* status) {
+                    const PartDest& pd, int splits, int* status, bool reduce) {
   const int wb = awq_wbuf();
-  if (wb >= 8) awq_launch<BN, 8>(x, qt, sz, N, out, pd, splits, status);
-  else if (wb >= 4) awq_launch<BN, 4>(x, qt, sz, N, out, pd, splits, status);
-  else if (wb == 1) awq_launch<BN, 1>(x, qt, sz, N, out, pd, splits, status);
-  else awq_launch<BN, 2>(x, qt, sz, N, out, pd, splits, status);
+  if (wb >= 8) awq_launch<BN, 8>(x, qt, sz, N, out, pd, splits, status, reduce);
+  else if (wb >= 4) awq_launch<BN, 4>(x, qt, sz, N, out, pd, splits, status, reduce);
+  else if (wb == 1) awq_launch<BN, 1>(x, qt, sz, N, out, pd, splits, status, reduce);
+  else awq_launch<BN, 2>(x, qt, sz, N, out, pd, splits, status, reduce);
 }
 
 void awq_dispatch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* o, const PartDest& pd,
-                  int splits, int* st) {
+                  int splits, int* st, bool reduce = false) {
   const int T = x.size(0);
-  if (T <= 16) awq_launch_any<16>(x, qt, sz, N, o, pd, splits, st);
-  else if (T <= 32) awq_launch_any<32>(x, qt, sz, N, o, pd, splits, st);
-  else if (T <= 64) awq_launch_any<64>(x, qt, sz, N, o, pd, splits, st);
-  else if (T <= 128) awq_launch_any<128>(x, qt, sz, N, o, pd, splits, st);
-  else awq_launch_any<256>(x, qt, sz, N, o, pd, splits, st);
+  if (T <= 16) awq_launch_any<16>(x, qt, sz, N, o, pd, splits, st, reduce);
+  else if (T <= 32) awq_launch_any<32>(x, qt, sz, N, o, pd, splits, st, reduce);
+  else if (T <= 64) awq_launch_any<64>(x, qt, sz, N, o, pd, splits, st, reduce);
+  else if (T <= 128) awq_launch_any<128>(x, qt, sz, N, o, pd, splits, st, reduce);
+  else {
+    TORCH_CHECK(!reduce, "llmserve_b200: AWQ cluster reduction is for T <= 128");
+    awq_launch_any<256>(x, qt, sz, N, o, pd, splits, st, false);
+  }
 }
 
 void check_awq_operands(const at::Tensor& x, const at::Tensor& qtiles, const at::Tensor& sztiles, int N) {
@@ -407,6 +490,21 @@ void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztile
   if (T == 0 || N == 0) return;
   const at::cuda::CUDAGuard g(x.device());
   awq_dispatch(x, qtiles, sztiles, N, o, local_part_dest(p, T, (int)splits), (int)splits, status_ptr(status));
+}
+
+// bf16 out [T, N] = x . dequant(W)^T with K split over `splits` CTAs that reduce in a cluster
+// (T <= 128, splits 2..8): no partial planes, no reduction kernel.
+void awq_gemm_reduced(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, int64_t splits,
+                      at::Tensor status) {
+  const int T = x.size(0), N = (int)n;
+  check_awq_operands(x, qtiles, sztiles, N);
+  TORCH_CHECK(splits >= 2 && splits <= 8 && T <= 128, "llmserve_b200: cluster-reduced AWQ needs 2..8 splits, T <= 128");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == (int64_t)T * N,
+              "llmserve_b200: bad AWQ out");
+  if (T == 0 || N == 0) return;
+  const at::cuda::CUDAGuard g(x.device());
+  awq_dispatch(x, qtiles, sztiles, N, (bf16*)out.data_ptr(), local_part_dest(nullptr, T, 1), (int)splits,
+               status_ptr(status), true);
 }
 
 // Row-parallel W4A16 projection under tensor parallelism: partial planes of token row t go to the

@@ -47,6 +47,8 @@ void gemm_bf16_reduced(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, bo
                        int64_t splits, at::Tensor status, int64_t max_stages);
 void gemm_bf16_silu_reduced(at::Tensor out, at::Tensor x, at::Tensor w, int64_t n, bool packed, int64_t splits,
                             at::Tensor status, int64_t max_stages);
+void awq_gemm_reduced(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, int64_t splits,
+                      at::Tensor status);
 void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, std::vector<int64_t> inboxes,
                         int64_t rank, int64_t rows_per_rank, int64_t splits, int64_t epoch_ptr, at::Tensor status);
 void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages);
@@ -114,6 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_reduced", &lsb::gemm_bf16_reduced);
   m.def("gemm_bf16_silu_reduced", &lsb::gemm_bf16_silu_reduced);
   m.def("awq_gemm_to_owners", &lsb::awq_gemm_to_owners);
+  m.def("awq_gemm_reduced", &lsb::awq_gemm_reduced);
   m.def("gemm_bf16_silu", &lsb::gemm_bf16_silu);
   m.def("splitk_silu", &lsb::splitk_silu);
   m.def("silu_and_mul_interleaved", &lsb::silu_and_mul_interleaved);

@@ -77,3 +77,25 @@ def test_awq_partials_sum(splits):
     torch.cuda.synchronize()
     assert parts.shape == (splits, 48, 512)
     assert rel_err(parts.sum(0).cpu(), x.float() @ dense) < 1e-3
+
+
+@pytest.mark.parametrize("T", [1, 7, 64, 100])
+@pytest.mark.parametrize("splits", [2, 3, 8])
+@pytest.mark.parametrize("N,K", [(512, 2048), (6144, 4096)])
+def test_awq_cluster_reduced_matches_dequantized_fp32(T, splits, N, K):
+    """The W4A16 GEMM whose K-split CTAs reduce in a thread-block cluster (bf16 out, no partial
+    planes) against the fp32 product of the dequantised weight, for several split counts."""
+    from llmserve_b200.ops._ext import C, status
+    g = torch.Generator().manual_seed(T * 7 + splits + N)
+    w = torch.randn(N, K, generator=g) * 0.05
+    qw, qz, sc = awq_quantize_dense(w)
+    sc = sc.bfloat16()
+    dense = dequantize_awq_gemm(qw, qz, sc, group_size=128).float()
+    packed = awq_ops.prepare_awq_weights(qw.to(DEV), qz.to(DEV), sc.to(DEV), 128)
+    x = torch.randn(T, K, generator=g).bfloat16()
+    ref = x.float() @ dense
+    out = torch.empty(T, N, dtype=torch.bfloat16, device=DEV)
+    for _ in range(2):
+        C().awq_gemm_reduced(out, x.to(DEV), packed.qtiles, packed.sztiles, N, splits, status(torch.device(DEV)))
+        torch.cuda.synchronize()
+        assert rel_err(out.cpu(), ref) < 1e-2
