@@ -510,7 +510,8 @@ void awq_gemm_reduced(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tenso
 // Row-parallel W4A16 projection under tensor parallelism: partial planes of token row t go to the
 // inbox of the rank owning t (see PartDest) as epoch-tagged words stored by the epilogue.
 void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, std::vector<int64_t> inboxes,
-                        int64_t rank, int64_t rows_per_rank, int64_t splits, int64_t epoch_ptr, at::Tensor status) {
+                        int64_t rank, int64_t rows_per_rank, int64_t splits, bool reduce, int64_t epoch_ptr,
+                        at::Tensor status) {
   const int T = x.size(0), N = (int)n, W = (int)inboxes.size();
   check_awq_operands(x, qtiles, sztiles, N);
   TORCH_CHECK(W >= 1 && W <= kMaxOwners && rank >= 0 && rank < W, "llmserve_b200: one inbox per rank (<= 8)");
@@ -521,13 +522,15 @@ void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int
   for (int r = 0; r < W; ++r) pd.base[r] = reinterpret_cast<float*>(inboxes[r]);
   pd.rows = (int)rows_per_rank;
   pd.slot = (int)rank;
-  pd.planes = (int)splits;
+  TORCH_CHECK(!reduce || (splits >= 2 && splits <= 8 && T <= 128 && N % 4 == 0),
+              "llmserve_b200: cluster-reduced AWQ needs 2..8 splits, T <= 128, N % 4 == 0");
+  pd.planes = reduce ? 1 : (int)splits;   // a cluster-reduced projection sends one plane per rank
   pd.owners = W;
   TORCH_CHECK(epoch_ptr != 0, "llmserve_b200: the collective's inboxes need an epoch word");
   pd.ll = 1;
   pd.epoch = reinterpret_cast<const uint32_t*>(epoch_ptr);
   const at::cuda::CUDAGuard g(x.device());
-  awq_dispatch(x, qtiles, sztiles, N, nullptr, pd, (int)splits, status_ptr(status));
+  awq_dispatch(x, qtiles, sztiles, N, nullptr, pd, (int)splits, status_ptr(status), reduce);
 }
 
 }  // namespace lsb

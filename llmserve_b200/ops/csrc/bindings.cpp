@@ -50,7 +50,8 @@ void gemm_bf16_silu_reduced(at::Tensor out, at::Tensor x, at::Tensor w, int64_t 
 void awq_gemm_reduced(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, int64_t splits,
                       at::Tensor status);
 void awq_gemm_to_owners(at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, std::vector<int64_t> inboxes,
-                        int64_t rank, int64_t rows_per_rank, int64_t splits, int64_t epoch_ptr, at::Tensor status);
+                        int64_t rank, int64_t rows_per_rank, int64_t splits, bool reduce, int64_t epoch_ptr,
+                        at::Tensor status);
 void gemm_bf16_silu(at::Tensor out, at::Tensor x, at::Tensor w, at::Tensor status, int64_t max_stages);
 void splitk_silu(at::Tensor out, at::Tensor partials);
 void silu_and_mul_interleaved(at::Tensor out, at::Tensor x);

@@ -123,11 +123,13 @@ class FusedComm:
         rows = _rows_per_rank(T, self.world)
         st = status(x.device)
         if isinstance(weight, awq_ops.AWQPacked):
-            # W4A16: plain K splits, each plane of a row crosses NVLink once (as the GEMM's stores)
+            # W4A16
             splits = min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS)
-            planes = splits
+            # decode-sized: the K splits reduce in a cluster and one plane crosses NVLink
+            reduce = awq_ops.AWQ_CLUSTER and splits > 1 and T <= 128
+            planes = 1 if reduce else splits
             C().awq_gemm_to_owners(x, weight.qtiles, weight.sztiles, weight.n, self.inbox_ptrs, self.rank, rows,
-                                   splits, self.epoch_ptr, st)
+                                   splits, reduce, self.epoch_ptr, st)
         else:
             # dense: the K splits reduce on chip, one fp32 plane per rank crosses NVLink
             data, n, packed = gemm._operand(weight)
