@@ -44,13 +44,15 @@ constexpr int kDecThreads = 160;   // 4 consumer warps + 1 producer warp
 // Shared memory: [stages x (K tile | V tile)] [barriers] [merge buffer: o (4 warps x G rows x HD)
 // + m, l (4 warps x 16 rows)].  Sized so two CTAs fit on one SM for G <= 8 (8 consumer warps per
 // SM hide each other's mma / global latency).
-template <int HD>
+// ST: ring depth (default 96 KiB of ring for either head dim); a verify chunk (up to 16 tile rows)
+// has a 4x larger merge buffer and takes one stage less so that two CTAs still fit per SM.
+template <int HD, int ST = (HD == 128 ? 3 : 6)>
 struct DecLayout {
   static constexpr int kHalves = HD / 64;                    // 128-byte column halves
   static constexpr int kHalfBytes = kDecKeys * 128;          // 8 KiB
   static constexpr int kTileBytes = kHalves * kHalfBytes;    // K (or V) of one stage
   static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kStages = HD == 128 ? 3 : 6;          // 96 KiB of ring either way
+  static constexpr int kStages = ST;
   static constexpr int kBarOff = kStages * kStageBytes;
   static constexpr int kMergeOff = kBarOff + 128;
   static int smem_bytes(int G) { return kMergeOff + (4 * G * HD + 2 * 64) * 4 + 1024; }
@@ -149,14 +151,14 @@ __device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, int* 
   return ok;
 }
 
-template <int HD>
+template <int HD, int ST>
 __global__ void __launch_bounds__(kDecThreads, 2) decode_tma_kernel(
     const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v, bf16* __restrict__ out,
     const bf16* __restrict__ q, const int* __restrict__ block_tables, int bt_stride,
     const int* __restrict__ context_lens, float scale_log2, float* __restrict__ part_o, float* __restrict__ part_ml,
     int* __restrict__ counters, int max_splits, int partition, int max_chunks, int B, int nh, int nkv, int bs,
     int box_rows, int nblk, int nq, int* __restrict__ status) {
-  using LY = DecLayout<HD>;
+  using LY = DecLayout<HD, ST>;
   constexpr int S = LY::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -517,21 +519,27 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
   const float sl = (float)scale * kLog2e;
   auto stream = at::cuda::getCurrentCUDAStream();
   int* st = status_ptr(status);
-#define LSB_DEC_TMA(HD)                                                                                             \
+#define LSB_DEC_TMA(HD, ST)                                                                                         \
   do {                                                                                                              \
-    const int smem = DecLayout<HD>::smem_bytes(G * (int)nq);                                                      \
-    ensure_dynamic_smem((const void*)decode_tma_kernel<HD>, smem);                                                \
+    const int smem = DecLayout<HD, ST>::smem_bytes(G * (int)nq);                                                  \
+    ensure_dynamic_smem((const void*)decode_tma_kernel<HD, ST>, smem);                                            \
     int per_sm = 1;                                                                                                 \
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_tma_kernel<HD>, kDecThreads, smem);               \
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_tma_kernel<HD, ST>, kDecThreads, smem);           \
     const int grid = (int)std::min<int64_t>(n_items, (int64_t)sm_count() * std::max(per_sm, 1));                   \
-    launch_pdl(decode_tma_kernel<HD>, dim3(grid), dim3(kDecThreads), smem, stream, mk, mv,                          \
+    launch_pdl(decode_tma_kernel<HD, ST>, dim3(grid), dim3(kDecThreads), smem, stream, mk, mv,                      \
                (bf16*)out.data_ptr(), (const bf16*)q.data_ptr(), block_tables.data_ptr<int>(),                      \
                (int)block_tables.size(1), context_lens.data_ptr<int>(), sl, part_o.data_ptr<float>(),               \
                part_ml.data_ptr<float>(), counters.data_ptr<int>(), (int)max_splits, (int)partition, max_chunks, B, \
                nh, nkv, bs, box_rows, (int)kc.size(0), (int)nq, st);                                                \
   } while (0)
-  if (hd == 128) LSB_DEC_TMA(128);
-  else LSB_DEC_TMA(64);
+  const bool wide = G * nq > 8;   // verify chunks: a 4x merge buffer, one ring stage less
+  if (hd == 128) {
+    if (wide) LSB_DEC_TMA(128, 2);
+    else LSB_DEC_TMA(128, 3);
+  } else {
+    if (wide) LSB_DEC_TMA(64, 5);
+    else LSB_DEC_TMA(64, 6);
+  }
 #undef LSB_DEC_TMA
 }
 
