@@ -253,7 +253,7 @@ def test_decode_attention_out_of_range_blocks_and_long_context(tma):
 
 @pytest.mark.parametrize("nq", [1, 2, 4])
 @pytest.mark.parametrize("bs", [16, 256])
-@pytest.mark.parametrize("hd,nh,nkv", [(128, 32, 8), (64, 8, 4)])
+@pytest.mark.parametrize("hd,nh,nkv", [(128, 32, 8), (64, 8, 4), (64, 16, 2)])
 def test_verify_attention_on_decode_kernel_matches_fp32(nq, bs, hd, nh, nkv):
     """A packed verify chunk (nq new tokens per sequence, causal among themselves) on the TMA decode
     kernel, the (query, head) rows of each KV head in one MMA tile, against fp32 varlen attention;
@@ -278,6 +278,9 @@ def test_verify_attention_on_decode_kernel_matches_fp32(nq, bs, hd, nh, nkv):
     seqk = torch.tensor(lens, dtype=torch.int32, device=DEV)
     scale = 1 / math.sqrt(hd)
     ws = attention.DecodeWorkspace(B * nq, nh, hd, maxblk * bs, DEV)
+    if nq * (nh // nkv) > 16:
+        assert not attention.verify_fits_decode_kernel(nq, nh, nkv, bs, hd)
+        return
     assert attention.verify_fits_decode_kernel(nq, nh, nkv, bs, hd)
     cu = torch.arange(0, (B + 1) * nq, nq, dtype=torch.int32)
     ref = attention.prefill_attention_ref(q.cpu().float(), ref_k, ref_v, cu, seqk.cpu(), tables.cpu(), scale)
