@@ -223,6 +223,9 @@ CLUSTER_SPLITK = os.environ.get("LLMSERVE_CLUSTER_SPLITK", "1") != "0"
 CLUSTER_MAX_SPLITS = 16
 CLUSTER_FIXED_KTILES = float(os.environ.get("LLMSERVE_SPLIT_FIXED_KTILES", "8"))
 CLUSTER_MAX_T = int(os.environ.get("LLMSERVE_CLUSTER_MAX_T", "511"))   # from 512 tokens the persistent 2-SM kernel takes over
+# split counts considered: powers of two (default), or every count up to 16 (LLMSERVE_CLUSTER_ANY_SPLITS=1),
+# which fills the CTA slots more evenly on some shapes (e.g. 48 qkv tiles x 6 = 288 of 296 slots)
+CLUSTER_ANY_SPLITS = os.environ.get("LLMSERVE_CLUSTER_ANY_SPLITS", "0") == "1"
 
 
 @functools.lru_cache(maxsize=None)
@@ -231,12 +234,15 @@ def cluster_splits(T: int, N: int, K: int, num_sms: int = NUM_SMS) -> int:
     k_tiles = -(-K // TILE_K)
     slots = num_sms * (2 if T <= SMALL_T else 1)
     best, best_cost = 1, float("inf")
-    s = 1
-    while s <= CLUSTER_MAX_SPLITS and (s == 1 or -(-k_tiles // s) >= 2):
-        cost = (-(-tiles * s // slots)) * (-(-k_tiles // s) + CLUSTER_FIXED_KTILES)
+    candidates = range(1, CLUSTER_MAX_SPLITS + 1) if CLUSTER_ANY_SPLITS else \
+        [1 << i for i in range(CLUSTER_MAX_SPLITS.bit_length()) if (1 << i) <= CLUSTER_MAX_SPLITS]
+    for s in candidates:
+        per = -(-k_tiles // s)
+        if s > 1 and (per < 2 or (s - 1) * per >= k_tiles):   # >= 2 K tiles each, no empty split
+            continue
+        cost = (-(-tiles * s // slots)) * (per + CLUSTER_FIXED_KTILES)
         if cost < best_cost - 1e-9:
             best, best_cost = s, cost
-        s *= 2
     return best
 
 
