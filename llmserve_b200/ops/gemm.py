@@ -223,8 +223,9 @@ CLUSTER_SPLITK = os.environ.get("LLMSERVE_CLUSTER_SPLITK", "1") != "0"
 CLUSTER_MAX_SPLITS = 16
 CLUSTER_FIXED_KTILES = float(os.environ.get("LLMSERVE_SPLIT_FIXED_KTILES", "8"))
 CLUSTER_MAX_T = int(os.environ.get("LLMSERVE_CLUSTER_MAX_T", "511"))   # from 512 tokens the persistent 2-SM kernel takes over
-# split counts considered: powers of two (default), or every count up to 16 (LLMSERVE_CLUSTER_ANY_SPLITS=1),
-# which fills the CTA slots more evenly on some shapes (e.g. 48 qkv tiles x 6 = 288 of 296 slots)
+# split counts considered: powers of two (default), or every count up to 16 (LLMSERVE_CLUSTER_ANY_SPLITS=1).
+# The latter fills the CTA slots more evenly on paper (48 qkv tiles x 6 = 288 of 296 slots) but measured
+# slower on a B200 (Qwen3-8B decode step at C = 64: 5.85-5.90 ms against 4.48-4.53 ms), so it stays off.
 CLUSTER_ANY_SPLITS = os.environ.get("LLMSERVE_CLUSTER_ANY_SPLITS", "0") == "1"
 
 
