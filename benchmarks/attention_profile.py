@@ -1,4 +1,4 @@
-"""Prefill attention kernels on one GPU: the tcgen05 kernel, the mma.sync kernel and flash-attn.
+"""Prefill and tree-verify attention kernels on one GPU: tcgen05 vs mma.sync / CUDA-core vs flash-attn / SDPA.
 
 ``python -m benchmarks.attention_profile [--heads 32] [--kv-heads 8] [--head-dim 128] [--iters 20]``
 
@@ -9,6 +9,12 @@ blocks):
 * ``batch8x512``   eight 512-token prompts;
 * ``chunk2048``    a 2048-token chunk after a cached 2048-token prefix (chunked prefill);
 * ``mixed``        the mixed-serving shape: 4 x 128 + 1 x 4096 prompts in one step.
+
+Tree-verify workloads (``--workloads tree10_p2048,...``; EAGLE3 tree speculation of one sequence:
+``n`` draft-tree nodes against a ``p``-token prefix in the pool plus the tree's own keys under the
+ancestor mask of the fixed tree topology): the tcgen05 tree kernel, the CUDA-core tree kernel and
+the reference's formulation (gather the prefix pages, concatenate the tree keys, masked SDPA), with
+the K/V bytes each KV head must read once as the roofline.
 
 Each kernel is timed with CUDA events around ``--iters`` back-to-back calls after warm-up (inputs
 stay L2-resident only for the smallest workloads; the numbers are per call).  FLOPs count the
@@ -38,6 +44,78 @@ WORKLOADS = {
     "chunk2048": [(2048, 4096)],
     "mixed": [(128, 128)] * 4 + [(4096, 4096)],
 }
+
+
+TREE_WORKLOADS = {          # (draft nodes of the fixed EAGLE3 tree, prefix tokens)
+    "tree6_p512": (6, 512),
+    "tree10_p2048": (10, 2048),
+    "tree10_p4096": (10, 4096),
+}
+
+
+def _hbm_peak():
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 6650.0
+
+
+def tree_row(name, nh, nkv, hd, bs, timed, dev, g):
+    """One tree-verify workload: tcgen05 kernel vs CUDA-core kernel vs gather + masked SDPA."""
+    import torch
+    import torch.nn.functional as F
+
+    from llmserve_b200.ops import attention
+    from llmserve_b200.speculative.tree import build_fixed_tree_topology
+    n, prefix = TREE_WORKLOADS[name]
+    topo = build_fixed_tree_topology(n)
+    n = len(topo.parents)
+    nblk = -(-prefix // bs)
+    kc = (torch.randn(nblk, nkv, bs, hd, device=dev, generator=g) * 0.5).bfloat16()
+    vc = torch.randn(nblk, nkv, bs, hd, device=dev, generator=g).bfloat16()
+    table = torch.randperm(nblk, device=dev).to(torch.int32)
+    q = torch.randn(n, nh, hd, device=dev, generator=g).bfloat16()
+    tk = (torch.randn(n, nkv, hd, device=dev, generator=g) * 0.5).bfloat16()
+    tv = torch.randn(n, nkv, hd, device=dev, generator=g).bfloat16()
+    mask = topo.attention_mask(dev)
+    w = 1 << torch.arange(n, dtype=torch.int64, device=dev)
+    bits = (mask.long() * w).sum(1).to(torch.int32)
+    scale = 1.0 / math.sqrt(hd)
+
+    def run(tc):
+        saved = attention.TREE_TC
+        attention.TREE_TC = tc
+        try:
+            return attention.tree_attention(q, kc, vc, table, prefix, tk, tv, mask, scale, bits)
+        finally:
+            attention.TREE_TC = saved
+
+    full_mask = torch.cat([torch.ones(n, prefix, dtype=torch.bool, device=dev), mask], 1)
+
+    def sdpa():
+        k = torch.cat([attention._gather_pages(kc, table, prefix), tk], 0)
+        v = torch.cat([attention._gather_pages(vc, table, prefix), tv], 0)
+        G = nh // nkv
+        kk = k.transpose(0, 1).repeat_interleave(G, 0)
+        vv = v.transpose(0, 1).repeat_interleave(G, 0)
+        return F.scaled_dot_product_attention(q.transpose(0, 1), kk, vv, attn_mask=full_mask,
+                                              scale=scale).transpose(0, 1)
+
+    tc, cc, ref = run(True), run(False), sdpa()
+    torch.cuda.synchronize()
+    err = lambda a: float(((a.float() - ref.float()).norm() / ref.float().norm()).item())
+    kv_bytes = 2 * (prefix + n) * nkv * hd * 2
+    row = {"workload": name, "tree_nodes": n, "prefix": prefix, "heads": nh, "kv_heads": nkv, "head_dim": hd,
+           "block_size": bs, "kv_mb": round(kv_bytes / 1e6, 2), "tc_rel_err_vs_sdpa": err(tc),
+           "cuda_core_rel_err_vs_sdpa": err(cc)}
+    for key, fn in (("tc", lambda: run(True)), ("cuda_core", lambda: run(False)), ("sdpa", sdpa)):
+        us = timed(fn)
+        row[f"{key}_us"] = round(us, 1)
+        row[f"{key}_gbs"] = round(kv_bytes / us / 1e3, 1)
+    row["tc_fraction_of_measured_hbm"] = round(row["tc_gbs"] / _hbm_peak(), 3)
+    return row
 
 
 def _peak():
@@ -84,6 +162,9 @@ def main(argv=None):
 
     g = torch.Generator(device=dev).manual_seed(0)
     for name in args.workloads.split(","):
+        if name in TREE_WORKLOADS:
+            print(json.dumps(tree_row(name, nh, nkv, hd, bs, timed, dev, g)), flush=True)
+            continue
         shapes = WORKLOADS[name]
         nblk_seq = [-(-k // bs) for _, k in shapes]
         nblk = sum(nblk_seq)

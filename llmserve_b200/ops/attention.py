@@ -15,7 +15,9 @@ region for the prefill->decode KV push.
   covers plain prefill, chunked prefill, prefix-cache hits and the packed EAGLE3 verify.
   Query ``j`` of a chunk of ``q_len`` against ``k_len`` keys sees keys ``< k_len - q_len + j + 1``.
 * ``tree_attention``    -- EAGLE3 tree verify: prefix keys from the pool (all visible) plus the
-  tree nodes' own keys under an ancestor mask (``attention.py:77-109`` of the reference).
+  tree nodes' own keys under an ancestor mask (``attention.py:77-109`` of the reference).  On the
+  tcgen05 kernel (``tree_sm100.cu``) the (node, head) rows of one KV head share a 128-row MMA tile
+  and the prefix is split over the SMs; the CUDA-core kernel takes the shapes it does not.
 """
 import math
 import os
@@ -191,6 +193,10 @@ def prefill_attention(q, k_cache, v_cache, cu_seqlens_q, seqlens_k, block_tables
     return out
 
 
+# tree verify on the tcgen05 kernel (LLMSERVE_TREE_TC=0: the CUDA-core kernel)
+TREE_TC = os.environ.get("LLMSERVE_TREE_TC", "1") != "0"
+
+
 def tree_attention(q, k_cache, v_cache, block_table, prefix_len, tree_k, tree_v, tree_mask, scale,
                    mask_bits=None):
     """``tree_mask [n_q, n_tree]`` bool; on CUDA the kernel takes one int32 ancestor bitmask per
@@ -203,6 +209,13 @@ def tree_attention(q, k_cache, v_cache, block_table, prefix_len, tree_k, tree_v,
         w = 1 << torch.arange(n, dtype=torch.int64, device=q.device)
         mask_bits = (tree_mask.to(q.device).long() * w).sum(1).to(torch.int32)
     out = torch.empty_like(q)
+    n_tree = tree_k.shape[0]
+    if TREE_TC and C().tree_tc_supported(q.shape[0], q.shape[1], k_cache.shape[1], n_tree, k_cache.shape[2],
+                                         q.shape[2]):
+        C().tree_attention_tc(out, q.contiguous(), k_cache, v_cache, block_table.to(torch.int32).contiguous(),
+                              int(prefix_len), tree_k.contiguous(), tree_v.contiguous(), mask_bits.to(torch.int32),
+                              float(scale), status(q.device))
+        return out
     C().tree_attention(out, q.contiguous(), k_cache, v_cache, block_table.to(torch.int32), int(prefix_len),
                        tree_k.contiguous(), tree_v.contiguous(), mask_bits, float(scale), status(q.device))
     return out

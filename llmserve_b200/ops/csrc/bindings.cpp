@@ -65,6 +65,9 @@ void decode_attention_tma(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
                           at::Tensor status);
 bool decode_tma_supported(int64_t block_size, int64_t head_dim);
 bool prefill_tc_supported(int64_t block_size, int64_t head_dim);
+bool tree_tc_supported(int64_t n_q, int64_t nh, int64_t nkv, int64_t n_tree, int64_t block_size, int64_t head_dim);
+void tree_attention_tc(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor bt, int64_t prefix_len,
+                       at::Tensor tk, at::Tensor tv, at::Tensor mask_bits, double scale, at::Tensor status);
 void prefill_attention_tc(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor cu_q,
                           at::Tensor seqlens_k, at::Tensor block_tables, double scale, int64_t max_q,
                           at::Tensor status);
@@ -104,6 +107,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention_tc", &lsb::prefill_attention_tc);
   m.def("prefill_tc_supported", &lsb::prefill_tc_supported);
   m.def("tree_attention", &lsb::tree_attention);
+  m.def("tree_attention_tc", &lsb::tree_attention_tc);
+  m.def("tree_tc_supported", &lsb::tree_tc_supported);
   m.def("comm_alloc", &lsb::comm_alloc);
   m.def("comm_free", &lsb::comm_free);
   m.def("comm_ipc_handle", &lsb::comm_ipc_handle);
