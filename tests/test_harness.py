@@ -409,3 +409,14 @@ def test_b200_tp1_suite_expands_and_runs_with_a_fake_engine():
     assert all(kw["tensor_parallel_size"] == 1 for kw in seen)
     assert sum(bool(kw.get("enable_chunked_prefill")) for kw in seen) == 4
     assert sum(bool(kw.get("speculative_cuda_graphs")) for kw in seen) == 2
+
+
+def test_b200_two_gpu_suite_expands_to_tp2_and_pd_points():
+    """The two-GPU B200 suite: TP = 2 with the NCCL path and the fused collective at C = 1 / 64, and
+    the 1P1D disaggregated variant beside its one-GPU baseline at C = 16."""
+    suite = json.load(open("benchmarks/suites/b200-serving-2gpu.json"))
+    points = expand_suite(suite)
+    got = sorted((p["experiment"], p["variant"], p["max_concurrency"]) for p in points)
+    assert got == sorted([("bf16-closed-loop-tp2", v, c) for v in ("baseline", "fused") for c in (1, 64)] +
+                         [("pd-closed-loop-1p1d", v, 16) for v in ("baseline", "pd")])
+    assert all(p["runtime"]["tensor_parallel_size"] == 2 for p in points if p["experiment"].endswith("tp2"))

@@ -525,7 +525,8 @@ def _wrap_dev(ptr, nbytes, dtype):
 
 
 @pytest.mark.parametrize("reduce", [False, True])
-@pytest.mark.parametrize("world,T,packed", [(1, 5, False), (2, 64, True), (4, 7, True), (4, 64, False)])
+@pytest.mark.parametrize("world,T,packed", [(1, 5, False), (2, 64, True), (4, 7, True), (4, 64, False),
+                                            (8, 64, True), (8, 13, False)])
 @pytest.mark.parametrize("calls", [1, 2])
 def test_row_parallel_push_layout_single_gpu(world, T, packed, reduce, calls):
     """The fused row-parallel path's data layout on one GPU: each emulated rank's GEMM stores its
