@@ -7,14 +7,17 @@
 //                    features (load-time repacked so one feature's 64 codes are 8 consecutive
 //                    words), the 1 KiB scale/zero words of the tile's group, and the activation
 //                    tile (2-D tensor copy, 128B swizzle) into a ring (6 stages for decode).
-//   warps 2..9     : dequantisers (two CTAs per SM).  Thread t owns half of feature t % 128: each
-//                    32-bit word holds 8 codes placed
+//   warps 2..9     : dequantisers (two CTAs per SM).  Each thread owns half (32 K) of one feature
+//                    row: each 32-bit word holds 8 codes placed
 //                    so that (word >> 4i) & 0x000F000F | 0x43004300 is the bf16 pair (128+q, 128+q')
 //                    (exponent 2^7, codes in the low mantissa bits, exact); (pair - (128+z)) * s in
-//                    bf16x2 gives round((q - z) * s).  The result is stored into a double-buffered
-//                    bf16 operand tile in the 128B-swizzled K-major layout the MMA reads.
-//   warp 1, lane 0 : MMA issuer, four tcgen05.mma (K = 16) per K step into a TMEM accumulator;
-//                    commits free the ring stage and the operand buffer.
+//                    bf16x2 gives round((q - z) * s).  For decode-sized T the 16 pairs go straight
+//                    into a double-buffered operand in tensor memory (tcgen05.st, the row's TMEM
+//                    lane, so a warp writes the 32 rows of its lane quadrant); otherwise into a
+//                    double-buffered bf16 tile in the 128B-swizzled K-major layout in shared memory.
+//   warp 1, lane 0 : MMA issuer, four tcgen05.mma (K = 16) per K step into a TMEM accumulator, A
+//                    from tensor memory (or shared memory), B = the activation tile; commits free
+//                    the ring stage and the operand buffer.
 //   warps 2..9     : epilogue (tcgen05.ld), bf16 output or fp32 split-K partials.
 // Every wait is bounded (a timeout records an error code and the roles drain and return).
 // Every CTA issues its own TMA loads.
@@ -66,6 +69,13 @@ template <int BN>
 constexpr int qtmem_cols() {
   return BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
 }
+// With the dequantised operand in TMEM (TA): the accumulator's BN columns, then WB operand buffers of
+// 32 columns (128 rows x 64 K as bf16 pairs), rounded up to an allocatable power of two.
+template <int BN, int WB, bool TA>
+constexpr int qtmem_alloc() {
+  constexpr int need = TA ? (BN < 32 ? 32 : BN) + 32 * WB : qtmem_cols<BN>();
+  return need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
+}
 
 __device__ __forceinline__ uint64_t qdesc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
@@ -99,6 +109,23 @@ __device__ __forceinline__ void qmma(uint32_t tmem_d, uint64_t da, uint64_t db, 
       "l"(da), "l"(db), "r"(idesc), "r"(acc));
 }
 
+// A from tensor memory (the dequantised weight tile), B from shared memory (the activation tile)
+__device__ __forceinline__ void qmma_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void qst16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void qcommit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -121,7 +148,7 @@ __device__ __forceinline__ uint32_t bf2_sub_mul(uint32_t w, uint32_t z2, uint32_
   return *reinterpret_cast<uint32_t*>(&a);
 }
 
-template <int BN, int STAGES, int WB>
+template <int BN, int STAGES, int WB, bool TA = false>
 __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                           const uint32_t* __restrict__ qtiles,
                                                           const uint2* __restrict__ sztiles, bf16* __restrict__ out,
@@ -166,7 +193,7 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(qtmem_cols<BN>()));
+                 "r"(qtmem_alloc<BN, WB, TA>()));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -230,10 +257,18 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t wa = smem_u32(smem + L::kWOff + b * kWTile);
         const uint32_t xa = smem_u32(smem + s * L::kStage);
+        if constexpr (TA) {
+          // operand buffer b: TMEM columns [acc + 32 b, +32), 8 columns (16 K) per MMA
+          const uint32_t ta = tmem + (uint32_t)((BN < 32 ? 32 : BN) + 32 * b);
 #pragma unroll
-        for (int k = 0; k < QBK / 16; ++k) qmma(tmem, qdesc_sw128(wa + k * 32), qdesc_sw128(xa + k * 32), idesc, (i | k) != 0);
+          for (int k = 0; k < QBK / 16; ++k) qmma_ta(tmem, ta + k * 8, qdesc_sw128(xa + k * 32), idesc, (i | k) != 0);
+        } else {
+          const uint32_t wa = smem_u32(smem + L::kWOff + b * kWTile);
+#pragma unroll
+          for (int k = 0; k < QBK / 16; ++k)
+            qmma(tmem, qdesc_sw128(wa + k * 32), qdesc_sw128(xa + k * 32), idesc, (i | k) != 0);
+        }
         qcommit(&empty[s]);
         qcommit(&wempty[b]);
       }
@@ -244,11 +279,15 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
     // ---- dequantise: thread t owns half h = t / 128 (words 4h..4h+3) of feature row r = t % 128 ----
     pdl_wait();
     const int t = threadIdx.x - 64;
-    const int r = t & 127, h = t >> 7;
+    // TA: a warp may only reach TMEM lanes 32 (warp % 4) .. +31, so row r follows the warp's lanes
+    const int r = TA ? (warp & 3) * 32 + lane : t & 127;
+    const int h = TA ? (warp - 2) >> 2 : t >> 7;
     bool ok = true;
     for (int i = 0; i < nk; ++i) {
       const int s = i % STAGES, b = i % WB;
-      if (!mbar_wait(&full[s], (i / STAGES) & 1) || !mbar_wait(&wempty[b], ((i / WB) & 1) ^ 1) || *aborted) {
+      bool ready = mbar_wait(&full[s], (i / STAGES) & 1) && mbar_wait(&wempty[b], ((i / WB) & 1) ^ 1) && !*aborted;
+      if (TA) ready = __all_sync(0xffffffffu, ready);   // tcgen05.st below is warp-collective
+      if (!ready) {
         record_error(status, kTimeoutTmaFull);
         *aborted = 1;
         ok = false;
@@ -262,19 +301,32 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
                    : "=r"(words[0]), "=r"(words[1]), "=r"(words[2]), "=r"(words[3])
                    : "r"(st + L::kX + r * 32 + h * 16));
       asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(sz.x), "=r"(sz.y) : "r"(st + L::kX + kQTile + r * 8));
-      const uint32_t wbase = smem_u32(smem + L::kWOff + b * kWTile) + r * 128;
+      if constexpr (TA) {
+        // 32 K elements of row r as 16 bf16 pairs -> TMEM lane r, columns [acc + 32 b + 16 h, +16)
+        uint32_t d[16];
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const int c = h * 4 + cc;
-        const uint32_t v = words[cc];
-        uint32_t d[4];
+        for (int cc = 0; cc < 4; ++cc)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) d[j] = bf2_sub_mul(((v >> (4 * j)) & 0x000F000Fu) | 0x43004300u, sz.y, sz.x);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(wbase + (((c ^ (r & 7))) << 4)), "r"(d[0]),
-                     "r"(d[1]), "r"(d[2]), "r"(d[3])
-                     : "memory");
+          for (int j = 0; j < 4; ++j)
+            d[cc * 4 + j] = bf2_sub_mul(((words[cc] >> (4 * j)) & 0x000F000Fu) | 0x43004300u, sz.y, sz.x);
+        qst16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((BN < 32 ? 32 : BN) + 32 * b + 16 * h), d);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      } else {
+        const uint32_t wbase = smem_u32(smem + L::kWOff + b * kWTile) + r * 128;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = h * 4 + cc;
+          const uint32_t v = words[cc];
+          uint32_t d[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) d[j] = bf2_sub_mul(((v >> (4 * j)) & 0x000F000Fu) | 0x43004300u, sz.y, sz.x);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(wbase + (((c ^ (r & 7))) << 4)), "r"(d[0]),
+                       "r"(d[1]), "r"(d[2]), "r"(d[3])
+                       : "memory");
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
       }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&wfull[b])) : "memory");
     }
@@ -376,13 +428,13 @@ __global__ void __launch_bounds__(kQThreads, 1) awq_gemm_kernel(const __grid_con
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(qtmem_cols<BN>()));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(qtmem_alloc<BN, WB, TA>()));
   }
 }
 
 // reduce: the `splits` K slices of a tile reduce in a thread-block cluster (splits <= 8, the tile
 // [BN][128] fp32 fitting in the ring + operand memory) and write bf16 `out` or one plane via `pd`.
-template <int BN, int WB>
+template <int BN, int WB, bool TA = false>
 void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out,
                 const PartDest& pd, int splits, int* status, bool reduce = false) {
   constexpr int ST = qstages<BN, WB>();
@@ -392,7 +444,7 @@ void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz,
   const int k_tiles = K / QBK;
   const int kps = (k_tiles + splits - 1) / splits;
   const CUtensorMap mx = activation_map(x, BN);
-  auto kern = awq_gemm_kernel<BN, ST, WB>;
+  auto kern = awq_gemm_kernel<BN, ST, WB, TA>;
   ensure_dynamic_smem((const void*)kern, L::kBytes);
   dim3 grid(((N + QBM - 1) / QBM) * ((T + BN - 1) / BN), 1, splits);
   const int cred = reduce && splits > 1 ? splits : 0;
@@ -420,6 +472,18 @@ void awq_launch(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz,
                      k_tiles, kps, cred, status);
 }
 
+// For decode-sized T (<= 128) with two operand buffers the dequantisers write the bf16 weight
+// operand into tensor memory (the MMA's A operand): no shared-memory stores and no async-proxy
+// fence per K step (Qwen3-8B AWQ decode step at C = 64: 4.73 ms against 5.02 ms through shared
+// memory).  LLMSERVE_AWQ_TMEM_A=0 selects the shared-memory operand.
+bool awq_tmem_a() {
+  static bool v = [] {
+    const char* e = std::getenv("LLMSERVE_AWQ_TMEM_A");
+    return !(e && std::atoi(e) == 0);
+  }();
+  return v;
+}
+
 int awq_wbuf() {
   static int v = [] {
     const char* e = std::getenv("LLMSERVE_AWQ_WBUF");
@@ -432,6 +496,12 @@ template <int BN>
 void awq_launch_any(const at::Tensor& x, const at::Tensor& qt, const at::Tensor& sz, int N, bf16* out,
                     const PartDest& pd, int splits, int* status, bool reduce) {
   const int wb = awq_wbuf();
+  if constexpr (BN <= 128) {
+    if (wb == 2 && awq_tmem_a()) {
+      awq_launch<BN, 2, true>(x, qt, sz, N, out, pd, splits, status, reduce);
+      return;
+    }
+  }
   if (wb >= 8) awq_launch<BN, 8>(x, qt, sz, N, out, pd, splits, status, reduce);
   else if (wb >= 4) awq_launch<BN, 4>(x, qt, sz, N, out, pd, splits, status, reduce);
   else if (wb == 1) awq_launch<BN, 1>(x, qt, sz, N, out, pd, splits, status, reduce);
