@@ -118,7 +118,7 @@ def main(argv=None):
         for T in tokens:
             x = torch.randn(T, k, device=dev, generator=g).bfloat16()
             res = torch.randn(T, args.hidden, device=dev, generator=g).bfloat16()
-            splits = min(gemm.splits_for(T, w, streamk=False), 8)
+            splits = min(gemm.splits_for(T, w), 8)
             # with the cluster-reduced GEMM the K splits meet on chip: one fp32 plane per row crosses
             planes = 1 if gemm.use_cluster(T, w) else splits
             row = {"tokens": T, "world": world, "hidden": args.hidden, "inner_shard": k, "planes": planes}
@@ -127,7 +127,7 @@ def main(argv=None):
             if planes == 1:
                 row["gemm_us"] = timed(lambda: gemm.linear_reduced(x, next_w(), plane=True))
             else:
-                row["gemm_us"] = timed(lambda: gemm.linear_partials(x, next_w(), splits, streamk=False))
+                row["gemm_us"] = timed(lambda: gemm.linear_partials(x, next_w(), splits))
 
             def nccl():
                 y = gemm.linear(x, next_w())

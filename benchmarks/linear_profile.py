@@ -157,7 +157,7 @@ def measure_dense_cuda(shape: LinearShape, *, num_tokens: int, device, warmup: i
         check_status(device)
         out = {"ms": ms, "weight_bytes": wbytes, "l2_rotation_copies": copies,
                "achieved_weight_gbps": wbytes / (ms * 1e-3) / 1e9,
-               "path": "stream-K + reduce" if gemm.streamk_plan(num_tokens, shape.output_size, shape.input_size)
+               "path": "cluster split-K tile kernel" if gemm.use_cluster(num_tokens, packed[0][1])
                else "tile kernel"}
         if hbm_gbs:
             out["fraction_of_measured_hbm"] = out["achieved_weight_gbps"] / hbm_gbs

@@ -136,10 +136,6 @@ class MergedColumnParallelLinear(ColumnParallelLinear):
     def forward_silu(self, x):
         if self.interleaved:
             return gemm.linear_silu(x, self.gemm_weight)
-        if x.is_cuda and self.quant_method is None and self.bias is None:
-            y = gemm.gate_up_silu(x, self.gemm_weight)
-            if y is not None:
-                return y
         from llmserve_b200.ops import activation
         return activation.silu_and_mul(self.forward(x))
 

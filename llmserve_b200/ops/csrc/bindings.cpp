@@ -73,10 +73,6 @@ void prefill_attention_tc(at::Tensor out, at::Tensor q, at::Tensor kc, at::Tenso
                           at::Tensor status);
 void awq_gemm(at::Tensor out, at::Tensor x, at::Tensor qtiles, at::Tensor sztiles, int64_t n, at::Tensor partials,
               int64_t splits, at::Tensor status);
-void gemm_bf16_streamk(at::Tensor partials, at::Tensor x, at::Tensor w, int64_t n, int64_t grid, int64_t stages,
-                       at::Tensor status);
-int64_t streamk_slots(int64_t m_tiles, int64_t k_tiles, int64_t grid);
-void splitk_silu_halves(at::Tensor out, at::Tensor partials);
 void greedy_accept(at::Tensor out, at::Tensor target, at::Tensor draft, at::Tensor start);
 void feed_ids(at::Tensor out, at::Tensor ids, at::Tensor feed, at::Tensor prev, at::Tensor status);
 void kv_push(at::Tensor src_k, at::Tensor src_v, at::Tensor dst_k, at::Tensor dst_v, at::Tensor src_ids,
@@ -127,9 +123,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("splitk_silu", &lsb::splitk_silu);
   m.def("silu_and_mul_interleaved", &lsb::silu_and_mul_interleaved);
   m.def("gemm_bf16_silu_packed", &lsb::gemm_bf16_silu_packed);
-  m.def("splitk_silu_halves", &lsb::splitk_silu_halves);
-  m.def("gemm_bf16_streamk", &lsb::gemm_bf16_streamk);
-  m.def("streamk_slots", &lsb::streamk_slots);
   m.def("kv_push", &lsb::kv_push);
   m.def("feed_ids", &lsb::feed_ids);
   m.def("greedy_accept", &lsb::greedy_accept);

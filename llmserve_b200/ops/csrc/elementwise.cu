@@ -925,17 +925,6 @@ void splitk_silu(at::Tensor out, at::Tensor partials) {
 }
 
 // Same for a [gate | up] projection (the layout the checkpoint loader writes).
-void splitk_silu_halves(at::Tensor out, at::Tensor partials) {
-  check_bf16(out, "out");
-  LSB_CHECK(partials.scalar_type() == at::kFloat && partials.is_contiguous() && partials.dim() == 3, "bad partials");
-  const int S = partials.size(0), T = partials.size(1), N = partials.size(2);
-  LSB_CHECK(N % 2 == 0 && out.numel() == (int64_t)T * (N / 2), "gate/up shape mismatch");
-  if (T == 0) return;
-  const at::cuda::CUDAGuard g(out.device());
-  launch_pdl(splitk_silu_kernel<false>, grid_for((int64_t)T * N / 2, 256), 256, 0, stream(), (bf16*)out.data_ptr(),
-             partials.data_ptr<float>(), S, T, N);
-}
-
 void argmax_rows(at::Tensor out_idx, at::Tensor out_val, at::Tensor logits) {
   LSB_CHECK(logits.is_cuda() && logits.is_contiguous() && logits.dim() == 2, "logits must be a contiguous CUDA matrix");
   const int64_t B = logits.size(0), V = logits.size(1);

@@ -111,60 +111,6 @@ def linear_ref(x: torch.Tensor, w, bias: torch.Tensor | None = None) -> torch.Te
     return F.linear(x, w, bias)
 
 
-# Stream-K decode GEMM: opt-in (LLMSERVE_STREAMK_MAX_T=64).  Measured on B200 at T = 16 and 64 for the
-# Qwen3-8B projections it was 0-12% slower than the split-K tile kernel with two CTAs per SM, so
-# the engine keeps the tile kernel by default.
-STREAMK_MAX_T = int(os.environ.get("LLMSERVE_STREAMK_MAX_T", "0"))
-STREAMK_MAX_SLOTS = 8          # partial planes the reducers take
-STREAMK_MIN_UNITS = int(os.environ.get("LLMSERVE_STREAMK_MIN_UNITS", "8"))   # 128 x 64 weight tiles per CTA
-STREAMK_CTAS_PER_SM = int(os.environ.get("LLMSERVE_STREAMK_CTAS", "2"))      # 2: 4-stage rings, 1: 8-stage
-
-
-def _owner(u: int, U: int, G: int) -> int:
-    """CTA whose stream-K range [floor(c U / G), floor((c + 1) U / G)) holds unit ``u``."""
-    return ((u + 1) * G + U - 1) // U - 1
-
-
-def streamk_slots(m_tiles: int, k_tiles: int, grid: int) -> int:
-    """Partial planes the stream-K schedule needs: the most CTAs that share one weight tile
-    (the same arithmetic as the kernel)."""
-    U = m_tiles * k_tiles
-    return max(_owner((m + 1) * k_tiles - 1, U, grid) - _owner(m * k_tiles, U, grid) + 1 for m in range(m_tiles))
-
-
-@functools.lru_cache(maxsize=None)
-def streamk_plan(T: int, N: int, K: int, num_sms: int = NUM_SMS):
-    """``(grid, slots, stages)`` of the persistent stream-K GEMM for a decode-sized product, or None when
-    the plain tile kernel is the better fit (prefill-sized T, or more weight tiles than two waves
-    -- e.g. the LM head -- where balancing gains little and fp32 partials would cost more)."""
-    if T < 1 or T > STREAMK_MAX_T:
-        return None
-    return streamk_schedule(N, K, num_sms)
-
-
-def streamk_schedule(N: int, K: int, num_sms: int = NUM_SMS, ctas_per_sm: int | None = None):
-    """``(grid, slots, stages)`` for an [N, K] weight, whatever the token count (the kernel takes
-    up to 128 tokens); None when the weight has two waves of tiles or more."""
-    ctas = ctas_per_sm or STREAMK_CTAS_PER_SM
-    m_tiles, k_tiles = -(-N // TILE_M), -(-K // TILE_K)
-    if m_tiles >= 2 * num_sms:
-        return None
-    U = m_tiles * k_tiles
-    grid = max(1, min(ctas * num_sms, U // STREAMK_MIN_UNITS))
-    while grid > 1 and streamk_slots(m_tiles, k_tiles, grid) > STREAMK_MAX_SLOTS:
-        grid -= 1
-    slots = streamk_slots(m_tiles, k_tiles, grid)
-    if slots > STREAMK_MAX_SLOTS:
-        return None
-    return grid, slots, (8 if ctas == 1 else 4)
-
-
-def _streamk_for(T: int, w, allow: bool):
-    if not allow or not isinstance(w, PackedWeight) or not w.data.is_cuda:
-        return None
-    return streamk_plan(T, w.n, w.k, _num_sms(w.data.device))
-
-
 @functools.lru_cache(maxsize=None)
 def _num_sms_cached(index: int) -> int:
     return torch.cuda.get_device_properties(index).multi_processor_count
@@ -174,29 +120,22 @@ def _num_sms(device) -> int:
     return _num_sms_cached(device.index if device.index is not None else torch.cuda.current_device())
 
 
-def splits_for(T: int, w, streamk: bool = True) -> int:
-    """Partial planes of a [T, K] x W^T product: the stream-K slot count for a decode-sized
-    product over a tile-packed weight (``streamk``), else the K split count.  AWQ splits are
-    rounded down to a power of two, at most 8."""
+def splits_for(T: int, w) -> int:
+    """Partial planes of a [T, K] x W^T product: the K split count.  AWQ splits are rounded down
+    to a power of two, at most 8."""
     from llmserve_b200.ops import awq as awq_ops
     if isinstance(w, awq_ops.AWQPacked):
         s = min(awq_ops.choose_awq_splits(T, w.n, w.k), 8)
         return 1 << (s.bit_length() - 1)
-    plan = _streamk_for(T, w, streamk)
-    if plan is not None:
-        return plan[1]
     return choose_splits(T, w.shape[0], w.shape[1])
 
 
-def _gemm(out, x, w, partials, splits, T, streamk: bool = True):
+def _gemm(out, x, w, partials, splits, T):
     from llmserve_b200.ops import awq as awq_ops
     if isinstance(w, awq_ops.AWQPacked):
         C().awq_gemm(out, x, w.qtiles, w.sztiles, w.n, partials, splits, status(x.device))
         return
-    plan = _streamk_for(T, w, streamk) if splits > 1 else None
-    if plan is not None and plan[1] == splits:
-        C().gemm_bf16_streamk(partials.view(splits, T, w.n), x, w.data, w.n, plan[0], plan[2], status(x.device))
-    elif isinstance(w, PackedWeight):
+    if isinstance(w, PackedWeight):
         C().gemm_bf16_packed(out, x, w.data, w.n, partials, splits, status(x.device), _stages(T))
     else:
         C().gemm_bf16(out, x, w, partials, splits, status(x.device), _stages(T))
@@ -289,7 +228,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -
     out = torch.empty(T, N, dtype=x.dtype, device=x.device)
     if T == 0:
         return out.view(*x.shape[:-1], N)
-    if use_cluster(T, w) and _streamk_for(T, w, True) is None:
+    if use_cluster(T, w):
         linear_reduced(x2, w, out)
         if bias is not None:
             out += bias
@@ -306,32 +245,15 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -
     return out.view(*x.shape[:-1], N)
 
 
-def linear_partials(x: torch.Tensor, w: torch.Tensor, splits: int, partials: torch.Tensor | None = None,
-                    streamk: bool = True):
+def linear_partials(x: torch.Tensor, w: torch.Tensor, splits: int, partials: torch.Tensor | None = None):
     """fp32 partial planes ``[splits, T, N]`` (not reduced) whose sum is ``x @ w^T``; ``splits``
-    comes from :func:`splits_for` with the same ``streamk`` choice."""
+    comes from :func:`splits_for`."""
     T, K = x.shape
     N = w.shape[0]
     if partials is None:
         partials = torch.empty(splits, T, N, dtype=torch.float32, device=x.device)
-    _gemm(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits, T, streamk)
+    _gemm(_empty(x.device, x.dtype), x.contiguous(), w, partials, splits, T)
     return partials
-
-
-def gate_up_silu(x: torch.Tensor, w) -> torch.Tensor | None:
-    """``silu(x @ gate^T) * (x @ up^T)`` for a ``[gate | up]`` weight when the decode stream-K
-    plan applies (the SiLU-mul kernel reduces the partial planes); None otherwise."""
-    x2 = x.reshape(-1, x.shape[-1])
-    T = x2.shape[0]
-    if not x.is_cuda or T == 0 or _streamk_for(T, w, True) is None:
-        return None
-    splits = splits_for(T, w)
-    if splits == 1:
-        return None
-    partials = linear_partials(x2.contiguous(), w, splits)
-    out = torch.empty(T, w.shape[0] // 2, dtype=x.dtype, device=x.device)
-    C().splitk_silu_halves(out, partials)
-    return out
 
 
 def interleave_gate_up(w: torch.Tensor) -> torch.Tensor:

@@ -124,7 +124,7 @@ class FusedComm:
         st = status(x.device)
         if isinstance(weight, awq_ops.AWQPacked):
             # W4A16
-            splits = min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS)
+            splits = min(gemm.splits_for(T, weight), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS)
             # decode-sized: the K splits reduce in a cluster and one plane crosses NVLink
             reduce = awq_ops.AWQ_CLUSTER and splits > 1 and T <= 128
             planes = 1 if reduce else splits
@@ -135,7 +135,7 @@ class FusedComm:
             data, n, packed = gemm._operand(weight)
             reduce = gemm.use_cluster(T, weight)
             splits = (gemm.cluster_splits(T, n, K) if reduce
-                      else min(gemm.splits_for(T, weight, streamk=False), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS))
+                      else min(gemm.splits_for(T, weight), ROW_PARALLEL_MAX_SPLITS, MAX_SPLITS))
             planes = 1 if reduce else splits
             C().gemm_bf16_to_owners(x, data, n, packed, self.inbox_ptrs, self.rank, rows, splits, reduce,
                                     self.epoch_ptr, st, gemm.stages_for_tokens(T))

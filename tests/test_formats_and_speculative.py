@@ -193,23 +193,6 @@ def test_awq_repack_matches_autoawq_dequant():
     assert torch.equal(awq_ops.dequantize_packed(packed), ref.t().contiguous())
 
 
-def test_streamk_schedule_slots_match_brute_force():
-    """The host plan's slot count equals the largest number of CTAs sharing a weight tile when
-    the units are dealt out in the kernel's contiguous ranges."""
-    from llmserve_b200.ops import gemm
-    for m, k, G in [(48, 64, 148), (32, 64, 148), (192, 64, 148), (32, 192, 148), (6, 64, 48), (32, 8, 32),
-                    (3, 5, 7), (1, 64, 8)]:
-        U = m * k
-        owners = [max(c for c in range(G) if c * U // G <= u) for u in range(U)]
-        want = max(len(set(owners[t * k:(t + 1) * k])) for t in range(m))
-        assert gemm.streamk_slots(m, k, G) == want
-    for T, N, K in [(64, 6144, 4096), (64, 4096, 4096), (64, 24576, 4096), (64, 4096, 12288), (1, 768, 4096)]:
-        grid, slots, stages = gemm.streamk_schedule(N, K)
-        assert 1 <= slots <= gemm.STREAMK_MAX_SLOTS and 1 <= grid <= 2 * 148 and stages in (4, 8)
-    assert gemm.streamk_schedule(151936, 4096) is None          # LM head: plain tiles
-    assert gemm.streamk_plan(300, 4096, 4096) is None           # prefill-sized T
-
-
 def test_packed_greedy_accept_matches_per_sequence_rule():
     from llmserve_b200.speculative.sampling import greedy_accept_packed
     g = torch.Generator().manual_seed(4)
