@@ -278,3 +278,16 @@ def test_awq_engine_on_the_host_matches_dequantized_dense_and_shards_over_gloo(t
     assert _gen(awq, 1) == ref
     assert _gen(awq, 2) == ref
     assert _gen(awq, 2, ckpts[1]) == ref          # with an EAGLE3 draft, tensor parallel
+
+
+@pytest.mark.parametrize("tp", [4, 8])
+def test_tp4_and_tp8_gloo_match_tp1(tmp_path, tp):
+    """The host side of TP = 4 / 8 (head, KV-head, MLP and vocab shards -- one KV head per rank at
+    TP = 8 --, seven RPC workers, the vocab-parallel argmax, an EAGLE3 draft on every rank) on gloo
+    CPU ranks: tokens equal TP = 1."""
+    cfg = dict(TINY, num_attention_heads=16, num_key_value_heads=8, head_dim=16)
+    path = write_qwen3_checkpoint(str(tmp_path / "t"), cfg, seed=3)
+    draft = write_eagle3_checkpoint(str(tmp_path / "d"), cfg, draft_vocab=512, seed=3)
+    ref = _gen(path, 1)
+    assert _gen(path, tp) == ref
+    assert _gen(path, tp, draft) == ref          # EAGLE3 chain speculation on every rank
