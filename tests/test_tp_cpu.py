@@ -291,3 +291,26 @@ def test_tp4_and_tp8_gloo_match_tp1(tmp_path, tp):
     ref = _gen(path, 1)
     assert _gen(path, tp) == ref
     assert _gen(path, tp, draft) == ref          # EAGLE3 chain speculation on every rank
+
+
+def test_disaggregated_tp4_prefill_tp4_decode_over_gloo(tmp_path):
+    """The disaggregated shape the benchmark asks for -- prefill TP = 4 on devices 0-3, decode TP = 4
+    on devices 4-7, each rank pushing its KV-head shard to its decode peer -- on gloo CPU ranks:
+    tokens equal a single TP = 1 engine's."""
+    cfg = dict(TINY, num_attention_heads=16, num_key_value_heads=8, head_dim=16)
+    path = write_qwen3_checkpoint(str(tmp_path / "t"), cfg, seed=5)
+    ref = _gen(path, 1)
+    g = torch.Generator().manual_seed(11)
+    prompts = [torch.randint(0, 1024, (int(n),), generator=g).tolist() for n in (9, 33, 17, 50)]
+    llm = LLM(path, device="cpu", enforce_eager=True, num_kvcache_blocks=64, kvcache_block_size=16, max_model_len=256,
+              tensor_parallel_size=4, comm_timeout_s=60, pd_disaggregation=True, pd_prefill_devices=(0, 1, 2, 3),
+              pd_decode_devices=(4, 5, 6, 7))
+    try:
+        llm.model_runner.sampler = GreedySampler()
+        out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=12, ignore_eos=True),
+                                                    use_tqdm=False)]
+        m = llm.get_metrics()["summary"]
+    finally:
+        llm.exit()
+    assert out == ref
+    assert m["pd"]["handoffs"] == 4 and m["pd"]["blocks_pushed"] > 0
